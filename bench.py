@@ -1,0 +1,365 @@
+#!/usr/bin/env python
+"""Benchmark of the quantized-GEMV hot path (BASELINE config c2).
+
+Workload ("step"): one decode token's FFN GEMVs of the Qwen2.5-0.5B shape with
+Q4_K weights - 24 layers x {gate 4864x896, up 4864x896, down 896x4864} = 72
+fused GEMVs over 72 distinct resident weight matrices (159.7 MB per step, above
+the 126 MB L2, so every step streams its weights from HBM).  Each GEMV
+quantizes its fp32 input to Q8_0 on the device and runs the fused integer
+GEMV, exactly the work of the reference's matmul_q_fused (src/quant.c:441).
+Weights and activations are seeded synthetic data (no checkpoints offline).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+value  : whole-job GB/s of algorithmic bytes (packed weights + fp32 x + fp32
+         out), inputs resident in HBM, one CUDA graph replay per step, CUDA
+         events on the launching stream, max over ranks.
+e2e    : the same metric through the reference-facing C ABI
+         (matmul_q_fused_batch with HOST arrays; weights registered once, like
+         the reference's load-time mmap), host<->device copies inside.
+N > 1  : every rank runs its own replica of the step on its GPU (the GEMV
+         metric shards by independent work; no collective on the data path),
+         so scaling is weak.
+--impl reference : the reference's own quant.c (oracle/_ref, the fastest
+         build this host runs, all host threads) on the same workload, rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "quantr-in-c_b200")
+sys.path.insert(0, PKG)
+
+import synth  # noqa: E402
+
+METRIC = "quantized GEMV HBM GB/s (% of 8 TB/s); decode tok/s at 1/2/4/8 B200 vs host CPU"
+HIDDEN, FFN, LAYERS = 896, 4864, 24
+Q4_K = 12
+NOMINAL_HBM_GBS = 8000.0
+FALLBACK_HBM_GBS = 6650.0
+# DRAM bytes (read + write) of one c2 GEMV launch pair, from the ncu capture
+# summarised in profiles/gemv_q4k_c2.md; None until captured.
+NCU_TRAFFIC_PER_GEMV = None
+
+
+def row_bytes(t, d):
+    return (d // synth.BLOCK_ELEMS[t]) * synth.BLOCK_BYTES[t]
+
+
+def step_shapes(layers):
+    """(type, n, d, input-kind) per GEMV of one step, in model order."""
+    out = []
+    for _ in range(layers):
+        out += [(Q4_K, FFN, HIDDEN, "x"), (Q4_K, FFN, HIDDEN, "x"), (Q4_K, HIDDEN, FFN, "h")]
+    return out
+
+
+def gemv_bytes(t, n, d, B):
+    return n * row_bytes(t, d) + 4 * d * B + 4 * n * B
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.device)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.strip()]
+        os.unlink(self.path)
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------- CPU reference --
+
+def cpu_reference_run(layers, B, steps, warmup, budget_s=None):
+    """Times the reference's matmul_q_fused on this host (oracle/_ref build).
+
+    Returns (GB/s, seconds, steps done, threads, variant, kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    threads = os.cpu_count() or 1
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
+    import oracle  # test infrastructure: the CPU baseline leg only
+    variant = oracle.best_cpu_variant()
+    if oracle.ref_available(variant):
+        lib, kind = oracle.RefLib(variant), "reference"
+    else:
+        lib, kind, variant = oracle.Oracle(), "port", "restatement"
+    rng = synth.rng_for(11)
+    shapes = step_shapes(layers)
+    ws = [synth.matrix(rng, t, n, d) for t, n, d, _ in shapes]
+    xs = {d: synth.activations(rng, B, d) for d in (HIDDEN, FFN)}
+    f = lib.fn["matmul_q_fused"]
+    import ctypes
+    outs = {n: np.empty(n, np.float32) for n in (HIDDEN, FFN)}
+
+    def one_step():
+        for (t, n, d, _), w in zip(shapes, ws):
+            for b in range(B):
+                f(outs[n].ctypes.data_as(ctypes.c_void_p), xs[d][b].ctypes.data_as(ctypes.c_void_p),
+                  w.ctypes.data_as(ctypes.c_void_p), t, n, d, threads)
+
+    for _ in range(warmup):
+        one_step()
+    done = 0
+    t0 = time.perf_counter()
+    while True:
+        one_step()
+        done += 1
+        el = time.perf_counter() - t0
+        if budget_s is None and done >= steps:
+            break
+        if budget_s is not None and (el >= budget_s or done >= 100000) and done >= 3:
+            break
+    el = time.perf_counter() - t0
+    nbytes = sum(gemv_bytes(t, n, d, B) for t, n, d, _ in shapes)
+    return nbytes * done / el / 1e9, el, done, threads, variant, kind
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    gbs, el, done, threads, variant, kind = cpu_reference_run(args.layers, args.batch, args.steps, args.warmup)
+    sample = (f"{done} full steps ({3 * args.layers} GEMVs each) of the workload, reference src/quant.c "
+              f"{variant} build, OpenMP threads={threads}")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": done, "warmup": args.warmup, "ms_per_step": round(el / done * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": config_dict(args),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    if kind == "reference" and variant != "scalar":
+        line["note"] = ("the reference's Q4_K kernel reads fp16 scales as integers (src/quant.c:302-303), so "
+                        "its values are wrong, but its memory traffic and instruction mix are the same")
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(args):
+    return {
+        "workload": (f"c2: Qwen2.5-0.5B FFN GEMVs, Q4_K weights, {args.layers} layers x "
+                     f"(gate {FFN}x{HIDDEN}, up {FFN}x{HIDDEN}, down {HIDDEN}x{FFN}), batch {args.batch}, "
+                     "Q8_0 activations quantized on the fly"),
+        "type": "Q4_K", "batch": args.batch, "layers": args.layers,
+        "weight_bytes_per_step": sum(n * row_bytes(t, d) for t, n, d, _ in step_shapes(args.layers)),
+        "l2": "inputs larger than L2: 159.7 MB of distinct weights cycled per step vs 126 MB L2",
+        "launch": "cuda_graph + programmatic dependent launch",
+        "parallelism": f"replicas x{args.gpus}",
+    }
+
+
+# ------------------------------------------------------------------- ours --
+
+def ours_arm(args):
+    import torch
+    import torch.distributed as dist
+
+    import quantr
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    L = quantr.lib()
+    assert L.quantr_gpu_init(local) == 0
+    dev = torch.device("cuda", local)
+    B = args.batch
+    shapes = step_shapes(args.layers)
+    rng = synth.rng_for(11)
+    host_w = [synth.matrix(rng, t, n, d) for t, n, d, _ in shapes]
+    dev_w = [torch.from_numpy(w).to(dev) for w in host_w]
+    xin = [torch.from_numpy(synth.activations(rng, B, HIDDEN if k == "x" else FFN)).to(dev)
+           for _, _, _, k in shapes]
+    outs = [torch.empty(B, n, device=dev) for _, n, _, _ in shapes]
+    ws_bytes = max(quantr.workspace_bytes(d, B) for _, _, d, _ in shapes)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    nbytes = sum(gemv_bytes(t, n, d, B) for t, n, d, _ in shapes)
+
+    def step(stream):
+        for (t, n, d, _), w, x, o in zip(shapes, dev_w, xin, outs):
+            quantr.gemv_dev(o.data_ptr(), n, x.data_ptr(), d, w.data_ptr(), t, n, d, B, ws.data_ptr(), ws_bytes,
+                            stream)
+
+    s = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(s):
+        c0 = quantr.launch_count()
+        step(s.cuda_stream)  # eager warm-up: sets kernel attributes before capture
+        launches_per_step = quantr.launch_count() - c0
+        s.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            step(s.cuda_stream)
+    torch.cuda.synchronize()
+    assert quantr.device_status(0) == 0
+
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    # Clock soak: untimed replays so the sampler sees the GPU under this load
+    # for ~1.5 s around the (much shorter) timed region.
+    t_soak = time.perf_counter()
+    while time.perf_counter() - t_soak < 1.5:
+        for _ in range(50):
+            graph.replay()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        ev0.record(s)
+        for _ in range(args.steps):
+            graph.replay()
+        ev1.record(s)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    assert quantr.device_status(0) == 0
+    gbs = world * nbytes * args.steps / (ms / 1e3) / 1e9
+    per_gpu = nbytes * args.steps / (ms / 1e3) / 1e9
+
+    # End to end through the reference-facing C ABI with host arrays.
+    for w in host_w:
+        quantr.register_weights(w)
+    hx = [synth.activations(rng, B, HIDDEN if k == "x" else FFN) for _, _, _, k in shapes]
+    h2d = sum(x.nbytes for x in hx)
+    d2h = sum(4 * B * n for _, n, _, _ in shapes)
+
+    def e2e_step():
+        for (t, n, d, _), w, x in zip(shapes, host_w, hx):
+            quantr.matmul_q_fused_batch(x, w, t, n, d)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e2e_s = time.perf_counter() - t0
+    te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_gbs = world * nbytes * args.steps / float(te.item()) / 1e9
+    for w in host_w:
+        quantr.unregister_weights(w)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        gbs_c, el, done, threads, variant, kind = cpu_reference_run(args.layers, B, 0, 1, budget_s=args.cpu_seconds)
+        cpu = {"value": round(gbs_c, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+               "sample": (f"{done} full steps ({len(shapes)} GEMVs each, {el:.1f} s) of the same workload, "
+                          f"reference src/quant.c {variant} build")}
+
+    peak, peak_kind = load_peaks()
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": config_dict(args),
+            "pct_of_8TBs_per_gpu": round(100.0 * per_gpu / NOMINAL_HBM_GBS, 2),
+            "tok_per_s": round(world * B * args.steps / (ms / 1e3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(per_gpu / peak, 4), "peak_source": peak_kind,
+                         "traffic": NCU_TRAFFIC_PER_GEMV,
+                         "kernel": "quantize(Q8_0) -> fused Q4_K GEMV pair, per step of 72 pairs"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "api": "matmul_q_fused_batch (host pointers)"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=LAYERS)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        ours_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,176 @@
+/*
+ * quantr_cuda.h -- C ABI of the B200 (sm_100a) quantized-GEMV library
+ * libquantr_cuda.so.
+ *
+ * Part 1 is a drop-in for the reference's hot-path API: the same symbol names,
+ * argument types and meanings as quantr-in-c's include/quant.h:84-92, so the
+ * reference's runtime (src/runtime.c:58-70 matmul_q -> matmul_q_fused) links
+ * against this library instead of src/quant.o unchanged.  These calls take
+ * HOST pointers and are synchronous, exactly like the CPU versions: results are
+ * in `out` when the call returns.  Weights passed as `w` are served from a
+ * device-resident copy when the host range was registered with
+ * quantr_gpu_register_weights(), otherwise they are copied up on every call.
+ *
+ * Part 2 is additive: device selection, weight registration, a sticky error
+ * code (the reference's entry points return void), a batched variant, and a
+ * stream-ordered device-pointer API for callers that keep activations in HBM.
+ *
+ * Numerics: every output is bit-identical to the reference's scalar build of
+ * src/quant.c (quantized activations, int32 unit sums and fp32 outputs), with
+ * one documented exception: for Q4_K the reference's vec_dot_q4K_q8_0
+ * (src/quant.c:291-369) reads fp16 scales as raw integers; this library
+ * computes the Q4_K dot product that the reference's dequantize_row defines
+ * (src/quant.c:180-195), combined per 32-element sub-block as
+ * (sc*isum - m*bsum)*d_x like its Q5_K kernel (src/quant.c:399).
+ */
+#ifndef QUANTR_CUDA_H
+#define QUANTR_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; everything declared here is
+ * exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* Block layouts, identical to include/quant.h:28-50 (packed, little-endian).
+ * Skipped when the reference's quant.h was included first. */
+#ifndef QUANT_H
+#define QK8_0 32
+#define QK_K 256
+#define K_SCALE_SIZE 12
+#pragma pack(push, 1)
+typedef struct { uint16_t d; int8_t qs[QK8_0]; } block_q8_0;
+typedef struct { uint16_t d; uint16_t dmin; uint8_t scales[K_SCALE_SIZE]; uint8_t qs[QK_K / 2]; } block_q4_K;
+typedef struct {
+    uint16_t d; uint16_t dmin; uint8_t scales[K_SCALE_SIZE]; uint8_t qh[QK_K / 8]; uint8_t qs[QK_K / 2];
+} block_q5_K;
+#pragma pack(pop)
+#endif
+
+/* GGML type ids accepted as `type` (reference include/gguf.h:28-42). */
+#define QUANTR_TYPE_F32  0u
+#define QUANTR_TYPE_Q8_0 8u
+#define QUANTR_TYPE_Q4_K 12u
+#define QUANTR_TYPE_Q5_K 13u
+#define QUANTR_TYPE_Q6_K 14u
+
+/* ---------------------------------------------------------------------------
+ * Part 1: reference-compatible entry points (host pointers, synchronous).
+ * -------------------------------------------------------------------------*/
+
+/* Replaces src/quant.c:143 quantize_row_q8_0 (include/quant.h:84).  x: k
+ * floats; y: k/32 blocks; a tail of k%32 elements is ignored. */
+void quantize_row_q8_0(const float* x, block_q8_0* y, int k);
+
+/* Replaces src/quant.c:160 dequantize_row (include/quant.h:85).  NULL src or
+ * an unknown type writes zeros, as the reference does. */
+void dequantize_row(float* out, const void* src, uint32_t type, int n);
+
+/* Replace src/quant.c:242/291/372/406 (include/quant.h:86-89).  `a` is one
+ * packed weight row of k columns, `b` k/32 Q8_0 activation blocks. */
+float vec_dot_q4K_q8_0(const block_q4_K* a, const block_q8_0* b, int k);
+float vec_dot_q5K_q8_0(const block_q5_K* a, const block_q8_0* b, int k);
+float vec_dot_q6K_q8_0(const void* a, const block_q8_0* b, int k);
+float vec_dot_q8_0_q8_0(const block_q8_0* a, const block_q8_0* b, int k);
+
+/* Replaces src/quant.c:441 matmul_q_fused (include/quant.h:91-92):
+ * out[i] = row_i(w) . x for n rows of d columns.  NULL w writes zeros; type 0
+ * is an fp32 GEMV; Q8_0/Q4_K/Q5_K/Q6_K quantize x to Q8_0 on the device and
+ * run the fused integer GEMV; any other type writes zeros (the reference's
+ * dequantize fallback yields zeros for types it cannot decode).  `threads` is
+ * accepted for signature compatibility and ignored. */
+void matmul_q_fused(float* out, const float* x, const void* w, uint32_t type, int n, int d, int threads);
+
+/* ---------------------------------------------------------------------------
+ * Part 2: additive API.
+ * -------------------------------------------------------------------------*/
+
+/* Error codes.  The reference-compatible calls return void and keep the
+ * reference's degrade-to-zeros behaviour; the first failure since the last
+ * quantr_gpu_clear_error() is kept and readable here. */
+enum {
+    QUANTR_OK = 0,
+    QUANTR_ERR_CUDA = 1,             /* a CUDA runtime call failed */
+    QUANTR_ERR_NO_DEVICE = 2,        /* no usable CUDA device */
+    QUANTR_ERR_BAD_ARG = 3,          /* NULL pointer / negative size / bad stride */
+    QUANTR_ERR_UNSUPPORTED_TYPE = 4, /* type is not F32/Q8_0/Q4_K/Q5_K/Q6_K */
+    QUANTR_ERR_OOM = 5,              /* device or pinned allocation failed */
+    QUANTR_ERR_DEVICE_TIMEOUT = 6,   /* a bounded in-kernel wait gave up */
+    QUANTR_ERR_TOO_LARGE = 7,        /* shape exceeds a kernel limit */
+    QUANTR_ERR_WORKSPACE = 8         /* caller workspace too small */
+};
+int quantr_gpu_last_error(void);
+void quantr_gpu_clear_error(void);
+const char* quantr_gpu_error_string(int code);
+
+/* Selects the CUDA device used by the Part 1 calls (default: device 0, or
+ * $QUANTR_DEVICE).  Idempotent; Part 1 calls initialise lazily. */
+int quantr_gpu_init(int device);
+/* Releases device buffers, registrations and the stream. */
+void quantr_gpu_shutdown(void);
+/* Number of kernel launches this library has issued (all devices). */
+uint64_t quantr_gpu_launch_count(void);
+
+/* Uploads `bytes` of read-only weights at host address `host` (e.g. the whole
+ * GGUF mapping, src/model.c:451-482) once; later Part 1 calls whose `w` lies
+ * inside a registered range read the device copy.  Overlapping ranges are
+ * rejected.  The host bytes must not change while registered. */
+int quantr_gpu_register_weights(const void* host, size_t bytes);
+int quantr_gpu_unregister_weights(const void* host);
+/* Device address backing host address `host`, or NULL if unregistered. */
+void* quantr_gpu_device_ptr(const void* host);
+
+/* B independent matmul_q_fused calls sharing the weights: out is B x n and x
+ * is B x d, both row-major host arrays.  Oracle: B separate reference calls. */
+void matmul_q_fused_batch(float* out, const float* x, const void* w, uint32_t type, int n, int d, int B);
+
+/* ---- stream-ordered device API (all pointers are device pointers) ------ */
+
+/* Workspace bytes quantr_gemv_dev needs for B tokens of d columns. */
+size_t quantr_gemv_workspace_bytes(int d, int B);
+
+/* out[t*ldo + r] = row_r(w) . x[t*ldx ...] for t < B, r < n, with on-device Q8_0
+ * quantization of x into `workspace`.  Asynchronous on `stream`
+ * (a cudaStream_t; NULL = legacy default stream).  Launches use programmatic
+ * dependent launch, so the weight stream of this GEMV overlaps the kernel that
+ * produced x.  Returns a QUANTR_* code. */
+int quantr_gemv_dev(float* out, long long ldo, const float* x, long long ldx, const void* w, uint32_t type,
+                    int n, int d, int B, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Q8_0 quantization of B rows of k floats into packed block_q8_0 arrays
+ * (B * (k/32) blocks), bit-identical to the reference quantize_row_q8_0. */
+int quantr_quantize_q8_0_dev(block_q8_0* y, const float* x, long long ldx, int k, int B, void* stream);
+
+/* GEMV over already-quantized activations given as packed block_q8_0 rows
+ * (B rows of d/32 blocks): the device counterpart of B vec_dot calls per row. */
+int quantr_gemv_q8act_dev(float* out, long long ldo, const block_q8_0* xq, const void* w, uint32_t type,
+                          int n, int d, int B, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Debug variant of quantr_gemv_dev that also writes the int32 partial sums of
+ * every 32-element unit: isum/bsum[(t*n + r)*U + u], U = units per row
+ * (d/32 for Q8_0, 8*(d/256) for the K types).  isum is sum(w_q * x_q) (Q6_K:
+ * w_q already offset by -32), bsum is sum(x_q).  Used by the parity tests to
+ * pin the integer stage bit for bit. */
+int quantr_gemv_partials_dev(float* out, int32_t* isum, int32_t* bsum, const float* x, const void* w,
+                             uint32_t type, int n, int d, int B, void* workspace, size_t workspace_bytes,
+                             void* stream);
+
+/* Device error word of the current device (DEVICE_TIMEOUT if any bounded
+ * in-kernel wait gave up since the last reset); synchronises `stream`. */
+int quantr_gpu_device_status(void* stream, int reset);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QUANTR_CUDA_H */

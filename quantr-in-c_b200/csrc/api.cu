@@ -1,0 +1,617 @@
+// api.cu -- C ABI of libquantr_cuda.so (declared in include/quantr_cuda.h).
+//
+// Part 1 (reference-compatible, host pointers, synchronous) keeps the
+// reference's contracts (src/quant.c:441-523): NULL weights or any failure give
+// a zero-filled `out`, nothing aborts, and the first failure is kept as a
+// sticky code.  Part 2 is the stream-ordered device API.
+#include "quantr_cuda.h"
+
+#include "formats.cuh"
+#include "kernels.cuh"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+
+namespace {
+
+using namespace qr;
+
+struct Region {
+    size_t bytes;
+    uint8_t* dev;
+};
+
+// One context serves the Part 1 calls (the reference calls them from one host
+// thread; the mutex only makes concurrent misuse safe, not parallel).
+struct Ctx {
+    bool ready = false;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    void* ws = nullptr;  // quantized-activation workspace
+    size_t ws_bytes = 0;
+    uint8_t* dbuf = nullptr;  // device staging: x | out+err | blocks | unregistered weights
+    size_t dbuf_bytes = 0;
+    uint8_t* hbuf = nullptr;  // pinned host staging
+    size_t hbuf_bytes = 0;
+    std::map<uintptr_t, Region> regions;  // keyed by host start address
+};
+
+std::recursive_mutex g_mu;
+Ctx g;
+int g_err = QUANTR_OK;
+bool g_warned = false;
+
+// Per-device error word for the device API.
+int* g_dev_err[64] = {};
+
+void set_err(int code)
+{
+    if (code == QUANTR_OK) return;
+    if (g_err == QUANTR_OK) g_err = code;
+    if (!g_warned) {
+        g_warned = true;
+        std::fprintf(stderr, "[quantr_cuda] error %d: %s\n", code, quantr_gpu_error_string(code));
+    }
+}
+
+int code_of(cudaError_t e)
+{
+    if (e == cudaSuccess) return QUANTR_OK;
+    if (e == cudaErrorMemoryAllocation) return QUANTR_ERR_OOM;
+    if (e == cudaErrorNoDevice || e == cudaErrorInsufficientDriver || e == cudaErrorInvalidDevice)
+        return QUANTR_ERR_NO_DEVICE;
+    if (e == cudaErrorInvalidConfiguration) return QUANTR_ERR_TOO_LARGE;
+    return QUANTR_ERR_CUDA;
+}
+
+size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
+
+int ensure_ready()
+{
+    if (g.ready) return QUANTR_OK;
+    int dev = 0;
+    if (const char* s = std::getenv("QUANTR_DEVICE")) dev = std::atoi(s);
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count <= 0) {
+        cudaGetLastError();
+        return QUANTR_ERR_NO_DEVICE;
+    }
+    if (dev < 0 || dev >= count) return QUANTR_ERR_NO_DEVICE;
+    cudaError_t e = cudaSetDevice(dev);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return code_of(e);
+    g.device = dev;
+    g.ready = true;
+    return QUANTR_OK;
+}
+
+int grow_dev(void** p, size_t* cap, size_t need)
+{
+    if (*cap >= need) return QUANTR_OK;
+    if (*p) {
+        cudaStreamSynchronize(g.stream);
+        cudaFree(*p);
+        *p = nullptr;
+        *cap = 0;
+    }
+    size_t sz = std::max(need, (size_t)1 << 20);
+    if (cudaMalloc(p, sz) != cudaSuccess) {
+        cudaGetLastError();
+        return QUANTR_ERR_OOM;
+    }
+    *cap = sz;
+    return QUANTR_OK;
+}
+
+int grow_host(size_t need)
+{
+    if (g.hbuf_bytes >= need) return QUANTR_OK;
+    if (g.hbuf) {
+        cudaStreamSynchronize(g.stream);
+        cudaFreeHost(g.hbuf);
+        g.hbuf = nullptr;
+        g.hbuf_bytes = 0;
+    }
+    size_t sz = std::max(need, (size_t)1 << 20);
+    if (cudaMallocHost((void**)&g.hbuf, sz) != cudaSuccess) {
+        cudaGetLastError();
+        return QUANTR_ERR_OOM;
+    }
+    g.hbuf_bytes = sz;
+    return QUANTR_OK;
+}
+
+// Device copy of [host, host+len) if a registered region covers it.
+const uint8_t* lookup(const void* host, size_t len)
+{
+    const uintptr_t h = (uintptr_t)host;
+    auto it = g.regions.upper_bound(h);
+    if (it == g.regions.begin()) return nullptr;
+    --it;
+    if (h + len > it->first + it->second.bytes) return nullptr;
+    return it->second.dev + (h - it->first);
+}
+
+// Device layout of one Part 1 call's staging buffer.
+struct Stage {
+    size_t x_off, out_off, err_off, blk_off, w_off, total;
+};
+
+Stage plan(size_t xbytes, size_t obytes, size_t blkbytes, size_t wbytes)
+{
+    Stage s{};
+    s.x_off = 0;
+    s.out_off = a256(xbytes);
+    s.err_off = s.out_off + ((obytes + 15) & ~size_t(15));
+    s.blk_off = a256(s.err_off + 16);
+    s.w_off = a256(s.blk_off + blkbytes);
+    s.total = s.w_off + a256(wbytes);
+    return s;
+}
+
+void zero_out(float* out, size_t count)
+{
+    if (out && count) std::memset(out, 0, count * sizeof(float));
+}
+
+// Shared body of matmul_q_fused / matmul_q_fused_batch.
+int fused_host(float* out, const float* x, const void* w, uint32_t type, int n, int d, int B)
+{
+    if (n <= 0 || B <= 0) return QUANTR_OK;
+    if (!out || !x || d < 0) return QUANTR_ERR_BAD_ARG;
+    if (type != T_F32 && !type_supported(type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
+    int rc = ensure_ready();
+    if (rc) return rc;
+    const size_t xbytes = (size_t)B * d * 4, obytes = (size_t)B * n * 4;
+    const size_t wbytes = (size_t)n * (size_t)row_bytes(type, d);
+    const uint8_t* wdev = lookup(w, wbytes);
+    Stage st = plan(xbytes, obytes, 0, wdev ? 0 : wbytes);
+    if ((rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total))) return rc;
+    if ((rc = grow_host(st.err_off + 16))) return rc;
+    const size_t need_ws = actq_bytes(d, B);
+    if (type != T_F32 && (rc = grow_dev(&g.ws, &g.ws_bytes, need_ws))) return rc;
+
+    float* dx = (float*)(g.dbuf + st.x_off);
+    float* dout = (float*)(g.dbuf + st.out_off);
+    int* derr = (int*)(g.dbuf + st.err_off);
+    std::memcpy(g.hbuf, x, xbytes);
+    cudaError_t e = cudaMemcpyAsync(dx, g.hbuf, xbytes, cudaMemcpyHostToDevice, g.stream);
+    if (!wdev && e == cudaSuccess) {
+        wdev = g.dbuf + st.w_off;
+        e = cudaMemcpyAsync((void*)wdev, w, wbytes, cudaMemcpyHostToDevice, g.stream);
+    }
+    LaunchCfg c;
+    c.stream = g.stream;
+    if (e == cudaSuccess) {
+        if (type == T_F32) {
+            e = cudaMemsetAsync(derr, 0, 4, g.stream);
+            if (e == cudaSuccess)
+                e = launch_gemv_f32((const float*)wdev, dx, d, dout, n, n, d, B, c);
+        } else {
+            ActQ a = actq_carve(g.ws, d, B);
+            e = launch_quantize(dx, d, d, B, a, nullptr, derr, c);
+            GemvArgs ga;
+            ga.w = wdev;
+            ga.type = type;
+            ga.n = n;
+            ga.d = d;
+            ga.x = a;
+            ga.out = dout;
+            ga.ldo = n;
+            ga.B = B;
+            ga.err = derr;
+            if (e == cudaSuccess) e = launch_gemv(ga, c);
+        }
+    }
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(g.hbuf, dout, st.err_off + 4 - st.out_off, cudaMemcpyDeviceToHost, g.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return code_of(e);
+    }
+    int dev_err = 0;
+    std::memcpy(&dev_err, g.hbuf + (st.err_off - st.out_off), 4);
+    if (dev_err) return QUANTR_ERR_DEVICE_TIMEOUT;
+    std::memcpy(out, g.hbuf, obytes);
+    return QUANTR_OK;
+}
+
+// Runs one GEMV row against pre-quantized activation blocks (vec_dot_*).
+float vec_dot_host(const void* a, const void* b, int k, uint32_t type)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (k <= 0 || row_bytes(type, k) == 0) return 0.0f;
+    if (!a || !b) {
+        set_err(QUANTR_ERR_BAD_ARG);
+        return 0.0f;
+    }
+    int rc = ensure_ready();
+    const size_t wbytes = (size_t)row_bytes(type, k);
+    const int nbx = k / 32;
+    const size_t blkbytes = (size_t)nbx * 34;
+    Stage st = plan(0, 4, blkbytes, wbytes);
+    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total);
+    if (!rc) rc = grow_host(std::max(blkbytes, (size_t)32));
+    if (!rc) rc = grow_dev(&g.ws, &g.ws_bytes, actq_bytes(k, 1));
+    if (rc) {
+        set_err(rc);
+        return 0.0f;
+    }
+    uint8_t* dblk = g.dbuf + st.blk_off;
+    uint8_t* dw = g.dbuf + st.w_off;
+    float* dout = (float*)(g.dbuf + st.out_off);
+    int* derr = (int*)(g.dbuf + st.err_off);
+    std::memcpy(g.hbuf, b, blkbytes);
+    cudaError_t e = cudaMemcpyAsync(dblk, g.hbuf, blkbytes, cudaMemcpyHostToDevice, g.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dw, a, wbytes, cudaMemcpyHostToDevice, g.stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(derr, 0, 4, g.stream);
+    LaunchCfg c;
+    c.stream = g.stream;
+    ActQ act = actq_carve(g.ws, k, 1);
+    if (e == cudaSuccess) e = launch_repack(dblk, nbx, 1, act, c);
+    GemvArgs ga;
+    ga.w = dw;
+    ga.type = type;
+    ga.n = 1;
+    ga.d = k;
+    ga.x = act;
+    ga.out = dout;
+    ga.ldo = 1;
+    ga.B = 1;
+    ga.err = derr;
+    if (e == cudaSuccess) e = launch_gemv(ga, c);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g.hbuf, dout, st.err_off + 4 - st.out_off, cudaMemcpyDeviceToHost, g.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_err(code_of(e));
+        return 0.0f;
+    }
+    int dev_err = 0;
+    std::memcpy(&dev_err, g.hbuf + (st.err_off - st.out_off), 4);
+    if (dev_err) {
+        set_err(QUANTR_ERR_DEVICE_TIMEOUT);
+        return 0.0f;
+    }
+    float r;
+    std::memcpy(&r, g.hbuf, 4);
+    return r;
+}
+
+int* dev_err_word()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    if (!g_dev_err[dev]) {
+        int* p = nullptr;
+        if (cudaMalloc(&p, 16) != cudaSuccess) {
+            cudaGetLastError();
+            return nullptr;
+        }
+        cudaMemset(p, 0, 16);
+        g_dev_err[dev] = p;
+    }
+    return g_dev_err[dev];
+}
+
+} // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------------ errors --
+
+int quantr_gpu_last_error(void) { return g_err; }
+
+void quantr_gpu_clear_error(void)
+{
+    g_err = QUANTR_OK;
+    g_warned = false;
+}
+
+const char* quantr_gpu_error_string(int code)
+{
+    switch (code) {
+    case QUANTR_OK: return "ok";
+    case QUANTR_ERR_CUDA: return "CUDA runtime call failed";
+    case QUANTR_ERR_NO_DEVICE: return "no usable CUDA device";
+    case QUANTR_ERR_BAD_ARG: return "invalid argument";
+    case QUANTR_ERR_UNSUPPORTED_TYPE: return "unsupported quantization type";
+    case QUANTR_ERR_OOM: return "allocation failed";
+    case QUANTR_ERR_DEVICE_TIMEOUT: return "bounded in-kernel wait timed out";
+    case QUANTR_ERR_TOO_LARGE: return "shape exceeds a kernel limit";
+    case QUANTR_ERR_WORKSPACE: return "workspace too small";
+    default: return "unknown error";
+    }
+}
+
+// ------------------------------------------------------------- lifecycle --
+
+int quantr_gpu_init(int device)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (g.ready) return g.device == device ? QUANTR_OK : QUANTR_ERR_BAD_ARG;
+    char buf[16];
+    std::snprintf(buf, sizeof buf, "%d", device);
+    setenv("QUANTR_DEVICE", buf, 1);
+    int rc = ensure_ready();
+    if (rc) set_err(rc);
+    return rc;
+}
+
+void quantr_gpu_shutdown(void)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!g.ready) return;
+    cudaStreamSynchronize(g.stream);
+    for (auto& kv : g.regions) cudaFree(kv.second.dev);
+    g.regions.clear();
+    if (g.ws) cudaFree(g.ws);
+    if (g.dbuf) cudaFree(g.dbuf);
+    if (g.hbuf) cudaFreeHost(g.hbuf);
+    cudaStreamDestroy(g.stream);
+    g = Ctx{};
+}
+
+uint64_t quantr_gpu_launch_count(void) { return (uint64_t)launch_count(); }
+
+// --------------------------------------------------------------- registry --
+
+int quantr_gpu_register_weights(const void* host, size_t bytes)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (!host || bytes == 0) return QUANTR_ERR_BAD_ARG;
+    int rc = ensure_ready();
+    if (rc) return rc;
+    const uintptr_t h = (uintptr_t)host;
+    auto it = g.regions.lower_bound(h);
+    if (it != g.regions.end() && it->first < h + bytes) return QUANTR_ERR_BAD_ARG;
+    if (it != g.regions.begin()) {
+        auto pv = std::prev(it);
+        if (pv->first + pv->second.bytes > h) return QUANTR_ERR_BAD_ARG;
+    }
+    uint8_t* dev = nullptr;
+    // 16 spare bytes keep every bulk-copy window of the last row in bounds.
+    if (cudaMalloc((void**)&dev, bytes + 16) != cudaSuccess) {
+        cudaGetLastError();
+        return QUANTR_ERR_OOM;
+    }
+    cudaError_t e = cudaMemcpy(dev, host, bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        cudaFree(dev);
+        cudaGetLastError();
+        return code_of(e);
+    }
+    g.regions[h] = Region{bytes, dev};
+    return QUANTR_OK;
+}
+
+int quantr_gpu_unregister_weights(const void* host)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    auto it = g.regions.find((uintptr_t)host);
+    if (it == g.regions.end()) return QUANTR_ERR_BAD_ARG;
+    cudaStreamSynchronize(g.stream);
+    cudaFree(it->second.dev);
+    g.regions.erase(it);
+    return QUANTR_OK;
+}
+
+void* quantr_gpu_device_ptr(const void* host)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    return (void*)lookup(host, 1);
+}
+
+// ------------------------------------------------- reference entry points --
+
+void matmul_q_fused(float* out, const float* x, const void* w, uint32_t type, int n, int d, int threads)
+{
+    (void)threads;
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (n <= 0) return;
+    if (!w) {  // src/quant.c:443-446
+        zero_out(out, (size_t)n);
+        return;
+    }
+    int rc = fused_host(out, x, w, type, n, d, 1);
+    if (rc) {
+        set_err(rc);
+        zero_out(out, (size_t)n);
+    }
+}
+
+void matmul_q_fused_batch(float* out, const float* x, const void* w, uint32_t type, int n, int d, int B)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (n <= 0 || B <= 0) return;
+    if (!w) {
+        zero_out(out, (size_t)n * B);
+        return;
+    }
+    int rc = fused_host(out, x, w, type, n, d, B);
+    if (rc) {
+        set_err(rc);
+        zero_out(out, (size_t)n * B);
+    }
+}
+
+void quantize_row_q8_0(const float* x, block_q8_0* y, int k)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    const int nbx = k / 32;
+    if (nbx <= 0) return;
+    if (!x || !y) {
+        set_err(QUANTR_ERR_BAD_ARG);
+        return;
+    }
+    const size_t xbytes = (size_t)nbx * 32 * 4, blkbytes = (size_t)nbx * 34;
+    Stage st = plan(xbytes, 0, blkbytes, 0);
+    int rc = ensure_ready();
+    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total);
+    if (!rc) rc = grow_host(std::max(xbytes, blkbytes));
+    if (!rc) rc = grow_dev(&g.ws, &g.ws_bytes, actq_bytes(k, 1));
+    if (rc) {
+        set_err(rc);
+        std::memset(y, 0, blkbytes);
+        return;
+    }
+    std::memcpy(g.hbuf, x, xbytes);
+    LaunchCfg c;
+    c.stream = g.stream;
+    cudaError_t e = cudaMemcpyAsync(g.dbuf + st.x_off, g.hbuf, xbytes, cudaMemcpyHostToDevice, g.stream);
+    if (e == cudaSuccess)
+        e = launch_quantize((const float*)(g.dbuf + st.x_off), k, k, 1, actq_carve(g.ws, k, 1), g.dbuf + st.blk_off,
+                            nullptr, c);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g.hbuf, g.dbuf + st.blk_off, blkbytes, cudaMemcpyDeviceToHost, g.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_err(code_of(e));
+        std::memset(y, 0, blkbytes);
+        return;
+    }
+    std::memcpy(y, g.hbuf, blkbytes);
+}
+
+void dequantize_row(float* out, const void* src, uint32_t type, int n)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    if (n <= 0) return;
+    if (!src) {  // src/quant.c:161-164
+        zero_out(out, (size_t)n);
+        return;
+    }
+    if (type == T_F32) {  // src/quant.c:165-168: a plain copy, no arithmetic
+        std::memcpy(out, src, (size_t)n * 4);
+        return;
+    }
+    if (!type_supported(type)) {  // src/quant.c:239
+        zero_out(out, (size_t)n);
+        return;
+    }
+    const size_t sbytes = (size_t)row_bytes(type, n), obytes = (size_t)n * 4;
+    Stage st = plan(0, obytes, 0, sbytes);
+    int rc = ensure_ready();
+    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total);
+    if (!rc) rc = grow_host(obytes);
+    if (rc) {
+        set_err(rc);
+        zero_out(out, (size_t)n);
+        return;
+    }
+    float* dout = (float*)(g.dbuf + st.out_off);
+    LaunchCfg c;
+    c.stream = g.stream;
+    cudaError_t e = cudaMemsetAsync(dout, 0, obytes, g.stream);  // tail past the last block stays 0
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g.dbuf + st.w_off, src, sbytes, cudaMemcpyHostToDevice, g.stream);
+    if (e == cudaSuccess) e = launch_dequantize(dout, g.dbuf + st.w_off, type, n, c);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(g.hbuf, dout, obytes, cudaMemcpyDeviceToHost, g.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        set_err(code_of(e));
+        zero_out(out, (size_t)n);
+        return;
+    }
+    std::memcpy(out, g.hbuf, obytes);
+}
+
+float vec_dot_q8_0_q8_0(const block_q8_0* a, const block_q8_0* b, int k) { return vec_dot_host(a, b, k, T_Q8_0); }
+float vec_dot_q4K_q8_0(const block_q4_K* a, const block_q8_0* b, int k) { return vec_dot_host(a, b, k, T_Q4_K); }
+float vec_dot_q5K_q8_0(const block_q5_K* a, const block_q8_0* b, int k) { return vec_dot_host(a, b, k, T_Q5_K); }
+float vec_dot_q6K_q8_0(const void* a, const block_q8_0* b, int k) { return vec_dot_host(a, b, k, T_Q6_K); }
+
+// ------------------------------------------------------------- device API --
+
+size_t quantr_gemv_workspace_bytes(int d, int B) { return actq_bytes(d, B > 0 ? B : 1); }
+
+static int gemv_dev_common(float* out, long long ldo, const float* x, long long ldx, const uint8_t* xblocks,
+                           const void* w, uint32_t type, int n, int d, int B, void* ws, size_t ws_bytes,
+                           void* stream, int32_t* isum, int32_t* bsum)
+{
+    if (n <= 0 || B <= 0) return QUANTR_OK;
+    if (!out || !w || (!x && !xblocks) || d < 0 || ldo < n) return QUANTR_ERR_BAD_ARG;
+    if (x && ldx < d) return QUANTR_ERR_BAD_ARG;
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    cudaError_t e;
+    if (type == T_F32) {
+        if (!x || isum) return QUANTR_ERR_BAD_ARG;
+        e = launch_gemv_f32((const float*)w, x, ldx, out, ldo, n, d, B, c);
+        return code_of(e);
+    }
+    if (!type_supported(type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
+    if (!ws || ws_bytes < actq_bytes(d, B)) return QUANTR_ERR_WORKSPACE;
+    int* err = dev_err_word();
+    ActQ a = actq_carve(ws, d, B);
+    if (x)
+        e = launch_quantize(x, ldx, d, B, a, nullptr, nullptr, c);
+    else
+        e = launch_repack(xblocks, d / 32, B, a, c);
+    if (e != cudaSuccess) return code_of(e);
+    GemvArgs ga;
+    ga.w = (const uint8_t*)w;
+    ga.type = type;
+    ga.n = n;
+    ga.d = d;
+    ga.x = a;
+    ga.out = out;
+    ga.ldo = ldo;
+    ga.B = B;
+    ga.dbg_isum = isum;
+    ga.dbg_bsum = bsum;
+    ga.err = err;
+    return code_of(launch_gemv(ga, c));
+}
+
+int quantr_gemv_dev(float* out, long long ldo, const float* x, long long ldx, const void* w, uint32_t type, int n,
+                    int d, int B, void* workspace, size_t workspace_bytes, void* stream)
+{
+    return gemv_dev_common(out, ldo, x, ldx, nullptr, w, type, n, d, B, workspace, workspace_bytes, stream, nullptr,
+                           nullptr);
+}
+
+int quantr_gemv_q8act_dev(float* out, long long ldo, const block_q8_0* xq, const void* w, uint32_t type, int n, int d,
+                          int B, void* workspace, size_t workspace_bytes, void* stream)
+{
+    if (type == T_F32) return QUANTR_ERR_UNSUPPORTED_TYPE;
+    return gemv_dev_common(out, ldo, nullptr, 0, (const uint8_t*)xq, w, type, n, d, B, workspace, workspace_bytes,
+                           stream, nullptr, nullptr);
+}
+
+int quantr_gemv_partials_dev(float* out, int32_t* isum, int32_t* bsum, const float* x, const void* w, uint32_t type,
+                             int n, int d, int B, void* workspace, size_t workspace_bytes, void* stream)
+{
+    if (!isum || !bsum || type == T_F32) return QUANTR_ERR_BAD_ARG;
+    return gemv_dev_common(out, n, x, d, nullptr, w, type, n, d, B, workspace, workspace_bytes, stream, isum, bsum);
+}
+
+int quantr_quantize_q8_0_dev(block_q8_0* y, const float* x, long long ldx, int k, int B, void* stream)
+{
+    if (k / 32 <= 0 || B <= 0) return QUANTR_OK;
+    if (!y || !x || ldx < k) return QUANTR_ERR_BAD_ARG;
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    ActQ none{};  // packed blocks only
+    return code_of(launch_quantize(x, ldx, k, B, none, (uint8_t*)y, nullptr, c));
+}
+
+int quantr_gpu_device_status(void* stream, int reset)
+{
+    int* w = dev_err_word();
+    if (!w) return QUANTR_ERR_CUDA;
+    int v = 0;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) {
+        cudaGetLastError();
+        return QUANTR_ERR_CUDA;
+    }
+    if (cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return QUANTR_ERR_CUDA;
+    if (reset) cudaMemset(w, 0, 4);
+    return v ? QUANTR_ERR_DEVICE_TIMEOUT : QUANTR_OK;
+}
+
+} // extern "C"

@@ -1,0 +1,71 @@
+// kernels.cuh -- launch interface of the quantized-GEMV kernels (internal; the
+// public C ABI is include/quantr_cuda.h).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace qr {
+
+// Quantized activations in the layout the GEMV kernels read: for token t and
+// 32-element block b, q[(t*nbx + b)*32 .. +31] are the int8 quants (natural
+// element order), d[t*nbx + b] the fp32 decode of the block's fp16 scale and
+// s[t*nbx + b] the int32 sum of its quants (the K-quant min term needs it).
+struct ActQ {
+    int8_t* q;
+    float* d;
+    int32_t* s;
+    int nbx;  // blocks per token
+};
+
+// Bytes of workspace an ActQ for B tokens of d columns needs (40 per block).
+size_t actq_bytes(int d, int B);
+ActQ actq_carve(void* ws, int d, int B);
+
+// Device error word written by kernels whose bounded waits give up.
+enum : int { DEV_OK = 0, DEV_ERR_WAIT_TIMEOUT = 1 };
+
+struct LaunchCfg {
+    cudaStream_t stream = nullptr;
+    bool pdl = true;  // programmatic dependent launch on this stream
+};
+
+// x: B rows of ldx floats -> ActQ (skipped when a.q is null) and, if blocks
+// is non-null, the reference's packed block_q8_0 array (B*nbx blocks of 34
+// bytes).  If err_reset is non-null the kernel zeroes that error word first,
+// so a following GEMV on the same stream reports only its own timeouts.
+cudaError_t launch_quantize(const float* x, long long ldx, int d, int B, ActQ a,
+                            uint8_t* blocks, int* err_reset, const LaunchCfg& c);
+
+// Packed block_q8_0 activations (B*nbx blocks) -> ActQ.
+cudaError_t launch_repack(const uint8_t* blocks, int nbx, int B, ActQ a, const LaunchCfg& c);
+
+struct GemvArgs {
+    const uint8_t* w = nullptr;  // packed rows, n * row_bytes(type, d)
+    uint32_t type = 0;
+    int n = 0, d = 0;
+    ActQ x{};
+    float* out = nullptr;
+    long long ldo = 0;  // out[t*ldo + r]
+    int B = 1;
+    int32_t* dbg_isum = nullptr;  // optional per-unit partials, [B][n][U]
+    int32_t* dbg_bsum = nullptr;
+    int* err = nullptr;           // device error word (may be null)
+};
+
+// Quantized GEMV over already-quantized activations.
+cudaError_t launch_gemv(const GemvArgs& g, const LaunchCfg& c);
+
+// F32 weights (type 0): out[t*ldo + r] = sequential sum_j w[r*d+j]*x[t*ldx+j].
+cudaError_t launch_gemv_f32(const float* w, const float* x, long long ldx, float* out,
+                            long long ldo, int n, int d, int B, const LaunchCfg& c);
+
+// Reference dequantize_row on device (src/quant.c:160-240).
+cudaError_t launch_dequantize(float* out, const uint8_t* src, uint32_t type, int n,
+                              const LaunchCfg& c);
+
+int device_sm_count();
+
+// Kernel launches issued by this library since load.
+unsigned long long launch_count();
+
+} // namespace qr

@@ -1,0 +1,201 @@
+"""Python mirror of quantr-in-c's quantized-GEMV API over libquantr_cuda.so.
+
+The names, argument meanings and error behaviour follow the reference's C API
+(include/quant.h:84-92): ``quantize_row_q8_0``, ``dequantize_row``,
+``vec_dot_*_q8_0``, ``matmul_q_fused``.  Arrays are numpy host arrays, exactly
+like the C functions take host pointers; every call runs on the GPU through the
+C ABI declared in include/quantr_cuda.h.  There is no CPU path: if the CUDA
+library cannot be loaded the import fails, and a device failure raises
+``QuantrError`` carrying the library's sticky error code (the C calls
+themselves zero their outputs, as the reference does).
+
+The ``*_dev`` functions take device addresses (ints, e.g. ``tensor.data_ptr()``)
+and a ``cudaStream_t`` handle (int) and are stream-ordered.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libquantr_cuda.so")
+
+F32, Q8_0, Q4_K, Q5_K, Q6_K = 0, 8, 12, 13, 14
+TYPE_NAMES = {F32: "F32", Q8_0: "Q8_0", Q4_K: "Q4_K", Q5_K: "Q5_K", Q6_K: "Q6_K"}
+BLOCK_BYTES = {Q8_0: 34, Q4_K: 144, Q5_K: 176, Q6_K: 210}
+BLOCK_ELEMS = {Q8_0: 32, Q4_K: 256, Q5_K: 256, Q6_K: 256}
+
+# Exported symbols of include/quantr_cuda.h with their ctypes signatures.
+_c = ctypes
+_vp, _i, _u32, _sz, _ll, _f = _c.c_void_p, _c.c_int, _c.c_uint32, _c.c_size_t, _c.c_longlong, _c.c_float
+SIGNATURES = {
+    "quantize_row_q8_0": (None, [_vp, _vp, _i]),
+    "dequantize_row": (None, [_vp, _vp, _u32, _i]),
+    "vec_dot_q4K_q8_0": (_f, [_vp, _vp, _i]),
+    "vec_dot_q5K_q8_0": (_f, [_vp, _vp, _i]),
+    "vec_dot_q6K_q8_0": (_f, [_vp, _vp, _i]),
+    "vec_dot_q8_0_q8_0": (_f, [_vp, _vp, _i]),
+    "matmul_q_fused": (None, [_vp, _vp, _vp, _u32, _i, _i, _i]),
+    "matmul_q_fused_batch": (None, [_vp, _vp, _vp, _u32, _i, _i, _i]),
+    "quantr_gpu_last_error": (_i, []),
+    "quantr_gpu_clear_error": (None, []),
+    "quantr_gpu_error_string": (_c.c_char_p, [_i]),
+    "quantr_gpu_init": (_i, [_i]),
+    "quantr_gpu_shutdown": (None, []),
+    "quantr_gpu_launch_count": (_c.c_uint64, []),
+    "quantr_gpu_register_weights": (_i, [_vp, _sz]),
+    "quantr_gpu_unregister_weights": (_i, [_vp]),
+    "quantr_gpu_device_ptr": (_vp, [_vp]),
+    "quantr_gemv_workspace_bytes": (_sz, [_i, _i]),
+    "quantr_gemv_dev": (_i, [_vp, _ll, _vp, _ll, _vp, _u32, _i, _i, _i, _vp, _sz, _vp]),
+    "quantr_quantize_q8_0_dev": (_i, [_vp, _vp, _ll, _i, _i, _vp]),
+    "quantr_gemv_q8act_dev": (_i, [_vp, _ll, _vp, _vp, _u32, _i, _i, _i, _vp, _sz, _vp]),
+    "quantr_gemv_partials_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _i, _i, _i, _vp, _sz, _vp]),
+    "quantr_gpu_device_status": (_i, [_vp, _i]),
+}
+
+
+class QuantrError(RuntimeError):
+    def __init__(self, code, where=""):
+        msg = lib().quantr_gpu_error_string(code).decode()
+        super().__init__(f"{where}: quantr error {code} ({msg})" if where else f"quantr error {code} ({msg})")
+        self.code = code
+
+
+_lib = None
+
+
+def lib():
+    """Loads libquantr_cuda.so (raises OSError if it was not built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise OSError(f"{LIB_PATH} is missing: run quantr-in-c_b200/build.py (or __graft_entry__.build())")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+def _check(where):
+    code = lib().quantr_gpu_last_error()
+    if code:
+        lib().quantr_gpu_clear_error()
+        raise QuantrError(code, where)
+
+
+def row_bytes(type_, d):
+    """Packed bytes of one row of d columns (src/quant.c:477-484)."""
+    if type_ == F32:
+        return 4 * d
+    return (d // BLOCK_ELEMS[type_]) * BLOCK_BYTES[type_]
+
+
+# ---------------------------------------------------------------- Part 1 --
+
+def quantize_row_q8_0(x):
+    """x: float32[k] -> uint8[(k//32)*34] packed block_q8_0 (src/quant.c:143)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    y = np.zeros((x.size // 32) * 34, dtype=np.uint8)
+    lib().quantize_row_q8_0(_ptr(x), _ptr(y), x.size)
+    _check("quantize_row_q8_0")
+    return y
+
+
+def dequantize_row(src, type_, n):
+    """Packed row bytes -> float32[n] (src/quant.c:160)."""
+    out = np.zeros(n, dtype=np.float32)
+    s = None if src is None else np.ascontiguousarray(src)
+    lib().dequantize_row(_ptr(out), _ptr(s), type_, n)
+    _check("dequantize_row")
+    return out
+
+
+def vec_dot(type_, a, b, k):
+    """One packed weight row `a` (k columns) . packed Q8_0 activations `b`."""
+    a = np.ascontiguousarray(a, dtype=np.uint8)
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    fn = {Q8_0: "vec_dot_q8_0_q8_0", Q4_K: "vec_dot_q4K_q8_0", Q5_K: "vec_dot_q5K_q8_0",
+          Q6_K: "vec_dot_q6K_q8_0"}[type_]
+    r = getattr(lib(), fn)(_ptr(a), _ptr(b), k)
+    _check(fn)
+    return np.float32(r)
+
+
+def matmul_q_fused(x, w, type_, n, d, threads=1, out=None):
+    """out[i] = row_i(w) . x (src/quant.c:441).  w: packed bytes (host)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    if out is None:
+        out = np.empty(n, dtype=np.float32)
+    wp = None if w is None else (w if isinstance(w, ctypes.c_void_p) else _ptr(np.ascontiguousarray(w)))
+    lib().matmul_q_fused(_ptr(out), _ptr(x), wp, type_, n, d, threads)
+    _check("matmul_q_fused")
+    return out
+
+
+def matmul_q_fused_batch(x, w, type_, n, d):
+    """x: float32[B, d] -> float32[B, n]; B independent matmul_q_fused calls."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    B = x.shape[0]
+    out = np.empty((B, n), dtype=np.float32)
+    lib().matmul_q_fused_batch(_ptr(out), _ptr(x), _ptr(np.ascontiguousarray(w)), type_, n, d, B)
+    _check("matmul_q_fused_batch")
+    return out
+
+
+def register_weights(w):
+    """Makes the host bytes of `w` device-resident for later Part 1 calls."""
+    rc = lib().quantr_gpu_register_weights(_ptr(w), w.nbytes)
+    if rc:
+        raise QuantrError(rc, "quantr_gpu_register_weights")
+
+
+def unregister_weights(w):
+    rc = lib().quantr_gpu_unregister_weights(_ptr(w))
+    if rc:
+        raise QuantrError(rc, "quantr_gpu_unregister_weights")
+
+
+def launch_count():
+    return int(lib().quantr_gpu_launch_count())
+
+
+# ------------------------------------------------------------ device API --
+
+def workspace_bytes(d, B=1):
+    return int(lib().quantr_gemv_workspace_bytes(d, B))
+
+
+def gemv_dev(out, ldo, x, ldx, w, type_, n, d, B, ws, ws_bytes, stream=0):
+    rc = lib().quantr_gemv_dev(out, ldo, x, ldx, w, type_, n, d, B, ws, ws_bytes, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_gemv_dev")
+
+
+def gemv_q8act_dev(out, ldo, xq, w, type_, n, d, B, ws, ws_bytes, stream=0):
+    rc = lib().quantr_gemv_q8act_dev(out, ldo, xq, w, type_, n, d, B, ws, ws_bytes, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_gemv_q8act_dev")
+
+
+def quantize_q8_0_dev(y, x, ldx, k, B, stream=0):
+    rc = lib().quantr_quantize_q8_0_dev(y, x, ldx, k, B, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_quantize_q8_0_dev")
+
+
+def gemv_partials_dev(out, isum, bsum, x, w, type_, n, d, B, ws, ws_bytes, stream=0):
+    rc = lib().quantr_gemv_partials_dev(out, isum, bsum, x, w, type_, n, d, B, ws, ws_bytes, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_gemv_partials_dev")
+
+
+def device_status(stream=0, reset=True):
+    return int(lib().quantr_gpu_device_status(stream or None, 1 if reset else 0))
