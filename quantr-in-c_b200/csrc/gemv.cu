@@ -122,6 +122,16 @@ __device__ __forceinline__ void ld_words(const uint32_t* s32, uint32_t off, uint
 
 // --------------------------------------------------------------- quantizer --
 
+// (int8_t)lrintf(v) as the x86-64 reference computes it: lrintf converts to a
+// 64-bit long (cvtss2si), and a NaN or |v| >= 2^63 yields the "integer
+// indefinite" 0x8000000000000000, whose low byte is 0.  CUDA's conversions
+// saturate instead, so out-of-range values are mapped explicitly.  (Reached
+// when a denormal block scale makes 1/d overflow to infinity.)
+__device__ __forceinline__ int8_t lrintf_to_i8(float v)
+{
+    return fabsf(v) < 9.2233720368547758e18f ? (int8_t)__float2ll_rn(v) : (int8_t)0;
+}
+
 // One warp per 32-element block: reference quantize_row_q8_0
 // (src/quant.c:143-158) with IEEE division, the fp32 reciprocal of the
 // unrounded scale, round-half-even and the truncating fp16 store.
@@ -147,7 +157,7 @@ __global__ void __launch_bounds__(kThreads)
         const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, abits));
         const float dd = __fdiv_rn(amax, 127.0f);
         const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
-        const int8_t qq = (int8_t)__float2int_rn(__fmul_rn(v, id));
+        const int8_t qq = lrintf_to_i8(__fmul_rn(v, id));
         const int sum = __reduce_add_sync(0xffffffffu, (int)qq);
         if (act) q[wb * 32 + lane] = qq;
         if (lane == 0) {
