@@ -166,6 +166,26 @@ int quantr_gemv_partials_dev(float* out, int32_t* isum, int32_t* bsum, const flo
  * in-kernel wait gave up since the last reset); synchronises `stream`. */
 int quantr_gpu_device_status(void* stream, int reset);
 
+/* Allocation-free quantized GEMV.  No counterpart in the reference: an
+ * addition for callers that cannot call cudaMalloc - embedders whose own
+ * memory manager owns all device memory, plugin hosts that pass only input and
+ * output buffers, and latency-critical paths that cannot take cudaMalloc's
+ * implicit synchronisation.  Same arguments and results as quantr_gemv_dev
+ * (Q8_0/Q4_K/Q5_K/Q6_K only), but the quantized activations live in a fixed
+ * scratch array inside the library (QUANTR_NOALLOC_SCRATCH_BYTES, held by every
+ * GPU that loads the library until exit) and nothing is allocated or freed.
+ * Limit: 256 + quantr_gemv_workspace_bytes(d, B) must not exceed
+ * QUANTR_NOALLOC_SCRATCH_BYTES (1 MiB: B * (d/32) up to 26,180 activation
+ * blocks, e.g. d up to 52,360 at B = 16); larger shapes return
+ * QUANTR_ERR_TOO_LARGE.  The
+ * first call on each device looks up the scratch address (cudaGetSymbolAddress)
+ * with that device current; make that first call before any stream capture.
+ * All calls on a device share the one array: calls that overlap on the GPU
+ * (different streams, or other threads) race, so serialise them. */
+#define QUANTR_NOALLOC_SCRATCH_BYTES (1u << 20)
+int quantr_gemv_noalloc_dev(float* out, long long ldo, const float* x, long long ldx, const void* w,
+                            uint32_t type, int n, int d, int B, void* stream);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libquantr_cuda.so")
-SOURCES = ["gemv.cu", "api.cu"]
+SOURCES = ["gemv.cu", "api.cu", "noalloc.cu"]
 HEADERS = ["formats.cuh", "kernels.cuh"]
 
 NVCC_FLAGS = [

@@ -52,6 +52,7 @@ SIGNATURES = {
     "quantr_gemv_q8act_dev": (_i, [_vp, _ll, _vp, _vp, _u32, _i, _i, _i, _vp, _sz, _vp]),
     "quantr_gemv_partials_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _i, _i, _i, _vp, _sz, _vp]),
     "quantr_gpu_device_status": (_i, [_vp, _i]),
+    "quantr_gemv_noalloc_dev": (_i, [_vp, _ll, _vp, _ll, _vp, _u32, _i, _i, _i, _vp]),
 }
 
 
@@ -195,6 +196,13 @@ def gemv_partials_dev(out, isum, bsum, x, w, type_, n, d, B, ws, ws_bytes, strea
     rc = lib().quantr_gemv_partials_dev(out, isum, bsum, x, w, type_, n, d, B, ws, ws_bytes, stream or None)
     if rc:
         raise QuantrError(rc, "quantr_gemv_partials_dev")
+
+
+def gemv_noalloc_dev(out, ldo, x, ldx, w, type_, n, d, B, stream=0):
+    """quantr_gemv_dev without a workspace: uses the library's fixed scratch."""
+    rc = lib().quantr_gemv_noalloc_dev(out, ldo, x, ldx, w, type_, n, d, B, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_gemv_noalloc_dev")
 
 
 def device_status(stream=0, reset=True):
