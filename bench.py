@@ -12,8 +12,11 @@ Weights and activations are seeded synthetic data (no checkpoints offline).
   python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
 
 value  : whole-job GB/s of algorithmic bytes (packed weights + fp32 x + fp32
-         out), inputs resident in HBM, one CUDA graph replay per step, CUDA
-         events on the launching stream, max over ranks.
+         out), inputs resident in HBM, CUDA events on the launching stream, max
+         over ranks.  The 72 GEMVs of a step run as one engine program
+         (quantr_program_run: activation quantizer + persistent GEMV engine),
+         replayed as a CUDA graph; per_call_value times the same step as 72
+         separate quantr_gemv_dev calls.
 e2e    : the same metric through the reference-facing C ABI
          (matmul_q_fused_batch with HOST arrays; weights registered once, like
          the reference's load-time mmap), host<->device copies inside.
@@ -45,9 +48,9 @@ HIDDEN, FFN, LAYERS = 896, 4864, 24
 Q4_K = 12
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one c2 GEMV launch pair, from the ncu capture
-# summarised in profiles/gemv_q4k_c2.md; None until captured.
-NCU_TRAFFIC_PER_GEMV = None
+# DRAM bytes (read + write) of one step's engine launch, from the ncu capture
+# summarised in profiles/; None until captured.
+NCU_TRAFFIC_PER_STEP = None
 
 
 def row_bytes(t, d):
@@ -195,7 +198,8 @@ def config_dict(args):
         "type": "Q4_K", "batch": args.batch, "layers": args.layers,
         "weight_bytes_per_step": sum(n * row_bytes(t, d) for t, n, d, _ in step_shapes(args.layers)),
         "l2": "inputs larger than L2: 159.7 MB of distinct weights cycled per step vs 126 MB L2",
-        "launch": "cuda_graph + programmatic dependent launch",
+        "launch": ("one engine program per step (72 independent GEMVs: quantizer launch + persistent "
+                   "engine launch, programmatic dependent launch), replayed as a CUDA graph"),
         "parallelism": f"replicas x{args.gpus}",
     }
 
@@ -231,7 +235,14 @@ def ours_arm(args):
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     nbytes = sum(gemv_bytes(t, n, d, B) for t, n, d, _ in shapes)
 
+    # One engine program holds the step's 72 independent GEMVs.
+    prog = quantr.Program([(w.data_ptr(), t, n, d, B, x.data_ptr(), d, o.data_ptr(), n)
+                           for (t, n, d, _), w, x, o in zip(shapes, dev_w, xin, outs)])
+
     def step(stream):
+        prog.run(stream)
+
+    def step_per_call(stream):
         for (t, n, d, _), w, x, o in zip(shapes, dev_w, xin, outs):
             quantr.gemv_dev(o.data_ptr(), n, x.data_ptr(), d, w.data_ptr(), t, n, d, B, ws.data_ptr(), ws_bytes,
                             stream)
@@ -241,10 +252,14 @@ def ours_arm(args):
         c0 = quantr.launch_count()
         step(s.cuda_stream)  # eager warm-up: sets kernel attributes before capture
         launches_per_step = quantr.launch_count() - c0
+        step_per_call(s.cuda_stream)
         s.synchronize()
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph, stream=s):
             step(s.cuda_stream)
+        graph_pc = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_pc, stream=s):
+            step_per_call(s.cuda_stream)
     torch.cuda.synchronize()
     assert quantr.device_status(0) == 0
 
@@ -281,6 +296,18 @@ def ours_arm(args):
     assert quantr.device_status(0) == 0
     gbs = world * nbytes * args.steps / (ms / 1e3) / 1e9
     per_gpu = nbytes * args.steps / (ms / 1e3) / 1e9
+
+    # The same step as 72 separate GEMV calls (one engine launch pair each).
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            graph_pc.replay()
+        ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev2.record(s)
+        for _ in range(args.steps):
+            graph_pc.replay()
+        ev3.record(s)
+    torch.cuda.synchronize()
+    per_call_gbs = nbytes * args.steps / (ev2.elapsed_time(ev3) / 1e3) / 1e9
 
     # End to end through the reference-facing C ABI with host arrays.
     for w in host_w:
@@ -327,8 +354,10 @@ def ours_arm(args):
             "tok_per_s": round(world * B * args.steps / (ms / 1e3), 1),
             "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu / peak, 4), "peak_source": peak_kind,
-                         "traffic": NCU_TRAFFIC_PER_GEMV,
-                         "kernel": "quantize(Q8_0) -> fused Q4_K GEMV pair, per step of 72 pairs"},
+                         "traffic": NCU_TRAFFIC_PER_STEP,
+                         "kernel": "k_program (persistent GEMV engine) + k_quant_tasks, one launch pair per step"},
+            "per_call_value": round(per_call_gbs, 3),
+            "per_call_note": "same step as 72 quantr_gemv_dev calls (one quantizer + engine launch each)",
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "matmul_q_fused_batch (host pointers)"},
@@ -336,7 +365,8 @@ def ours_arm(args):
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
-    del graph
+    del graph, graph_pc
+    prog.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -166,6 +166,39 @@ int quantr_gemv_partials_dev(float* out, int32_t* isum, int32_t* bsum, const flo
  * in-kernel wait gave up since the last reset); synchronises `stream`. */
 int quantr_gpu_device_status(void* stream, int reset);
 
+/* ---- GEMV programs: many independent GEMVs per launch ------------------ */
+
+/* One GEMV of a program: out[t*ldo + r] = row_r(w) . x[t*ldx ...] for t < B
+ * (B <= 16), with the reference's numerics (the same as matmul_q_fused per
+ * token).  All pointers are device pointers; w must be 16-byte aligned. */
+typedef struct {
+    const void* w;
+    uint32_t type;       /* QUANTR_TYPE_Q8_0 / Q4_K / Q5_K / Q6_K */
+    int n, d, B;
+    const float* x;
+    long long ldx;
+    float* out;
+    long long ldo;
+} quantr_gemv_job;
+
+typedef struct quantr_program quantr_program;
+
+/* Plans a program on the current device: tiles every job, lays out the
+ * quantized activations (inputs shared by several jobs are quantized once)
+ * and uploads the job table.  The jobs are independent: no job may read
+ * another job's output within one run (chain dependent GEMVs as separate
+ * runs, or separate programs, on one stream).  This call allocates; runs do
+ * not.  No counterpart in the reference, whose runtime issues one
+ * matmul_q_fused per GEMV (src/runtime.c:124-287); a program is the batched
+ * device form of such a sequence. */
+int quantr_program_create(quantr_program** prog, const quantr_gemv_job* jobs, int njobs);
+/* Runs the program on `stream` (two launches: activation quantizer, then the
+ * persistent GEMV engine; programmatic dependent launch between them). */
+int quantr_program_run(quantr_program* prog, void* stream);
+void quantr_program_destroy(quantr_program* prog);
+/* Work items (row tiles), persistent CTAs and shared memory per CTA. */
+int quantr_program_info(const quantr_program* prog, int* items, int* grid, int* smem_bytes);
+
 /* Allocation-free quantized GEMV.  No counterpart in the reference: an
  * addition for callers that cannot call cudaMalloc - embedders whose own
  * memory manager owns all device memory, plugin hosts that pass only input and

@@ -171,7 +171,7 @@ int fused_host(float* out, const float* x, const void* w, uint32_t type, int n, 
     Stage st = plan(xbytes, obytes, 0, wdev ? 0 : wbytes);
     if ((rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total))) return rc;
     if ((rc = grow_host(st.err_off + 16))) return rc;
-    const size_t need_ws = actq_bytes(d, B);
+    const size_t need_ws = quantr_gemv_workspace_bytes(d, B);
     if (type != T_F32 && (rc = grow_dev(&g.ws, &g.ws_bytes, need_ws))) return rc;
 
     float* dx = (float*)(g.dbuf + st.x_off);
@@ -191,19 +191,24 @@ int fused_host(float* out, const float* x, const void* w, uint32_t type, int n, 
             if (e == cudaSuccess)
                 e = launch_gemv_f32((const float*)wdev, dx, d, dout, n, n, d, B, c);
         } else {
-            ActQ a = actq_carve(g.ws, d, B);
-            e = launch_quantize(dx, d, d, B, a, nullptr, derr, c);
-            GemvArgs ga;
-            ga.w = wdev;
-            ga.type = type;
-            ga.n = n;
-            ga.d = d;
-            ga.x = a;
-            ga.out = dout;
-            ga.ldo = n;
-            ga.B = B;
-            ga.err = derr;
-            if (e == cudaSuccess) e = launch_gemv(ga, c);
+            e = cudaMemsetAsync(derr, 0, 4, g.stream);
+            if (e == cudaSuccess)
+                e = launch_gemv_engine(wdev, type, n, d, B, dx, d, dout, n, g.ws, g.ws_bytes, derr, g.stream);
+            if (e == cudaErrorNotSupported) {  // shapes the engine does not take
+                ActQ a = actq_carve(g.ws, d, B);
+                e = launch_quantize(dx, d, d, B, a, nullptr, derr, c);
+                GemvArgs ga;
+                ga.w = wdev;
+                ga.type = type;
+                ga.n = n;
+                ga.d = d;
+                ga.x = a;
+                ga.out = dout;
+                ga.ldo = n;
+                ga.B = B;
+                ga.err = derr;
+                if (e == cudaSuccess) e = launch_gemv(ga, c);
+            }
         }
     }
     if (e == cudaSuccess)
@@ -282,10 +287,13 @@ float vec_dot_host(const void* a, const void* b, int k, uint32_t type)
     return r;
 }
 
-int* dev_err_word()
+} // namespace
+
+int* qr::device_error_word()
 {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
     if (!g_dev_err[dev]) {
         int* p = nullptr;
         if (cudaMalloc(&p, 16) != cudaSuccess) {
@@ -297,8 +305,6 @@ int* dev_err_word()
     }
     return g_dev_err[dev];
 }
-
-} // namespace
 
 extern "C" {
 
@@ -527,7 +533,13 @@ float vec_dot_q6K_q8_0(const void* a, const block_q8_0* b, int k) { return vec_d
 
 // ------------------------------------------------------------- device API --
 
-size_t quantr_gemv_workspace_bytes(int d, int B) { return actq_bytes(d, B > 0 ? B : 1); }
+// Covers both the general kernel's layout (actq_bytes) and the engine's
+// compact one, which pads each token's scale rows to 4 entries.
+size_t quantr_gemv_workspace_bytes(int d, int B)
+{
+    B = B > 0 ? B : 1;
+    return actq_bytes(d, B) + 256 + 32 * (size_t)B;
+}
 
 static int gemv_dev_common(float* out, long long ldo, const float* x, long long ldx, const uint8_t* xblocks,
                            const void* w, uint32_t type, int n, int d, int B, void* ws, size_t ws_bytes,
@@ -546,7 +558,12 @@ static int gemv_dev_common(float* out, long long ldo, const float* x, long long 
     }
     if (!type_supported(type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
     if (!ws || ws_bytes < actq_bytes(d, B)) return QUANTR_ERR_WORKSPACE;
-    int* err = dev_err_word();
+    int* err = device_error_word();
+    if (x && !isum && ((uintptr_t)ws & 15) == 0) {
+        // Fast path: the persistent engine (16-byte aligned weights, B <= 16).
+        e = launch_gemv_engine((const uint8_t*)w, type, n, d, B, x, ldx, out, ldo, ws, ws_bytes, err, c.stream);
+        if (e != cudaErrorNotSupported) return code_of(e);
+    }
     ActQ a = actq_carve(ws, d, B);
     if (x)
         e = launch_quantize(x, ldx, d, B, a, nullptr, nullptr, c);
@@ -602,7 +619,7 @@ int quantr_quantize_q8_0_dev(block_q8_0* y, const float* x, long long ldx, int k
 
 int quantr_gpu_device_status(void* stream, int reset)
 {
-    int* w = dev_err_word();
+    int* w = device_error_word();
     if (!w) return QUANTR_ERR_CUDA;
     int v = 0;
     if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) {

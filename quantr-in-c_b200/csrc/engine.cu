@@ -1,0 +1,739 @@
+// engine.cu -- persistent, warp-specialized quantized-GEMV engine (sm_100a).
+//
+// One launch executes a "program": a list of independent GEMV jobs
+// (out_j = W_j . x_j for B_j tokens).  Each job's rows are cut into tiles of
+// R_j rows; the (job, tile) items are dealt round-robin to one persistent CTA
+// per SM.  Inside a CTA three warp roles form a pipeline:
+//
+//   producer (1 warp)   streams each item's packed weight rows (one
+//                       contiguous, 16-byte aligned range) and the job's
+//                       quantized activations into a ring of S shared-memory
+//                       slots with cp.async.bulk; mbarrier transaction
+//                       counts signal "slot full".  It runs up to S items ahead,
+//                       so HBM streaming never waits for compute.
+//   consumers (8 warps) decode one row x super-block (or Q8_0 block) per thread
+//                       and evaluate the reference's exact per-unit terms
+//                       (dp4a integer sums, explicitly rounded fp32 ops) into
+//                       one of T term buffers.
+//   chain (2 warps)     sum each (row, token)'s terms left to right - the
+//                       reference's accumulation order, src/quant.c:279-285,
+//                       :384-401, :422-435 - and store the fp32 outputs, while
+//                       the consumers already work on the next item.
+//
+// All waits are bounded (250 ms) and a CTA-wide abort flag stops every role if
+// one of them gives up; slots with copies in flight are drained (bounded)
+// before the CTA exits.  No multicast is used.  The quantized activations of
+// every job are produced by k_quant_tasks (one launch per program run, the
+// reference's quantize_row_q8_0 per input) in the compact, weight-type
+// permuted layout the consumers read; the program kernel issues its first
+// weight copies before griddepcontrol.wait, so under programmatic dependent
+// launch the weight stream overlaps the quantizer.
+#include "quantr_cuda.h"
+
+#include "device_common.cuh"
+#include "formats.cuh"
+#include "kernels.cuh"
+#include "launch_util.cuh"
+#include "quant_decode.cuh"
+
+#include <algorithm>
+#include <cstring>
+#include <map>
+#include <new>
+#include <numeric>
+#include <tuple>
+#include <vector>
+
+namespace qr {
+namespace eng {
+
+constexpr int kConsumerWarps = 12;
+constexpr int kChainWarps = 2;
+constexpr int kWarps = 1 + kConsumerWarps + kChainWarps;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kConsumerThreads = 32 * kConsumerWarps;
+constexpr int kMaxS = 4, kMaxT = 4;
+constexpr int kMaxB = 16;
+constexpr size_t kSmemMax = 227 * 1024;
+constexpr uint32_t kBulkChunk = 32768;
+
+// Device-side job description (built by the host planner).
+struct JobDesc {
+    const uint8_t* w;    // 16-byte aligned packed rows
+    float* out;          // out[t*ldo + r]
+    const uint8_t* act;  // quantized activations: q[B][U][32] | d[B][U4] | s[B][U4]
+    long long rb, ldo;
+    uint32_t act_bytes;  // bytes of the act region (all three parts)
+    uint32_t act_d_off, act_s_off;
+    int type, n, U, U4, nblk, B, R, TS, tiles, item0;
+    unsigned long long nblk_magic;  // floor(it / nblk) == (it * magic) >> 40
+};
+
+struct ProgParams {
+    const JobDesc* jobs;  // null: use inline_job
+    int njobs, total_items;
+    uint32_t slot_bytes, slot_x_off, term_bytes, S, T;
+    uint32_t slot_off, term_off;
+    int* err;
+    JobDesc inline_job;
+};
+
+// One quantization task: B rows of fp32 x -> the compact act layout.
+struct QTask {
+    const float* x;
+    uint8_t* act;
+    long long ldx;
+    long long blk0;  // first global block index of this task
+    int U, U4, B, type;
+};
+
+struct QParams {
+    const QTask* tasks;  // null: use inline_task
+    int ntasks;
+    long long total_blocks;
+    QTask inline_task;
+};
+
+// Position of element e (0..31) of a unit in the permuted activation layout.
+__device__ __forceinline__ int perm_pos(uint32_t type, int e)
+{
+    if (type == T_Q4_K || type == T_Q5_K) return (e & ~7) + ((e & 1) << 2) + ((e & 7) >> 1);
+    if (type == T_Q6_K) return (e & ~15) + ((e & 3) << 2) + ((e & 15) >> 2);
+    return e;
+}
+
+// Reference quantize_row_q8_0 (src/quant.c:143-158), one warp per block,
+// writing the engine's compact layout for the consuming job's weight type.
+__global__ void __launch_bounds__(256) k_quant_tasks(const __grid_constant__ QParams p)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const QTask* tasks = p.tasks ? p.tasks : &p.inline_task;
+    const long long step = (long long)gridDim.x * 8;
+    for (long long gb = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); gb < p.total_blocks; gb += step) {
+        int lo = 0, hi = p.ntasks - 1;  // last task with blk0 <= gb
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (tasks[mid].blk0 <= gb) lo = mid; else hi = mid - 1;
+        }
+        const QTask& T = tasks[lo];
+        const long long local = gb - T.blk0;
+        const int t = (int)(local / T.U), b = (int)(local - (long long)t * T.U);
+        const float v = T.x[(long long)t * T.ldx + (long long)b * 32 + lane];
+        // Stored unit: K-quant activations go sub-block-major (block 8s+j of
+        // the row -> unit j*nsb + s) so consumer lanes on neighbouring
+        // super-blocks read neighbouring units; Q8_0 keeps block order.
+        const int u = T.type == T_Q8_0 ? b : (b & 7) * (T.U >> 3) + (b >> 3);
+        const float a = fabsf(v);
+        const uint32_t abits = (a == a) ? __float_as_uint(a) : 0u;
+        const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, abits));
+        const float dd = __fdiv_rn(amax, 127.0f);
+        const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
+        const int8_t qq = lrintf_to_i8(__fmul_rn(v, id));
+        const int sum = __reduce_add_sync(0xffffffffu, (int)qq);
+        T.act[((long long)t * T.U + u) * 32 + perm_pos(T.type, lane)] = (uint8_t)qq;
+        if (lane == 0) {
+            const long long di = (long long)T.B * T.U * 32;
+            reinterpret_cast<float*>(T.act + di)[t * T.U4 + u] = h2f_ref(f2h_ref(dd));
+            reinterpret_cast<int32_t*>(T.act + di + (long long)T.B * T.U4 * 4)[t * T.U4 + u] = sum;
+        }
+    }
+}
+
+__device__ __forceinline__ int job_of(const JobDesc* jobs, int njobs, int item, int jc)
+{
+    while (jc + 1 < njobs && item >= jobs[jc + 1].item0) ++jc;
+    return jc;
+}
+
+// ------------------------------------------------------------ consumers --
+
+// Everything the consumers need for one item, copied into registers once per
+// item (reading it through the job table inside the loops would force a
+// reload after every shared-memory store).
+struct Item {
+    uint32_t w;                        // shared-memory byte offset of the tile (16-byte aligned)
+    const int8_t* __restrict__ xq;     // [B][U][32] permuted activation quants
+    const float* __restrict__ xd;      // [B][U4] decoded block scales
+    const int32_t* __restrict__ xs;    // [B][U4] quant sums
+    float* __restrict__ terms;         // [U][TS] per-unit terms, natural unit order
+    int rb, nblk, B, U, U4, TS;
+};
+
+// Activation unit of sub-block j of super-block s (see k_quant_tasks).
+__device__ __forceinline__ int xunit(const Item& it, int s, int j) { return j * it.nblk + s; }
+
+// Terms of one unit for every token.  kind: 0 = Q8_0, 1 = Q4_K/Q5_K, 2 = Q6_K.
+template <int KIND>
+__device__ __forceinline__ void put_terms(const Item& it, int g, int tu, int xu, float a, float b,
+                                          const uint32_t (&wq)[8])
+{
+    for (int t = 0; t < it.B; ++t) {
+        const uint4* xv = reinterpret_cast<const uint4*>(it.xq + (t * it.U + xu) * 32);
+        int isum = dot8(wq, xv[0], xv[1]);
+        const int bsum = it.xs[t * it.U4 + xu];
+        const float dx = it.xd[t * it.U4 + xu];
+        float term;
+        if (KIND == 0) term = unit_term<T_Q8_0>(a, b, isum, bsum, dx);
+        else if (KIND == 2) term = unit_term<T_Q6_K>(a, b, isum - 32 * bsum, bsum, dx);
+        else term = unit_term<T_Q4_K>(a, b, isum, bsum, dx);
+        it.terms[tu * it.TS + g * it.B + t] = term;
+    }
+}
+
+// Q4_K / Q5_K super-block (16-byte aligned): header and quants by 128-bit
+// loads.  Q4_K keeps the high nibble in place and divides its dp4a product
+// by 16 (exact: every product is a multiple of 16).
+template <uint32_t TYPE>
+__device__ __forceinline__ void consume_k45(const uint8_t* __restrict__ sm, const Item& it, int g, int s)
+{
+    const uint8_t* sb = sm + it.w + g * it.rb + s * block_bytes(TYPE);
+    const uint4 hdr = *reinterpret_cast<const uint4*>(sb);
+    const float d = h2f_ref(hdr.x & 0xFFFFu), dmin = h2f_ref(hdr.x >> 16);
+    uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = qh0;
+    if (TYPE == T_Q5_K) {
+        qh0 = *reinterpret_cast<const uint4*>(sb + 16);
+        qh1 = *reinterpret_cast<const uint4*>(sb + 32);
+    }
+    const uint8_t* qs = sb + (TYPE == T_Q4_K ? 16 : 48);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t scb = ((j < 4 ? hdr.y : hdr.z) >> (8 * (j & 3))) & 0xFFu;
+        const float sc = __fmul_rn((float)(scb & 63u), d);    // src/quant.c:385
+        const float m = __fmul_rn((float)(scb >> 6), dmin);   // src/quant.c:386
+        const uint4 q = *reinterpret_cast<const uint4*>(qs + 16 * j);
+        const int tu = 8 * s + j, xu = xunit(it, s, j);
+        if (TYPE == T_Q4_K) {
+            const uint32_t l0 = q.x & 0x0F0F0F0Fu, l1 = q.y & 0x0F0F0F0Fu, l2 = q.z & 0x0F0F0F0Fu,
+                           l3 = q.w & 0x0F0F0F0Fu;
+            const uint32_t h0 = q.x & 0xF0F0F0F0u, h1 = q.y & 0xF0F0F0F0u, h2 = q.z & 0xF0F0F0F0u,
+                           h3 = q.w & 0xF0F0F0F0u;
+            for (int t = 0; t < it.B; ++t) {
+                const uint4* xv = reinterpret_cast<const uint4*>(it.xq + (t * it.U + xu) * 32);
+                const uint4 xa = xv[0], xb = xv[1];
+                int lo = __dp4a((int)l0, (int)xa.x, 0);
+                lo = __dp4a((int)l1, (int)xa.z, lo);
+                lo = __dp4a((int)l2, (int)xb.x, lo);
+                lo = __dp4a((int)l3, (int)xb.z, lo);
+                int hi = dp4a_us(h0, (int)xa.y, 0);
+                hi = dp4a_us(h1, (int)xa.w, hi);
+                hi = dp4a_us(h2, (int)xb.y, hi);
+                hi = dp4a_us(h3, (int)xb.w, hi);
+                const int isum = lo + (hi >> 4);
+                const int bsum = it.xs[t * it.U4 + xu];
+                it.terms[tu * it.TS + g * it.B + t] = unit_term<T_Q4_K>(sc, m, isum, bsum, it.xd[t * it.U4 + xu]);
+            }
+        } else {
+            const uint32_t H = (j < 4) ? (j == 0 ? qh0.x : j == 1 ? qh0.y : j == 2 ? qh0.z : qh0.w)
+                                       : (j == 4 ? qh1.x : j == 5 ? qh1.y : j == 6 ? qh1.z : qh1.w);
+            uint32_t wq[8];
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t hb = (H >> (8 * i)) & 0xFFu;
+                wq[2 * i] = (qw[i] & 0x0F0F0F0Fu) | spread_even_bits_to_b4(hb);
+                wq[2 * i + 1] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | spread_even_bits_to_b4(hb >> 1);
+            }
+            put_terms<1>(it, g, tu, xu, sc, m, wq);
+        }
+    }
+}
+
+// Q6_K super-block (2-byte aligned: 210-byte blocks) by funnel-shifted words.
+__device__ __forceinline__ void consume_q6k(const uint8_t* __restrict__ sm, const Item& it, int g, int s)
+{
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
+    const uint32_t sb = it.w + (uint32_t)(g * it.rb) + 210u * (uint32_t)s;
+    uint32_t scw[2];
+    ld_words<2>(s32, sb + 192, scw);
+    const float d = h2f_ref(ld_u32(s32, sb + 208) & 0xFFFFu);
+#pragma unroll 2
+    for (int j = 0; j < 8; ++j) {
+        const float sc = __fmul_rn((float)(int8_t)((scw[j >> 2] >> (8 * (j & 3))) & 0xFFu), d);  // :423
+        uint32_t ql[4], qh[2], wq[8];
+        ld_words<4>(s32, sb + 16u * j, ql);
+        ld_words<2>(s32, sb + 128u + 8u * j, qh);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t s0 = __byte_perm(ql[2 * h], ql[2 * h + 1], 0x6420);
+            const uint32_t s1 = __byte_perm(ql[2 * h], ql[2 * h + 1], 0x7531);
+            const uint32_t nib[4] = {s0 & 0x0F0F0F0Fu, (s0 >> 4) & 0x0F0F0F0Fu, s1 & 0x0F0F0F0Fu,
+                                     (s1 >> 4) & 0x0F0F0F0Fu};
+#pragma unroll
+            for (int m = 0; m < 4; ++m) wq[4 * h + m] = nib[m] | (((qh[h] >> (2 * m)) & 0x03030303u) << 4);
+        }
+        put_terms<2>(it, g, 8 * s + j, xunit(it, s, j), sc, 0.0f, wq);
+    }
+}
+
+// Q8_0 block (34 bytes, 2-byte aligned).
+__device__ __forceinline__ void consume_q80(const uint8_t* __restrict__ sm, const Item& it, int g, int u)
+{
+    const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
+    const uint32_t blk = it.w + (uint32_t)(g * it.rb) + 34u * (uint32_t)u;
+    const float dw = h2f_ref(ld_u32(s32, blk) & 0xFFFFu);
+    uint32_t wq[8];
+    ld_words<8>(s32, blk + 2, wq);
+    put_terms<0>(it, g, u, u, dw, 0.0f, wq);
+}
+
+template <uint32_t TYPE>
+__device__ __forceinline__ void consume_item_t(const uint8_t* __restrict__ sm, const Item& it, int rows,
+                                               unsigned long long magic, int ctid)
+{
+    const int total = rows * it.nblk;
+    for (int i = ctid; i < total; i += kConsumerThreads) {
+        const int g = (int)(((unsigned long long)i * magic) >> 40);
+        const int s = i - g * it.nblk;
+        if (TYPE == T_Q4_K || TYPE == T_Q5_K) consume_k45<TYPE>(sm, it, g, s);
+        else if (TYPE == T_Q6_K) consume_q6k(sm, it, g, s);
+        else consume_q80(sm, it, g, s);
+    }
+}
+
+// ---------------------------------------------------------------- kernel --
+
+__global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__ ProgParams p)
+{
+    extern __shared__ __align__(1024) uint8_t sm[];
+    uint64_t* wfull = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* wempty = wfull + kMaxS;
+    uint64_t* tfull = wempty + kMaxS;
+    uint64_t* tempty = tfull + kMaxT;
+    int* ctl = reinterpret_cast<int*>(tempty + kMaxT);  // [0] abort, [1..S] fills issued per slot
+    volatile int* abort_flag = ctl;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int P = gridDim.x, c = blockIdx.x;
+    const JobDesc* jobs = p.jobs ? p.jobs : &p.inline_job;
+    const int S = (int)p.S, T = (int)p.T;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], kConsumerWarps);
+            ctl[1 + s] = 0;
+        }
+        for (int t = 0; t < T; ++t) {
+            mbar_init(&tfull[t], kConsumerWarps);
+            mbar_init(&tempty[t], 1);
+        }
+        ctl[0] = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    pdl_trigger();
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer --
+        if (lane == 0) {
+            int jc = 0, k = 0, i = c;
+            int pend_job[kMaxS];
+            auto issue_w = [&](const JobDesc& J, int item, int slot) {
+                const int r0 = (item - J.item0) * J.R;
+                const int rows = min(J.R, J.n - r0);
+                const uint8_t* src = J.w + (long long)r0 * J.rb;
+                uint8_t* dst = sm + p.slot_off + (size_t)slot * p.slot_bytes;
+                const uint32_t bytes = (uint32_t)(rows * J.rb);
+                const uint32_t body = bytes & ~15u;
+                for (uint32_t b = body; b < bytes; ++b) dst[b] = src[b];  // < 16 ragged bytes
+                mbar_arrive_expect_tx(&wfull[slot], body + J.act_bytes);
+                for (uint32_t off = 0; off < body; off += kBulkChunk)
+                    bulk_g2s(dst + off, src + off, min(kBulkChunk, body - off), &wfull[slot]);
+                ctl[1 + slot] += 1;
+            };
+            auto issue_x = [&](const JobDesc& J, int slot) {
+                uint8_t* dst = sm + p.slot_off + (size_t)slot * p.slot_bytes + p.slot_x_off;
+                bulk_g2s(dst, J.act, J.act_bytes, &wfull[slot]);
+            };
+            // Prologue: weights of the first S items before waiting for the
+            // quantizer grid (weights never depend on it).
+            for (; k < S && i < p.total_items; ++k, i += P) {
+                jc = job_of(jobs, p.njobs, i, jc);
+                issue_w(jobs[jc], i, k);
+                pend_job[k] = jc;
+            }
+            pdl_wait();
+            for (int q = 0; q < k; ++q) issue_x(jobs[pend_job[q]], q);
+            for (; i < p.total_items; ++k, i += P) {
+                jc = job_of(jobs, p.njobs, i, jc);
+                const int slot = k % S;
+                if (!mbar_wait_bounded(&wempty[slot], ((k / S) - 1) & 1, p.err, abort_flag)) break;
+                issue_w(jobs[jc], i, slot);
+                issue_x(jobs[jc], slot);
+            }
+        }
+    } else if (warp <= kConsumerWarps) {
+        // ----------------------------------------------------- consumers --
+        const int ctid = (warp - 1) * 32 + lane;
+        int jc = 0;
+        for (int k = 0, i = c; i < p.total_items; ++k, i += P) {
+            jc = job_of(jobs, p.njobs, i, jc);
+            const JobDesc& J = jobs[jc];
+            const int slot = k % S, tb = k % T;
+            if (!mbar_wait_bounded(&wfull[slot], (k / S) & 1, p.err, abort_flag)) break;
+            if (k >= T && !mbar_wait_bounded(&tempty[tb], ((k / T) - 1) & 1, p.err, abort_flag)) break;
+            Item it;
+            it.w = p.slot_off + (uint32_t)slot * p.slot_bytes;
+            const uint8_t* xb = sm + it.w + p.slot_x_off;
+            it.xq = reinterpret_cast<const int8_t*>(xb);
+            it.xd = reinterpret_cast<const float*>(xb + J.act_d_off);
+            it.xs = reinterpret_cast<const int32_t*>(xb + J.act_s_off);
+            it.terms = reinterpret_cast<float*>(sm + p.term_off + (size_t)tb * p.term_bytes);
+            it.rb = (int)J.rb;
+            it.nblk = J.nblk;
+            it.B = J.B;
+            it.U = J.U;
+            it.U4 = J.U4;
+            it.TS = J.TS;
+            const int type = J.type;
+            const unsigned long long magic = J.nblk_magic;
+            const int rows = min(J.R, J.n - (i - J.item0) * J.R);
+            switch (type) {
+            case T_Q4_K: consume_item_t<T_Q4_K>(sm, it, rows, magic, ctid); break;
+            case T_Q5_K: consume_item_t<T_Q5_K>(sm, it, rows, magic, ctid); break;
+            case T_Q6_K: consume_item_t<T_Q6_K>(sm, it, rows, magic, ctid); break;
+            default: consume_item_t<T_Q8_0>(sm, it, rows, magic, ctid); break;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&tfull[tb]);
+                mbar_arrive(&wempty[slot]);
+            }
+        }
+    } else {
+        // --------------------------------------------------------- chain --
+        const int ch = warp - 1 - kConsumerWarps;
+        int jc = 0;
+        for (int k = ch, i = c + ch * P; i < p.total_items; k += kChainWarps, i += kChainWarps * P) {
+            jc = job_of(jobs, p.njobs, i, jc);
+            const JobDesc& J = jobs[jc];
+            const int tb = k % T;
+            if (!mbar_wait_bounded(&tfull[tb], (k / T) & 1, p.err, abort_flag)) break;
+            const float* __restrict__ terms =
+                reinterpret_cast<const float*>(sm + p.term_off + (size_t)tb * p.term_bytes);
+            const int r0 = (i - J.item0) * J.R;
+            const int rows = min(J.R, J.n - r0);
+            const int B = J.B, U = J.U, TS = J.TS;
+            float* __restrict__ out = J.out + r0;
+            const long long ldo = J.ldo;
+            for (int q = lane; q < rows * B; q += 32) {
+                const int g = q / B, t = q - g * B;
+                const float* tp = terms + q;
+                float acc = 0.0f;
+#pragma unroll 8
+                for (int u = 0; u < U; ++u) acc = __fadd_rn(acc, tp[u * TS]);
+                out[(long long)t * ldo + g] = acc;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[tb]);
+        }
+    }
+
+    __syncthreads();
+    if (*abort_flag && threadIdx.x == 0) {
+        // Some role gave up: let every copy this CTA issued land (bounded)
+        // before its shared memory is released.
+        for (int s = 0; s < S; ++s)
+            if (ctl[1 + s] > 0) mbar_wait_bounded(&wfull[s], (ctl[1 + s] - 1) & 1, nullptr);
+    }
+}
+
+// ------------------------------------------------------------ host side --
+
+int gcd_int(long long a, long long b) { return (int)std::gcd(a, b); }
+
+unsigned long long magic40(int dvs) { return ((1ULL << 40) + (unsigned long long)dvs - 1) / (unsigned long long)dvs; }
+
+struct Plan {
+    std::vector<JobDesc> jobs;
+    std::vector<QTask> tasks;
+    long long total_blocks = 0;
+    size_t act_total = 0;
+    ProgParams pp{};
+    QParams qp{};
+    int grid = 0;
+    size_t smem = 0;
+};
+
+struct JobIn {
+    const uint8_t* w;
+    uint32_t type;
+    int n, d, B;
+    const float* x;
+    long long ldx;
+    float* out;
+    long long ldo;
+};
+
+size_t act_bytes_for(uint32_t type, int d, int B)
+{
+    const int U = (d / block_elems(type)) * block_units(type);
+    const int U4 = (U + 3) & ~3;
+    return (size_t)B * U * 32 + 2 * (size_t)B * U4 * 4;
+}
+
+// Validates the jobs and lays out tiles, activations and shared memory.
+// act_base == nullptr plans the sizes only.
+int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
+{
+    pl = Plan{};
+    if (njobs <= 0) return QUANTR_ERR_BAD_ARG;
+    std::map<std::tuple<const float*, long long, int, int, int, int>, int> dedupe;  // x,ldx,d,B,U,perm -> task
+    constexpr size_t kSlotW = 40 * 1024, kTermMax = 16 * 1024;
+    for (int j = 0; j < njobs; ++j) {
+        const JobIn& a = in[j];
+        if (!type_supported(a.type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
+        if (!a.w || !a.x || !a.out || a.n <= 0 || a.B <= 0 || a.B > kMaxB || a.ldx < a.d || a.ldo < a.n)
+            return QUANTR_ERR_BAD_ARG;
+        if (((uintptr_t)a.w & 15) != 0) return QUANTR_ERR_BAD_ARG;
+        const long long rb = row_bytes(a.type, a.d);
+        if (rb <= 0) return QUANTR_ERR_BAD_ARG;
+        JobDesc J{};
+        J.w = a.w;
+        J.out = a.out;
+        J.rb = rb;
+        J.ldo = a.ldo;
+        J.type = (int)a.type;
+        J.n = a.n;
+        J.B = a.B;
+        J.U = (a.d / block_elems(a.type)) * block_units(a.type);
+        J.U4 = (J.U + 3) & ~3;
+        J.nblk = a.type == T_Q8_0 ? J.U : J.U / 8;
+        J.nblk_magic = magic40(J.nblk);
+        const int gR = 16 / gcd_int(rb, 16);  // R*rb % 16 == 0 keeps every tile 16-byte aligned
+        auto round_dn = [&](long long v) { return std::max<long long>(gR, (v / gR) * gR); };
+        long long R = round_dn((long long)(kSlotW / rb));
+        const long long Rt = round_dn((long long)((kTermMax / (4 * (size_t)J.U) - 1) / a.B));
+        R = std::min(R, Rt);
+        R = std::min<long long>(R, ((a.n + gR - 1) / gR) * gR);
+        J.R = (int)R;
+        const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
+        auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, J.U, perm);
+        auto it = dedupe.find(key);
+        int ti;
+        if (it == dedupe.end()) {
+            QTask t{};
+            t.x = a.x;
+            t.ldx = a.ldx;
+            t.U = J.U;
+            t.U4 = J.U4;
+            t.B = a.B;
+            t.type = (int)a.type;
+            t.blk0 = pl.total_blocks;
+            t.act = act_base ? act_base + pl.act_total : nullptr;
+            pl.total_blocks += (long long)a.B * J.U;
+            pl.act_total += (act_bytes_for(a.type, a.d, a.B) + 255) & ~size_t(255);
+            ti = (int)pl.tasks.size();
+            pl.tasks.push_back(t);
+            dedupe[key] = ti;
+        } else {
+            ti = it->second;
+        }
+        J.act = pl.tasks[ti].act;
+        J.act_d_off = (uint32_t)((size_t)a.B * J.U * 32);
+        J.act_s_off = J.act_d_off + (uint32_t)((size_t)a.B * J.U4 * 4);
+        J.act_bytes = J.act_s_off + (uint32_t)((size_t)a.B * J.U4 * 4);
+        pl.jobs.push_back(J);
+    }
+    // Enough items to keep every SM busy: shrink tiles while there are fewer
+    // than two items per SM.
+    auto count_items = [&]() {
+        long long t = 0;
+        for (auto& J : pl.jobs) t += (J.n + J.R - 1) / J.R;
+        return t;
+    };
+    for (int iter = 0; iter < 16 && count_items() < 2LL * sms; ++iter) {
+        bool changed = false;
+        for (auto& J : pl.jobs) {
+            const int gR = 16 / gcd_int(J.rb, 16);
+            const int nr = std::max(gR, ((J.R / 2) / gR) * gR);
+            if (nr < J.R) {
+                J.R = nr;
+                changed = true;
+            }
+        }
+        if (!changed) break;
+    }
+    size_t slot_w = 0, slot_x = 0, term = 0;
+    int item = 0;
+    for (auto& J : pl.jobs) {
+        J.TS = (J.R * J.B) | 1;
+        J.tiles = (J.n + J.R - 1) / J.R;
+        J.item0 = item;
+        item += J.tiles;
+        slot_w = std::max(slot_w, (size_t)((long long)J.R * J.rb));
+        slot_x = std::max(slot_x, (size_t)J.act_bytes);
+        term = std::max(term, (size_t)J.U * J.TS * 4);
+    }
+    auto up128 = [](size_t v) { return (v + 127) & ~size_t(127); };
+    slot_w = up128(slot_w);
+    slot_x = up128(slot_x);
+    term = up128(term);
+    const size_t bars = 1024;
+    int T = kMaxT, S = 0;
+    for (; T >= 3; --T) {
+        const size_t avail = kSmemMax - bars - (size_t)T * term;
+        if (avail > kSmemMax) continue;  // underflow
+        S = (int)std::min<size_t>(kMaxS, avail / (slot_w + slot_x));
+        if (S >= 2) break;
+    }
+    if (S < 2) return QUANTR_ERR_TOO_LARGE;
+    ProgParams& pp = pl.pp;
+    pp.njobs = njobs;
+    pp.total_items = item;
+    pp.slot_bytes = (uint32_t)(slot_w + slot_x);
+    pp.slot_x_off = (uint32_t)slot_w;
+    pp.term_bytes = (uint32_t)term;
+    pp.S = (uint32_t)S;
+    pp.T = (uint32_t)T;
+    pp.slot_off = (uint32_t)bars;
+    pp.term_off = (uint32_t)(bars + (size_t)S * pp.slot_bytes);
+    pl.smem = pp.term_off + (size_t)T * term;
+    pl.grid = std::min(sms, item);
+    pl.qp.ntasks = (int)pl.tasks.size();
+    pl.qp.total_blocks = pl.total_blocks;
+    return QUANTR_OK;
+}
+
+cudaError_t launch_plan(Plan& pl, const JobDesc* d_jobs, const QTask* d_tasks, int* err, cudaStream_t stream)
+{
+    LaunchCfg c;
+    c.stream = stream;
+    static int configured_dev = -1;
+    cudaError_t e = ensure_smem_attr(&k_program, (int)kSmemMax, configured_dev);
+    if (e != cudaSuccess) return e;
+    QParams qp = pl.qp;
+    qp.tasks = d_tasks;
+    if (!d_tasks) qp.inline_task = pl.tasks[0];
+    const long long qgrid = std::max(1LL, std::min<long long>((qp.total_blocks + 7) / 8, 8LL * device_sm_count()));
+    e = launch_ex(&k_quant_tasks, dim3((unsigned)qgrid), dim3(256), 0, c, qp);
+    if (e != cudaSuccess) return e;
+    ProgParams pp = pl.pp;
+    pp.jobs = d_jobs;
+    if (!d_jobs) pp.inline_job = pl.jobs[0];
+    pp.err = err;
+    return launch_ex(&k_program, dim3(pl.grid), dim3(kThreads), pl.smem, c, pp);
+}
+
+} // namespace eng
+
+// Single GEMV through the engine (no allocation: activations go to `ws`).
+// Returns cudaErrorNotSupported when the engine cannot take this shape, so the
+// caller can use the general kernel instead.
+cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, int B, const float* x, long long ldx,
+                               float* out, long long ldo, void* ws, size_t ws_bytes, int* err, cudaStream_t stream)
+{
+    if (!type_supported(type) || ((uintptr_t)w & 15) || B > eng::kMaxB || row_bytes(type, d) <= 0)
+        return cudaErrorNotSupported;
+    if (eng::act_bytes_for(type, d, B) > ws_bytes) return cudaErrorNotSupported;
+    eng::JobIn in{w, type, n, d, B, x, ldx, out, ldo};
+    eng::Plan pl;
+    if (eng::make_plan(&in, 1, static_cast<uint8_t*>(ws), device_sm_count(), pl) != QUANTR_OK)
+        return cudaErrorNotSupported;
+    return eng::launch_plan(pl, nullptr, nullptr, err, stream);
+}
+
+size_t engine_act_bytes(uint32_t type, int d, int B) { return eng::act_bytes_for(type, d, B); }
+
+} // namespace qr
+
+// ----------------------------------------------------------- program API --
+
+struct quantr_program {
+    int device;
+    qr::eng::Plan plan;
+    qr::eng::JobDesc* d_jobs = nullptr;
+    qr::eng::QTask* d_tasks = nullptr;
+    uint8_t* d_act = nullptr;
+};
+
+extern "C" {
+
+int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int njobs)
+{
+    using namespace qr;
+    if (!out || !jobs || njobs <= 0) return QUANTR_ERR_BAD_ARG;
+    *out = nullptr;
+    std::vector<eng::JobIn> in((size_t)njobs);
+    for (int j = 0; j < njobs; ++j)
+        in[j] = eng::JobIn{static_cast<const uint8_t*>(jobs[j].w), jobs[j].type, jobs[j].n, jobs[j].d, jobs[j].B,
+                           jobs[j].x, jobs[j].ldx, jobs[j].out, jobs[j].ldo};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return QUANTR_ERR_NO_DEVICE;
+    }
+    const int sms = device_sm_count();
+    eng::Plan sizing;
+    int rc = eng::make_plan(in.data(), njobs, nullptr, sms, sizing);
+    if (rc) return rc;
+    quantr_program* p = new (std::nothrow) quantr_program();
+    if (!p) return QUANTR_ERR_OOM;
+    p->device = dev;
+    if (cudaMalloc((void**)&p->d_act, std::max<size_t>(sizing.act_total, 256)) != cudaSuccess) {
+        cudaGetLastError();
+        delete p;
+        return QUANTR_ERR_OOM;
+    }
+    rc = eng::make_plan(in.data(), njobs, p->d_act, sms, p->plan);
+    cudaError_t e = cudaSuccess;
+    if (!rc) {
+        e = cudaMalloc((void**)&p->d_jobs, p->plan.jobs.size() * sizeof(eng::JobDesc));
+        if (e == cudaSuccess) e = cudaMalloc((void**)&p->d_tasks, p->plan.tasks.size() * sizeof(eng::QTask));
+        if (e == cudaSuccess)
+            e = cudaMemcpy(p->d_jobs, p->plan.jobs.data(), p->plan.jobs.size() * sizeof(eng::JobDesc),
+                           cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(p->d_tasks, p->plan.tasks.data(), p->plan.tasks.size() * sizeof(eng::QTask),
+                           cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) rc = e == cudaErrorMemoryAllocation ? QUANTR_ERR_OOM : QUANTR_ERR_CUDA;
+    }
+    if (rc) {
+        cudaGetLastError();
+        quantr_program_destroy(p);
+        return rc;
+    }
+    *out = p;
+    return QUANTR_OK;
+}
+
+int quantr_program_run(quantr_program* p, void* stream)
+{
+    if (!p) return QUANTR_ERR_BAD_ARG;
+    int dev = -1;
+    cudaGetDevice(&dev);
+    if (dev != p->device) return QUANTR_ERR_BAD_ARG;
+    cudaError_t e = qr::eng::launch_plan(p->plan, p->d_jobs, p->d_tasks, qr::device_error_word(),
+                                         static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return QUANTR_ERR_CUDA;
+    }
+    return QUANTR_OK;
+}
+
+void quantr_program_destroy(quantr_program* p)
+{
+    if (!p) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p->device);
+    cudaDeviceSynchronize();
+    cudaFree(p->d_jobs);
+    cudaFree(p->d_tasks);
+    cudaFree(p->d_act);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete p;
+}
+
+int quantr_program_info(const quantr_program* p, int* items, int* grid, int* smem_bytes)
+{
+    if (!p) return QUANTR_ERR_BAD_ARG;
+    if (items) *items = p->plan.pp.total_items;
+    if (grid) *grid = p->plan.grid;
+    if (smem_bytes) *smem_bytes = (int)p->plan.smem;
+    return QUANTR_OK;
+}
+
+} // extern "C"

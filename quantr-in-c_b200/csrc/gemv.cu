@@ -1,4 +1,4 @@
-// gemv.cu -- activation quantizer and fused quantized GEMV for sm_100a.
+// gemv.cu -- activation quantizer and the per-call fused quantized GEMV.
 //
 // Parity design.  The reference (src/quant.c:242-437, scalar build) computes
 // every output row as a left-to-right fp32 sum over 32-element units of a term
@@ -11,126 +11,35 @@
 // The result is bit-identical to the reference's scalar build; the parity
 // tests assert that, which is stronger than the 1e-5 rel / 1e-6 abs bar.
 //
-// Data movement.  A CTA owns G consecutive rows.  Their packed bytes are one
-// contiguous range, staged into shared memory with cp.async.bulk (the 16-byte
-// aligned body) plus plain loads for the <16-byte head and tail, so every
-// block layout (34/144/176/210-byte blocks, any row alignment) streams from
-// HBM with full coalescing.  The bulk copies are issued before
-// griddepcontrol.wait, so under programmatic dependent launch the weight
-// stream of this GEMV overlaps the tail of the kernel that produces x.
+// k_gemv is the general kernel (any weight alignment, any shape that fits one
+// row group in shared memory).  A CTA owns G consecutive rows.  Their packed
+// bytes are one contiguous range, staged into shared memory with
+// cp.async.bulk (the 16-byte aligned body) plus plain loads for the <16-byte
+// head and tail.  The bulk copies are issued before griddepcontrol.wait, so
+// under programmatic dependent launch the weight stream overlaps the tail of
+// the kernel that produces x.  The persistent engine (engine.cu) is the fast
+// path for 16-byte aligned weights.
+#include "device_common.cuh"
 #include "formats.cuh"
 #include "kernels.cuh"
+#include "launch_util.cuh"
+#include "quant_decode.cuh"
 
 #include <algorithm>
-#include <atomic>
-#include <utility>
 #include <cuda_runtime.h>
 
 namespace qr {
 
-static std::atomic<unsigned long long> g_launches{0};
+std::atomic<unsigned long long> g_launches{0};
 
 unsigned long long launch_count() { return g_launches.load(); }
 
 namespace {
 
 constexpr int kThreads = 256;
-constexpr uint32_t kChunk = 16384;               // bytes per bulk copy
-constexpr unsigned long long kWaitNs = 250000000ull;  // bounded waits: 250 ms
-
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-
-__device__ __forceinline__ uint32_t sptr(const void* p)
-{
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ unsigned long long gtimer()
-{
-    unsigned long long t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count)
-{
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sptr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes)
-{
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sptr(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
-{
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(sptr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Waits for the barrier phase; gives up after kWaitNs and records the timeout
-// in *err (when given).  Never spins unboundedly.
-__device__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err)
-{
-    if (mbar_try_wait(bar, parity)) return true;
-    const unsigned long long t0 = gtimer();
-    while (!mbar_try_wait(bar, parity)) {
-        if (gtimer() - t0 > kWaitNs) {
-            if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);
-            return false;
-        }
-    }
-    return true;
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
-{
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            sptr(dst)),
-        "l"(src), "r"(bytes), "r"(sptr(bar))
-        : "memory");
-}
-
-// 32-bit word starting at an arbitrary shared-memory byte offset `off`.
-__device__ __forceinline__ uint32_t ld_u32(const uint32_t* s32, uint32_t off)
-{
-    const uint32_t a = s32[off >> 2], b = s32[(off >> 2) + 1];
-    return __funnelshift_r(a, b, (off & 3) * 8);
-}
-
-// N consecutive 32-bit words starting at an arbitrary byte offset.
-template <int N>
-__device__ __forceinline__ void ld_words(const uint32_t* s32, uint32_t off, uint32_t* out)
-{
-    uint32_t r[N + 1];
-    const uint32_t base = off >> 2, sh = (off & 3) * 8;
-#pragma unroll
-    for (int k = 0; k <= N; ++k) r[k] = s32[base + k];
-#pragma unroll
-    for (int k = 0; k < N; ++k) out[k] = __funnelshift_r(r[k], r[k + 1], sh);
-}
+constexpr uint32_t kChunk = 16384;  // bytes per bulk copy
 
 // --------------------------------------------------------------- quantizer --
-
-// (int8_t)lrintf(v) as the x86-64 reference computes it: lrintf converts to a
-// 64-bit long (cvtss2si), and a NaN or |v| >= 2^63 yields the "integer
-// indefinite" 0x8000000000000000, whose low byte is 0.  CUDA's conversions
-// saturate instead, so out-of-range values are mapped explicitly.  (Reached
-// when a denormal block scale makes 1/d overflow to infinity.)
-__device__ __forceinline__ int8_t lrintf_to_i8(float v)
-{
-    return fabsf(v) < 9.2233720368547758e18f ? (int8_t)__float2ll_rn(v) : (int8_t)0;
-}
 
 // One warp per 32-element block: reference quantize_row_q8_0
 // (src/quant.c:143-158) with IEEE division, the fp32 reciprocal of the
@@ -215,104 +124,6 @@ struct KParams {
     uint32_t w_off, x_off, xd_off, xs_off, t_off;  // shared-memory carve-up
 };
 
-// Activation words are stored in shared memory in the order the weight
-// decoder produces its operands, so one dp4a pairs matching elements:
-//   Q8_0      natural order;
-//   Q4_K/Q5_K per 8 elements: [even 4 | odd 4] (nibble-interleaved weights);
-//   Q6_K      per 16 elements: 4x4 byte transpose (lane k of operand m is
-//             element 4k+m, matching the 2-bit qh fields of one byte).
-template <uint32_t TYPE>
-__device__ __forceinline__ uint4 permute_x16(uint4 v)
-{
-    if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-        return make_uint4(__byte_perm(v.x, v.y, 0x6420), __byte_perm(v.x, v.y, 0x7531),
-                          __byte_perm(v.z, v.w, 0x6420), __byte_perm(v.z, v.w, 0x7531));
-    } else if (TYPE == T_Q6_K) {
-        const uint32_t p01l = __byte_perm(v.x, v.y, 0x5140), p01h = __byte_perm(v.x, v.y, 0x7362);
-        const uint32_t p23l = __byte_perm(v.z, v.w, 0x5140), p23h = __byte_perm(v.z, v.w, 0x7362);
-        return make_uint4(__byte_perm(p01l, p23l, 0x5410), __byte_perm(p01l, p23l, 0x7632),
-                          __byte_perm(p01h, p23h, 0x5410), __byte_perm(p01h, p23h, 0x7632));
-    }
-    return v;
-}
-
-// Spreads bits 0,2,4,6 of a byte to bit 4 of byte lanes 0..3.  Collisions of
-// the multiply only carry into bits 11, 17 and 23, which the mask drops.
-__device__ __forceinline__ uint32_t spread_even_bits_to_b4(uint32_t hb)
-{
-    return ((hb & 0x55u) * 0x410410u) & 0x10101010u;
-}
-
-// Decoded unit: 8 dp4a operands plus the per-unit scale data.
-struct Unit {
-    uint32_t wq[8];
-    float a, b;   // Q8_0: a = d_w | K4/K5: a = sc, b = m | Q6_K: a = sc
-};
-
-template <uint32_t TYPE>
-__device__ __forceinline__ void decode_unit(const uint32_t* s32, const uint8_t* s8, uint32_t row_off, int u,
-                                            Unit& o)
-{
-    if (TYPE == T_Q8_0) {
-        const uint32_t blk = row_off + 34u * u;
-        o.a = h2f_ref(ld_u32(s32, blk) & 0xFFFFu);
-        ld_words<8>(s32, blk + 2, o.wq);
-    } else if (TYPE == T_Q4_K || TYPE == T_Q5_K) {
-        const int j = u & 7;
-        const uint32_t sb = row_off + (uint32_t)block_bytes(TYPE) * (uint32_t)(u >> 3);
-        const uint32_t hdr = ld_u32(s32, sb);
-        const uint32_t sc = s8[sb + 4 + j];
-        // src/quant.c:385-386: sc = (scales[j]&63)*d, m = (scales[j]>>6)*dmin.
-        o.a = __fmul_rn((float)(sc & 63u), h2f_ref(hdr & 0xFFFFu));
-        o.b = __fmul_rn((float)(sc >> 6), h2f_ref(hdr >> 16));
-        uint32_t qw[4];
-        ld_words<4>(s32, sb + (TYPE == T_Q4_K ? 16u : 48u) + 16u * j, qw);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            o.wq[2 * i] = qw[i] & 0x0F0F0F0Fu;
-            o.wq[2 * i + 1] = (qw[i] >> 4) & 0x0F0F0F0Fu;
-        }
-        if (TYPE == T_Q5_K) {
-            const uint32_t H = ld_u32(s32, sb + 16u + 4u * j);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t hb = (H >> (8 * i)) & 0xFFu;
-                o.wq[2 * i] |= spread_even_bits_to_b4(hb);
-                o.wq[2 * i + 1] |= spread_even_bits_to_b4(hb >> 1);
-            }
-        }
-    } else {  // Q6_K
-        const int j = u & 7;
-        const uint32_t sb = row_off + 210u * (uint32_t)(u >> 3);
-        const float d = h2f_ref(ld_u32(s32, sb + 208) & 0xFFFFu);
-        o.a = __fmul_rn((float)(int8_t)s8[sb + 192 + j], d);  // src/quant.c:423
-        uint32_t ql[4], qh[2];
-        ld_words<4>(s32, sb + 16u * j, ql);
-        ld_words<2>(s32, sb + 128u + 8u * j, qh);
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            const uint32_t s0 = __byte_perm(ql[2 * h], ql[2 * h + 1], 0x6420);
-            const uint32_t s1 = __byte_perm(ql[2 * h], ql[2 * h + 1], 0x7531);
-            const uint32_t nib[4] = {s0 & 0x0F0F0F0Fu, (s0 >> 4) & 0x0F0F0F0Fu, s1 & 0x0F0F0F0Fu,
-                                     (s1 >> 4) & 0x0F0F0F0Fu};
-#pragma unroll
-            for (int m = 0; m < 4; ++m) o.wq[4 * h + m] = nib[m] | (((qh[h] >> (2 * m)) & 0x03030303u) << 4);
-        }
-    }
-}
-
-// The reference's per-unit term, operation for operation.
-template <uint32_t TYPE>
-__device__ __forceinline__ float unit_term(const Unit& o, int isum, int bsum, float dx)
-{
-    if (TYPE == T_Q8_0)  // src/quant.c:284: (float)isum * d_w * d_x
-        return __fmul_rn(__fmul_rn((float)isum, o.a), dx);
-    if (TYPE == T_Q6_K)  // src/quant.c:433: sc * (float)isum * bd
-        return __fmul_rn(__fmul_rn(o.a, (float)isum), dx);
-    // src/quant.c:399: (sc*(float)isum - m*(float)bsum) * bd
-    return __fmul_rn(__fsub_rn(__fmul_rn(o.a, (float)isum), __fmul_rn(o.b, (float)bsum)), dx);
-}
-
 template <uint32_t TYPE, int BT, bool DBG>
 __global__ void __launch_bounds__(kThreads) k_gemv(KParams p)
 {
@@ -336,7 +147,7 @@ __global__ void __launch_bounds__(kThreads) k_gemv(KParams p)
 
     if (tid == 0) {
         mbar_init(bar, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_fence_init();
     }
     __syncthreads();
     if (tid == 0) {
@@ -387,19 +198,10 @@ __global__ void __launch_bounds__(kThreads) k_gemv(KParams p)
         for (int t = 0; t < BT; ++t) {
             if (t < p.B) {
                 const uint4* xv = reinterpret_cast<const uint4*>(xq + (t * U + u) * 32);
-                const uint4 xa = xv[0], xb = xv[1];
-                int isum = 0;
-                isum = __dp4a((int)o.wq[0], (int)xa.x, isum);
-                isum = __dp4a((int)o.wq[1], (int)xa.y, isum);
-                isum = __dp4a((int)o.wq[2], (int)xa.z, isum);
-                isum = __dp4a((int)o.wq[3], (int)xa.w, isum);
-                isum = __dp4a((int)o.wq[4], (int)xb.x, isum);
-                isum = __dp4a((int)o.wq[5], (int)xb.y, isum);
-                isum = __dp4a((int)o.wq[6], (int)xb.z, isum);
-                isum = __dp4a((int)o.wq[7], (int)xb.w, isum);
+                int isum = dot8(o.wq, xv[0], xv[1]);
                 const int bsum = xs[t * U + u];
                 if (TYPE == T_Q6_K) isum -= 32 * bsum;  // quants stored with +32 offset
-                terms[u * TS + g * BT + t] = unit_term<TYPE>(o, isum, bsum, xd[t * U + u]);
+                terms[u * TS + g * BT + t] = unit_term<TYPE>(o.a, o.b, isum, bsum, xd[t * U + u]);
                 if (DBG) {
                     const long long k = ((long long)t * p.n + r0 + g) * U + u;
                     p.dbg_isum[k] = isum;
@@ -479,24 +281,6 @@ __global__ void k_dequantize(float* __restrict__ out, const uint8_t* __restrict_
     }
 }
 
-template <typename... KArgs, typename... Args>
-cudaError_t launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, const LaunchCfg& c,
-                      Args&&... args)
-{
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = grid;
-    cfg.blockDim = block;
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = c.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = c.pdl ? 1 : 0;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    g_launches.fetch_add(1, std::memory_order_relaxed);
-    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-}
-
 int grid_for_warps(long long warps)
 {
     const long long per = kThreads / 32;
@@ -554,14 +338,9 @@ cudaError_t gemv_typed(const GemvArgs& g, const LaunchCfg& c, int B0, int nb)
     kp.dbg_bsum = g.dbg_bsum ? g.dbg_bsum + (long long)B0 * g.n * U : nullptr;
     kp.err = g.err;
     auto kern = &k_gemv<TYPE, BT, DBG>;
-    static int configured_dev = -1;  // one attribute call per device is enough
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (configured_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax);
-        if (e != cudaSuccess) return e;
-        configured_dev = dev;
-    }
+    static int configured_dev = -1;
+    cudaError_t e = ensure_smem_attr(kern, (int)kSmemMax, configured_dev);
+    if (e != cudaSuccess) return e;
     const int grid = (g.n + G - 1) / G;
     return launch_ex(kern, dim3(grid), dim3(kThreads), smem, c, kp);
 }

@@ -68,4 +68,18 @@ int device_sm_count();
 // Kernel launches issued by this library since load.
 unsigned long long launch_count();
 
+// Per-device error word that kernels launched through the device API report
+// bounded-wait timeouts into (allocated on first use; api.cu).
+int* device_error_word();
+
+// Single GEMV through the persistent engine (engine.cu): x is quantized into
+// `ws` (engine_act_bytes of it) and the engine program runs one job.  Returns
+// cudaErrorNotSupported when the engine cannot take the call (unaligned
+// weights, B > 16, workspace too small, shape too large), so the caller can
+// use launch_quantize + launch_gemv instead.
+cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, int B, const float* x,
+                               long long ldx, float* out, long long ldo, void* ws, size_t ws_bytes, int* err,
+                               cudaStream_t stream);
+size_t engine_act_bytes(uint32_t type, int d, int B);
+
 } // namespace qr

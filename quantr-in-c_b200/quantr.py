@@ -53,7 +53,17 @@ SIGNATURES = {
     "quantr_gemv_partials_dev": (_i, [_vp, _vp, _vp, _vp, _vp, _u32, _i, _i, _i, _vp, _sz, _vp]),
     "quantr_gpu_device_status": (_i, [_vp, _i]),
     "quantr_gemv_noalloc_dev": (_i, [_vp, _ll, _vp, _ll, _vp, _u32, _i, _i, _i, _vp]),
+    "quantr_program_create": (_i, [_c.POINTER(_vp), _vp, _i]),
+    "quantr_program_run": (_i, [_vp, _vp]),
+    "quantr_program_destroy": (None, [_vp]),
+    "quantr_program_info": (_i, [_vp, _c.POINTER(_i), _c.POINTER(_i), _c.POINTER(_i)]),
 }
+
+
+class GemvJob(ctypes.Structure):
+    """quantr_gemv_job (include/quantr_cuda.h)."""
+    _fields_ = [("w", _vp), ("type", _u32), ("n", _i), ("d", _i), ("B", _i), ("x", _vp), ("ldx", _ll),
+                ("out", _vp), ("ldo", _ll)]
 
 
 class QuantrError(RuntimeError):
@@ -203,6 +213,44 @@ def gemv_noalloc_dev(out, ldo, x, ldx, w, type_, n, d, B, stream=0):
     rc = lib().quantr_gemv_noalloc_dev(out, ldo, x, ldx, w, type_, n, d, B, stream or None)
     if rc:
         raise QuantrError(rc, "quantr_gemv_noalloc_dev")
+
+
+class Program:
+    """A GEMV program: many independent device GEMVs run by one engine launch.
+
+    jobs: iterable of (w_ptr, type, n, d, B, x_ptr, ldx, out_ptr, ldo) with
+    device addresses as ints.  Created on the current CUDA device."""
+
+    def __init__(self, jobs):
+        jobs = list(jobs)
+        arr = (GemvJob * len(jobs))(*[GemvJob(*j) for j in jobs])
+        h = ctypes.c_void_p()
+        rc = lib().quantr_program_create(ctypes.byref(h), ctypes.cast(arr, ctypes.c_void_p), len(jobs))
+        if rc:
+            raise QuantrError(rc, "quantr_program_create")
+        self._h = h
+        self.njobs = len(jobs)
+
+    def run(self, stream=0):
+        rc = lib().quantr_program_run(self._h, stream or None)
+        if rc:
+            raise QuantrError(rc, "quantr_program_run")
+
+    def info(self):
+        a, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        lib().quantr_program_info(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        return {"items": a.value, "grid": b.value, "smem": c.value}
+
+    def close(self):
+        if self._h:
+            lib().quantr_program_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def device_status(stream=0, reset=True):

@@ -47,8 +47,9 @@ def test_error_strings_without_device():
 
 
 def test_workspace_size_is_host_arithmetic():
-    # 40 bytes per 32-element block, each region 256-byte aligned.
-    assert quantr.workspace_bytes(2048, 1) == 2048 + 256 + 256
+    # 40 bytes per 32-element block, each region 256-byte aligned, plus the
+    # engine's per-token padding allowance.
+    assert quantr.workspace_bytes(2048, 1) == 2048 + 256 + 256 + 256 + 32
     assert quantr.workspace_bytes(4864, 16) >= 16 * 152 * 40
 
 
