@@ -85,6 +85,54 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// Explicit shared-memory accesses by 32-bit shared-window address (always
+// LDS/STS, never generic loads).
+__device__ __forceinline__ uint4 lds128(uint32_t a)
+{
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint2 lds64(uint32_t a)
+{
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a)
+{
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ float ldsf(uint32_t a)
+{
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void stsf(uint32_t a, float v)
+{
+    asm volatile("st.shared.f32 [%0], %1;" ::"r"(a), "f"(v) : "memory");
+}
+// 32-bit word at an arbitrary shared byte address (two aligned loads).
+__device__ __forceinline__ uint32_t lds32_u(uint32_t a)
+{
+    const uint32_t b = a & ~3u;
+    return __funnelshift_r(lds32(b), lds32(b + 4), (a & 3) * 8);
+}
+// N words from an arbitrary shared byte address.
+template <int N>
+__device__ __forceinline__ void lds_words_u(uint32_t a, uint32_t* out)
+{
+    uint32_t r[N + 1];
+    const uint32_t b = a & ~3u, sh = (a & 3) * 8;
+#pragma unroll
+    for (int k = 0; k <= N; ++k) r[k] = lds32(b + 4 * k);
+#pragma unroll
+    for (int k = 0; k < N; ++k) out[k] = __funnelshift_r(r[k], r[k + 1], sh);
+}
+
 // 32-bit word starting at an arbitrary shared-memory byte offset `off`.
 __device__ __forceinline__ uint32_t ld_u32(const uint32_t* s32, uint32_t off)
 {

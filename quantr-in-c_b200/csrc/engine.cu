@@ -5,20 +5,23 @@
 // R_j rows; the (job, tile) items are dealt round-robin to one persistent CTA
 // per SM.  Inside a CTA three warp roles form a pipeline:
 //
-//   producer (1 warp)   streams each item's packed weight rows (one
-//                       contiguous, 16-byte aligned range) and the job's
-//                       quantized activations into a ring of S shared-memory
-//                       slots with cp.async.bulk; mbarrier transaction
-//                       counts signal "slot full".  It runs up to S items ahead,
-//                       so HBM streaming never waits for compute.
-//   consumers (8 warps) decode one row x super-block (or Q8_0 block) per thread
-//                       and evaluate the reference's exact per-unit terms
-//                       (dp4a integer sums, explicitly rounded fp32 ops) into
-//                       one of T term buffers.
-//   chain (2 warps)     sum each (row, token)'s terms left to right - the
-//                       reference's accumulation order, src/quant.c:279-285,
-//                       :384-401, :422-435 - and store the fp32 outputs, while
-//                       the consumers already work on the next item.
+//   producer (1 warp)    streams each item's packed weight rows (one
+//                        contiguous, 16-byte aligned range) and the job's
+//                        quantized activations into a ring of S shared-memory
+//                        slots with cp.async.bulk, plus a small item header;
+//                        mbarrier transaction counts signal "slot full".  It
+//                        runs up to S items ahead, so HBM streaming never waits
+//                        for compute.
+//   consumers (12 warps) decode one row x super-block (or Q8_0 block) per
+//                        thread and evaluate the reference's exact per-unit
+//                        terms (dp4a integer sums, explicitly rounded fp32
+//                        ops) into one of T term buffers.  Work is dealt
+//                        round-robin over the concatenation of all items, so a
+//                        thread idle at the end of one tile starts the next.
+//   chain (2 warps)      sum each (row, token)'s terms left to right - the
+//                        reference's accumulation order, src/quant.c:279-285,
+//                        :384-401, :422-435 - and store the fp32 outputs,
+//                        while the consumers already work on later items.
 //
 // All waits are bounded (250 ms) and a CTA-wide abort flag stops every role if
 // one of them gives up; slots with copies in flight are drained (bounded)
@@ -56,18 +59,28 @@ constexpr int kMaxS = 4, kMaxT = 4;
 constexpr int kMaxB = 16;
 constexpr size_t kSmemMax = 227 * 1024;
 constexpr uint32_t kBulkChunk = 32768;
+constexpr uint32_t kHdr = 128;  // bytes reserved for the item header in slots and term buffers
 
 // Device-side job description (built by the host planner).
 struct JobDesc {
     const uint8_t* w;    // 16-byte aligned packed rows
     float* out;          // out[t*ldo + r]
-    const uint8_t* act;  // quantized activations: q[B][U][32] | d[B][U4] | s[B][U4]
+    const uint8_t* act;  // quantized activations: q[B][U][32] | ds[B][U] (fp32 scale, int32 sum)
     long long rb, ldo;
-    uint32_t act_bytes;  // bytes of the act region (all three parts)
-    uint32_t act_d_off, act_s_off;
-    int type, n, U, U4, nblk, B, R, TS, tiles, item0;
+    uint32_t act_bytes, ds_off;
+    int type, n, U, nblk, B, R, TS, tiles, item0;
     unsigned long long nblk_magic;  // floor(it / nblk) == (it * magic) >> 40
 };
+
+// Item header the producer writes at the start of a slot (and the consumers
+// forward to the chain in the term buffer).
+struct ItemHdr {
+    float* out;  // first output row of the tile
+    long long ldo;
+    uint32_t type, rb, nblk, B, U, TS, ds_off, rows;
+    unsigned long long magic;
+};
+static_assert(sizeof(ItemHdr) <= kHdr, "item header too large");
 
 struct ProgParams {
     const JobDesc* jobs;  // null: use inline_job
@@ -84,7 +97,8 @@ struct QTask {
     uint8_t* act;
     long long ldx;
     long long blk0;  // first global block index of this task
-    int U, U4, B, type;
+    int U, B, type;
+    uint32_t ds_off;
 };
 
 struct QParams {
@@ -126,18 +140,16 @@ __global__ void __launch_bounds__(256) k_quant_tasks(const __grid_constant__ QPa
         // super-blocks read neighbouring units; Q8_0 keeps block order.
         const int u = T.type == T_Q8_0 ? b : (b & 7) * (T.U >> 3) + (b >> 3);
         const float a = fabsf(v);
-        const uint32_t abits = (a == a) ? __float_as_uint(a) : 0u;
+        const uint32_t abits = (a == a) ? __float_as_uint(a) : 0u;  // the reference skips NaN
         const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, abits));
         const float dd = __fdiv_rn(amax, 127.0f);
         const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
         const int8_t qq = lrintf_to_i8(__fmul_rn(v, id));
         const int sum = __reduce_add_sync(0xffffffffu, (int)qq);
         T.act[((long long)t * T.U + u) * 32 + perm_pos(T.type, lane)] = (uint8_t)qq;
-        if (lane == 0) {
-            const long long di = (long long)T.B * T.U * 32;
-            reinterpret_cast<float*>(T.act + di)[t * T.U4 + u] = h2f_ref(f2h_ref(dd));
-            reinterpret_cast<int32_t*>(T.act + di + (long long)T.B * T.U4 * 4)[t * T.U4 + u] = sum;
-        }
+        if (lane == 0)
+            reinterpret_cast<uint2*>(T.act + T.ds_off)[t * T.U + u] =
+                make_uint2(__float_as_uint(h2f_ref(f2h_ref(dd))), (uint32_t)sum);
     }
 }
 
@@ -148,70 +160,73 @@ __device__ __forceinline__ int job_of(const JobDesc* jobs, int njobs, int item, 
 }
 
 // ------------------------------------------------------------ consumers --
+//
+// All shared-memory accesses below are `sm + 32-bit offset` with `sm` the
+// kernel's __shared__ base, so they compile to shared-window loads/stores.
 
-// Everything the consumers need for one item, copied into registers once per
-// item (reading it through the job table inside the loops would force a
-// reload after every shared-memory store).
+// Per-item values, read from the item header into registers once per item.
 struct Item {
-    uint32_t w;                        // shared-memory byte offset of the tile (16-byte aligned)
-    const int8_t* __restrict__ xq;     // [B][U][32] permuted activation quants
-    const float* __restrict__ xd;      // [B][U4] decoded block scales
-    const int32_t* __restrict__ xs;    // [B][U4] quant sums
-    float* __restrict__ terms;         // [U][TS] per-unit terms, natural unit order
-    int rb, nblk, B, U, U4, TS;
+    uint32_t tile;   // offset of the weight tile
+    uint32_t xq;     // offset of q[B][U][32]
+    uint32_t ds;     // offset of ds[B][U] (8 bytes each)
+    uint32_t terms;  // offset of terms[U][TS]
+    int rb, nblk, B, U, TS;
 };
 
-// Activation unit of sub-block j of super-block s (see k_quant_tasks).
-__device__ __forceinline__ int xunit(const Item& it, int s, int j) { return j * it.nblk + s; }
-
-// Terms of one unit for every token.  kind: 0 = Q8_0, 1 = Q4_K/Q5_K, 2 = Q6_K.
-template <int KIND>
-__device__ __forceinline__ void put_terms(const Item& it, int g, int tu, int xu, float a, float b,
+template <bool ONE, int KIND>
+__device__ __forceinline__ void put_terms(uint8_t* sm, const Item& it, int g, int tu, int xu, float a, float b,
                                           const uint32_t (&wq)[8])
 {
-    for (int t = 0; t < it.B; ++t) {
-        const uint4* xv = reinterpret_cast<const uint4*>(it.xq + (t * it.U + xu) * 32);
-        int isum = dot8(wq, xv[0], xv[1]);
-        const int bsum = it.xs[t * it.U4 + xu];
-        const float dx = it.xd[t * it.U4 + xu];
+    const int nb = ONE ? 1 : it.B;
+    for (int t = 0; t < nb; ++t) {
+        const uint32_t xo = it.xq + (uint32_t)((t * it.U + xu) * 32);
+        const uint4 xa = *reinterpret_cast<const uint4*>(sm + xo);
+        const uint4 xb = *reinterpret_cast<const uint4*>(sm + xo + 16);
+        const uint2 ds = *reinterpret_cast<const uint2*>(sm + it.ds + (uint32_t)((t * it.U + xu) * 8));
+        int isum = dot8(wq, xa, xb);
+        const int bsum = (int)ds.y;
+        const float dx = __uint_as_float(ds.x);
         float term;
         if (KIND == 0) term = unit_term<T_Q8_0>(a, b, isum, bsum, dx);
         else if (KIND == 2) term = unit_term<T_Q6_K>(a, b, isum - 32 * bsum, bsum, dx);
         else term = unit_term<T_Q4_K>(a, b, isum, bsum, dx);
-        it.terms[tu * it.TS + g * it.B + t] = term;
+        *reinterpret_cast<float*>(sm + it.terms + (uint32_t)((tu * it.TS + g * nb + t) * 4)) = term;
     }
 }
 
 // Q4_K / Q5_K super-block (16-byte aligned): header and quants by 128-bit
 // loads.  Q4_K keeps the high nibble in place and divides its dp4a product
 // by 16 (exact: every product is a multiple of 16).
-template <uint32_t TYPE>
-__device__ __forceinline__ void consume_k45(const uint8_t* __restrict__ sm, const Item& it, int g, int s)
+template <uint32_t TYPE, bool ONE>
+__device__ __forceinline__ void consume_k45(uint8_t* sm, const Item& it, int g, int s)
 {
-    const uint8_t* sb = sm + it.w + g * it.rb + s * block_bytes(TYPE);
-    const uint4 hdr = *reinterpret_cast<const uint4*>(sb);
+    const uint32_t sb = it.tile + (uint32_t)(g * it.rb + s * block_bytes(TYPE));
+    const uint4 hdr = *reinterpret_cast<const uint4*>(sm + sb);
     const float d = h2f_ref(hdr.x & 0xFFFFu), dmin = h2f_ref(hdr.x >> 16);
     uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = qh0;
     if (TYPE == T_Q5_K) {
-        qh0 = *reinterpret_cast<const uint4*>(sb + 16);
-        qh1 = *reinterpret_cast<const uint4*>(sb + 32);
+        qh0 = *reinterpret_cast<const uint4*>(sm + sb + 16);
+        qh1 = *reinterpret_cast<const uint4*>(sm + sb + 32);
     }
-    const uint8_t* qs = sb + (TYPE == T_Q4_K ? 16 : 48);
+    const uint32_t qs = sb + (TYPE == T_Q4_K ? 16u : 48u);
+    const int nb = ONE ? 1 : it.B;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint32_t scb = ((j < 4 ? hdr.y : hdr.z) >> (8 * (j & 3))) & 0xFFu;
         const float sc = __fmul_rn((float)(scb & 63u), d);    // src/quant.c:385
         const float m = __fmul_rn((float)(scb >> 6), dmin);   // src/quant.c:386
-        const uint4 q = *reinterpret_cast<const uint4*>(qs + 16 * j);
-        const int tu = 8 * s + j, xu = xunit(it, s, j);
+        const uint4 q = *reinterpret_cast<const uint4*>(sm + qs + 16 * j);
+        const int tu = 8 * s + j, xu = j * it.nblk + s;
         if (TYPE == T_Q4_K) {
             const uint32_t l0 = q.x & 0x0F0F0F0Fu, l1 = q.y & 0x0F0F0F0Fu, l2 = q.z & 0x0F0F0F0Fu,
                            l3 = q.w & 0x0F0F0F0Fu;
             const uint32_t h0 = q.x & 0xF0F0F0F0u, h1 = q.y & 0xF0F0F0F0u, h2 = q.z & 0xF0F0F0F0u,
                            h3 = q.w & 0xF0F0F0F0u;
-            for (int t = 0; t < it.B; ++t) {
-                const uint4* xv = reinterpret_cast<const uint4*>(it.xq + (t * it.U + xu) * 32);
-                const uint4 xa = xv[0], xb = xv[1];
+            for (int t = 0; t < nb; ++t) {
+                const uint32_t xo = it.xq + (uint32_t)((t * it.U + xu) * 32);
+                const uint4 xa = *reinterpret_cast<const uint4*>(sm + xo);
+                const uint4 xb = *reinterpret_cast<const uint4*>(sm + xo + 16);
+                const uint2 ds = *reinterpret_cast<const uint2*>(sm + it.ds + (uint32_t)((t * it.U + xu) * 8));
                 int lo = __dp4a((int)l0, (int)xa.x, 0);
                 lo = __dp4a((int)l1, (int)xa.z, lo);
                 lo = __dp4a((int)l2, (int)xb.x, lo);
@@ -221,8 +236,8 @@ __device__ __forceinline__ void consume_k45(const uint8_t* __restrict__ sm, cons
                 hi = dp4a_us(h2, (int)xb.y, hi);
                 hi = dp4a_us(h3, (int)xb.w, hi);
                 const int isum = lo + (hi >> 4);
-                const int bsum = it.xs[t * it.U4 + xu];
-                it.terms[tu * it.TS + g * it.B + t] = unit_term<T_Q4_K>(sc, m, isum, bsum, it.xd[t * it.U4 + xu]);
+                const float term = unit_term<T_Q4_K>(sc, m, isum, (int)ds.y, __uint_as_float(ds.x));
+                *reinterpret_cast<float*>(sm + it.terms + (uint32_t)((tu * it.TS + g * nb + t) * 4)) = term;
             }
         } else {
             const uint32_t H = (j < 4) ? (j == 0 ? qh0.x : j == 1 ? qh0.y : j == 2 ? qh0.z : qh0.w)
@@ -235,16 +250,17 @@ __device__ __forceinline__ void consume_k45(const uint8_t* __restrict__ sm, cons
                 wq[2 * i] = (qw[i] & 0x0F0F0F0Fu) | spread_even_bits_to_b4(hb);
                 wq[2 * i + 1] = ((qw[i] >> 4) & 0x0F0F0F0Fu) | spread_even_bits_to_b4(hb >> 1);
             }
-            put_terms<1>(it, g, tu, xu, sc, m, wq);
+            put_terms<ONE, 1>(sm, it, g, tu, xu, sc, m, wq);
         }
     }
 }
 
 // Q6_K super-block (2-byte aligned: 210-byte blocks) by funnel-shifted words.
-__device__ __forceinline__ void consume_q6k(const uint8_t* __restrict__ sm, const Item& it, int g, int s)
+template <bool ONE>
+__device__ __forceinline__ void consume_q6k(uint8_t* sm, const Item& it, int g, int s)
 {
     const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
-    const uint32_t sb = it.w + (uint32_t)(g * it.rb) + 210u * (uint32_t)s;
+    const uint32_t sb = it.tile + (uint32_t)(g * it.rb) + 210u * (uint32_t)s;
     uint32_t scw[2];
     ld_words<2>(s32, sb + 192, scw);
     const float d = h2f_ref(ld_u32(s32, sb + 208) & 0xFFFFu);
@@ -263,33 +279,41 @@ __device__ __forceinline__ void consume_q6k(const uint8_t* __restrict__ sm, cons
 #pragma unroll
             for (int m = 0; m < 4; ++m) wq[4 * h + m] = nib[m] | (((qh[h] >> (2 * m)) & 0x03030303u) << 4);
         }
-        put_terms<2>(it, g, 8 * s + j, xunit(it, s, j), sc, 0.0f, wq);
+        put_terms<ONE, 2>(sm, it, g, 8 * s + j, j * it.nblk + s, sc, 0.0f, wq);
     }
 }
 
 // Q8_0 block (34 bytes, 2-byte aligned).
-__device__ __forceinline__ void consume_q80(const uint8_t* __restrict__ sm, const Item& it, int g, int u)
+template <bool ONE>
+__device__ __forceinline__ void consume_q80(uint8_t* sm, const Item& it, int g, int u)
 {
     const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
-    const uint32_t blk = it.w + (uint32_t)(g * it.rb) + 34u * (uint32_t)u;
+    const uint32_t blk = it.tile + (uint32_t)(g * it.rb) + 34u * (uint32_t)u;
     const float dw = h2f_ref(ld_u32(s32, blk) & 0xFFFFu);
     uint32_t wq[8];
     ld_words<8>(s32, blk + 2, wq);
-    put_terms<0>(it, g, u, u, dw, 0.0f, wq);
+    put_terms<ONE, 0>(sm, it, g, u, u, dw, 0.0f, wq);
+}
+
+template <uint32_t TYPE, bool ONE>
+__device__ __forceinline__ void consume_range(uint8_t* sm, const Item& it, int first, int total,
+                                              unsigned long long magic)
+{
+    for (int i = first; i < total; i += kConsumerThreads) {
+        const int g = (int)(((unsigned long long)i * magic) >> 40);
+        const int s = i - g * it.nblk;
+        if (TYPE == T_Q4_K || TYPE == T_Q5_K) consume_k45<TYPE, ONE>(sm, it, g, s);
+        else if (TYPE == T_Q6_K) consume_q6k<ONE>(sm, it, g, s);
+        else consume_q80<ONE>(sm, it, g, s);
+    }
 }
 
 template <uint32_t TYPE>
-__device__ __forceinline__ void consume_item_t(const uint8_t* __restrict__ sm, const Item& it, int rows,
-                                               unsigned long long magic, int ctid)
+__device__ __forceinline__ void consume_typed(uint8_t* sm, const Item& it, int first, int total,
+                                              unsigned long long magic)
 {
-    const int total = rows * it.nblk;
-    for (int i = ctid; i < total; i += kConsumerThreads) {
-        const int g = (int)(((unsigned long long)i * magic) >> 40);
-        const int s = i - g * it.nblk;
-        if (TYPE == T_Q4_K || TYPE == T_Q5_K) consume_k45<TYPE>(sm, it, g, s);
-        else if (TYPE == T_Q6_K) consume_q6k(sm, it, g, s);
-        else consume_q80(sm, it, g, s);
-    }
+    if (it.B == 1) consume_range<TYPE, true>(sm, it, first, total, magic);
+    else consume_range<TYPE, false>(sm, it, first, total, magic);
 }
 
 // ---------------------------------------------------------------- kernel --
@@ -305,7 +329,6 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
     volatile int* abort_flag = ctl;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int P = gridDim.x, c = blockIdx.x;
-    const JobDesc* jobs = p.jobs ? p.jobs : &p.inline_job;
     const int S = (int)p.S, T = (int)p.T;
 
     if (threadIdx.x == 0) {
@@ -327,13 +350,27 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
     if (warp == 0) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
+            const JobDesc* jobs = p.jobs ? p.jobs : &p.inline_job;
             int jc = 0, k = 0, i = c;
-            int pend_job[kMaxS];
+            int pend_job[kMaxS] = {0, 0, 0, 0};
             auto issue_w = [&](const JobDesc& J, int item, int slot) {
                 const int r0 = (item - J.item0) * J.R;
                 const int rows = min(J.R, J.n - r0);
                 const uint8_t* src = J.w + (long long)r0 * J.rb;
-                uint8_t* dst = sm + p.slot_off + (size_t)slot * p.slot_bytes;
+                uint8_t* base = sm + p.slot_off + (size_t)slot * p.slot_bytes;
+                ItemHdr* h = reinterpret_cast<ItemHdr*>(base);
+                h->out = J.out + r0;
+                h->ldo = J.ldo;
+                h->type = (uint32_t)J.type;
+                h->rb = (uint32_t)J.rb;
+                h->nblk = (uint32_t)J.nblk;
+                h->B = (uint32_t)J.B;
+                h->U = (uint32_t)J.U;
+                h->TS = (uint32_t)J.TS;
+                h->ds_off = J.ds_off;
+                h->rows = (uint32_t)rows;
+                h->magic = J.nblk_magic;
+                uint8_t* dst = base + kHdr;
                 const uint32_t bytes = (uint32_t)(rows * J.rb);
                 const uint32_t body = bytes & ~15u;
                 for (uint32_t b = body; b < bytes; ++b) dst[b] = src[b];  // < 16 ragged bytes
@@ -366,35 +403,34 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
     } else if (warp <= kConsumerWarps) {
         // ----------------------------------------------------- consumers --
         const int ctid = (warp - 1) * 32 + lane;
-        int jc = 0;
+        int rot = 0;  // sum of earlier items' work, mod kConsumerThreads
         for (int k = 0, i = c; i < p.total_items; ++k, i += P) {
-            jc = job_of(jobs, p.njobs, i, jc);
-            const JobDesc& J = jobs[jc];
             const int slot = k % S, tb = k % T;
             if (!mbar_wait_bounded(&wfull[slot], (k / S) & 1, p.err, abort_flag)) break;
             if (k >= T && !mbar_wait_bounded(&tempty[tb], ((k / T) - 1) & 1, p.err, abort_flag)) break;
+            const uint32_t base = p.slot_off + (uint32_t)slot * p.slot_bytes;
+            const ItemHdr h = *reinterpret_cast<const ItemHdr*>(sm + base);
             Item it;
-            it.w = p.slot_off + (uint32_t)slot * p.slot_bytes;
-            const uint8_t* xb = sm + it.w + p.slot_x_off;
-            it.xq = reinterpret_cast<const int8_t*>(xb);
-            it.xd = reinterpret_cast<const float*>(xb + J.act_d_off);
-            it.xs = reinterpret_cast<const int32_t*>(xb + J.act_s_off);
-            it.terms = reinterpret_cast<float*>(sm + p.term_off + (size_t)tb * p.term_bytes);
-            it.rb = (int)J.rb;
-            it.nblk = J.nblk;
-            it.B = J.B;
-            it.U = J.U;
-            it.U4 = J.U4;
-            it.TS = J.TS;
-            const int type = J.type;
-            const unsigned long long magic = J.nblk_magic;
-            const int rows = min(J.R, J.n - (i - J.item0) * J.R);
-            switch (type) {
-            case T_Q4_K: consume_item_t<T_Q4_K>(sm, it, rows, magic, ctid); break;
-            case T_Q5_K: consume_item_t<T_Q5_K>(sm, it, rows, magic, ctid); break;
-            case T_Q6_K: consume_item_t<T_Q6_K>(sm, it, rows, magic, ctid); break;
-            default: consume_item_t<T_Q8_0>(sm, it, rows, magic, ctid); break;
+            it.tile = base + kHdr;
+            it.xq = base + p.slot_x_off;
+            it.ds = it.xq + h.ds_off;
+            it.terms = p.term_off + (uint32_t)tb * p.term_bytes + kHdr;
+            it.rb = (int)h.rb;
+            it.nblk = (int)h.nblk;
+            it.B = (int)h.B;
+            it.U = (int)h.U;
+            it.TS = (int)h.TS;
+            const int total = (int)h.rows * it.nblk;
+            const int first = (ctid - rot + kConsumerThreads) % kConsumerThreads;
+            rot = (rot + total) % kConsumerThreads;
+            switch (h.type) {
+            case T_Q4_K: consume_typed<T_Q4_K>(sm, it, first, total, h.magic); break;
+            case T_Q5_K: consume_typed<T_Q5_K>(sm, it, first, total, h.magic); break;
+            case T_Q6_K: consume_typed<T_Q6_K>(sm, it, first, total, h.magic); break;
+            default: consume_typed<T_Q8_0>(sm, it, first, total, h.magic); break;
             }
+            if (ctid == 0)  // forward the header to the chain warps
+                *reinterpret_cast<ItemHdr*>(sm + p.term_off + (uint32_t)tb * p.term_bytes) = h;
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&tfull[tb]);
@@ -404,19 +440,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
     } else {
         // --------------------------------------------------------- chain --
         const int ch = warp - 1 - kConsumerWarps;
-        int jc = 0;
         for (int k = ch, i = c + ch * P; i < p.total_items; k += kChainWarps, i += kChainWarps * P) {
-            jc = job_of(jobs, p.njobs, i, jc);
-            const JobDesc& J = jobs[jc];
             const int tb = k % T;
             if (!mbar_wait_bounded(&tfull[tb], (k / T) & 1, p.err, abort_flag)) break;
-            const float* __restrict__ terms =
-                reinterpret_cast<const float*>(sm + p.term_off + (size_t)tb * p.term_bytes);
-            const int r0 = (i - J.item0) * J.R;
-            const int rows = min(J.R, J.n - r0);
-            const int B = J.B, U = J.U, TS = J.TS;
-            float* __restrict__ out = J.out + r0;
-            const long long ldo = J.ldo;
+            const uint32_t tbase = p.term_off + (uint32_t)tb * p.term_bytes;
+            const ItemHdr h = *reinterpret_cast<const ItemHdr*>(sm + tbase);
+            const float* terms = reinterpret_cast<const float*>(sm + tbase + kHdr);
+            const int B = (int)h.B, U = (int)h.U, TS = (int)h.TS, rows = (int)h.rows;
+            float* out = h.out;
+            const long long ldo = h.ldo;
             for (int q = lane; q < rows * B; q += 32) {
                 const int g = q / B, t = q - g * B;
                 const float* tp = terms + q;
@@ -466,11 +498,13 @@ struct JobIn {
     long long ldo;
 };
 
+int units_of(uint32_t type, int d) { return (d / block_elems(type)) * block_units(type); }
+
+// Activation region of one input: q[B][U][32] then 8-byte (scale, sum) pairs.
+size_t act_ds_off(uint32_t type, int d, int B) { return (size_t)B * units_of(type, d) * 32; }
 size_t act_bytes_for(uint32_t type, int d, int B)
 {
-    const int U = (d / block_elems(type)) * block_units(type);
-    const int U4 = (U + 3) & ~3;
-    return (size_t)B * U * 32 + 2 * (size_t)B * U4 * 4;
+    return act_ds_off(type, d, B) + (((size_t)B * units_of(type, d) * 8 + 15) & ~size_t(15));
 }
 
 // Validates the jobs and lays out tiles, activations and shared memory.
@@ -497,8 +531,7 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
         J.type = (int)a.type;
         J.n = a.n;
         J.B = a.B;
-        J.U = (a.d / block_elems(a.type)) * block_units(a.type);
-        J.U4 = (J.U + 3) & ~3;
+        J.U = units_of(a.type, a.d);
         J.nblk = a.type == T_Q8_0 ? J.U : J.U / 8;
         J.nblk_magic = magic40(J.nblk);
         const int gR = 16 / gcd_int(rb, 16);  // R*rb % 16 == 0 keeps every tile 16-byte aligned
@@ -517,9 +550,9 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
             t.x = a.x;
             t.ldx = a.ldx;
             t.U = J.U;
-            t.U4 = J.U4;
             t.B = a.B;
             t.type = (int)a.type;
+            t.ds_off = (uint32_t)act_ds_off(a.type, a.d, a.B);
             t.blk0 = pl.total_blocks;
             t.act = act_base ? act_base + pl.act_total : nullptr;
             pl.total_blocks += (long long)a.B * J.U;
@@ -531,9 +564,8 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
             ti = it->second;
         }
         J.act = pl.tasks[ti].act;
-        J.act_d_off = (uint32_t)((size_t)a.B * J.U * 32);
-        J.act_s_off = J.act_d_off + (uint32_t)((size_t)a.B * J.U4 * 4);
-        J.act_bytes = J.act_s_off + (uint32_t)((size_t)a.B * J.U4 * 4);
+        J.ds_off = pl.tasks[ti].ds_off;
+        J.act_bytes = (uint32_t)act_bytes_for(a.type, a.d, a.B);
         pl.jobs.push_back(J);
     }
     // Enough items to keep every SM busy: shrink tiles while there are fewer
@@ -569,26 +601,26 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
     auto up128 = [](size_t v) { return (v + 127) & ~size_t(127); };
     slot_w = up128(slot_w);
     slot_x = up128(slot_x);
-    term = up128(term);
+    term = kHdr + up128(term);
+    const size_t slot = kHdr + slot_w + slot_x;
     const size_t bars = 1024;
     int T = kMaxT, S = 0;
     for (; T >= 3; --T) {
-        const size_t avail = kSmemMax - bars - (size_t)T * term;
-        if (avail > kSmemMax) continue;  // underflow
-        S = (int)std::min<size_t>(kMaxS, avail / (slot_w + slot_x));
+        if (bars + (size_t)T * term >= kSmemMax) continue;
+        S = (int)std::min<size_t>(kMaxS, (kSmemMax - bars - (size_t)T * term) / slot);
         if (S >= 2) break;
     }
     if (S < 2) return QUANTR_ERR_TOO_LARGE;
     ProgParams& pp = pl.pp;
     pp.njobs = njobs;
     pp.total_items = item;
-    pp.slot_bytes = (uint32_t)(slot_w + slot_x);
-    pp.slot_x_off = (uint32_t)slot_w;
+    pp.slot_bytes = (uint32_t)slot;
+    pp.slot_x_off = (uint32_t)(kHdr + slot_w);
     pp.term_bytes = (uint32_t)term;
     pp.S = (uint32_t)S;
     pp.T = (uint32_t)T;
     pp.slot_off = (uint32_t)bars;
-    pp.term_off = (uint32_t)(bars + (size_t)S * pp.slot_bytes);
+    pp.term_off = (uint32_t)(bars + (size_t)S * slot);
     pl.smem = pp.term_off + (size_t)T * term;
     pl.grid = std::min(sms, item);
     pl.qp.ntasks = (int)pl.tasks.size();
@@ -624,7 +656,8 @@ cudaError_t launch_plan(Plan& pl, const JobDesc* d_jobs, const QTask* d_tasks, i
 cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, int B, const float* x, long long ldx,
                                float* out, long long ldo, void* ws, size_t ws_bytes, int* err, cudaStream_t stream)
 {
-    if (!type_supported(type) || ((uintptr_t)w & 15) || B > eng::kMaxB || row_bytes(type, d) <= 0)
+    if (!type_supported(type) || ((uintptr_t)w & 15) || ((uintptr_t)ws & 15) || B > eng::kMaxB ||
+        row_bytes(type, d) <= 0)
         return cudaErrorNotSupported;
     if (eng::act_bytes_for(type, d, B) > ws_bytes) return cudaErrorNotSupported;
     eng::JobIn in{w, type, n, d, B, x, ldx, out, ldo};
