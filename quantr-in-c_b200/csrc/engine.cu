@@ -71,6 +71,12 @@ struct JobDesc {
     int type, n, U, nblk, B, R, TS, tiles, item0;
     unsigned long long nblk_magic;  // floor(it / nblk) == (it * magic) >> 40
 };
+static_assert(sizeof(JobDesc) % 16 == 0, "job table is copied in 16-byte words");
+
+// Jobs per engine launch: the launch keeps its job table in shared memory
+// (read by the producer for every item; global reads would sit behind the
+// weight stream in L2).  Larger programs are split into several launches.
+constexpr int kMaxJobsPerLaunch = 96;
 
 // Item header the producer writes at the start of a slot (and the consumers
 // forward to the chain in the term buffer).
@@ -86,7 +92,7 @@ struct ProgParams {
     const JobDesc* jobs;  // null: use inline_job
     int njobs, total_items;
     uint32_t slot_bytes, slot_x_off, term_bytes, S, T;
-    uint32_t slot_off, term_off;
+    uint32_t slot_off, term_off, jobs_off;
     int* err;
     JobDesc inline_job;
 };
@@ -344,13 +350,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
         ctl[0] = 0;
         mbar_fence_init();
     }
+    if (p.jobs) {  // job table -> shared memory (written by the host before any launch)
+        const uint4* src = reinterpret_cast<const uint4*>(p.jobs);
+        uint4* dst = reinterpret_cast<uint4*>(sm + p.jobs_off);
+        const int words = p.njobs * (int)(sizeof(JobDesc) / 16);
+        for (int w = threadIdx.x; w < words; w += kThreads) dst[w] = src[w];
+    }
     __syncthreads();
     pdl_trigger();
 
     if (warp == 0) {
         // ------------------------------------------------------ producer --
         if (lane == 0) {
-            const JobDesc* jobs = p.jobs ? p.jobs : &p.inline_job;
+            const JobDesc* jobs = p.jobs ? reinterpret_cast<const JobDesc*>(sm + p.jobs_off) : &p.inline_job;
             int jc = 0, k = 0, i = c;
             int pend_job[kMaxS] = {0, 0, 0, 0};
             auto issue_w = [&](const JobDesc& J, int item, int slot) {
@@ -477,15 +489,21 @@ int gcd_int(long long a, long long b) { return (int)std::gcd(a, b); }
 
 unsigned long long magic40(int dvs) { return ((1ULL << 40) + (unsigned long long)dvs - 1) / (unsigned long long)dvs; }
 
-struct Plan {
+// One engine launch: its jobs, tiling and shared-memory layout.
+struct SubPlan {
     std::vector<JobDesc> jobs;
+    ProgParams pp{};
+    int grid = 0;
+    size_t smem = 0;
+    JobDesc* d_jobs = nullptr;  // device job table; null for a single inline job
+};
+
+struct Plan {
     std::vector<QTask> tasks;
     long long total_blocks = 0;
     size_t act_total = 0;
-    ProgParams pp{};
     QParams qp{};
-    int grid = 0;
-    size_t smem = 0;
+    std::vector<SubPlan> subs;
 };
 
 struct JobIn {
@@ -507,14 +525,81 @@ size_t act_bytes_for(uint32_t type, int d, int B)
     return act_ds_off(type, d, B) + (((size_t)B * units_of(type, d) * 8 + 15) & ~size_t(15));
 }
 
+// Tiles and shared-memory layout of one launch.  `table`: the launch keeps a
+// job table in shared memory (otherwise its single job travels inline).
+int layout_sub(SubPlan& sp, int sms, bool table)
+{
+    // Enough items to keep every SM busy: shrink tiles while there are fewer
+    // than two items per SM.
+    auto count_items = [&]() {
+        long long t = 0;
+        for (auto& J : sp.jobs) t += (J.n + J.R - 1) / J.R;
+        return t;
+    };
+    for (int iter = 0; iter < 16 && count_items() < 2LL * sms; ++iter) {
+        bool changed = false;
+        for (auto& J : sp.jobs) {
+            const int gR = 16 / gcd_int(J.rb, 16);
+            const int nr = std::max(gR, ((J.R / 2) / gR) * gR);
+            if (nr < J.R) {
+                J.R = nr;
+                changed = true;
+            }
+        }
+        if (!changed) break;
+    }
+    size_t slot_w = 0, slot_x = 0, term = 0;
+    int item = 0;
+    for (auto& J : sp.jobs) {
+        J.TS = (J.R * J.B) | 1;
+        J.tiles = (J.n + J.R - 1) / J.R;
+        J.item0 = item;
+        item += J.tiles;
+        slot_w = std::max(slot_w, (size_t)((long long)J.R * J.rb));
+        slot_x = std::max(slot_x, (size_t)J.act_bytes);
+        term = std::max(term, (size_t)J.U * J.TS * 4);
+    }
+    auto up128 = [](size_t v) { return (v + 127) & ~size_t(127); };
+    slot_w = up128(slot_w);
+    slot_x = up128(slot_x);
+    term = kHdr + up128(term);
+    const size_t slot = kHdr + slot_w + slot_x;
+    const size_t bars = 1024;
+    const size_t tbl = table ? up128(sp.jobs.size() * sizeof(JobDesc)) : 0;
+    int T = kMaxT, S = 0;
+    for (; T >= 3; --T) {
+        if (bars + tbl + (size_t)T * term >= kSmemMax) continue;
+        S = (int)std::min<size_t>(kMaxS, (kSmemMax - bars - tbl - (size_t)T * term) / slot);
+        if (S >= 2) break;
+    }
+    if (S < 2) return QUANTR_ERR_TOO_LARGE;
+    ProgParams& pp = sp.pp;
+    pp.njobs = (int)sp.jobs.size();
+    pp.total_items = item;
+    pp.slot_bytes = (uint32_t)slot;
+    pp.slot_x_off = (uint32_t)(kHdr + slot_w);
+    pp.term_bytes = (uint32_t)term;
+    pp.S = (uint32_t)S;
+    pp.T = (uint32_t)T;
+    pp.slot_off = (uint32_t)bars;
+    pp.term_off = (uint32_t)(bars + (size_t)S * slot);
+    pp.jobs_off = pp.term_off + (uint32_t)((size_t)T * term);
+    sp.smem = pp.jobs_off + tbl;
+    sp.grid = std::min(sms, item);
+    return QUANTR_OK;
+}
+
 // Validates the jobs and lays out tiles, activations and shared memory.
 // act_base == nullptr plans the sizes only.
-int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
+// `tables`: every launch reads a device job table copied into shared memory
+// (programs); false only for a single job passed inline (single-GEMV calls).
+int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool tables, Plan& pl)
 {
     pl = Plan{};
     if (njobs <= 0) return QUANTR_ERR_BAD_ARG;
     std::map<std::tuple<const float*, long long, int, int, int, int>, int> dedupe;  // x,ldx,d,B,U,perm -> task
-    constexpr size_t kSlotW = 40 * 1024, kTermMax = 16 * 1024;
+    constexpr size_t kSlotW = 36 * 1024, kTermMax = 16 * 1024;
+    std::vector<JobDesc> all;
     for (int j = 0; j < njobs; ++j) {
         const JobIn& a = in[j];
         if (!type_supported(a.type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
@@ -566,69 +651,24 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, Plan& pl)
         J.act = pl.tasks[ti].act;
         J.ds_off = pl.tasks[ti].ds_off;
         J.act_bytes = (uint32_t)act_bytes_for(a.type, a.d, a.B);
-        pl.jobs.push_back(J);
+        all.push_back(J);
     }
-    // Enough items to keep every SM busy: shrink tiles while there are fewer
-    // than two items per SM.
-    auto count_items = [&]() {
-        long long t = 0;
-        for (auto& J : pl.jobs) t += (J.n + J.R - 1) / J.R;
-        return t;
-    };
-    for (int iter = 0; iter < 16 && count_items() < 2LL * sms; ++iter) {
-        bool changed = false;
-        for (auto& J : pl.jobs) {
-            const int gR = 16 / gcd_int(J.rb, 16);
-            const int nr = std::max(gR, ((J.R / 2) / gR) * gR);
-            if (nr < J.R) {
-                J.R = nr;
-                changed = true;
-            }
-        }
-        if (!changed) break;
+    for (int j0 = 0; j0 < njobs; j0 += kMaxJobsPerLaunch) {
+        SubPlan sp;
+        sp.jobs.assign(all.begin() + j0, all.begin() + std::min(njobs, j0 + kMaxJobsPerLaunch));
+        if (!tables && sp.jobs.size() != 1) return QUANTR_ERR_BAD_ARG;
+        const int rc = layout_sub(sp, sms, tables);
+        if (rc) return rc;
+        pl.subs.push_back(std::move(sp));
     }
-    size_t slot_w = 0, slot_x = 0, term = 0;
-    int item = 0;
-    for (auto& J : pl.jobs) {
-        J.TS = (J.R * J.B) | 1;
-        J.tiles = (J.n + J.R - 1) / J.R;
-        J.item0 = item;
-        item += J.tiles;
-        slot_w = std::max(slot_w, (size_t)((long long)J.R * J.rb));
-        slot_x = std::max(slot_x, (size_t)J.act_bytes);
-        term = std::max(term, (size_t)J.U * J.TS * 4);
-    }
-    auto up128 = [](size_t v) { return (v + 127) & ~size_t(127); };
-    slot_w = up128(slot_w);
-    slot_x = up128(slot_x);
-    term = kHdr + up128(term);
-    const size_t slot = kHdr + slot_w + slot_x;
-    const size_t bars = 1024;
-    int T = kMaxT, S = 0;
-    for (; T >= 3; --T) {
-        if (bars + (size_t)T * term >= kSmemMax) continue;
-        S = (int)std::min<size_t>(kMaxS, (kSmemMax - bars - (size_t)T * term) / slot);
-        if (S >= 2) break;
-    }
-    if (S < 2) return QUANTR_ERR_TOO_LARGE;
-    ProgParams& pp = pl.pp;
-    pp.njobs = njobs;
-    pp.total_items = item;
-    pp.slot_bytes = (uint32_t)slot;
-    pp.slot_x_off = (uint32_t)(kHdr + slot_w);
-    pp.term_bytes = (uint32_t)term;
-    pp.S = (uint32_t)S;
-    pp.T = (uint32_t)T;
-    pp.slot_off = (uint32_t)bars;
-    pp.term_off = (uint32_t)(bars + (size_t)S * slot);
-    pl.smem = pp.term_off + (size_t)T * term;
-    pl.grid = std::min(sms, item);
     pl.qp.ntasks = (int)pl.tasks.size();
     pl.qp.total_blocks = pl.total_blocks;
     return QUANTR_OK;
 }
 
-cudaError_t launch_plan(Plan& pl, const JobDesc* d_jobs, const QTask* d_tasks, int* err, cudaStream_t stream)
+// Launches the quantizer over every task, then one engine launch per
+// sub-plan (a single job travels inline when the sub-plan has no table).
+cudaError_t launch_plan(Plan& pl, const QTask* d_tasks, int* err, cudaStream_t stream)
 {
     LaunchCfg c;
     c.stream = stream;
@@ -640,12 +680,15 @@ cudaError_t launch_plan(Plan& pl, const JobDesc* d_jobs, const QTask* d_tasks, i
     if (!d_tasks) qp.inline_task = pl.tasks[0];
     const long long qgrid = std::max(1LL, std::min<long long>((qp.total_blocks + 7) / 8, 8LL * device_sm_count()));
     e = launch_ex(&k_quant_tasks, dim3((unsigned)qgrid), dim3(256), 0, c, qp);
-    if (e != cudaSuccess) return e;
-    ProgParams pp = pl.pp;
-    pp.jobs = d_jobs;
-    if (!d_jobs) pp.inline_job = pl.jobs[0];
-    pp.err = err;
-    return launch_ex(&k_program, dim3(pl.grid), dim3(kThreads), pl.smem, c, pp);
+    for (auto& sp : pl.subs) {
+        if (e != cudaSuccess) return e;
+        ProgParams pp = sp.pp;
+        pp.jobs = sp.d_jobs;
+        if (!sp.d_jobs) pp.inline_job = sp.jobs[0];
+        pp.err = err;
+        e = launch_ex(&k_program, dim3(sp.grid), dim3(kThreads), sp.smem, c, pp);
+    }
+    return e;
 }
 
 } // namespace eng
@@ -662,9 +705,9 @@ cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, in
     if (eng::act_bytes_for(type, d, B) > ws_bytes) return cudaErrorNotSupported;
     eng::JobIn in{w, type, n, d, B, x, ldx, out, ldo};
     eng::Plan pl;
-    if (eng::make_plan(&in, 1, static_cast<uint8_t*>(ws), device_sm_count(), pl) != QUANTR_OK)
+    if (eng::make_plan(&in, 1, static_cast<uint8_t*>(ws), device_sm_count(), false, pl) != QUANTR_OK)
         return cudaErrorNotSupported;
-    return eng::launch_plan(pl, nullptr, nullptr, err, stream);
+    return eng::launch_plan(pl, nullptr, err, stream);
 }
 
 size_t engine_act_bytes(uint32_t type, int d, int B) { return eng::act_bytes_for(type, d, B); }
@@ -675,8 +718,7 @@ size_t engine_act_bytes(uint32_t type, int d, int B) { return eng::act_bytes_for
 
 struct quantr_program {
     int device;
-    qr::eng::Plan plan;
-    qr::eng::JobDesc* d_jobs = nullptr;
+    qr::eng::Plan plan;  // sub-plans own their device job tables
     qr::eng::QTask* d_tasks = nullptr;
     uint8_t* d_act = nullptr;
 };
@@ -699,7 +741,7 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     }
     const int sms = device_sm_count();
     eng::Plan sizing;
-    int rc = eng::make_plan(in.data(), njobs, nullptr, sms, sizing);
+    int rc = eng::make_plan(in.data(), njobs, nullptr, sms, true, sizing);
     if (rc) return rc;
     quantr_program* p = new (std::nothrow) quantr_program();
     if (!p) return QUANTR_ERR_OOM;
@@ -709,17 +751,22 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
         delete p;
         return QUANTR_ERR_OOM;
     }
-    rc = eng::make_plan(in.data(), njobs, p->d_act, sms, p->plan);
+    rc = eng::make_plan(in.data(), njobs, p->d_act, sms, true, p->plan);
     cudaError_t e = cudaSuccess;
     if (!rc) {
-        e = cudaMalloc((void**)&p->d_jobs, p->plan.jobs.size() * sizeof(eng::JobDesc));
-        if (e == cudaSuccess) e = cudaMalloc((void**)&p->d_tasks, p->plan.tasks.size() * sizeof(eng::QTask));
-        if (e == cudaSuccess)
-            e = cudaMemcpy(p->d_jobs, p->plan.jobs.data(), p->plan.jobs.size() * sizeof(eng::JobDesc),
-                           cudaMemcpyHostToDevice);
+        e = cudaMalloc((void**)&p->d_tasks, p->plan.tasks.size() * sizeof(eng::QTask));
         if (e == cudaSuccess)
             e = cudaMemcpy(p->d_tasks, p->plan.tasks.data(), p->plan.tasks.size() * sizeof(eng::QTask),
                            cudaMemcpyHostToDevice);
+        // Every sub-plan keeps a job table (even with one job), so a program
+        // run never depends on host-side state.
+        for (auto& sp : p->plan.subs) {
+            if (e != cudaSuccess) break;
+            e = cudaMalloc((void**)&sp.d_jobs, sp.jobs.size() * sizeof(eng::JobDesc));
+            if (e == cudaSuccess)
+                e = cudaMemcpy(sp.d_jobs, sp.jobs.data(), sp.jobs.size() * sizeof(eng::JobDesc),
+                               cudaMemcpyHostToDevice);
+        }
         if (e != cudaSuccess) rc = e == cudaErrorMemoryAllocation ? QUANTR_ERR_OOM : QUANTR_ERR_CUDA;
     }
     if (rc) {
@@ -737,7 +784,7 @@ int quantr_program_run(quantr_program* p, void* stream)
     int dev = -1;
     cudaGetDevice(&dev);
     if (dev != p->device) return QUANTR_ERR_BAD_ARG;
-    cudaError_t e = qr::eng::launch_plan(p->plan, p->d_jobs, p->d_tasks, qr::device_error_word(),
+    cudaError_t e = qr::eng::launch_plan(p->plan, p->d_tasks, qr::device_error_word(),
                                          static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -753,7 +800,7 @@ void quantr_program_destroy(quantr_program* p)
     cudaGetDevice(&prev);
     cudaSetDevice(p->device);
     cudaDeviceSynchronize();
-    cudaFree(p->d_jobs);
+    for (auto& sp : p->plan.subs) cudaFree(sp.d_jobs);
     cudaFree(p->d_tasks);
     cudaFree(p->d_act);
     if (prev >= 0) cudaSetDevice(prev);
@@ -763,9 +810,16 @@ void quantr_program_destroy(quantr_program* p)
 int quantr_program_info(const quantr_program* p, int* items, int* grid, int* smem_bytes)
 {
     if (!p) return QUANTR_ERR_BAD_ARG;
-    if (items) *items = p->plan.pp.total_items;
-    if (grid) *grid = p->plan.grid;
-    if (smem_bytes) *smem_bytes = (int)p->plan.smem;
+    int it = 0, g = 0;
+    size_t sm = 0;
+    for (auto& sp : p->plan.subs) {
+        it += sp.pp.total_items;
+        g = std::max(g, sp.grid);
+        sm = std::max(sm, sp.smem);
+    }
+    if (items) *items = it;
+    if (grid) *grid = g;
+    if (smem_bytes) *smem_bytes = (int)sm;
     return QUANTR_OK;
 }
 

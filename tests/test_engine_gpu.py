@@ -102,6 +102,23 @@ def test_program_ragged_tiles(qr_gpu, orc, spec):
     check_outputs(orc, host, keep)
 
 
+def test_program_split_over_launches(qr_gpu, orc):
+    """More jobs than one launch keeps in its shared-memory job table: the
+    program runs as several engine launches after one quantizer launch."""
+    specs = [(12, 64, 512, 1), (14, 32, 512, 2), (8, 48, 256, 1), (13, 40, 512, 3)] * 52  # 208 jobs
+    prog, host, keep = build_program(qr_gpu, specs, 9)
+    prog.run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    check_outputs(orc, host, keep)
+
+
+def test_program_single_job(qr_gpu, orc):
+    prog, host, keep = build_program(qr_gpu, [(14, 2048, 5632, 1)], 10)
+    prog.run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    check_outputs(orc, host, keep)
+
+
 def test_program_rerun_sees_new_inputs(qr_gpu, orc):
     specs = [(12, 1024, 2048, 2), (14, 512, 2048, 1)]
     prog, host, keep = build_program(qr_gpu, specs, 5)
