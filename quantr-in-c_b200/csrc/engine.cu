@@ -55,21 +55,36 @@ constexpr int kChainWarps = 2;
 constexpr int kWarps = 1 + kConsumerWarps + kChainWarps;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
-constexpr int kMaxS = 4, kMaxT = 4;
+// Ring depths: 3 weight slots of ~44 KB measured best on B200 for the c2
+// shapes (fewer, larger tiles amortise the per-tile hand-off across the 12
+// consumer warps; 3 x 44 KB in flight per SM still saturates HBM).
+constexpr int kMaxS = 3, kMaxT = 4;
 constexpr int kMaxB = 16;
 constexpr size_t kSmemMax = 227 * 1024;
 constexpr uint32_t kBulkChunk = 32768;
 constexpr uint32_t kHdr = 128;  // bytes reserved for the item header in slots and term buffers
 
 // Device-side job description (built by the host planner).
-struct JobDesc {
+// Item header the producer writes at the start of a slot (and the consumers
+// forward to the chain in the term buffer).
+// 16-byte aligned: headers are copied with 128-bit loads/stores, including
+// from a job passed inline in the kernel parameters.
+struct __align__(16) ItemHdr {
+    float* out;  // first output row of the tile
+    long long ldo;
+    uint32_t type, rb, nblk, B, U, TS, ds_off, rows, gfast;
+    float inv_rows;             // 1/rows (approximate; only seeds an exact divmod)
+    unsigned long long magic;   // floor(i / nblk) == (i * magic) >> 40
+};
+static_assert(sizeof(ItemHdr) == 64, "item header is copied as four 16-byte words");
+
+struct __align__(16) JobDesc {
+    ItemHdr hdr;         // template of every tile's header (out = job base, rows = R)
     const uint8_t* w;    // 16-byte aligned packed rows
-    float* out;          // out[t*ldo + r]
     const uint8_t* act;  // quantized activations: q[B][U][32] | ds[B][U] (fp32 scale, int32 sum)
-    long long rb, ldo;
-    uint32_t act_bytes, ds_off;
-    int type, n, U, nblk, B, R, TS, tiles, item0;
-    unsigned long long nblk_magic;  // floor(it / nblk) == (it * magic) >> 40
+    long long rb;
+    uint32_t act_bytes;
+    int n, U, R, tiles, item0, pad_[4];
 };
 static_assert(sizeof(JobDesc) % 16 == 0, "job table is copied in 16-byte words");
 
@@ -78,14 +93,6 @@ static_assert(sizeof(JobDesc) % 16 == 0, "job table is copied in 16-byte words")
 // weight stream in L2).  Larger programs are split into several launches.
 constexpr int kMaxJobsPerLaunch = 96;
 
-// Item header the producer writes at the start of a slot (and the consumers
-// forward to the chain in the term buffer).
-struct ItemHdr {
-    float* out;  // first output row of the tile
-    long long ldo;
-    uint32_t type, rb, nblk, B, U, TS, ds_off, rows;
-    unsigned long long magic;
-};
 static_assert(sizeof(ItemHdr) <= kHdr, "item header too large");
 
 struct ProgParams {
@@ -96,6 +103,7 @@ struct ProgParams {
     int* err;
     JobDesc inline_job;
 };
+static_assert(offsetof(ProgParams, inline_job) % 16 == 0, "inline job must be 16-byte aligned in param space");
 
 // One quantization task: B rows of fp32 x -> the compact act layout.
 struct QTask {
@@ -124,12 +132,22 @@ __device__ __forceinline__ int perm_pos(uint32_t type, int e)
 
 // Reference quantize_row_q8_0 (src/quant.c:143-158), one warp per block,
 // writing the engine's compact layout for the consuming job's weight type.
+constexpr int kMaxTasksInSmem = 256;
+
 __global__ void __launch_bounds__(256) k_quant_tasks(const __grid_constant__ QParams p)
 {
+    // The task table (written by the host at program creation) is searched
+    // once per block of 32 elements: keep it in shared memory.
+    __shared__ QTask stasks[kMaxTasksInSmem];
+    const QTask* tasks = p.tasks ? p.tasks : &p.inline_task;
+    if (p.tasks && p.ntasks <= kMaxTasksInSmem) {
+        for (int t = threadIdx.x; t < p.ntasks; t += blockDim.x) stasks[t] = p.tasks[t];
+        __syncthreads();
+        tasks = stasks;
+    }
     pdl_trigger();
     pdl_wait();
     const int lane = threadIdx.x & 31;
-    const QTask* tasks = p.tasks ? p.tasks : &p.inline_task;
     const long long step = (long long)gridDim.x * 8;
     for (long long gb = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); gb < p.total_blocks; gb += step) {
         int lo = 0, hi = p.ntasks - 1;  // last task with blk0 <= gb
@@ -301,13 +319,26 @@ __device__ __forceinline__ void consume_q80(uint8_t* sm, const Item& it, int g, 
     put_terms<ONE, 0>(sm, it, g, u, u, dw, 0.0f, wq);
 }
 
+// Work index -> (row g, block s).  Block-fastest by default (neighbouring
+// lanes read neighbouring blocks of one row).  Row-fastest (`gfast`) when the
+// planner found the row stride an odd number of 16-byte units (Q4_K/Q5_K):
+// a warp's lanes then share one super-block column, so activation reads are
+// broadcasts and weight reads still hit distinct banks.
 template <uint32_t TYPE, bool ONE>
 __device__ __forceinline__ void consume_range(uint8_t* sm, const Item& it, int first, int total,
-                                              unsigned long long magic)
+                                              unsigned long long magic, int rows, float inv_rows, bool gfast)
 {
     for (int i = first; i < total; i += kConsumerThreads) {
-        const int g = (int)(((unsigned long long)i * magic) >> 40);
-        const int s = i - g * it.nblk;
+        int g, s;
+        if (gfast) {
+            s = (int)((float)i * inv_rows);  // within one of the true quotient; corrected below
+            g = i - s * rows;
+            if (g < 0) { --s; g += rows; }
+            else if (g >= rows) { ++s; g -= rows; }
+        } else {
+            g = (int)(((unsigned long long)i * magic) >> 40);
+            s = i - g * it.nblk;
+        }
         if (TYPE == T_Q4_K || TYPE == T_Q5_K) consume_k45<TYPE, ONE>(sm, it, g, s);
         else if (TYPE == T_Q6_K) consume_q6k<ONE>(sm, it, g, s);
         else consume_q80<ONE>(sm, it, g, s);
@@ -315,11 +346,11 @@ __device__ __forceinline__ void consume_range(uint8_t* sm, const Item& it, int f
 }
 
 template <uint32_t TYPE>
-__device__ __forceinline__ void consume_typed(uint8_t* sm, const Item& it, int first, int total,
-                                              unsigned long long magic)
+__device__ __forceinline__ void consume_typed(uint8_t* sm, const Item& it, int first, int total, const ItemHdr& h)
 {
-    if (it.B == 1) consume_range<TYPE, true>(sm, it, first, total, magic);
-    else consume_range<TYPE, false>(sm, it, first, total, magic);
+    const bool gfast = (TYPE == T_Q4_K || TYPE == T_Q5_K) && h.gfast;
+    if (it.B == 1) consume_range<TYPE, true>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
+    else consume_range<TYPE, false>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
 }
 
 // ---------------------------------------------------------------- kernel --
@@ -364,24 +395,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
         if (lane == 0) {
             const JobDesc* jobs = p.jobs ? reinterpret_cast<const JobDesc*>(sm + p.jobs_off) : &p.inline_job;
             int jc = 0, k = 0, i = c;
-            int pend_job[kMaxS] = {0, 0, 0, 0};
+            int pend_job[kMaxS] = {};
             auto issue_w = [&](const JobDesc& J, int item, int slot) {
                 const int r0 = (item - J.item0) * J.R;
                 const int rows = min(J.R, J.n - r0);
                 const uint8_t* src = J.w + (long long)r0 * J.rb;
                 uint8_t* base = sm + p.slot_off + (size_t)slot * p.slot_bytes;
+                // Header: the job's template, patched for this tile.
+                const uint4* hs = reinterpret_cast<const uint4*>(&J.hdr);
+                uint4* hd = reinterpret_cast<uint4*>(base);
+                hd[0] = hs[0];
+                hd[1] = hs[1];
+                hd[2] = hs[2];
+                hd[3] = hs[3];
                 ItemHdr* h = reinterpret_cast<ItemHdr*>(base);
-                h->out = J.out + r0;
-                h->ldo = J.ldo;
-                h->type = (uint32_t)J.type;
-                h->rb = (uint32_t)J.rb;
-                h->nblk = (uint32_t)J.nblk;
-                h->B = (uint32_t)J.B;
-                h->U = (uint32_t)J.U;
-                h->TS = (uint32_t)J.TS;
-                h->ds_off = J.ds_off;
-                h->rows = (uint32_t)rows;
-                h->magic = J.nblk_magic;
+                if (r0) h->out = J.hdr.out + r0;
+                if (rows != J.R) {
+                    h->rows = (uint32_t)rows;
+                    h->inv_rows = __frcp_rn((float)rows);
+                }
                 uint8_t* dst = base + kHdr;
                 const uint32_t bytes = (uint32_t)(rows * J.rb);
                 const uint32_t body = bytes & ~15u;
@@ -433,13 +465,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
             it.U = (int)h.U;
             it.TS = (int)h.TS;
             const int total = (int)h.rows * it.nblk;
-            const int first = (ctid - rot + kConsumerThreads) % kConsumerThreads;
-            rot = (rot + total) % kConsumerThreads;
+            const int first = ctid >= rot ? ctid - rot : ctid - rot + kConsumerThreads;
+            rot = (int)(((unsigned)rot + (unsigned)total) % (unsigned)kConsumerThreads);
             switch (h.type) {
-            case T_Q4_K: consume_typed<T_Q4_K>(sm, it, first, total, h.magic); break;
-            case T_Q5_K: consume_typed<T_Q5_K>(sm, it, first, total, h.magic); break;
-            case T_Q6_K: consume_typed<T_Q6_K>(sm, it, first, total, h.magic); break;
-            default: consume_typed<T_Q8_0>(sm, it, first, total, h.magic); break;
+            case T_Q4_K: consume_typed<T_Q4_K>(sm, it, first, total, h); break;
+            case T_Q5_K: consume_typed<T_Q5_K>(sm, it, first, total, h); break;
+            case T_Q6_K: consume_typed<T_Q6_K>(sm, it, first, total, h); break;
+            default: consume_typed<T_Q8_0>(sm, it, first, total, h); break;
             }
             if (ctid == 0)  // forward the header to the chain warps
                 *reinterpret_cast<ItemHdr*>(sm + p.term_off + (uint32_t)tb * p.term_bytes) = h;
@@ -551,13 +583,15 @@ int layout_sub(SubPlan& sp, int sms, bool table)
     size_t slot_w = 0, slot_x = 0, term = 0;
     int item = 0;
     for (auto& J : sp.jobs) {
-        J.TS = (J.R * J.B) | 1;
+        J.hdr.TS = (uint32_t)((J.R * (int)J.hdr.B) | 1);
+        J.hdr.rows = (uint32_t)J.R;
+        J.hdr.inv_rows = 1.0f / (float)J.R;
         J.tiles = (J.n + J.R - 1) / J.R;
         J.item0 = item;
         item += J.tiles;
         slot_w = std::max(slot_w, (size_t)((long long)J.R * J.rb));
         slot_x = std::max(slot_x, (size_t)J.act_bytes);
-        term = std::max(term, (size_t)J.U * J.TS * 4);
+        term = std::max(term, (size_t)J.U * J.hdr.TS * 4);
     }
     auto up128 = [](size_t v) { return (v + 127) & ~size_t(127); };
     slot_w = up128(slot_w);
@@ -598,7 +632,7 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
     pl = Plan{};
     if (njobs <= 0) return QUANTR_ERR_BAD_ARG;
     std::map<std::tuple<const float*, long long, int, int, int, int>, int> dedupe;  // x,ldx,d,B,U,perm -> task
-    constexpr size_t kSlotW = 36 * 1024, kTermMax = 16 * 1024;
+    constexpr size_t kSlotW = 44 * 1024, kTermMax = 16 * 1024;
     std::vector<JobDesc> all;
     for (int j = 0; j < njobs; ++j) {
         const JobIn& a = in[j];
@@ -610,15 +644,21 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
         if (rb <= 0) return QUANTR_ERR_BAD_ARG;
         JobDesc J{};
         J.w = a.w;
-        J.out = a.out;
         J.rb = rb;
-        J.ldo = a.ldo;
-        J.type = (int)a.type;
         J.n = a.n;
-        J.B = a.B;
         J.U = units_of(a.type, a.d);
-        J.nblk = a.type == T_Q8_0 ? J.U : J.U / 8;
-        J.nblk_magic = magic40(J.nblk);
+        ItemHdr& H = J.hdr;
+        H.out = a.out;
+        H.ldo = a.ldo;
+        H.type = a.type;
+        H.rb = (uint32_t)rb;
+        H.B = (uint32_t)a.B;
+        H.U = (uint32_t)J.U;
+        H.nblk = (uint32_t)(a.type == T_Q8_0 ? J.U : J.U / 8);
+        H.magic = magic40((int)H.nblk);
+        // Row-fastest work order for 16-byte aligned super-blocks whose row
+        // stride is an odd number of 16-byte units (conflict-free rows).
+        H.gfast = (a.type == T_Q4_K || a.type == T_Q5_K) && ((rb / 16) & 1) ? 1u : 0u;
         const int gR = 16 / gcd_int(rb, 16);  // R*rb % 16 == 0 keeps every tile 16-byte aligned
         auto round_dn = [&](long long v) { return std::max<long long>(gR, (v / gR) * gR); };
         long long R = round_dn((long long)(kSlotW / rb));
@@ -649,7 +689,7 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
             ti = it->second;
         }
         J.act = pl.tasks[ti].act;
-        J.ds_off = pl.tasks[ti].ds_off;
+        H.ds_off = pl.tasks[ti].ds_off;
         J.act_bytes = (uint32_t)act_bytes_for(a.type, a.d, a.B);
         all.push_back(J);
     }
