@@ -228,9 +228,14 @@ def ours_arm(args):
     rng = synth.rng_for(11)
     host_w = [synth.matrix(rng, t, n, d) for t, n, d, _ in shapes]
     dev_w = [torch.from_numpy(w).to(dev) for w in host_w]
-    xin = [torch.from_numpy(synth.activations(rng, B, HIDDEN if k == "x" else FFN)).to(dev)
-           for _, _, _, k in shapes]
-    outs = [torch.empty(B, n, device=dev) for _, n, _, _ in shapes]
+    # All inputs and all outputs of a step are slices of one buffer each, so
+    # the end-to-end run moves them with one copy per direction.
+    x_sizes = [B * (HIDDEN if k == "x" else FFN) for _, _, _, k in shapes]
+    o_sizes = [B * n for _, n, _, _ in shapes]
+    xall = torch.from_numpy(np.concatenate([synth.activations(rng, 1, sz)[0] for sz in x_sizes])).to(dev)
+    oall = torch.empty(sum(o_sizes), device=dev)
+    xin = [v.view(B, -1) for v in torch.split(xall, x_sizes)]
+    outs = [v.view(B, -1) for v in torch.split(oall, o_sizes)]
     ws_bytes = max(quantr.workspace_bytes(d, B) for _, _, d, _ in shapes)
     ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     nbytes = sum(gemv_bytes(t, n, d, B) for t, n, d, _ in shapes)
@@ -309,12 +314,43 @@ def ours_arm(args):
     torch.cuda.synchronize()
     per_call_gbs = nbytes * args.steps / (ev2.elapsed_time(ev3) / 1e3) / 1e9
 
-    # End to end through the reference-facing C ABI with host arrays.
+    # End to end with HOST buffers, (a) through the C-ABI program call: every
+    # step copies all 72 inputs from pinned host memory to the device, runs
+    # the program, and copies all outputs back; CUDA events bracket the copies.
+    h2d = xall.numel() * 4
+    d2h = oall.numel() * 4
+    hx_pin = torch.empty(xall.numel(), dtype=torch.float32).pin_memory()
+    hx_pin.copy_(torch.from_numpy(synth.activations(rng, 1, xall.numel())[0]))
+    ho_pin = torch.empty(oall.numel(), dtype=torch.float32).pin_memory()
+
+    def e2e_prog_step():
+        xall.copy_(hx_pin, non_blocking=True)
+        prog.run(s.cuda_stream)
+        ho_pin.copy_(oall, non_blocking=True)
+
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            e2e_prog_step()
+        s.synchronize()
+        if world > 1:
+            dist.barrier()
+        ev4, ev5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev4.record(s)
+        for _ in range(args.steps):
+            e2e_prog_step()
+        ev5.record(s)
+    torch.cuda.synchronize()
+    te = torch.tensor([ev4.elapsed_time(ev5)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_gbs = world * nbytes * args.steps / (float(te.item()) / 1e3) / 1e9
+
+    # (b) through the reference's own entry point, one synchronous
+    # matmul_q_fused_batch per GEMV with host arrays (weights registered once,
+    # like the reference's load-time mmap).
     for w in host_w:
         quantr.register_weights(w)
     hx = [synth.activations(rng, B, HIDDEN if k == "x" else FFN) for _, _, _, k in shapes]
-    h2d = sum(x.nbytes for x in hx)
-    d2h = sum(4 * B * n for _, n, _, _ in shapes)
 
     def e2e_step():
         for (t, n, d, _), w, x in zip(shapes, host_w, hx):
@@ -332,7 +368,7 @@ def ours_arm(args):
     te = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_gbs = world * nbytes * args.steps / float(te.item()) / 1e9
+    e2e_dropin_gbs = world * nbytes * args.steps / float(te.item()) / 1e9
     for w in host_w:
         quantr.unregister_weights(w)
 
@@ -360,7 +396,12 @@ def ours_arm(args):
             "per_call_note": "same step as 72 quantr_gemv_dev calls (one quantizer + engine launch each)",
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "api": "matmul_q_fused_batch (host pointers)"},
+                    "d2h_bytes_per_step": d2h,
+                    "api": ("quantr_program_run with all step inputs copied from pinned host memory and all "
+                            "outputs copied back inside the timed region (CUDA events)")},
+            "e2e_dropin": {"value": round(e2e_dropin_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                           "d2h_bytes_per_step": d2h,
+                           "api": "72 synchronous matmul_q_fused_batch calls per step with host arrays"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }

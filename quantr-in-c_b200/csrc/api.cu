@@ -34,7 +34,8 @@ struct Ctx {
     size_t ws_bytes = 0;
     uint8_t* dbuf = nullptr;  // device staging: x | out+err | blocks | unregistered weights
     size_t dbuf_bytes = 0;
-    uint8_t* hbuf = nullptr;  // pinned host staging
+    uint8_t* hbuf = nullptr;      // pinned, device-mapped host staging (x | out | err | blocks)
+    uint8_t* hbuf_dev = nullptr;  // the same memory as seen by kernels
     size_t hbuf_bytes = 0;
     std::map<uintptr_t, Region> regions;  // keyed by host start address
 };
@@ -106,6 +107,9 @@ int grow_dev(void** p, size_t* cap, size_t need)
     return QUANTR_OK;
 }
 
+// Pinned, device-mapped host staging: kernels read x and write out and the
+// error word through it directly (zero-copy), so a Part 1 call issues no
+// copy operations of its own - only its kernels and one synchronisation.
 int grow_host(size_t need)
 {
     if (g.hbuf_bytes >= need) return QUANTR_OK;
@@ -113,16 +117,28 @@ int grow_host(size_t need)
         cudaStreamSynchronize(g.stream);
         cudaFreeHost(g.hbuf);
         g.hbuf = nullptr;
+        g.hbuf_dev = nullptr;
         g.hbuf_bytes = 0;
     }
     size_t sz = std::max(need, (size_t)1 << 20);
-    if (cudaMallocHost((void**)&g.hbuf, sz) != cudaSuccess) {
+    if (cudaHostAlloc((void**)&g.hbuf, sz, cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess) {
         cudaGetLastError();
+        g.hbuf = nullptr;
         return QUANTR_ERR_OOM;
+    }
+    if (cudaHostGetDevicePointer((void**)&g.hbuf_dev, g.hbuf, 0) != cudaSuccess) {
+        cudaGetLastError();
+        cudaFreeHost(g.hbuf);
+        g.hbuf = nullptr;
+        return QUANTR_ERR_CUDA;
     }
     g.hbuf_bytes = sz;
     return QUANTR_OK;
 }
+
+// Host-side read of a word the device wrote into mapped staging.
+int read_mapped_int(const uint8_t* p) { return *reinterpret_cast<const volatile int*>(p); }
+void write_mapped_int(uint8_t* p, int v) { *reinterpret_cast<volatile int*>(p) = v; }
 
 // Device copy of [host, host+len) if a registered region covers it.
 const uint8_t* lookup(const void* host, size_t len)
@@ -168,32 +184,30 @@ int fused_host(float* out, const float* x, const void* w, uint32_t type, int n, 
     const size_t xbytes = (size_t)B * d * 4, obytes = (size_t)B * n * 4;
     const size_t wbytes = (size_t)n * (size_t)row_bytes(type, d);
     const uint8_t* wdev = lookup(w, wbytes);
-    Stage st = plan(xbytes, obytes, 0, wdev ? 0 : wbytes);
-    if ((rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total))) return rc;
+    Stage st = plan(xbytes, obytes, 0, 0);
+    if (!wdev && (rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, a256(wbytes)))) return rc;
     if ((rc = grow_host(st.err_off + 16))) return rc;
     const size_t need_ws = quantr_gemv_workspace_bytes(d, B);
     if (type != T_F32 && (rc = grow_dev(&g.ws, &g.ws_bytes, need_ws))) return rc;
 
-    float* dx = (float*)(g.dbuf + st.x_off);
-    float* dout = (float*)(g.dbuf + st.out_off);
-    int* derr = (int*)(g.dbuf + st.err_off);
-    std::memcpy(g.hbuf, x, xbytes);
-    cudaError_t e = cudaMemcpyAsync(dx, g.hbuf, xbytes, cudaMemcpyHostToDevice, g.stream);
-    if (!wdev && e == cudaSuccess) {
-        wdev = g.dbuf + st.w_off;
+    // x, out and the error word live in mapped pinned staging.
+    const float* dx = (const float*)(g.hbuf_dev + st.x_off);
+    float* dout = (float*)(g.hbuf_dev + st.out_off);
+    int* derr = (int*)(g.hbuf_dev + st.err_off);
+    std::memcpy(g.hbuf + st.x_off, x, xbytes);
+    write_mapped_int(g.hbuf + st.err_off, 0);
+    cudaError_t e = cudaSuccess;
+    if (!wdev) {  // unregistered weights: copy this call's rows up
+        wdev = g.dbuf;
         e = cudaMemcpyAsync((void*)wdev, w, wbytes, cudaMemcpyHostToDevice, g.stream);
     }
     LaunchCfg c;
     c.stream = g.stream;
     if (e == cudaSuccess) {
         if (type == T_F32) {
-            e = cudaMemsetAsync(derr, 0, 4, g.stream);
-            if (e == cudaSuccess)
-                e = launch_gemv_f32((const float*)wdev, dx, d, dout, n, n, d, B, c);
+            e = launch_gemv_f32((const float*)wdev, dx, d, dout, n, n, d, B, c);
         } else {
-            e = cudaMemsetAsync(derr, 0, 4, g.stream);
-            if (e == cudaSuccess)
-                e = launch_gemv_engine(wdev, type, n, d, B, dx, d, dout, n, g.ws, g.ws_bytes, derr, g.stream);
+            e = launch_gemv_engine(wdev, type, n, d, B, dx, d, dout, n, g.ws, g.ws_bytes, derr, g.stream);
             if (e == cudaErrorNotSupported) {  // shapes the engine does not take
                 ActQ a = actq_carve(g.ws, d, B);
                 e = launch_quantize(dx, d, d, B, a, nullptr, derr, c);
@@ -211,17 +225,13 @@ int fused_host(float* out, const float* x, const void* w, uint32_t type, int n, 
             }
         }
     }
-    if (e == cudaSuccess)
-        e = cudaMemcpyAsync(g.hbuf, dout, st.err_off + 4 - st.out_off, cudaMemcpyDeviceToHost, g.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return code_of(e);
     }
-    int dev_err = 0;
-    std::memcpy(&dev_err, g.hbuf + (st.err_off - st.out_off), 4);
-    if (dev_err) return QUANTR_ERR_DEVICE_TIMEOUT;
-    std::memcpy(out, g.hbuf, obytes);
+    if (read_mapped_int(g.hbuf + st.err_off)) return QUANTR_ERR_DEVICE_TIMEOUT;
+    std::memcpy(out, g.hbuf + st.out_off, obytes);
     return QUANTR_OK;
 }
 
@@ -238,22 +248,23 @@ float vec_dot_host(const void* a, const void* b, int k, uint32_t type)
     const size_t wbytes = (size_t)row_bytes(type, k);
     const int nbx = k / 32;
     const size_t blkbytes = (size_t)nbx * 34;
-    Stage st = plan(0, 4, blkbytes, wbytes);
-    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total);
-    if (!rc) rc = grow_host(std::max(blkbytes, (size_t)32));
+    Stage st = plan(0, 4, blkbytes, 0);
+    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, a256(wbytes));
+    if (!rc) rc = grow_host(st.total);
     if (!rc) rc = grow_dev(&g.ws, &g.ws_bytes, actq_bytes(k, 1));
     if (rc) {
         set_err(rc);
         return 0.0f;
     }
-    uint8_t* dblk = g.dbuf + st.blk_off;
-    uint8_t* dw = g.dbuf + st.w_off;
-    float* dout = (float*)(g.dbuf + st.out_off);
-    int* derr = (int*)(g.dbuf + st.err_off);
-    std::memcpy(g.hbuf, b, blkbytes);
-    cudaError_t e = cudaMemcpyAsync(dblk, g.hbuf, blkbytes, cudaMemcpyHostToDevice, g.stream);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(dw, a, wbytes, cudaMemcpyHostToDevice, g.stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(derr, 0, 4, g.stream);
+    // Activation blocks, result and error word in mapped staging; the weight
+    // row goes to device memory (the GEMV streams weights with bulk copies).
+    const uint8_t* dblk = g.hbuf_dev + st.blk_off;
+    uint8_t* dw = g.dbuf;
+    float* dout = (float*)(g.hbuf_dev + st.out_off);
+    int* derr = (int*)(g.hbuf_dev + st.err_off);
+    std::memcpy(g.hbuf + st.blk_off, b, blkbytes);
+    write_mapped_int(g.hbuf + st.err_off, 0);
+    cudaError_t e = cudaMemcpyAsync(dw, a, wbytes, cudaMemcpyHostToDevice, g.stream);
     LaunchCfg c;
     c.stream = g.stream;
     ActQ act = actq_carve(g.ws, k, 1);
@@ -269,21 +280,18 @@ float vec_dot_host(const void* a, const void* b, int k, uint32_t type)
     ga.B = 1;
     ga.err = derr;
     if (e == cudaSuccess) e = launch_gemv(ga, c);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(g.hbuf, dout, st.err_off + 4 - st.out_off, cudaMemcpyDeviceToHost, g.stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         set_err(code_of(e));
         return 0.0f;
     }
-    int dev_err = 0;
-    std::memcpy(&dev_err, g.hbuf + (st.err_off - st.out_off), 4);
-    if (dev_err) {
+    if (read_mapped_int(g.hbuf + st.err_off)) {
         set_err(QUANTR_ERR_DEVICE_TIMEOUT);
         return 0.0f;
     }
     float r;
-    std::memcpy(&r, g.hbuf, 4);
+    std::memcpy(&r, g.hbuf + st.out_off, 4);
     return r;
 }
 
@@ -457,22 +465,20 @@ void quantize_row_q8_0(const float* x, block_q8_0* y, int k)
     const size_t xbytes = (size_t)nbx * 32 * 4, blkbytes = (size_t)nbx * 34;
     Stage st = plan(xbytes, 0, blkbytes, 0);
     int rc = ensure_ready();
-    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total);
-    if (!rc) rc = grow_host(std::max(xbytes, blkbytes));
-    if (!rc) rc = grow_dev(&g.ws, &g.ws_bytes, actq_bytes(k, 1));
+    if (!rc) rc = grow_host(st.total);
     if (rc) {
         set_err(rc);
         std::memset(y, 0, blkbytes);
         return;
     }
-    std::memcpy(g.hbuf, x, xbytes);
+    // Zero-copy: the quantizer reads x from and writes the packed blocks to
+    // mapped pinned staging (no activation workspace needed: blocks only).
+    std::memcpy(g.hbuf + st.x_off, x, xbytes);
     LaunchCfg c;
     c.stream = g.stream;
-    cudaError_t e = cudaMemcpyAsync(g.dbuf + st.x_off, g.hbuf, xbytes, cudaMemcpyHostToDevice, g.stream);
-    if (e == cudaSuccess)
-        e = launch_quantize((const float*)(g.dbuf + st.x_off), k, k, 1, actq_carve(g.ws, k, 1), g.dbuf + st.blk_off,
-                            nullptr, c);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(g.hbuf, g.dbuf + st.blk_off, blkbytes, cudaMemcpyDeviceToHost, g.stream);
+    ActQ none{};
+    cudaError_t e = launch_quantize((const float*)(g.hbuf_dev + st.x_off), k, k, 1, none, g.hbuf_dev + st.blk_off,
+                                    nullptr, c);
     if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
@@ -480,7 +486,7 @@ void quantize_row_q8_0(const float* x, block_q8_0* y, int k)
         std::memset(y, 0, blkbytes);
         return;
     }
-    std::memcpy(y, g.hbuf, blkbytes);
+    std::memcpy(y, g.hbuf + st.blk_off, blkbytes);
 }
 
 void dequantize_row(float* out, const void* src, uint32_t type, int n)
@@ -499,31 +505,33 @@ void dequantize_row(float* out, const void* src, uint32_t type, int n)
         zero_out(out, (size_t)n);
         return;
     }
-    const size_t sbytes = (size_t)row_bytes(type, n), obytes = (size_t)n * 4;
+    // The reference decodes whole blocks only and leaves out[] past the last
+    // block untouched (src/quant.c:171-177, :182-194): so does this call.
+    const int done = (n / block_elems(type)) * block_elems(type);
+    if (done == 0) return;
+    const size_t sbytes = (size_t)row_bytes(type, n), obytes = (size_t)done * 4;
     Stage st = plan(0, obytes, 0, sbytes);
     int rc = ensure_ready();
-    if (!rc) rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, st.total);
-    if (!rc) rc = grow_host(obytes);
+    if (!rc) rc = grow_host(st.w_off + sbytes);
     if (rc) {
         set_err(rc);
-        zero_out(out, (size_t)n);
+        zero_out(out, (size_t)done);
         return;
     }
-    float* dout = (float*)(g.dbuf + st.out_off);
+    // Zero-copy: the kernel reads the packed row from and writes the floats
+    // to mapped pinned staging.
+    std::memcpy(g.hbuf + st.w_off, src, sbytes);
     LaunchCfg c;
     c.stream = g.stream;
-    cudaError_t e = cudaMemsetAsync(dout, 0, obytes, g.stream);  // tail past the last block stays 0
-    if (e == cudaSuccess) e = cudaMemcpyAsync(g.dbuf + st.w_off, src, sbytes, cudaMemcpyHostToDevice, g.stream);
-    if (e == cudaSuccess) e = launch_dequantize(dout, g.dbuf + st.w_off, type, n, c);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(g.hbuf, dout, obytes, cudaMemcpyDeviceToHost, g.stream);
+    cudaError_t e = launch_dequantize((float*)(g.hbuf_dev + st.out_off), g.hbuf_dev + st.w_off, type, n, c);
     if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
     if (e != cudaSuccess) {
         cudaGetLastError();
         set_err(code_of(e));
-        zero_out(out, (size_t)n);
+        zero_out(out, (size_t)done);
         return;
     }
-    std::memcpy(out, g.hbuf, obytes);
+    std::memcpy(out, g.hbuf + st.out_off, obytes);
 }
 
 float vec_dot_q8_0_q8_0(const block_q8_0* a, const block_q8_0* b, int k) { return vec_dot_host(a, b, k, T_Q8_0); }

@@ -42,6 +42,7 @@
 #include <algorithm>
 #include <cstring>
 #include <map>
+#include <mutex>
 #include <new>
 #include <numeric>
 #include <tuple>
@@ -743,10 +744,29 @@ cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, in
         row_bytes(type, d) <= 0)
         return cudaErrorNotSupported;
     if (eng::act_bytes_for(type, d, B) > ws_bytes) return cudaErrorNotSupported;
-    eng::JobIn in{w, type, n, d, B, x, ldx, out, ldo};
+    // Plans depend only on these arguments and the device; repeated calls
+    // (a decoder's per-layer GEMVs) reuse them instead of re-planning.
+    int dev = 0;
+    cudaGetDevice(&dev);
+    using Key = std::tuple<int, const uint8_t*, uint32_t, int, int, int, const float*, long long, float*, long long,
+                           void*>;
+    static std::mutex mu;
+    static std::map<Key, eng::Plan> cache;
+    const Key key{dev, w, type, n, d, B, x, ldx, out, ldo, ws};
     eng::Plan pl;
-    if (eng::make_plan(&in, 1, static_cast<uint8_t*>(ws), device_sm_count(), false, pl) != QUANTR_OK)
-        return cudaErrorNotSupported;
+    {
+        std::lock_guard<std::mutex> lk(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) {
+            pl = it->second;
+        } else {
+            eng::JobIn in{w, type, n, d, B, x, ldx, out, ldo};
+            if (eng::make_plan(&in, 1, static_cast<uint8_t*>(ws), device_sm_count(), false, pl) != QUANTR_OK)
+                return cudaErrorNotSupported;
+            if (cache.size() >= 4096) cache.clear();
+            cache.emplace(key, pl);
+        }
+    }
     return eng::launch_plan(pl, nullptr, err, stream);
 }
 
