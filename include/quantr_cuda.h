@@ -104,7 +104,9 @@ enum {
     QUANTR_ERR_OOM = 5,              /* device or pinned allocation failed */
     QUANTR_ERR_DEVICE_TIMEOUT = 6,   /* a bounded in-kernel wait gave up */
     QUANTR_ERR_TOO_LARGE = 7,        /* shape exceeds a kernel limit */
-    QUANTR_ERR_WORKSPACE = 8         /* caller workspace too small */
+    QUANTR_ERR_WORKSPACE = 8,        /* caller workspace too small */
+    QUANTR_ERR_ROUTING = 9,          /* a token's router probabilities were not finite */
+    QUANTR_ERR_UNREGISTERED = 10     /* host weights not covered by quantr_gpu_register_weights */
 };
 int quantr_gpu_last_error(void);
 void quantr_gpu_clear_error(void);
@@ -198,6 +200,52 @@ int quantr_program_run(quantr_program* prog, void* stream);
 void quantr_program_destroy(quantr_program* prog);
 /* Work items (row tiles), persistent CTAs and shared memory per CTA. */
 int quantr_program_info(const quantr_program* prog, int* items, int* grid, int* smem_bytes);
+
+/* ---- routed mixture-of-experts FFN block -------------------------------- */
+
+/* One expert projection: E matrices of one type and shape.  Expert e lives at
+ * base + e*stride (the merged *_exps tensors, src/model.c:409-419) or, when
+ * table is non-NULL, at table[e] (a device array of E device pointers: the
+ * per-expert tensors of src/model.c:421-435). */
+typedef struct {
+    const void* base;
+    long long stride;
+    const void* const* table;
+    uint32_t type; /* QUANTR_TYPE_Q8_0 / Q4_K / Q5_K / Q6_K */
+} quantr_expert_weights;
+
+/* Workspace bytes quantr_moe_dev needs. */
+size_t quantr_moe_workspace_bytes(int T, int E, int k, int dim, int hidden);
+
+/* The reference's routed-MoE branch (src/runtime.c:202-269) for T tokens, each
+ * as one forward_runtime call would compute it: router logits (F32 matmul of
+ * `router`, E x dim, in matmul_ref order; or the given T x E `logits` when
+ * router is NULL), softmax, top-k by repeated strict arg-max, renormalised
+ * weights, and per selected expert in order hb = W1.xb, hb2 = W3.xb,
+ * hb = silu(hb)*hb2, o = W2.hb, out += o*ew from out = 0.  W1 is the tensor
+ * the reference binds to ffn_up; W1/W3 are hidden x dim, W2 dim x hidden.
+ * out is T x dim (out[t*ldo + i]); the caller adds the residual (x += out).
+ * sel / wts (T x k, optional) receive the routing.  E <= 256, k <= 16
+ * (the reference's fixed buffers), k <= E.  All expert GEMVs are bit-identical
+ * to matmul_q_fused; softmax and silu use correctly rounded expf, which can
+ * differ from glibc's expf in the last bit.  A token whose probabilities are
+ * not finite (NaN logits) gets no experts and out = 0, and the device status
+ * reports QUANTR_ERR_ROUTING.  The workspace must be 256-byte aligned.
+ * Asynchronous on `stream`. */
+int quantr_moe_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
+                   const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
+                   const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden, int* sel,
+                   float* wts, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Host-pointer, synchronous form for the reference's runtime: w1/w3/w2 are the
+ * per-layer arrays of E expert pointers (w->expert_w1[l], ..., include/types.h:
+ * 68-70), each inside a range registered with quantr_gpu_register_weights
+ * (else QUANTR_ERR_UNREGISTERED); router is w->ffn_gate_inp[l] (E x dim F32,
+ * registered or not) or NULL with `logits` given.  On failure out is zeroed and
+ * the sticky error is set.  Returns a QUANTR_* code. */
+int quantr_moe_layer(float* out, const float* xb, int T, const float* router, const float* logits, int E, int k,
+                     const void* const* w1, uint32_t t1, const void* const* w3, uint32_t t3, const void* const* w2,
+                     uint32_t t2, int dim, int hidden, int* sel, float* wts);
 
 /* Allocation-free quantized GEMV.  No counterpart in the reference: an
  * addition for callers that cannot call cudaMalloc - embedders whose own

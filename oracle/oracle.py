@@ -116,6 +116,10 @@ class Oracle(_QuantLib):
         L.qo_fp32_to_fp16.argtypes = [_f]
         L.qo_unit_partials.restype = _i
         L.qo_unit_partials.argtypes = [_vp, _vp, _vp, _u32, _i, _i, _vp]
+        L.qo_softmax.restype = None
+        L.qo_softmax.argtypes = [_vp, _i]
+        L.qo_matmul_f32.restype = None
+        L.qo_matmul_f32.argtypes = [_vp, _vp, _vp, _i, _i]
         L.qo_moe_token.restype = _i
         L.qo_moe_token.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _u32, _l, _vp, _u32, _l,
                                    _vp, _u32, _l, _i, _i]
@@ -133,6 +137,17 @@ class Oracle(_QuantLib):
         self.L.qo_unit_partials(_p(isum), _p(bsum), _p(np.ascontiguousarray(w)), type_, n, d,
                                 _p(np.ascontiguousarray(xq)))
         return isum, bsum
+
+    def softmax(self, x):
+        y = np.array(x, dtype=np.float32, copy=True)
+        self.L.qo_softmax(_p(y), y.size)
+        return y
+
+    def matmul_f32(self, x, w, n, d):
+        out = np.zeros(n, dtype=np.float32)
+        self.L.qo_matmul_f32(_p(out), _p(np.ascontiguousarray(x, np.float32)),
+                             _p(np.ascontiguousarray(w, np.float32)), n, d)
+        return out
 
     def moe_token(self, xb, E, k, w1, t1, b1, w3, t3, b3, w2, t2, b2, dim, hidden, router=None, logits=None):
         out = np.zeros(dim, dtype=np.float32)
@@ -157,6 +172,23 @@ class RefLib(_QuantLib):
         L.ref_fp16_to_fp32.argtypes = [ctypes.c_uint16]
         L.ref_fp32_to_fp16.restype = ctypes.c_uint16
         L.ref_fp32_to_fp16.argtypes = [_f]
+        L.ref_softmax.restype = None
+        L.ref_softmax.argtypes = [_vp, _i]
+        L.ref_matmul_f32.restype = None
+        L.ref_matmul_f32.argtypes = [_vp, _vp, _vp, _i, _i, _i]
+
+    def softmax(self, x):
+        """KernelOps softmax of the scalar backend (src/kernels.c:191-207)."""
+        y = np.array(x, dtype=np.float32, copy=True)
+        self.L.ref_softmax(_p(y), y.size)
+        return y
+
+    def matmul_f32(self, x, w, n, d, backend=0):
+        """KernelOps matmul of `backend` (0 = matmul_ref, src/kernels.c:18-28)."""
+        out = np.zeros(n, dtype=np.float32)
+        self.L.ref_matmul_f32(_p(out), _p(np.ascontiguousarray(x, np.float32)),
+                              _p(np.ascontiguousarray(w, np.float32)), n, d, backend)
+        return out
 
     def fp16_to_fp32(self, h):
         return np.float32(self.L.ref_fp16_to_fp32(int(h)))

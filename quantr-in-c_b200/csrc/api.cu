@@ -14,6 +14,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <vector>
 
 namespace {
 
@@ -66,6 +67,14 @@ int code_of(cudaError_t e)
         return QUANTR_ERR_NO_DEVICE;
     if (e == cudaErrorInvalidConfiguration) return QUANTR_ERR_TOO_LARGE;
     return QUANTR_ERR_CUDA;
+}
+
+// Device error word value -> QUANTR_* code.
+int dev_code(int v)
+{
+    if (v == DEV_OK) return QUANTR_OK;
+    if (v == DEV_ERR_ROUTING) return QUANTR_ERR_ROUTING;
+    return QUANTR_ERR_DEVICE_TIMEOUT;
 }
 
 size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -338,6 +347,8 @@ const char* quantr_gpu_error_string(int code)
     case QUANTR_ERR_DEVICE_TIMEOUT: return "bounded in-kernel wait timed out";
     case QUANTR_ERR_TOO_LARGE: return "shape exceeds a kernel limit";
     case QUANTR_ERR_WORKSPACE: return "workspace too small";
+    case QUANTR_ERR_ROUTING: return "router probabilities not finite for some token";
+    case QUANTR_ERR_UNREGISTERED: return "weights not registered with quantr_gpu_register_weights";
     default: return "unknown error";
     }
 }
@@ -625,6 +636,202 @@ int quantr_quantize_q8_0_dev(block_q8_0* y, const float* x, long long ldx, int k
     return code_of(launch_quantize(x, ldx, k, B, none, (uint8_t*)y, nullptr, c));
 }
 
+// ------------------------------------------------------------------- MoE --
+
+size_t quantr_moe_workspace_bytes(int T, int E, int k, int dim, int hidden)
+{
+    return moe_workspace_bytes(T, E, k, dim, hidden);
+}
+
+static bool expert_ok(const quantr_expert_weights* w)
+{
+    return w && (w->base || w->table) && type_supported(w->type) && w->type != T_F32;
+}
+
+static int moe_check(const float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
+                     const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
+                     const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden)
+{
+    if (T < 0 || !out || !xb || dim <= 0 || hidden <= 0 || ldx < dim || ldo < dim) return QUANTR_ERR_BAD_ARG;
+    if (E <= 0 || E > kMoeMaxExperts || k <= 0 || k > kMoeMaxK || k > E) return QUANTR_ERR_BAD_ARG;
+    if (!router && (!logits || ldl < E)) return QUANTR_ERR_BAD_ARG;
+    if (!w1 || !w3 || !w2) return QUANTR_ERR_BAD_ARG;
+    if (!expert_ok(w1) || !expert_ok(w3) || !expert_ok(w2)) {
+        if ((w1->base || w1->table) && (w3->base || w3->table) && (w2->base || w2->table))
+            return QUANTR_ERR_UNSUPPORTED_TYPE;
+        return QUANTR_ERR_BAD_ARG;
+    }
+    return QUANTR_OK;
+}
+
+static ExpertMats mats_of(const quantr_expert_weights* w)
+{
+    ExpertMats m;
+    m.base = (const uint8_t*)w->base;
+    m.stride = w->stride;
+    m.table = (const uint8_t* const*)w->table;
+    m.type = w->type;
+    return m;
+}
+
+int quantr_moe_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
+                   const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
+                   const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden, int* sel,
+                   float* wts, void* workspace, size_t workspace_bytes, void* stream)
+{
+    int rc = moe_check(out, ldo, xb, ldx, T, router, logits, ldl, E, k, w1, w3, w2, dim, hidden);
+    if (rc || T == 0) return rc;
+    if (!workspace || workspace_bytes < moe_workspace_bytes(T, E, k, dim, hidden) || ((uintptr_t)workspace & 255))
+        return QUANTR_ERR_WORKSPACE;
+    MoeArgs a;
+    a.out = out;
+    a.ldo = ldo;
+    a.xb = xb;
+    a.ldx = ldx;
+    a.T = T;
+    a.router = router;
+    a.logits = logits;
+    a.ldl = ldl;
+    a.E = E;
+    a.k = k;
+    a.dim = dim;
+    a.hidden = hidden;
+    a.w1 = mats_of(w1);
+    a.w3 = mats_of(w3);
+    a.w2 = mats_of(w2);
+    a.sel = sel;
+    a.wts = wts;
+    a.ws = workspace;
+    a.ws_bytes = workspace_bytes;
+    a.err = device_error_word();
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    return code_of(launch_moe(a, c));
+}
+
+// Resolves an array of E host expert pointers to device memory: a uniform
+// stride when the experts are evenly spaced (returns QUANTR_OK), else the
+// caller needs a pointer table (returns -1).
+static int resolve_experts(const void* const* host, int E, size_t mat_bytes, uint32_t type,
+                           quantr_expert_weights* w, const uint8_t** devs)
+{
+    if (!host) return QUANTR_ERR_BAD_ARG;
+    for (int e = 0; e < E; ++e) {
+        if (!host[e]) return QUANTR_ERR_BAD_ARG;
+        devs[e] = lookup(host[e], mat_bytes);
+        if (!devs[e]) return QUANTR_ERR_UNREGISTERED;
+    }
+    const long long stride = E > 1 ? (long long)(devs[1] - devs[0]) : 0;
+    bool uniform = true;
+    for (int e = 1; e < E && uniform; ++e) uniform = (long long)(devs[e] - devs[0]) == (long long)e * stride;
+    w->base = devs[0];
+    w->stride = uniform ? stride : 0;
+    w->table = nullptr;
+    w->type = type;
+    return uniform ? QUANTR_OK : -1;
+}
+
+int quantr_moe_layer(float* out, const float* xb, int T, const float* router, const float* logits, int E, int k,
+                     const void* const* w1, uint32_t t1, const void* const* w3, uint32_t t3, const void* const* w2,
+                     uint32_t t2, int dim, int hidden, int* sel, float* wts)
+{
+    std::lock_guard<std::recursive_mutex> lk(g_mu);
+    auto fail = [&](int rc) {
+        if (out && T > 0 && dim > 0) zero_out(out, (size_t)T * dim);
+        set_err(rc);
+        return rc;
+    };
+    if (T == 0) return QUANTR_OK;
+    // Validate shapes and types with stand-in (non-null) expert descriptors.
+    const quantr_expert_weights v1{(const void*)1, 0, nullptr, t1}, v3{(const void*)1, 0, nullptr, t3},
+        v2{(const void*)1, 0, nullptr, t2};
+    int rc = moe_check(out, dim, xb, dim, T, router, logits, E, E, k, &v1, &v3, &v2, dim, hidden);
+    if (!rc && (!w1 || !w3 || !w2)) rc = QUANTR_ERR_BAD_ARG;
+    if (rc) return fail(rc);
+    if ((rc = ensure_ready())) return fail(rc);
+
+    // Expert matrices: W1/W3 are hidden x dim, W2 dim x hidden
+    // (ggml_type_row_size slices, src/model.c:20-30, 412-414).
+    quantr_expert_weights w[3];
+    const void* const* hosts[3] = {w1, w3, w2};
+    const uint32_t types[3] = {t1, t3, t2};
+    const size_t mats[3] = {(size_t)hidden * row_bytes(t1, dim), (size_t)hidden * row_bytes(t3, dim),
+                            (size_t)dim * row_bytes(t2, hidden)};
+    std::vector<const uint8_t*> devs((size_t)3 * E);
+    bool need_table[3] = {false, false, false};
+    for (int m = 0; m < 3; ++m) {
+        rc = resolve_experts(hosts[m], E, std::max(mats[m], (size_t)1), types[m], &w[m], &devs[(size_t)m * E]);
+        if (rc == -1) need_table[m] = true;
+        else if (rc) return fail(rc);
+    }
+
+    // Host staging (mapped): x | logits | tables | out | sel | wts | err; the
+    // first three are copied to device memory with one copy.
+    const size_t xbytes = (size_t)T * dim * 4, lbytes = router ? 0 : (size_t)T * E * 4;
+    const size_t tbytes = (size_t)3 * E * sizeof(void*), rbytes = (size_t)E * dim * 4;
+    const size_t x_off = 0, l_off = a256(xbytes), t_off = l_off + a256(lbytes), in_end = t_off + a256(tbytes);
+    const size_t o_off = in_end, s_off = o_off + a256(xbytes), w_off = s_off + a256((size_t)T * k * 4);
+    const size_t e_off = w_off + a256((size_t)T * k * 4), h_total = e_off + 256;
+    const uint8_t* rdev = router ? lookup(router, rbytes) : nullptr;
+    const size_t r_off = in_end, d_total = in_end + (router && !rdev ? a256(rbytes) : 0);
+    if ((rc = grow_host(h_total))) return fail(rc);
+    if ((rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, d_total))) return fail(rc);
+    const size_t wsb = moe_workspace_bytes(T, E, k, dim, hidden);
+    if ((rc = grow_dev(&g.ws, &g.ws_bytes, wsb))) return fail(rc);
+
+    std::memcpy(g.hbuf + x_off, xb, xbytes);
+    if (!router) std::memcpy(g.hbuf + l_off, logits, lbytes);
+    const uint8_t** tab = reinterpret_cast<const uint8_t**>(g.hbuf + t_off);
+    for (size_t i = 0; i < (size_t)3 * E; ++i) tab[i] = devs[i];
+    for (int m = 0; m < 3; ++m)
+        if (need_table[m]) w[m].table = (const void* const*)(g.dbuf + t_off + (size_t)m * E * sizeof(void*));
+    write_mapped_int(g.hbuf + e_off, 0);
+    cudaError_t e = cudaMemcpyAsync(g.dbuf, g.hbuf, in_end, cudaMemcpyHostToDevice, g.stream);
+    if (e == cudaSuccess && router && !rdev) {
+        e = cudaMemcpyAsync(g.dbuf + r_off, router, rbytes, cudaMemcpyHostToDevice, g.stream);
+        rdev = g.dbuf + r_off;
+    }
+    MoeArgs a;
+    a.out = (float*)(g.hbuf_dev + o_off);
+    a.ldo = dim;
+    a.xb = (const float*)(g.dbuf + x_off);
+    a.ldx = dim;
+    a.T = T;
+    a.router = router ? (const float*)rdev : nullptr;
+    a.logits = router ? nullptr : (const float*)(g.dbuf + l_off);
+    a.ldl = E;
+    a.E = E;
+    a.k = k;
+    a.dim = dim;
+    a.hidden = hidden;
+    a.w1 = mats_of(&w[0]);
+    a.w3 = mats_of(&w[1]);
+    a.w2 = mats_of(&w[2]);
+    a.sel = (int*)(g.hbuf_dev + s_off);
+    a.wts = (float*)(g.hbuf_dev + w_off);
+    a.ws = g.ws;
+    a.ws_bytes = g.ws_bytes;
+    a.err = (int*)(g.hbuf_dev + e_off);
+    LaunchCfg c;
+    c.stream = g.stream;
+    if (e == cudaSuccess) e = launch_moe(a, c);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return fail(code_of(e));
+    }
+    const int dv = read_mapped_int(g.hbuf + e_off);
+    if (dv != DEV_OK && dv != DEV_ERR_ROUTING) return fail(dev_code(dv));
+    std::memcpy(out, g.hbuf + o_off, xbytes);
+    if (sel) std::memcpy(sel, g.hbuf + s_off, (size_t)T * k * 4);
+    if (wts) std::memcpy(wts, g.hbuf + w_off, (size_t)T * k * 4);
+    if (dv == DEV_ERR_ROUTING) {
+        set_err(QUANTR_ERR_ROUTING);
+        return QUANTR_ERR_ROUTING;
+    }
+    return QUANTR_OK;
+}
+
 int quantr_gpu_device_status(void* stream, int reset)
 {
     int* w = device_error_word();
@@ -636,7 +843,7 @@ int quantr_gpu_device_status(void* stream, int reset)
     }
     if (cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return QUANTR_ERR_CUDA;
     if (reset) cudaMemset(w, 0, 4);
-    return v ? QUANTR_ERR_DEVICE_TIMEOUT : QUANTR_OK;
+    return dev_code(v);
 }
 
 } // extern "C"

@@ -60,17 +60,11 @@ __global__ void __launch_bounds__(kThreads)
         const int t = (int)(wb / nbx);
         const int b = (int)(wb - (long long)t * nbx);
         const float v = x[(long long)t * ldx + (long long)b * 32 + lane];
-        const float a = fabsf(v);
-        // The reference skips NaN when taking the max (v > amax is false).
-        const uint32_t abits = (a == a) ? __float_as_uint(a) : 0u;
-        const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, abits));
-        const float dd = __fdiv_rn(amax, 127.0f);
-        const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
-        const int8_t qq = lrintf_to_i8(__fmul_rn(v, id));
-        const int sum = __reduce_add_sync(0xffffffffu, (int)qq);
+        uint32_t h;
+        int sum;
+        const int8_t qq = q8_block_warp(v, h, sum);
         if (act) q[wb * 32 + lane] = qq;
         if (lane == 0) {
-            const uint32_t h = f2h_ref(dd);
             if (act) {
                 dq[wb] = h2f_ref(h);
                 sq[wb] = sum;
@@ -221,34 +215,40 @@ __global__ void __launch_bounds__(kThreads) k_gemv(KParams p)
     }
 }
 
-// F32 weights: 128 rows per CTA, 32-column tiles through shared memory, one
-// thread per row summing sequentially (reference src/quant.c:455-461).
-__global__ void __launch_bounds__(128)
+// F32 weights (reference src/quant.c:455-461, which is KernelOps matmul_ref,
+// src/kernels.c:18-28): one thread per (row, token) summing row[j]*x[j] left
+// to right.  A CTA covers RT rows x TT tokens; 32-column tiles of the weights
+// and of x pass through shared memory.
+template <int RT, int TT>
+__global__ void __launch_bounds__(RT * TT)
     k_gemv_f32(const float* __restrict__ w, const float* __restrict__ x, long long ldx, float* __restrict__ out,
                long long ldo, int n, int d, int B)
 {
-    __shared__ float tile[128][33];
-    __shared__ float xt[32];
+    constexpr int kWarps = RT * TT / 32;
+    __shared__ float tile[RT][33];
+    __shared__ float xt[TT][33];
     pdl_trigger();
     pdl_wait();
-    const int r0 = blockIdx.x * 128;
+    const int r0 = blockIdx.x * RT, t0 = blockIdx.y * TT;
     const int tid = threadIdx.x;
+    const int rr = tid % RT, tt = tid / RT;
     const int lane = tid & 31, warp = tid >> 5;
-    for (int t = 0; t < B; ++t) {
-        float acc = 0.0f;
-        for (int c0 = 0; c0 < d; c0 += 32) {
-            const int cw = min(32, d - c0);
-            __syncthreads();
-            for (int rr = warp; rr < 128; rr += 4) {
-                const int r = r0 + rr;
-                tile[rr][lane] = (r < n && lane < cw) ? w[(long long)r * d + c0 + lane] : 0.0f;
-            }
-            if (tid < 32) xt[tid] = tid < cw ? x[(long long)t * ldx + c0 + tid] : 0.0f;
-            __syncthreads();
-            for (int c = 0; c < cw; ++c) acc = __fadd_rn(acc, __fmul_rn(tile[tid][c], xt[c]));
+    float acc = 0.0f;
+    for (int c0 = 0; c0 < d; c0 += 32) {
+        const int cw = min(32, d - c0);
+        __syncthreads();
+        for (int q = warp; q < RT; q += kWarps) {
+            const int r = r0 + q;
+            tile[q][lane] = (r < n && lane < cw) ? w[(long long)r * d + c0 + lane] : 0.0f;
         }
-        if (r0 + tid < n) out[(long long)t * ldo + r0 + tid] = acc;
+        for (int q = warp; q < TT; q += kWarps) {
+            const int t = t0 + q;
+            xt[q][lane] = (t < B && lane < cw) ? x[(long long)t * ldx + c0 + lane] : 0.0f;
+        }
+        __syncthreads();
+        for (int c = 0; c < cw; ++c) acc = __fadd_rn(acc, __fmul_rn(tile[rr][c], xt[tt][c]));
     }
+    if (r0 + rr < n && t0 + tt < B) out[(long long)(t0 + tt) * ldo + r0 + rr] = acc;
 }
 
 // Reference dequantize_row (src/quant.c:160-240), one thread per element.
@@ -448,7 +448,10 @@ cudaError_t launch_gemv_f32(const float* w, const float* x, long long ldx, float
                             int d, int B, const LaunchCfg& c)
 {
     if (n <= 0 || B <= 0) return cudaSuccess;
-    return launch_ex(&k_gemv_f32, dim3((n + 127) / 128), dim3(128), 0, c, w, x, ldx, out, ldo, n, d, B);
+    if (B == 1)
+        return launch_ex(&k_gemv_f32<128, 1>, dim3((n + 127) / 128), dim3(128), 0, c, w, x, ldx, out, ldo, n, d, B);
+    return launch_ex(&k_gemv_f32<32, 4>, dim3((n + 31) / 32, (B + 3) / 4), dim3(128), 0, c, w, x, ldx, out, ldo, n,
+                     d, B);
 }
 
 cudaError_t launch_dequantize(float* out, const uint8_t* src, uint32_t type, int n, const LaunchCfg& c)

@@ -22,7 +22,7 @@ size_t actq_bytes(int d, int B);
 ActQ actq_carve(void* ws, int d, int B);
 
 // Device error word written by kernels whose bounded waits give up.
-enum : int { DEV_OK = 0, DEV_ERR_WAIT_TIMEOUT = 1 };
+enum : int { DEV_OK = 0, DEV_ERR_WAIT_TIMEOUT = 1, DEV_ERR_ROUTING = 2 };
 
 struct LaunchCfg {
     cudaStream_t stream = nullptr;
@@ -81,5 +81,42 @@ cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, in
                                long long ldx, float* out, long long ldo, void* ws, size_t ws_bytes, int* err,
                                cudaStream_t stream);
 size_t engine_act_bytes(uint32_t type, int d, int B);
+
+// ---- routed MoE block (moe.cu) ----
+
+// The reference's fixed routing buffers: router_logits[256], active_experts[16]
+// (src/runtime.c:204, 210).
+constexpr int kMoeMaxExperts = 256;
+constexpr int kMoeMaxK = 16;
+
+// E matrices of one expert projection: expert e at base + e*stride, or
+// table[e] (a device array of device pointers) when table is non-null.
+struct ExpertMats {
+    const uint8_t* base = nullptr;
+    long long stride = 0;
+    const uint8_t* const* table = nullptr;
+    uint32_t type = 0;
+};
+
+struct MoeArgs {
+    float* out = nullptr;  // T x dim, out[t*ldo + i]
+    long long ldo = 0;
+    const float* xb = nullptr;  // T x dim
+    long long ldx = 0;
+    int T = 0;
+    const float* router = nullptr;  // E x dim F32 router weights, or null
+    const float* logits = nullptr;  // T x E router logits when router is null
+    long long ldl = 0;
+    int E = 0, k = 0, dim = 0, hidden = 0;
+    ExpertMats w1, w3, w2;  // w1/w3: hidden x dim, w2: dim x hidden
+    int* sel = nullptr;     // optional T x k selected experts
+    float* wts = nullptr;   // optional T x k renormalised weights
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    int* err = nullptr;
+};
+
+size_t moe_workspace_bytes(int T, int E, int k, int dim, int hidden);
+cudaError_t launch_moe(const MoeArgs& a, const LaunchCfg& c);
 
 } // namespace qr

@@ -129,4 +129,23 @@ __device__ __forceinline__ int dot8(const uint32_t* wq, uint4 xa, uint4 xb)
     return s;
 }
 
+// One Q8_0 block per warp, lane = element: reference quantize_row_q8_0
+// (src/quant.c:143-158) with IEEE division, the fp32 reciprocal of the
+// unrounded scale, round-half-even and the truncating fp16 store.  Returns the
+// lane's quant; h (fp16 bits of the scale) and sum (int sum of the block's
+// quants) are valid in every lane.  NaN is skipped when taking the maximum,
+// as the reference's `v > amax` test skips it.
+__device__ __forceinline__ int8_t q8_block_warp(float v, uint32_t& h, int& sum)
+{
+    const float a = fabsf(v);
+    const uint32_t abits = (a == a) ? __float_as_uint(a) : 0u;
+    const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, abits));
+    const float dd = __fdiv_rn(amax, 127.0f);
+    const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
+    const int8_t qq = lrintf_to_i8(__fmul_rn(v, id));
+    sum = __reduce_add_sync(0xffffffffu, (int)qq);
+    h = f2h_ref(dd);
+    return qq;
+}
+
 } // namespace qr

@@ -57,6 +57,10 @@ SIGNATURES = {
     "quantr_program_run": (_i, [_vp, _vp]),
     "quantr_program_destroy": (None, [_vp]),
     "quantr_program_info": (_i, [_vp, _c.POINTER(_i), _c.POINTER(_i), _c.POINTER(_i)]),
+    "quantr_moe_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
+    "quantr_moe_dev": (_i, [_vp, _ll, _vp, _ll, _i, _vp, _vp, _ll, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp,
+                            _sz, _vp]),
+    "quantr_moe_layer": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _vp, _u32, _vp, _u32, _vp, _u32, _i, _i, _vp, _vp]),
 }
 
 
@@ -64,6 +68,11 @@ class GemvJob(ctypes.Structure):
     """quantr_gemv_job (include/quantr_cuda.h)."""
     _fields_ = [("w", _vp), ("type", _u32), ("n", _i), ("d", _i), ("B", _i), ("x", _vp), ("ldx", _ll),
                 ("out", _vp), ("ldo", _ll)]
+
+
+class ExpertWeights(ctypes.Structure):
+    """quantr_expert_weights (include/quantr_cuda.h)."""
+    _fields_ = [("base", _vp), ("stride", _ll), ("table", _vp), ("type", _u32)]
 
 
 class QuantrError(RuntimeError):
@@ -251,6 +260,39 @@ class Program:
             self.close()
         except Exception:
             pass
+
+
+# ------------------------------------------------------------------- MoE --
+
+def moe_workspace_bytes(T, E, k, dim, hidden):
+    return int(lib().quantr_moe_workspace_bytes(T, E, k, dim, hidden))
+
+
+def moe_dev(out, ldo, xb, ldx, T, E, k, w1, w3, w2, dim, hidden, ws, ws_bytes, router=None, logits=None, ldl=0,
+            sel=None, wts=None, stream=0):
+    """quantr_moe_dev.  w1/w3/w2: ExpertWeights; pointers are device addresses."""
+    rc = lib().quantr_moe_dev(out, ldo, xb, ldx, T, router, logits, ldl, E, k, ctypes.byref(w1), ctypes.byref(w3),
+                              ctypes.byref(w2), dim, hidden, sel, wts, ws, ws_bytes, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_moe_dev")
+
+
+def moe_layer(xb, E, k, w1, t1, w3, t3, w2, t2, dim, hidden, router=None, logits=None):
+    """quantr_moe_layer with host arrays.  w1/w3/w2: lists of E host arrays
+    (views into registered arrays); returns (out, sel, wts, rc)."""
+    xb = np.ascontiguousarray(xb, np.float32).reshape(-1, dim)
+    T = xb.shape[0]
+    out = np.empty((T, dim), np.float32)
+    sel = np.empty((T, k), np.int32)
+    wts = np.empty((T, k), np.float32)
+    tabs = [(ctypes.c_void_p * E)(*[m.ctypes.data for m in mats]) for mats in (w1, w3, w2)]
+    r = None if router is None else np.ascontiguousarray(router, np.float32)
+    lg = None if logits is None else np.ascontiguousarray(logits, np.float32)
+    rc = lib().quantr_moe_layer(_ptr(out), _ptr(xb), T, _ptr(r), _ptr(lg), E, k, ctypes.cast(tabs[0], _vp), t1,
+                                ctypes.cast(tabs[1], _vp), t3, ctypes.cast(tabs[2], _vp), t2, dim, hidden, _ptr(sel),
+                                _ptr(wts))
+    lib().quantr_gpu_clear_error()
+    return out, sel, wts, rc
 
 
 def device_status(stream=0, reset=True):

@@ -19,6 +19,9 @@ Cases:
   vd_*          vec_dot_{q8_0,q5K,q6K}_q8_0; vd_q4k_ref_broken records what the
                 reference's Q4_K kernel returns (not a parity target)
   mm_*          matmul_q_fused for Q8_0 / Q5_K / Q6_K / F32, incl. ragged d
+  sm_*          KernelOps softmax (src/kernels.c:191-207): router-sized vectors,
+                ties, a wide range, one element
+  mr_*          KernelOps matmul_ref (src/kernels.c:18-28), the MoE router GEMV
 """
 import os
 import sys
@@ -121,6 +124,24 @@ def main():
     G["mm_f32_w"], G["mm_f32_x"] = wf.view(np.uint8).reshape(16, -1), xf
     G["mm_f32_shape"] = np.array([0, 16, 300], np.int32)
     G["mm_f32_out"] = ref.matmul_q_fused(xf, wf, 0, 16, 300)
+
+    # KernelOps softmax / matmul_ref (reference src/kernels.c), own seed so the
+    # arrays above do not move --------------------------------------------
+    r2 = synth.rng_for(20261202)
+    sm = {
+        "e60": r2.standard_normal(60, dtype=np.float32),
+        "e128w": (r2.standard_normal(128, dtype=np.float32) * np.float32(8.0)).astype(np.float32),
+        "ties": np.full(12, 0.5, np.float32),
+        "e256": (r2.uniform(-90, 20, 256)).astype(np.float32),
+        "one": np.array([3.25], np.float32),
+    }
+    for key, v in sm.items():
+        G[f"sm_{key}_in"] = v
+        G[f"sm_{key}_out"] = ref.softmax(v)
+    wr = (r2.standard_normal((24, 300), dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    xr = r2.standard_normal(300, dtype=np.float32)
+    G["mr_w"], G["mr_x"] = wr, xr
+    G["mr_out"] = ref.matmul_f32(xr, wr, 24, 300, backend=0)
 
     np.savez_compressed(OUT, **G)
     print(f"wrote {OUT}: {os.path.getsize(OUT)} bytes, {len(G)} arrays")

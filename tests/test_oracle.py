@@ -154,3 +154,70 @@ def test_unit_partials_reconstruct_dot(orc):
             for u in range(isum.shape[1]):
                 acc = np.float32(acc + np.float32(np.float32(np.float32(isum[0, u]) * np.float32(wd[u])) * np.float32(xd[u])))
             assert bits(acc) == bits(orc.matmul_q_fused(x, w, t, 3, d)[0])
+
+
+# ---- router pieces of the MoE block (src/runtime.c:202-229) ----
+
+@pytest.mark.parametrize("key", ["e60", "e128w", "ties", "e256", "one"])
+def test_softmax_golden(golden, orc, key):
+    """qo_softmax against the reference's KernelOps softmax (src/kernels.c:191-207)."""
+    got = orc.softmax(golden[f"sm_{key}_in"])
+    np.testing.assert_array_equal(got.view(np.uint32), golden[f"sm_{key}_out"].view(np.uint32))
+
+
+def test_matmul_ref_golden(golden, orc):
+    """qo_matmul_f32 against KernelOps matmul_ref (src/kernels.c:18-28)."""
+    got = orc.matmul_f32(golden["mr_x"], golden["mr_w"], 24, 300)
+    np.testing.assert_array_equal(got.view(np.uint32), golden["mr_out"].view(np.uint32))
+
+
+def _route(probs, k):
+    """src/runtime.c:208-229 restated in Python on already-softmaxed probs."""
+    p = probs.astype(np.float32).copy()
+    sel, w = [], []
+    for _ in range(k):
+        best, arg = np.float32(-1e9), -1
+        for e in range(p.size):
+            if p[e] > best:
+                best, arg = p[e], e
+        sel.append(arg)
+        w.append(best)
+        p[arg] = np.float32(-1e9)
+    tot = np.float32(0.0)
+    for v in w:
+        tot = np.float32(tot + v)
+    return np.array(sel, np.int32), np.array([np.float32(v / tot) for v in w], np.float32)
+
+
+@pytest.mark.parametrize("key,k", [("e60", 4), ("e128w", 8), ("ties", 4), ("e256", 16), ("one", 1)])
+def test_moe_token_routing(golden, orc, key, k):
+    """qo_moe_token's routing (softmax, strict arg-max top-k, renormalisation)
+    against the reference softmax output plus a direct restatement; the expert
+    weights are zero so the FFN part only has to run."""
+    logits = golden[f"sm_{key}_in"]
+    E = logits.size
+    dim, hidden = 32, 32
+    w = np.zeros((E, hidden, 34), np.uint8)  # Q8_0 rows of zeros
+    w2 = np.zeros((E, dim, 34), np.uint8)
+    xb = np.ones(dim, np.float32)
+    out, sel, wts = orc.moe_token(xb, E, k, w, 8, hidden * 34, w, 8, hidden * 34, w2, 8, dim * 34, dim, hidden,
+                                  logits=logits)
+    want_sel, want_w = _route(golden[f"sm_{key}_out"], k)
+    np.testing.assert_array_equal(sel, want_sel)
+    np.testing.assert_array_equal(wts.view(np.uint32), want_w.view(np.uint32))
+    assert np.all(out == 0.0)
+    if key == "ties":
+        assert list(sel) == [0, 1, 2, 3]
+
+
+@pytest.mark.skipif(not oracle.ref_available("scalar"), reason="oracle/_ref not built")
+def test_live_reference_softmax_and_matmul(orc):
+    ref = oracle.RefLib("scalar")
+    rng = np.random.Generator(np.random.PCG64(77))
+    for E in (1, 7, 60, 128, 256):
+        v = (rng.standard_normal(E) * 4).astype(np.float32)
+        np.testing.assert_array_equal(orc.softmax(v).view(np.uint32), ref.softmax(v).view(np.uint32))
+    w = rng.standard_normal((60, 2048)).astype(np.float32)
+    x = rng.standard_normal(2048).astype(np.float32)
+    np.testing.assert_array_equal(orc.matmul_f32(x, w, 60, 2048).view(np.uint32),
+                                  ref.matmul_f32(x, w, 60, 2048, backend=0).view(np.uint32))
