@@ -48,9 +48,11 @@ HIDDEN, FFN, LAYERS = 896, 4864, 24
 Q4_K = 12
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one step's engine launch, from the ncu capture
-# summarised in profiles/; None until captured.
-NCU_TRAFFIC_PER_STEP = None
+# DRAM bytes (read + write) of one k_program launch of the c2 step, from the
+# ncu capture summarised in profiles/k_program_c2_full.md: 159,996,160 read +
+# 5,175,552 written (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB
+# out per step).
+NCU_TRAFFIC_PER_STEP = 165171712
 
 
 def row_bytes(t, d):

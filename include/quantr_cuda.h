@@ -214,7 +214,9 @@ typedef struct {
     uint32_t type; /* QUANTR_TYPE_Q8_0 / Q4_K / Q5_K / Q6_K */
 } quantr_expert_weights;
 
-/* Workspace bytes quantr_moe_dev needs. */
+/* Workspace bytes quantr_moe_dev needs (also enough for the three stage calls
+ * below with the same T, E, k, dim, hidden; the experts stage may pass its
+ * local expert count as E). */
 size_t quantr_moe_workspace_bytes(int T, int E, int k, int dim, int hidden);
 
 /* The reference's routed-MoE branch (src/runtime.c:202-269) for T tokens, each
@@ -236,6 +238,27 @@ int quantr_moe_dev(float* out, long long ldo, const float* xb, long long ldx, in
                    const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
                    const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden, int* sel,
                    float* wts, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The same block as three stream-ordered stages, for expert-parallel use
+ * (each rank routes every token identically, computes only its experts, and
+ * the per-pair outputs are exchanged before the combine):
+ *   route:   sel/wts (T x k) from router weights or logits, as above;
+ *   experts: for every pair p = t*k + s with sel[p] in [e0, e0 + E_local),
+ *            o[p*dim + i] = (W2.(silu(W1.xb_t) * (W3.xb_t)))_i of expert
+ *            sel[p] (w1/w3/w2 describe the E_local local experts, expert
+ *            sel[p] - e0); rows of o of other pairs are left untouched;
+ *   combine: out[t*ldo + i] = sum over s in selection order of
+ *            o[(t*k+s)*dim + i] * wts[t*k+s] from +0.0, skipping sel < 0
+ *            (src/runtime.c:241, 262-264). */
+int quantr_moe_route_dev(int* sel, float* wts, const float* xb, long long ldx, int T, const float* router,
+                         const float* logits, long long ldl, int E, int k, int dim, void* workspace,
+                         size_t workspace_bytes, void* stream);
+int quantr_moe_experts_dev(float* o, const float* xb, long long ldx, int T, const int* sel, int k, int e0, int E_local,
+                           const quantr_expert_weights* w1, const quantr_expert_weights* w3,
+                           const quantr_expert_weights* w2, int dim, int hidden, void* workspace,
+                           size_t workspace_bytes, void* stream);
+int quantr_moe_combine_dev(float* out, long long ldo, const float* o, const int* sel, const float* wts, int T, int k,
+                           int dim, void* stream);
 
 /* Host-pointer, synchronous form for the reference's runtime: w1/w3/w2 are the
  * per-layer arrays of E expert pointers (w->expert_w1[l], ..., include/types.h:

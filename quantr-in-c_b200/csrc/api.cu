@@ -638,9 +638,26 @@ int quantr_quantize_q8_0_dev(block_q8_0* y, const float* x, long long ldx, int k
 
 // ------------------------------------------------------------------- MoE --
 
+// Public MoE workspace: the stage layout, then o (P x dim), sel and wts (P each)
+// for quantr_moe_dev's internal use.
+struct MoePublicWs {
+    size_t o, sel, wts, total;
+};
+
+static MoePublicWs moe_public(int T, int E, int k, int dim, int hidden)
+{
+    const size_t P = (size_t)std::max(T, 1) * std::max(k, 1);
+    MoePublicWs w;
+    w.o = a256(moe_workspace_bytes(T, E, k, dim, hidden));
+    w.sel = w.o + a256(P * std::max(dim, 1) * 4);
+    w.wts = w.sel + a256(P * 4);
+    w.total = w.wts + a256(P * 4);
+    return w;
+}
+
 size_t quantr_moe_workspace_bytes(int T, int E, int k, int dim, int hidden)
 {
-    return moe_workspace_bytes(T, E, k, dim, hidden);
+    return moe_public(T, E, k, dim, hidden).total;
 }
 
 static bool expert_ok(const quantr_expert_weights* w)
@@ -648,20 +665,28 @@ static bool expert_ok(const quantr_expert_weights* w)
     return w && (w->base || w->table) && type_supported(w->type) && w->type != T_F32;
 }
 
-static int moe_check(const float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
-                     const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
-                     const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden)
+static int experts_check(const quantr_expert_weights* w1, const quantr_expert_weights* w3,
+                         const quantr_expert_weights* w2)
 {
-    if (T < 0 || !out || !xb || dim <= 0 || hidden <= 0 || ldx < dim || ldo < dim) return QUANTR_ERR_BAD_ARG;
-    if (E <= 0 || E > kMoeMaxExperts || k <= 0 || k > kMoeMaxK || k > E) return QUANTR_ERR_BAD_ARG;
-    if (!router && (!logits || ldl < E)) return QUANTR_ERR_BAD_ARG;
     if (!w1 || !w3 || !w2) return QUANTR_ERR_BAD_ARG;
-    if (!expert_ok(w1) || !expert_ok(w3) || !expert_ok(w2)) {
-        if ((w1->base || w1->table) && (w3->base || w3->table) && (w2->base || w2->table))
-            return QUANTR_ERR_UNSUPPORTED_TYPE;
-        return QUANTR_ERR_BAD_ARG;
-    }
+    if (!(w1->base || w1->table) || !(w3->base || w3->table) || !(w2->base || w2->table)) return QUANTR_ERR_BAD_ARG;
+    if (!expert_ok(w1) || !expert_ok(w3) || !expert_ok(w2)) return QUANTR_ERR_UNSUPPORTED_TYPE;
     return QUANTR_OK;
+}
+
+static int route_check(const float* xb, long long ldx, int T, const float* router, const float* logits,
+                       long long ldl, int E, int k, int dim)
+{
+    if (T < 0 || dim <= 0) return QUANTR_ERR_BAD_ARG;
+    if (E <= 0 || E > kMoeMaxExperts || k <= 0 || k > kMoeMaxK || k > E) return QUANTR_ERR_BAD_ARG;
+    if (router && (!xb || ldx < dim)) return QUANTR_ERR_BAD_ARG;
+    if (!router && (!logits || ldl < E)) return QUANTR_ERR_BAD_ARG;
+    return QUANTR_OK;
+}
+
+static bool ws_ok(const void* ws, size_t have, size_t need)
+{
+    return ws && have >= need && ((uintptr_t)ws & 255) == 0;
 }
 
 static ExpertMats mats_of(const quantr_expert_weights* w)
@@ -674,39 +699,143 @@ static ExpertMats mats_of(const quantr_expert_weights* w)
     return m;
 }
 
-int quantr_moe_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
-                   const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
-                   const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden, int* sel,
-                   float* wts, void* workspace, size_t workspace_bytes, void* stream)
+int quantr_moe_route_dev(int* sel, float* wts, const float* xb, long long ldx, int T, const float* router,
+                         const float* logits, long long ldl, int E, int k, int dim, void* workspace,
+                         size_t workspace_bytes, void* stream)
 {
-    int rc = moe_check(out, ldo, xb, ldx, T, router, logits, ldl, E, k, w1, w3, w2, dim, hidden);
+    int rc = route_check(xb, ldx, T, router, logits, ldl, E, k, dim);
     if (rc || T == 0) return rc;
-    if (!workspace || workspace_bytes < moe_workspace_bytes(T, E, k, dim, hidden) || ((uintptr_t)workspace & 255))
+    if (!sel || !wts) return QUANTR_ERR_BAD_ARG;
+    if (!ws_ok(workspace, workspace_bytes, moe_workspace_bytes(T, E, k, dim, 1))) return QUANTR_ERR_WORKSPACE;
+    MoeRoute r;
+    r.sel = sel;
+    r.wts = wts;
+    r.xb = xb;
+    r.ldx = ldx;
+    r.T = T;
+    r.router = router;
+    r.logits = logits;
+    r.ldl = ldl;
+    r.E = E;
+    r.k = k;
+    r.dim = dim;
+    r.ws = workspace;
+    r.ws_bytes = workspace_bytes;
+    r.err = device_error_word();
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    return code_of(launch_moe_route(r, c));
+}
+
+int quantr_moe_experts_dev(float* o, const float* xb, long long ldx, int T, const int* sel, int k, int e0, int E_local,
+                           const quantr_expert_weights* w1, const quantr_expert_weights* w3,
+                           const quantr_expert_weights* w2, int dim, int hidden, void* workspace,
+                           size_t workspace_bytes, void* stream)
+{
+    if (T < 0 || !o || !xb || !sel || dim <= 0 || hidden <= 0 || ldx < dim || k <= 0 || k > kMoeMaxK || e0 < 0 ||
+        E_local <= 0 || E_local > kMoeMaxExperts)
+        return QUANTR_ERR_BAD_ARG;
+    int rc = experts_check(w1, w3, w2);
+    if (rc || T == 0) return rc;
+    if (!ws_ok(workspace, workspace_bytes, moe_workspace_bytes(T, E_local, k, dim, hidden)))
         return QUANTR_ERR_WORKSPACE;
-    MoeArgs a;
-    a.out = out;
-    a.ldo = ldo;
+    MoeExperts a;
+    a.o = o;
     a.xb = xb;
     a.ldx = ldx;
     a.T = T;
-    a.router = router;
-    a.logits = logits;
-    a.ldl = ldl;
-    a.E = E;
+    a.sel = sel;
     a.k = k;
+    a.e0 = e0;
+    a.El = E_local;
     a.dim = dim;
     a.hidden = hidden;
     a.w1 = mats_of(w1);
     a.w3 = mats_of(w3);
     a.w2 = mats_of(w2);
-    a.sel = sel;
-    a.wts = wts;
     a.ws = workspace;
     a.ws_bytes = workspace_bytes;
     a.err = device_error_word();
     LaunchCfg c;
     c.stream = (cudaStream_t)stream;
-    return code_of(launch_moe(a, c));
+    return code_of(launch_moe_experts(a, c));
+}
+
+int quantr_moe_combine_dev(float* out, long long ldo, const float* o, const int* sel, const float* wts, int T, int k,
+                           int dim, void* stream)
+{
+    if (T < 0 || !out || !o || !sel || !wts || dim <= 0 || ldo < dim || k <= 0 || k > kMoeMaxK)
+        return QUANTR_ERR_BAD_ARG;
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    return code_of(launch_moe_combine(out, ldo, o, sel, wts, T, k, dim, c));
+}
+
+// route -> experts (all E local) -> combine; o, and sel/wts when the caller
+// passes none, live in the workspace.
+static cudaError_t moe_full(float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
+                            const float* logits, long long ldl, int E, int k, const ExpertMats& w1,
+                            const ExpertMats& w3, const ExpertMats& w2, int dim, int hidden, int* sel, float* wts,
+                            void* ws, size_t ws_bytes, int* err, const LaunchCfg& c)
+{
+    const MoePublicWs L = moe_public(T, E, k, dim, hidden);
+    uint8_t* base = static_cast<uint8_t*>(ws);
+    float* o = reinterpret_cast<float*>(base + L.o);
+    if (!sel) sel = reinterpret_cast<int*>(base + L.sel);
+    if (!wts) wts = reinterpret_cast<float*>(base + L.wts);
+    MoeRoute r;
+    r.sel = sel;
+    r.wts = wts;
+    r.xb = xb;
+    r.ldx = ldx;
+    r.T = T;
+    r.router = router;
+    r.logits = logits;
+    r.ldl = ldl;
+    r.E = E;
+    r.k = k;
+    r.dim = dim;
+    r.ws = ws;
+    r.ws_bytes = L.o;
+    r.err = err;
+    cudaError_t e = launch_moe_route(r, c);
+    MoeExperts a;
+    a.o = o;
+    a.xb = xb;
+    a.ldx = ldx;
+    a.T = T;
+    a.sel = sel;
+    a.k = k;
+    a.e0 = 0;
+    a.El = E;
+    a.dim = dim;
+    a.hidden = hidden;
+    a.w1 = w1;
+    a.w3 = w3;
+    a.w2 = w2;
+    a.ws = ws;
+    a.ws_bytes = L.o;
+    a.err = err;
+    if (e == cudaSuccess) e = launch_moe_experts(a, c);
+    if (e == cudaSuccess) e = launch_moe_combine(out, ldo, o, sel, wts, T, k, dim, c);
+    return e;
+}
+
+int quantr_moe_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
+                   const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
+                   const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden, int* sel,
+                   float* wts, void* workspace, size_t workspace_bytes, void* stream)
+{
+    int rc = route_check(xb, ldx, T, router, logits, ldl, E, k, dim);
+    if (!rc && (!out || !xb || hidden <= 0 || ldx < dim || ldo < dim)) rc = QUANTR_ERR_BAD_ARG;
+    if (!rc) rc = experts_check(w1, w3, w2);
+    if (rc || T == 0) return rc;
+    if (!ws_ok(workspace, workspace_bytes, quantr_moe_workspace_bytes(T, E, k, dim, hidden)))
+        return QUANTR_ERR_WORKSPACE;
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    return code_of(moe_full(out, ldo, xb, ldx, T, router, logits, ldl, E, k, mats_of(w1), mats_of(w3), mats_of(w2),
+                            dim, hidden, sel, wts, workspace, workspace_bytes, device_error_word(), c));
 }
 
 // Resolves an array of E host expert pointers to device memory: a uniform
@@ -742,11 +871,13 @@ int quantr_moe_layer(float* out, const float* xb, int T, const float* router, co
         return rc;
     };
     if (T == 0) return QUANTR_OK;
-    // Validate shapes and types with stand-in (non-null) expert descriptors.
-    const quantr_expert_weights v1{(const void*)1, 0, nullptr, t1}, v3{(const void*)1, 0, nullptr, t3},
-        v2{(const void*)1, 0, nullptr, t2};
-    int rc = moe_check(out, dim, xb, dim, T, router, logits, E, E, k, &v1, &v3, &v2, dim, hidden);
-    if (!rc && (!w1 || !w3 || !w2)) rc = QUANTR_ERR_BAD_ARG;
+    int rc = route_check(xb, dim, T, router, logits, E, E, k, dim);
+    if (!rc && (!out || !xb || hidden <= 0 || !w1 || !w3 || !w2)) rc = QUANTR_ERR_BAD_ARG;
+    if (!rc) {
+        const quantr_expert_weights v1{(const void*)1, 0, nullptr, t1}, v3{(const void*)1, 0, nullptr, t3},
+            v2{(const void*)1, 0, nullptr, t2};
+        rc = experts_check(&v1, &v3, &v2);
+    }
     if (rc) return fail(rc);
     if ((rc = ensure_ready())) return fail(rc);
 
@@ -776,7 +907,7 @@ int quantr_moe_layer(float* out, const float* xb, int T, const float* router, co
     const size_t r_off = in_end, d_total = in_end + (router && !rdev ? a256(rbytes) : 0);
     if ((rc = grow_host(h_total))) return fail(rc);
     if ((rc = grow_dev((void**)&g.dbuf, &g.dbuf_bytes, d_total))) return fail(rc);
-    const size_t wsb = moe_workspace_bytes(T, E, k, dim, hidden);
+    const size_t wsb = quantr_moe_workspace_bytes(T, E, k, dim, hidden);
     if ((rc = grow_dev(&g.ws, &g.ws_bytes, wsb))) return fail(rc);
 
     std::memcpy(g.hbuf + x_off, xb, xbytes);
@@ -791,30 +922,13 @@ int quantr_moe_layer(float* out, const float* xb, int T, const float* router, co
         e = cudaMemcpyAsync(g.dbuf + r_off, router, rbytes, cudaMemcpyHostToDevice, g.stream);
         rdev = g.dbuf + r_off;
     }
-    MoeArgs a;
-    a.out = (float*)(g.hbuf_dev + o_off);
-    a.ldo = dim;
-    a.xb = (const float*)(g.dbuf + x_off);
-    a.ldx = dim;
-    a.T = T;
-    a.router = router ? (const float*)rdev : nullptr;
-    a.logits = router ? nullptr : (const float*)(g.dbuf + l_off);
-    a.ldl = E;
-    a.E = E;
-    a.k = k;
-    a.dim = dim;
-    a.hidden = hidden;
-    a.w1 = mats_of(&w[0]);
-    a.w3 = mats_of(&w[1]);
-    a.w2 = mats_of(&w[2]);
-    a.sel = (int*)(g.hbuf_dev + s_off);
-    a.wts = (float*)(g.hbuf_dev + w_off);
-    a.ws = g.ws;
-    a.ws_bytes = g.ws_bytes;
-    a.err = (int*)(g.hbuf_dev + e_off);
     LaunchCfg c;
     c.stream = g.stream;
-    if (e == cudaSuccess) e = launch_moe(a, c);
+    if (e == cudaSuccess)
+        e = moe_full((float*)(g.hbuf_dev + o_off), dim, (const float*)(g.dbuf + x_off), dim, T,
+                     router ? (const float*)rdev : nullptr, router ? nullptr : (const float*)(g.dbuf + l_off), E, E,
+                     k, mats_of(&w[0]), mats_of(&w[1]), mats_of(&w[2]), dim, hidden, (int*)(g.hbuf_dev + s_off),
+                     (float*)(g.hbuf_dev + w_off), g.ws, g.ws_bytes, (int*)(g.hbuf_dev + e_off), c);
     if (e == cudaSuccess) e = cudaStreamSynchronize(g.stream);
     if (e != cudaSuccess) {
         cudaGetLastError();

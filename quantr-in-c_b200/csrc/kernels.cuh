@@ -98,25 +98,49 @@ struct ExpertMats {
     uint32_t type = 0;
 };
 
-struct MoeArgs {
-    float* out = nullptr;  // T x dim, out[t*ldo + i]
-    long long ldo = 0;
-    const float* xb = nullptr;  // T x dim
+// Routing for T tokens: logits = router.xb (F32, matmul_ref order) or the
+// given logits; softmax, strict arg-max top-k, renormalisation -> sel/wts
+// (T x k; a token with non-finite probabilities gets sel = -1, wts = 0 and the
+// error word DEV_ERR_ROUTING).
+struct MoeRoute {
+    int* sel = nullptr;
+    float* wts = nullptr;
+    const float* xb = nullptr;
     long long ldx = 0;
     int T = 0;
-    const float* router = nullptr;  // E x dim F32 router weights, or null
-    const float* logits = nullptr;  // T x E router logits when router is null
+    const float* router = nullptr;
+    const float* logits = nullptr;
     long long ldl = 0;
-    int E = 0, k = 0, dim = 0, hidden = 0;
-    ExpertMats w1, w3, w2;  // w1/w3: hidden x dim, w2: dim x hidden
-    int* sel = nullptr;     // optional T x k selected experts
-    float* wts = nullptr;   // optional T x k renormalised weights
+    int E = 0, k = 0, dim = 0;
     void* ws = nullptr;
     size_t ws_bytes = 0;
     int* err = nullptr;
 };
 
+// Expert FFNs of the pairs p = t*k + s with sel[p] in [e0, e0 + El):
+// o[p*dim + i] = (W2_e . (silu(W1_e.xb_t) * (W3_e.xb_t)))_i for local expert
+// e = sel[p] - e0.  Rows of o for other pairs are not written.
+struct MoeExperts {
+    float* o = nullptr;  // (T*k) x dim
+    const float* xb = nullptr;
+    long long ldx = 0;
+    int T = 0;
+    const int* sel = nullptr;
+    int k = 0, e0 = 0, El = 0, dim = 0, hidden = 0;
+    ExpertMats w1, w3, w2;  // local experts 0..El-1; w1/w3 hidden x dim, w2 dim x hidden
+    void* ws = nullptr;
+    size_t ws_bytes = 0;
+    int* err = nullptr;
+};
+
+// Workspace bytes for T tokens, E experts (route: E = all experts; experts
+// stage: E = local experts; the full-E figure covers both).
 size_t moe_workspace_bytes(int T, int E, int k, int dim, int hidden);
-cudaError_t launch_moe(const MoeArgs& a, const LaunchCfg& c);
+cudaError_t launch_moe_route(const MoeRoute& r, const LaunchCfg& c);
+cudaError_t launch_moe_experts(const MoeExperts& a, const LaunchCfg& c);
+// out[t*ldo + i] = sum over s in order of o[(t*k+s)*dim + i] * wts[t*k+s]
+// from +0.0, skipping slots with sel < 0 (src/runtime.c:241, 262-264).
+cudaError_t launch_moe_combine(float* out, long long ldo, const float* o, const int* sel, const float* wts, int T,
+                               int k, int dim, const LaunchCfg& c);
 
 } // namespace qr

@@ -10,18 +10,19 @@
 //   hb = W1.xb, hb2 = W3.xb, hb = silu(hb)*hb2, o = W2.hb, xb2 += o*ew
 //   (W1 is the tensor the reference binds to ffn_up, src/model.c:401-418).
 //
-// Device plan (all launches stream-ordered, programmatic dependent launch):
-//   1. quantize xb once (the reference quantizes the same xb for every W1/W3
-//      call, src/quant.c:466-474, so one quantization is bit-identical);
-//   2. [router logits: F32 GEMV, one thread per (expert, token)];
-//   3. one CTA routes every token and groups the (token, slot) pairs by
-//      expert (a stable order: pair id ascending within each expert);
-//   4. grouped GEMVs: CTA (row tile, expert) streams its expert's rows once
-//      and serves every pair routed to that expert; experts nobody chose are
-//      never read;
-//   5. silu(h1)*h3 fused with the Q8_0 quantization of hb per pair;
-//   6. grouped GEMV for W2;
-//   7. combine: out = sum over slots in selection order of o*ew, from +0.0.
+// Three stages (all launches stream-ordered, programmatic dependent launch),
+// so that expert-parallel ranks can run the middle one on their own experts:
+//   route:   [router logits: F32 GEMV, one thread per (expert, token)], then
+//            one thread per token: softmax, top-k, renormalisation;
+//   experts: one CTA groups the (token, slot) pairs whose expert is local, by
+//            expert (pair id ascending within each expert); xb is quantized
+//            once (the reference quantizes the same xb for every W1/W3 call,
+//            src/quant.c:466-474, so one quantization is bit-identical);
+//            grouped GEMVs: CTA (row tile, expert) streams its expert's rows
+//            once and serves every pair routed to that expert (experts nobody
+//            chose are never read); silu(h1)*h3 fused with the Q8_0
+//            quantization of hb per pair; grouped GEMV for W2 -> o per pair;
+//   combine: out = sum over slots in selection order of o*ew, from +0.0.
 // Every GEMV output is bit-identical to the reference's matmul_q_fused for
 // that (row, pair).  expf is evaluated correctly rounded (through double
 // precision), which differs from glibc's expf in rare last-bit cases.
@@ -49,100 +50,101 @@ __device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_
 
 // ------------------------------------------------------- route and group --
 
-// One CTA.  Thread t routes token t (looping for T > blockDim.x), working on
-// its row of `probs` (T x E in the workspace; logits may alias it); then warps
-// count and list the pairs p = t*k + s per expert with ballots.
+// Thread t routes token t, working on its row of `probs` (T x E in the
+// workspace; logits may alias it).
+__global__ void __launch_bounds__(128)
+    k_moe_route(const float* logits, long long ldl, float* probs, int T, int E, int k, int* __restrict__ sel,
+                float* __restrict__ wts, int* err)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    float* p = probs + (long long)t * E;
+    const float* lg = logits + (long long)t * ldl;
+    // softmax_ref (src/kernels.c:191-207)
+    float m = lg[0];
+    for (int e = 1; e < E; ++e)
+        if (lg[e] > m) m = lg[e];
+    float sum = 0.0f;
+    for (int e = 0; e < E; ++e) {
+        const float v = expf_cr(__fsub_rn(lg[e], m));
+        p[e] = v;
+        sum = __fadd_rn(sum, v);
+    }
+    const float inv = __fdiv_rn(1.0f, sum);
+    for (int e = 0; e < E; ++e) p[e] = __fmul_rn(p[e], inv);
+    // top-k (src/runtime.c:208-221)
+    float w[kMoeMaxK];
+    int s_[kMoeMaxK];
+    bool bad = false;
+    for (int s = 0; s < k; ++s) {
+        float best = -1e9f;
+        int arg = -1;
+        for (int e = 0; e < E; ++e) {
+            const float v = p[e];
+            if (v > best) {
+                best = v;
+                arg = e;
+            }
+        }
+        if (arg < 0) {  // non-finite probabilities: the reference would index [-1]
+            bad = true;
+            break;
+        }
+        s_[s] = arg;
+        w[s] = best;
+        p[arg] = -1e9f;
+    }
+    // renormalisation (src/runtime.c:223-229)
+    float tot = 0.0f;
+    if (!bad)
+        for (int s = 0; s < k; ++s) tot = __fadd_rn(tot, w[s]);
+    for (int s = 0; s < k; ++s) {
+        sel[t * k + s] = bad ? -1 : s_[s];
+        wts[t * k + s] = bad ? 0.0f : __fdiv_rn(w[s], tot);
+    }
+    if (bad && err) atomicExch(err, DEV_ERR_ROUTING);
+}
+
+// One CTA: lists the pairs p = t*k + s whose expert lies in [e0, e0 + El),
+// per local expert in pair order (warp ballots), with counts and offsets.
 __global__ void __launch_bounds__(1024)
-    k_moe_route_group(const float* logits, long long ldl, float* probs, int T, int E, int k, int* __restrict__ sel,
-                      float* __restrict__ wts, int* __restrict__ sel_out, float* __restrict__ wts_out,
-                      int* __restrict__ counts, int* __restrict__ offsets, int* __restrict__ list, int* err)
+    k_moe_group(const int* __restrict__ sel, int P, int e0, int El, int* __restrict__ counts,
+                int* __restrict__ offsets, int* __restrict__ list)
 {
     __shared__ int cnt[kMoeMaxExperts];
     __shared__ int off[kMoeMaxExperts + 1];
     pdl_trigger();
     pdl_wait();
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        float* p = probs + (long long)t * E;
-        const float* lg = logits + (long long)t * ldl;
-        // softmax_ref (src/kernels.c:191-207)
-        float m = lg[0];
-        for (int e = 1; e < E; ++e)
-            if (lg[e] > m) m = lg[e];
-        float sum = 0.0f;
-        for (int e = 0; e < E; ++e) {
-            const float v = expf_cr(__fsub_rn(lg[e], m));
-            p[e] = v;
-            sum = __fadd_rn(sum, v);
-        }
-        const float inv = __fdiv_rn(1.0f, sum);
-        for (int e = 0; e < E; ++e) p[e] = __fmul_rn(p[e], inv);
-        // top-k (src/runtime.c:208-221)
-        float w[kMoeMaxK];
-        int s_[kMoeMaxK];
-        bool bad = false;
-        for (int s = 0; s < k; ++s) {
-            float best = -1e9f;
-            int arg = -1;
-            for (int e = 0; e < E; ++e) {
-                const float v = p[e];
-                if (v > best) {
-                    best = v;
-                    arg = e;
-                }
-            }
-            if (arg < 0) {  // non-finite probabilities: the reference would index [-1]
-                bad = true;
-                break;
-            }
-            s_[s] = arg;
-            w[s] = best;
-            p[arg] = -1e9f;
-        }
-        // renormalisation (src/runtime.c:223-229)
-        float tot = 0.0f;
-        if (!bad)
-            for (int s = 0; s < k; ++s) tot = __fadd_rn(tot, w[s]);
-        for (int s = 0; s < k; ++s) {
-            const int se = bad ? -1 : s_[s];
-            const float we = bad ? 0.0f : __fdiv_rn(w[s], tot);
-            sel[t * k + s] = se;
-            wts[t * k + s] = we;
-            if (sel_out) sel_out[t * k + s] = se;
-            if (wts_out) wts_out[t * k + s] = we;
-        }
-        if (bad && err) atomicExch(err, DEV_ERR_ROUTING);
-    }
-    __syncthreads();  // sel[] (global) is visible to the whole CTA from here
-
-    const int P = T * k;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    for (int e = warp; e < E; e += nw) {
+    for (int e = warp; e < El; e += nw) {
         int c = 0;
         for (int p0 = 0; p0 < P; p0 += 32) {
             const int q = p0 + lane;
-            c += __popc(__ballot_sync(0xffffffffu, q < P && sel[q] == e));
+            c += __popc(__ballot_sync(0xffffffffu, q < P && sel[q] == e0 + e));
         }
         if (lane == 0) cnt[e] = c;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         int a = 0;
-        for (int e = 0; e < E; ++e) {
+        for (int e = 0; e < El; ++e) {
             off[e] = a;
             a += cnt[e];
         }
-        off[E] = a;
+        off[El] = a;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e <= E; e += blockDim.x) {
+    for (int e = threadIdx.x; e <= El; e += blockDim.x) {
         offsets[e] = off[e];
-        if (e < E) counts[e] = cnt[e];
+        if (e < El) counts[e] = cnt[e];
     }
-    for (int e = warp; e < E; e += nw) {
+    for (int e = warp; e < El; e += nw) {
         int o = off[e];
         for (int p0 = 0; p0 < P; p0 += 32) {
             const int q = p0 + lane;
-            const bool hit = q < P && sel[q] == e;
+            const bool hit = q < P && sel[q] == e0 + e;
             const unsigned mk = __ballot_sync(0xffffffffu, hit);
             if (hit) list[o + __popc(mk & ((1u << lane) - 1u))] = q;
             o += __popc(mk);
@@ -277,7 +279,8 @@ __global__ void __launch_bounds__(kThreads) k_moe_gemv(const __grid_constant__ M
 // same step (the reference's matmul_q on W2 quantizes hb, src/quant.c:466-474).
 __global__ void __launch_bounds__(kThreads)
     k_moe_act(const float* __restrict__ h1, const float* __restrict__ h3, int hidden, int P,
-              const int* __restrict__ sel, int8_t* __restrict__ q, float* __restrict__ dq, int32_t* __restrict__ sq)
+              const int* __restrict__ sel, int e0, int El, int8_t* __restrict__ q, float* __restrict__ dq,
+              int32_t* __restrict__ sq)
 {
     pdl_trigger();
     pdl_wait();
@@ -288,7 +291,8 @@ __global__ void __launch_bounds__(kThreads)
     for (long long wb = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); wb < total; wb += step) {
         const int pr = (int)(wb / nbh);
         const int b = (int)(wb - (long long)pr * nbh);
-        if (sel[pr] < 0) continue;  // warp-uniform
+        const int se = sel[pr];
+        if (se < e0 || se >= e0 + El) continue;  // not a local pair (warp-uniform)
         const long long i = (long long)pr * hidden + b * 32 + lane;
         const float v = __fmul_rn(silu_ref(h1[i]), h3[i]);
         uint32_t h;
@@ -325,10 +329,27 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// Rows of o for local pairs when W2 has fewer columns than one block (the
+// reference's empty sum, 0.0f).
+__global__ void __launch_bounds__(kThreads)
+    k_moe_zero_rows(float* __restrict__ o, int dim, int P, const int* __restrict__ sel, int e0, int El)
+{
+    pdl_trigger();
+    pdl_wait();
+    const long long total = (long long)P * dim;
+    for (long long idx = (long long)blockIdx.x * kThreads + threadIdx.x; idx < total;
+         idx += (long long)gridDim.x * kThreads) {
+        const int se = sel[idx / dim];
+        if (se >= e0 && se < e0 + El) o[idx] = 0.0f;
+    }
+}
+
 // ------------------------------------------------------------- host side --
 
+// Workspace: probs (route) | counts | offsets | list | xb quants | h1 | h3 |
+// hb quants (experts).  One layout serves every stage.
 struct MoeWs {
-    size_t logits, sel, wts, counts, offsets, list, actx, h1, h3, acth, o, total;
+    size_t probs, counts, offsets, list, actx, h1, h3, acth, total;
 };
 
 size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -343,9 +364,7 @@ MoeWs moe_layout(int T, int E, int k, int dim, int hidden)
         off += a256(bytes);
         return at;
     };
-    w.logits = take((size_t)T * E * 4);
-    w.sel = take(P * 4);
-    w.wts = take(P * 4);
+    w.probs = take((size_t)T * E * 4);
     w.counts = take((size_t)E * 4);
     w.offsets = take((size_t)(E + 1) * 4);
     w.list = take(P * 4);
@@ -353,7 +372,6 @@ MoeWs moe_layout(int T, int E, int k, int dim, int hidden)
     w.h1 = take(P * hidden * 4);
     w.h3 = take(P * hidden * 4);
     w.acth = take(actq_bytes(hidden, (int)P));
-    w.o = take(P * dim * 4);
     w.total = off;
     return w;
 }
@@ -441,15 +459,32 @@ size_t moe_workspace_bytes(int T, int E, int k, int dim, int hidden)
     return moe_layout(std::max(T, 1), std::max(E, 1), std::max(k, 1), std::max(dim, 1), std::max(hidden, 1)).total;
 }
 
-cudaError_t launch_moe(const MoeArgs& a, const LaunchCfg& c)
+cudaError_t launch_moe_route(const MoeRoute& r, const LaunchCfg& c)
 {
-    if (a.T <= 0) return cudaSuccess;
-    const MoeWs L = moe_layout(a.T, a.E, a.k, a.dim, a.hidden);
+    if (r.T <= 0) return cudaSuccess;
+    const MoeWs L = moe_layout(r.T, r.E, r.k, r.dim, 1);
+    if (r.ws_bytes < L.probs + (size_t)r.T * r.E * 4) return cudaErrorInvalidValue;
+    float* probs = reinterpret_cast<float*>(static_cast<uint8_t*>(r.ws) + L.probs);
+    const float* lg = r.logits;
+    long long ldl = r.ldl;
+    cudaError_t e = cudaSuccess;
+    if (r.router) {
+        e = launch_gemv_f32(r.router, r.xb, r.ldx, probs, r.E, r.E, r.dim, r.T, c);
+        lg = probs;
+        ldl = r.E;
+    }
+    if (e == cudaSuccess)
+        e = launch_ex(&k_moe_route, dim3((r.T + 127) / 128), dim3(128), 0, c, lg, ldl, probs, r.T, r.E, r.k, r.sel,
+                      r.wts, r.err);
+    return e;
+}
+
+cudaError_t launch_moe_experts(const MoeExperts& a, const LaunchCfg& c)
+{
+    if (a.T <= 0 || a.El <= 0) return cudaSuccess;
+    const MoeWs L = moe_layout(a.T, a.El, a.k, a.dim, a.hidden);
     if (a.ws_bytes < L.total) return cudaErrorInvalidValue;
     uint8_t* ws = static_cast<uint8_t*>(a.ws);
-    float* logits = reinterpret_cast<float*>(ws + L.logits);
-    int* sel = reinterpret_cast<int*>(ws + L.sel);
-    float* wts = reinterpret_cast<float*>(ws + L.wts);
     int* counts = reinterpret_cast<int*>(ws + L.counts);
     int* offsets = reinterpret_cast<int*>(ws + L.offsets);
     int* list = reinterpret_cast<int*>(ws + L.list);
@@ -458,24 +493,14 @@ cudaError_t launch_moe(const MoeArgs& a, const LaunchCfg& c)
     float* h3 = reinterpret_cast<float*>(ws + L.h3);
     const int P = a.T * a.k;
     ActQ ah = actq_carve(ws + L.acth, a.hidden, P);
-    float* o = reinterpret_cast<float*>(ws + L.o);
 
-    cudaError_t e = launch_quantize(a.xb, a.ldx, a.dim, a.T, ax, nullptr, nullptr, c);
-    const float* lg = a.logits;
-    long long ldl = a.ldl;
-    if (e == cudaSuccess && a.router) {
-        e = launch_gemv_f32(a.router, a.xb, a.ldx, logits, a.E, a.E, a.dim, a.T, c);
-        lg = logits;
-        ldl = a.E;
-    }
-    if (e == cudaSuccess)
-        e = launch_ex(&k_moe_route_group, dim3(1), dim3(1024), 0, c, lg, ldl, logits, a.T, a.E, a.k, sel, wts,
-                      a.sel, a.wts, counts, offsets, list, a.err);
+    cudaError_t e = launch_ex(&k_moe_group, dim3(1), dim3(1024), 0, c, a.sel, P, a.e0, a.El, counts, offsets, list);
+    if (e == cudaSuccess) e = launch_quantize(a.xb, a.ldx, a.dim, a.T, ax, nullptr, nullptr, c);
     if (e != cudaSuccess) return e;
 
     auto grouped = [&](const ExpertMats* m, int nmat, float* const* outs, int n, int d, ActQ x, int in_div,
                        size_t zero_bytes) -> cudaError_t {
-        cudaError_t r = launch_grouped_rt(m[0].type, m, nmat, outs, n, d, x, in_div, counts, offsets, list, a.E,
+        cudaError_t r = launch_grouped_rt(m[0].type, m, nmat, outs, n, d, x, in_div, counts, offsets, list, a.El,
                                           a.err, c);
         if (r != cudaErrorNotSupported) return r;
         for (int z = 0; z < nmat; ++z) {
@@ -498,15 +523,26 @@ cudaError_t launch_moe(const MoeArgs& a, const LaunchCfg& c)
     }
     if (e == cudaSuccess && a.hidden / 32 > 0)
         e = launch_ex(&k_moe_act, dim3(grid_for((long long)P * (a.hidden / 32), kThreads / 32)), dim3(kThreads), 0,
-                      c, (const float*)h1, (const float*)h3, a.hidden, P, (const int*)sel, ah.q, ah.d, ah.s);
+                      c, (const float*)h1, (const float*)h3, a.hidden, P, a.sel, a.e0, a.El, ah.q, ah.d, ah.s);
     if (e == cudaSuccess) {
-        float* const oo[1] = {o};
-        e = grouped(&a.w2, 1, oo, a.dim, a.hidden, ah, 1, (size_t)P * a.dim * 4);
+        if (row_bytes(a.w2.type, a.hidden) == 0) {
+            // Empty W2 sums: zero only the local pairs' rows.
+            e = launch_ex(&k_moe_zero_rows, dim3(grid_for((long long)P * a.dim, kThreads)), dim3(kThreads), 0, c,
+                          a.o, a.dim, P, a.sel, a.e0, a.El);
+        } else {
+            float* const oo[1] = {a.o};
+            e = grouped(&a.w2, 1, oo, a.dim, a.hidden, ah, 1, 0);
+        }
     }
-    if (e == cudaSuccess)
-        e = launch_ex(&k_moe_combine, dim3(grid_for((long long)a.T * a.dim, kThreads)), dim3(kThreads), 0, c,
-                      (const float*)o, a.dim, a.T, a.k, (const int*)sel, (const float*)wts, a.out, a.ldo);
     return e;
+}
+
+cudaError_t launch_moe_combine(float* out, long long ldo, const float* o, const int* sel, const float* wts, int T,
+                               int k, int dim, const LaunchCfg& c)
+{
+    if (T <= 0 || dim <= 0) return cudaSuccess;
+    return launch_ex(&k_moe_combine, dim3(grid_for((long long)T * dim, kThreads)), dim3(kThreads), 0, c, o, dim, T,
+                     k, sel, wts, out, ldo);
 }
 
 } // namespace qr

@@ -60,6 +60,9 @@ SIGNATURES = {
     "quantr_moe_workspace_bytes": (_sz, [_i, _i, _i, _i, _i]),
     "quantr_moe_dev": (_i, [_vp, _ll, _vp, _ll, _i, _vp, _vp, _ll, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _vp, _vp,
                             _sz, _vp]),
+    "quantr_moe_route_dev": (_i, [_vp, _vp, _vp, _ll, _i, _vp, _vp, _ll, _i, _i, _i, _vp, _sz, _vp]),
+    "quantr_moe_experts_dev": (_i, [_vp, _vp, _ll, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
+    "quantr_moe_combine_dev": (_i, [_vp, _ll, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "quantr_moe_layer": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _vp, _u32, _vp, _u32, _vp, _u32, _i, _i, _vp, _vp]),
 }
 
@@ -275,6 +278,26 @@ def moe_dev(out, ldo, xb, ldx, T, E, k, w1, w3, w2, dim, hidden, ws, ws_bytes, r
                               ctypes.byref(w2), dim, hidden, sel, wts, ws, ws_bytes, stream or None)
     if rc:
         raise QuantrError(rc, "quantr_moe_dev")
+
+
+def moe_route_dev(sel, wts, xb, ldx, T, E, k, dim, ws, ws_bytes, router=None, logits=None, ldl=0, stream=0):
+    rc = lib().quantr_moe_route_dev(sel, wts, xb, ldx, T, router, logits, ldl, E, k, dim, ws, ws_bytes,
+                                    stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_moe_route_dev")
+
+
+def moe_experts_dev(o, xb, ldx, T, sel, k, e0, E_local, w1, w3, w2, dim, hidden, ws, ws_bytes, stream=0):
+    rc = lib().quantr_moe_experts_dev(o, xb, ldx, T, sel, k, e0, E_local, ctypes.byref(w1), ctypes.byref(w3),
+                                      ctypes.byref(w2), dim, hidden, ws, ws_bytes, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_moe_experts_dev")
+
+
+def moe_combine_dev(out, ldo, o, sel, wts, T, k, dim, stream=0):
+    rc = lib().quantr_moe_combine_dev(out, ldo, o, sel, wts, T, k, dim, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_moe_combine_dev")
 
 
 def moe_layer(xb, E, k, w1, t1, w3, t3, w2, t2, dim, hidden, router=None, logits=None):
