@@ -254,3 +254,40 @@ def test_moe_layer_host_api(qr_gpu, orc):
     o, s, w, rc = qr_gpu.moe_layer(c["xb"], 6, 2, list(mats[0]), Q5_K, list(mats[1]), Q5_K, list(mats[2]), Q6_K,
                                    512, 256, router=c["router"])
     assert rc == 10 and np.all(o == 0.0)
+
+
+def test_moe_stages_emulate_expert_parallel(qr_gpu, orc):
+    """route once, run the experts stage on two disjoint expert ranges into
+    zeroed buffers (what two expert-parallel ranks compute), add them (each row
+    has one non-zero contributor, so the sum is exact), combine: bit-identical
+    to quantr_moe_dev."""
+    c = make_case(13, T=9, E=10, k=3, dim=512, hidden=256, t1=Q5_K, t3=Q5_K, t2=Q6_K)
+    full = run_dev(qr_gpu, c)
+    T, E, k, dim, hidden = 9, 10, 3, 512, 256
+    s = torch.cuda.current_stream().cuda_stream
+    xb = _dev(c["xb"])
+    lg = _dev(c["logits"])
+    ws_bytes = qr_gpu.moe_workspace_bytes(T, E, k, dim, hidden)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    sel = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    wts = torch.empty(T, k, device="cuda")
+    qr_gpu.moe_route_dev(sel.data_ptr(), wts.data_ptr(), xb.data_ptr(), dim, T, E, k, dim, ws.data_ptr(), ws_bytes,
+                         logits=lg.data_ptr(), ldl=E, stream=s)
+    parts = []
+    for e0, e1 in ((0, 4), (4, 10)):
+        o = torch.zeros(T * k, dim, device="cuda")
+        ws_i = torch.empty(qr_gpu.moe_workspace_bytes(T, e1 - e0, k, dim, hidden), dtype=torch.uint8, device="cuda")
+        ew = []
+        for key in ("w1", "w3", "w2"):
+            ex = c[key]
+            ew.append(qr_gpu.ExpertWeights(ex.dev.data_ptr() + e0 * ex.stride, ex.stride, None, ex.type))
+        qr_gpu.moe_experts_dev(o.data_ptr(), xb.data_ptr(), dim, T, sel.data_ptr(), k, e0, e1 - e0, *ew, dim, hidden,
+                               ws_i.data_ptr(), ws_i.numel(), stream=s)
+        parts.append(o)
+    o = parts[0] + parts[1]
+    out = torch.empty(T, dim, device="cuda")
+    qr_gpu.moe_combine_dev(out.data_ptr(), dim, o.data_ptr(), sel.data_ptr(), wts.data_ptr(), T, k, dim, stream=s)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(sel.cpu().numpy(), full[1])
+    np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), full[2].view(np.uint32))
+    np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), full[0].view(np.uint32))
