@@ -17,7 +17,7 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libquantr_cuda.so")
-SOURCES = ["gemv.cu", "engine.cu", "moe.cu", "api.cu", "noalloc.cu"]
+SOURCES = ["gemv.cu", "engine.cu", "tc.cu", "moe.cu", "api.cu", "noalloc.cu"]
 HEADERS = ["formats.cuh", "kernels.cuh", "device_common.cuh", "quant_decode.cuh", "launch_util.cuh"]
 
 NVCC_FLAGS = [

@@ -776,11 +776,20 @@ size_t engine_act_bytes(uint32_t type, int d, int B) { return eng::act_bytes_for
 
 // ----------------------------------------------------------- program API --
 
+// Jobs with B >= kTcMinB tokens (up to kTcMaxB) run on the tensor-core kernel
+// (tc.cu), the others on the dp4a engine above.
+#ifndef QR_TC_MIN_B
+#define QR_TC_MIN_B 9
+#endif
+constexpr int kTcMinB = QR_TC_MIN_B;
+
 struct quantr_program {
     int device;
+    bool has_engine = false;
     qr::eng::Plan plan;  // sub-plans own their device job tables
     qr::eng::QTask* d_tasks = nullptr;
     uint8_t* d_act = nullptr;
+    std::vector<qr::TcPlan*> tc;  // tensor-core launches (<= kTcMaxJobs jobs each)
 };
 
 extern "C" {
@@ -790,10 +799,17 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     using namespace qr;
     if (!out || !jobs || njobs <= 0) return QUANTR_ERR_BAD_ARG;
     *out = nullptr;
-    std::vector<eng::JobIn> in((size_t)njobs);
-    for (int j = 0; j < njobs; ++j)
-        in[j] = eng::JobIn{static_cast<const uint8_t*>(jobs[j].w), jobs[j].type, jobs[j].n, jobs[j].d, jobs[j].B,
-                           jobs[j].x, jobs[j].ldx, jobs[j].out, jobs[j].ldo};
+    std::vector<eng::JobIn> in;
+    std::vector<GemvJobIn> tcj;
+    for (int j = 0; j < njobs; ++j) {
+        const quantr_gemv_job& J = jobs[j];
+        if (J.B >= kTcMinB && J.B <= kTcMaxB && J.type != T_F32)
+            tcj.push_back(GemvJobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out,
+                                    J.ldo});
+        else
+            in.push_back(eng::JobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out,
+                                    J.ldo});
+    }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         cudaGetLastError();
@@ -801,17 +817,31 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     }
     const int sms = device_sm_count();
     eng::Plan sizing;
-    int rc = eng::make_plan(in.data(), njobs, nullptr, sms, true, sizing);
+    int rc = in.empty() ? QUANTR_OK : eng::make_plan(in.data(), (int)in.size(), nullptr, sms, true, sizing);
     if (rc) return rc;
     quantr_program* p = new (std::nothrow) quantr_program();
     if (!p) return QUANTR_ERR_OOM;
     p->device = dev;
+    p->has_engine = !in.empty();
+    for (size_t j0 = 0; j0 < tcj.size(); j0 += kTcMaxJobs) {
+        TcPlan* tp = nullptr;
+        rc = tc_plan_create(tcj.data() + j0, (int)std::min<size_t>(kTcMaxJobs, tcj.size() - j0), &tp);
+        if (rc) {
+            quantr_program_destroy(p);
+            return rc;
+        }
+        p->tc.push_back(tp);
+    }
+    if (!p->has_engine) {
+        *out = p;
+        return QUANTR_OK;
+    }
     if (cudaMalloc((void**)&p->d_act, std::max<size_t>(sizing.act_total, 256)) != cudaSuccess) {
         cudaGetLastError();
         delete p;
         return QUANTR_ERR_OOM;
     }
-    rc = eng::make_plan(in.data(), njobs, p->d_act, sms, true, p->plan);
+    rc = eng::make_plan(in.data(), (int)in.size(), p->d_act, sms, true, p->plan);
     cudaError_t e = cudaSuccess;
     if (!rc) {
         e = cudaMalloc((void**)&p->d_tasks, p->plan.tasks.size() * sizeof(eng::QTask));
@@ -844,8 +874,11 @@ int quantr_program_run(quantr_program* p, void* stream)
     int dev = -1;
     cudaGetDevice(&dev);
     if (dev != p->device) return QUANTR_ERR_BAD_ARG;
-    cudaError_t e = qr::eng::launch_plan(p->plan, p->d_tasks, qr::device_error_word(),
-                                         static_cast<cudaStream_t>(stream));
+    int* err = qr::device_error_word();
+    cudaError_t e = cudaSuccess;
+    if (p->has_engine) e = qr::eng::launch_plan(p->plan, p->d_tasks, err, static_cast<cudaStream_t>(stream));
+    for (auto* tp : p->tc)
+        if (e == cudaSuccess) e = qr::tc_plan_run(tp, err, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {
         cudaGetLastError();
         return QUANTR_ERR_CUDA;
@@ -863,6 +896,7 @@ void quantr_program_destroy(quantr_program* p)
     for (auto& sp : p->plan.subs) cudaFree(sp.d_jobs);
     cudaFree(p->d_tasks);
     cudaFree(p->d_act);
+    for (auto* tp : p->tc) qr::tc_plan_destroy(tp);
     if (prev >= 0) cudaSetDevice(prev);
     delete p;
 }
@@ -876,6 +910,13 @@ int quantr_program_info(const quantr_program* p, int* items, int* grid, int* sme
         it += sp.pp.total_items;
         g = std::max(g, sp.grid);
         sm = std::max(sm, sp.smem);
+    }
+    for (auto* tp : p->tc) {
+        int ti = 0, tg = 0, ts = 0;
+        qr::tc_plan_info(tp, &ti, &tg, &ts);
+        it += ti;
+        g = std::max(g, tg);
+        sm = std::max(sm, (size_t)ts);
     }
     if (items) *items = it;
     if (grid) *grid = g;

@@ -82,6 +82,31 @@ cudaError_t launch_gemv_engine(const uint8_t* w, uint32_t type, int n, int d, in
                                cudaStream_t stream);
 size_t engine_act_bytes(uint32_t type, int d, int B);
 
+// ---- tensor-core GEMV programs for batched tokens (tc.cu) ----
+
+// One GEMV: out[t*ldo + r] = row_r(w) . x[t*ldx ...] for t < B, r < n.
+struct GemvJobIn {
+    const uint8_t* w;  // 16-byte aligned packed rows
+    uint32_t type;
+    int n, d, B;
+    const float* x;
+    long long ldx;
+    float* out;
+    long long ldo;
+};
+
+// Plans a tensor-core program (B <= kTcMaxB per job, at most kTcMaxJobs
+// jobs): allocates the activation operand buffer and the device job table.
+// Runs are two launches (quantizer, persistent tcgen05 kernel) and allocate
+// nothing.
+struct TcPlan;
+constexpr int kTcMaxB = 64;
+constexpr int kTcMaxJobs = 96;
+int tc_plan_create(const GemvJobIn* jobs, int njobs, TcPlan** out);
+cudaError_t tc_plan_run(TcPlan* plan, int* err, cudaStream_t stream);
+void tc_plan_destroy(TcPlan* plan);
+void tc_plan_info(const TcPlan* plan, int* items, int* grid, int* smem);
+
 // ---- routed MoE block (moe.cu) ----
 
 // The reference's fixed routing buffers: router_logits[256], active_experts[16]

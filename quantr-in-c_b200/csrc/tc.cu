@@ -1,0 +1,747 @@
+// tc.cu -- batched-token quantized GEMV on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, accumulators in TMEM), sm_100a.
+//
+// Every output of the reference (src/quant.c:242-437) is a left-to-right fp32
+// sum over 32-element units of a term computed from the unit's int32 dot
+// product isum = sum(w_q * x_q).  Here one tcgen05.mma per unit computes isum
+// for a 128-row x N-token tile exactly (M=128, K=32, int8 x int8 -> int32,
+// no accumulation across units), and epilogue warps read it from TMEM and
+// apply the reference's term and running sum in unit order with explicitly
+// rounded fp32 operations.  The integer products leave the CUDA cores, which
+// keep only the exact-term arithmetic the reference's semantics require.
+//
+// A launch runs a list of GEMV jobs (B <= 64 tokens each, N = B rounded up
+// to 16 columns) cut into 128-row tiles, dealt round-robin to one persistent
+// CTA per SM.  A tile's K dimension streams in stages of 8 units (one K-quant
+// super-block, or 8 Q8_0 blocks) through S shared-memory slots:
+//
+//   producer (warp 0)    per stage: two cp.async.bulk copies, the stage's
+//                        activation operand tiles and per-(unit, token) scale
+//                        records, on one mbarrier transaction count;
+//   MMA (warp 1, one     per unit: tcgen05.mma into one of NB TMEM buffers,
+//   thread)              tcgen05.commit to that buffer's barrier; after the
+//                        stage, a commit that frees the slot's operands;
+//   decoders (4 warps)   one thread per row: fetch the row's packed bytes for
+//                        the stage (16-byte cp.async of the aligned cover of
+//                        the segment, S-1 stages ahead, one async-copy group
+//                        per stage), unpack each unit's quants into the
+//                        canonical K-major no-swizzle operand layout (8x16-byte
+//                        core matrices) and the unit's scales;
+//   epilogue (8 warps)   TMEM lane quarter (warp % 4) x token half: per unit
+//                        tcgen05.ld the int32 sums, then term and running
+//                        sum per (row, token), in unit order.
+//
+// Activations are quantized by k_tc_quant (quantize_row_q8_0 per token, the
+// same kernel math as every other path) straight into operand tiles in the
+// element order each weight type's decode produces.  All waits are bounded
+// (250 ms); on a timeout every role stops, copies in flight are drained, the
+// last MMAs are awaited and TMEM is freed before the CTA exits.  No multicast.
+#include "quantr_cuda.h"
+
+#include "device_common.cuh"
+#include "formats.cuh"
+#include "kernels.cuh"
+#include "launch_util.cuh"
+#include "quant_decode.cuh"
+
+#include <algorithm>
+#include <map>
+#include <new>
+#include <tuple>
+#include <vector>
+
+namespace qr {
+namespace tc {
+
+constexpr int kM = 128;        // rows per tile (MMA M)
+constexpr int kUS = 8;         // units per stage
+constexpr int kDecWarps = 4;   // one decoder thread per tile row
+constexpr int kEpiWarps = 8;   // 4 lane quarters x 2 token halves
+constexpr int kWarps = 2 + kDecWarps + kEpiWarps;
+constexpr int kThreads = 32 * kWarps;
+constexpr int kMaxSlots = 3;
+constexpr int kMaxNB = 32;     // TMEM buffers
+constexpr int kMaxN = kTcMaxB; // tokens per job (MMA N after padding)
+constexpr size_t kSmemMax = 227 * 1024;
+constexpr uint32_t kATile = 4096;  // one unit's 128 x 32-byte operand tile
+
+// One GEMV of a launch (device view).
+struct __align__(16) TcJob {
+    const uint8_t* w;      // packed rows (16-byte aligned base)
+    const uint8_t* act;    // [U] x (N x 32-byte canonical operand tile)
+    const uint8_t* ds;     // [U] x N records {float dx, float bsum, int 32*bsum, 0}
+    float* out;
+    long long ldo;
+    long long rb;          // packed row bytes
+    uint32_t type, n, U, B;
+    uint32_t N, nst, seg, idesc;  // nst stages of kUS units; seg = packed bytes of a full stage per row
+    int tiles, item0, pad0, pad1;
+};
+static_assert(sizeof(TcJob) % 16 == 0, "job table is copied in 16-byte words");
+
+struct TcParams {
+    const TcJob* jobs;
+    int njobs, total_items;
+    uint32_t S, NB, ncol, tmem_cols;      // slots, TMEM buffers, columns per buffer, allocated columns
+    uint32_t segp;                        // staging bytes per row per slot
+    uint32_t w_off, a_off, b_off, d_off, s_off, slot_bytes, jobs_off;
+    int* err;
+};
+
+// ------------------------------------------------------------ tcgen05 --
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr)
+{
+    // Canonical K-major, no swizzle: core matrices of 8 rows x 16 bytes; the
+    // two K halves 128 bytes apart (LBO), 8-row groups 256 bytes apart (SBO);
+    // descriptor version 1 (sm_100) at bit 46.
+    uint64_t d = (uint64_t)((addr & 0x3FFFFu) >> 4);
+    d |= (uint64_t)(128u >> 4) << 16;
+    d |= (uint64_t)(256u >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    return d;
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc)
+{
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(z), "r"(z), "r"(z), "r"(z), "r"(z)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar)
+{
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sptr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+template <int NC>
+__device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&v)[NC]);
+
+template <>
+__device__ __forceinline__ void tmem_ld<8>(uint32_t addr, uint32_t (&v)[8])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(addr));
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<16>(uint32_t addr, uint32_t (&v)[16])
+{
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(addr));
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<32>(uint32_t addr, uint32_t (&v)[32])
+{
+    uint32_t (&a)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[0]);
+    uint32_t (&b)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16]);
+    tmem_ld<16>(addr, a);
+    tmem_ld<16>(addr + 16, b);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------------------- quantizer --
+
+struct TcQTask {
+    const float* x;
+    uint8_t* act;
+    uint8_t* ds;
+    long long ldx;
+    long long blk0;  // first global (token, unit) index of this task
+    int U, B, N, type;
+};
+
+struct TcQParams {
+    const TcQTask* tasks;
+    int ntasks;
+    long long total;
+};
+
+// Position of element e (0..31) of a unit in the element order the weight
+// type's decode produces (quant_decode.cuh permute_x16).
+__device__ __forceinline__ int tc_perm(int type, int e)
+{
+    if (type == T_Q4_K || type == T_Q5_K) return (e & ~7) + ((e & 1) << 2) + ((e & 7) >> 1);
+    if (type == T_Q6_K) return (e & ~15) + ((e & 3) << 2) + ((e & 15) >> 2);
+    return e;
+}
+
+// Reference quantize_row_q8_0 per (token, 32-element block), one warp each,
+// written into canonical operand tiles: token t, permuted element k of unit
+// u at u*N*32 + (t/8)*256 + (t%8)*16 + (k/16)*128 + k%16.
+__global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQParams p)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const long long step = (long long)gridDim.x * 8;
+    for (long long gb = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); gb < p.total; gb += step) {
+        int lo = 0, hi = p.ntasks - 1;  // last task with blk0 <= gb
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (p.tasks[mid].blk0 <= gb) lo = mid; else hi = mid - 1;
+        }
+        const TcQTask& T = p.tasks[lo];
+        const long long local = gb - T.blk0;
+        const int t = (int)(local / T.U), u = (int)(local - (long long)t * T.U);
+        const float v = T.x[(long long)t * T.ldx + (long long)u * 32 + lane];
+        uint32_t h;
+        int sum;
+        const int8_t q = q8_block_warp(v, h, sum);
+        const int k = tc_perm(T.type, lane);
+        T.act[(size_t)u * T.N * 32 + (t >> 3) * 256 + (t & 7) * 16 + (k >> 4) * 128 + (k & 15)] = (uint8_t)q;
+        if (lane == 0) {
+            float4 rec;
+            rec.x = h2f_ref(h);
+            rec.y = (float)sum;
+            rec.z = __int_as_float(32 * sum);
+            rec.w = 0.0f;
+            reinterpret_cast<float4*>(T.ds)[(size_t)u * T.N + t] = rec;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- kernel --
+
+__device__ __forceinline__ int job_of(const TcJob* jobs, int njobs, int item, int jc)
+{
+    while (jc + 1 < njobs && item >= jobs[jc + 1].item0) ++jc;
+    return jc;
+}
+
+// Epilogue of one unit for NT tokens of this warp: terms and running sums.
+template <int NT>
+__device__ __forceinline__ void epi_unit(uint32_t taddr, uint32_t type, int tok0, int B, float sc, float m,
+                                         const float4* ds, float (&acc)[NT])
+{
+    uint32_t v[NT];
+    tmem_ld<NT>(taddr, v);
+    tmem_wait_ld();
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+        if (tok0 + t < B) {
+            const float4 r = ds[tok0 + t];
+            const int isum = (int)v[t];
+            float term;
+            if (type == T_Q8_0) term = __fmul_rn(__fmul_rn((float)isum, sc), r.x);  // src/quant.c:284
+            else if (type == T_Q6_K)
+                term = __fmul_rn(__fmul_rn(sc, (float)(isum - __float_as_int(r.z))), r.x);  // :433
+            else term = __fmul_rn(__fsub_rn(__fmul_rn(sc, (float)isum), __fmul_rn(m, r.y)), r.x);  // :399
+            acc[t] = __fadd_rn(acc[t], term);
+        }
+    }
+}
+
+template <int NT>
+__device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, uint64_t* full_w,
+                              uint64_t* a_ready, uint64_t* st_free, uint64_t* t_full, uint64_t* t_empty,
+                              volatile int* abort_flag, uint32_t tmem, int warp, int lane)
+{
+    const int quarter = warp & 3, half = (warp - 2 - kDecWarps) >> 2;
+    const int row = 32 * quarter + lane;
+    const int S = (int)p.S, NB = (int)p.NB;
+    int gs = 0, gu = 0, jc = 0;
+    bool ok = true;
+    for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
+        jc = job_of(jobs, p.njobs, i, jc);
+        const TcJob& J = jobs[jc];
+        const int r0 = (i - J.item0) * kM;
+        const int rows = min(kM, (int)J.n - r0);
+        const int tok0 = half * NT;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+        for (int st = 0; st < (int)J.nst; ++st, ++gs) {
+            const int slot = gs % S, use = gs / S;
+            if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
+                !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag)) {
+                ok = false;
+                break;
+            }
+            const uint32_t base = p.slot_bytes * (uint32_t)slot;
+            const int us = min(kUS, (int)J.U - kUS * st);
+            for (int j = 0; j < us; ++j, ++gu) {
+                const int b = gu % NB;
+                if (!mbar_wait_bounded(&t_full[b], (gu / NB) & 1, p.err, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float2 scm =
+                    *reinterpret_cast<const float2*>(sm + p.s_off + base + (uint32_t)(j * kM + row) * 8);
+                const float4* ds =
+                    reinterpret_cast<const float4*>(sm + p.d_off + base + (uint32_t)(j * (int)J.N) * 16);
+                const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(b * (int)p.ncol + tok0);
+                if (tok0 < (int)J.B) epi_unit<NT>(taddr, J.type, tok0, (int)J.B, scm.x, scm.y, ds, acc);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&t_empty[b]);
+            }
+            if (!ok) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&st_free[slot]);
+        }
+        if (!ok) break;
+        if (row < rows)
+#pragma unroll
+            for (int t = 0; t < NT; ++t)
+                if (tok0 + t < (int)J.B) J.out[(long long)(tok0 + t) * J.ldo + r0 + row] = acc[t];
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constant__ TcParams p)
+{
+    extern __shared__ __align__(1024) uint8_t sm[];
+    uint64_t* full_w = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* a_ready = full_w + kMaxSlots;
+    uint64_t* st_free = a_ready + kMaxSlots;
+    uint64_t* t_full = st_free + kMaxSlots;
+    uint64_t* t_empty = t_full + kMaxNB;
+    uint32_t* misc = reinterpret_cast<uint32_t*>(t_empty + kMaxNB);  // [0] TMEM base, [1] abort, [2..] fills
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int S = (int)p.S, NB = (int)p.NB;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full_w[s], 1);
+            mbar_init(&a_ready[s], kDecWarps);
+            mbar_init(&st_free[s], 1 + kDecWarps + kEpiWarps);
+            misc[2 + s] = 0;
+        }
+        for (int b = 0; b < NB; ++b) {
+            mbar_init(&t_full[b], 1);
+            mbar_init(&t_empty[b], kEpiWarps);
+        }
+        misc[1] = 0;
+        mbar_fence_init();
+    }
+    {  // job table -> shared memory
+        const uint4* src = reinterpret_cast<const uint4*>(p.jobs);
+        uint4* dst = reinterpret_cast<uint4*>(sm + p.jobs_off);
+        const int words = p.njobs * (int)(sizeof(TcJob) / 16);
+        for (int w = threadIdx.x; w < words; w += kThreads) dst[w] = src[w];
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sptr(&misc[0])),
+                     "r"(p.tmem_cols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = misc[0];
+    const TcJob* jobs = reinterpret_cast<const TcJob*>(sm + p.jobs_off);
+    pdl_trigger();
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer --
+        pdl_wait();  // activations come from the quantizer grid
+        int gs = 0, jc = 0;
+        for (int i = blockIdx.x; i < p.total_items; i += gridDim.x) {
+            jc = job_of(jobs, p.njobs, i, jc);
+            const TcJob& J = jobs[jc];
+            bool stop = false;
+            for (int st = 0; st < (int)J.nst; ++st, ++gs) {
+                const int slot = gs % S, use = gs / S;
+                if (use > 0 && !mbar_wait_bounded(&st_free[slot], (use - 1) & 1, p.err, abort_flag)) {
+                    stop = true;
+                    break;
+                }
+                const int us = min(kUS, (int)J.U - kUS * st);
+                const uint32_t abytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
+                const uint32_t base = p.slot_bytes * (uint32_t)slot;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(&full_w[slot], abytes + dbytes);
+                    misc[2 + slot] += 1;
+                    bulk_g2s(sm + p.b_off + base, J.act + (size_t)kUS * st * J.N * 32, abytes, &full_w[slot]);
+                    bulk_g2s(sm + p.d_off + base, J.ds + (size_t)kUS * st * J.N * 16, dbytes, &full_w[slot]);
+                }
+                __syncwarp();
+            }
+            if (stop) break;
+        }
+    } else if (warp == 1) {
+        // ----------------------------------------------------------- MMA --
+        if (lane == 0) {
+            int gs = 0, gu = 0, jc = 0, last_b = -1, last_ph = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
+                jc = job_of(jobs, p.njobs, i, jc);
+                const TcJob& J = jobs[jc];
+                for (int st = 0; st < (int)J.nst; ++st, ++gs) {
+                    const int slot = gs % S, use = gs / S;
+                    if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
+                        !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t base = p.slot_bytes * (uint32_t)slot;
+                    const int us = min(kUS, (int)J.U - kUS * st);
+                    for (int j = 0; j < us; ++j, ++gu) {
+                        const int b = gu % NB;
+                        if (gu >= NB) {
+                            if (!mbar_wait_bounded(&t_empty[b], ((gu / NB) - 1) & 1, p.err, abort_flag)) {
+                                ok = false;
+                                break;
+                            }
+                            tc_fence_after();
+                        }
+                        const uint64_t ad = smem_desc(sptr(sm + p.a_off + base + (uint32_t)j * kATile));
+                        const uint64_t bd = smem_desc(sptr(sm + p.b_off + base + (uint32_t)(j * (int)J.N) * 32u));
+                        tc_mma(tmem + (uint32_t)(b * (int)p.ncol), ad, bd, J.idesc);
+                        tc_commit(&t_full[b]);
+                        last_b = b;
+                        last_ph = (gu / NB) & 1;
+                    }
+                    if (!ok) break;
+                    tc_commit(&st_free[slot]);
+                }
+            }
+            // The MMAs issued last complete before TMEM is released.
+            if (last_b >= 0) mbar_wait_bounded(&t_full[last_b], (uint32_t)last_ph, nullptr);
+        }
+        __syncwarp();
+    } else if (warp < 2 + kDecWarps) {
+        // ------------------------------------------------------ decoders --
+        const int row = (warp - 2) * 32 + lane;
+        const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
+        // Stage positions (item, stage within item, job) walked twice: once
+        // to issue a stage's copies S-1 stages ahead, once to decode it.
+        struct Pos {
+            int i, st, jc;
+        };
+        auto valid = [&](const Pos& q) { return q.i < p.total_items; };
+        auto next = [&](Pos q) {
+            if (++q.st >= (int)jobs[q.jc].nst) {
+                q.st = 0;
+                q.i += gridDim.x;
+                if (q.i < p.total_items) q.jc = job_of(jobs, p.njobs, q.i, q.jc);
+            }
+            return q;
+        };
+        Pos first{(int)blockIdx.x, 0, 0};
+        if (valid(first)) first.jc = job_of(jobs, p.njobs, first.i, 0);
+        bool ok = true;
+        // Issues stage g (at position q): after the slot's previous use is
+        // released, 16-byte async copies of this row's aligned segment cover;
+        // one commit group per stage (empty when there is nothing to fetch).
+        auto issue = [&](const Pos& q, int g) {
+            if (valid(q)) {
+                const int slot = g % S, use = g / S;
+                if (use > 0 && !mbar_wait_bounded(&st_free[slot], (use - 1) & 1, p.err, abort_flag)) ok = false;
+                const TcJob& J = jobs[q.jc];
+                const int r0 = (q.i - J.item0) * kM;
+                const int rows = min(kM, (int)J.n - r0);
+                if (ok && row < rows) {
+                    const int us = min(kUS, (int)J.U - kUS * q.st);
+                    const uint32_t segb = J.type == T_Q8_0 ? (uint32_t)us * 34u : J.seg;
+                    const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)q.st * J.seg);
+                    const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + segb + 15) & ~(uintptr_t)15;
+                    const uint32_t dst = sptr(sm + p.w_off + p.slot_bytes * (uint32_t)slot + (uint32_t)row * p.segp);
+                    for (uintptr_t off = a0; off < a1; off += 16)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + (uint32_t)(off - a0)),
+                                     "l"(off)
+                                     : "memory");
+                }
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        Pos iss = first;
+        int gi = 0;
+        for (int k = 0; k < S - 1; ++k) {  // prologue: S-1 groups, real or empty
+            issue(iss, gi);
+            if (valid(iss)) {
+                iss = next(iss);
+                ++gi;
+            }
+        }
+        int gs = 0;
+        for (Pos cur = first; ok && valid(cur); cur = next(cur), ++gs) {
+            // This stage's group is the oldest not yet waited for.
+            if (S == 3) asm volatile("cp.async.wait_group 1;" ::: "memory");
+            else asm volatile("cp.async.wait_group 0;" ::: "memory");
+            const TcJob& J = jobs[cur.jc];
+            const int slot = gs % S;
+            const uint32_t base = p.slot_bytes * (uint32_t)slot;
+            const int r0 = (cur.i - J.item0) * kM;
+            const int rows = min(kM, (int)J.n - r0);
+            const int us = min(kUS, (int)J.U - kUS * cur.st);
+            if (row < rows) {
+                const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
+                const uint32_t seg0 = p.w_off + base + (uint32_t)row * p.segp + (uint32_t)(a & 15);
+                const uint32_t arow = p.a_off + base + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
+                for (int j = 0; j < us; ++j) {
+                    Unit o;
+                    switch (J.type) {
+                    case T_Q4_K: decode_unit<T_Q4_K>(s32, sm, seg0, j, o); break;
+                    case T_Q5_K: decode_unit<T_Q5_K>(s32, sm, seg0, j, o); break;
+                    case T_Q6_K: decode_unit<T_Q6_K>(s32, sm, seg0, j, o); break;
+                    default: decode_unit<T_Q8_0>(s32, sm, seg0, j, o); break;
+                    }
+                    uint4* at = reinterpret_cast<uint4*>(sm + arow + (uint32_t)j * kATile);
+                    at[0] = make_uint4(o.wq[0], o.wq[1], o.wq[2], o.wq[3]);
+                    at[8] = make_uint4(o.wq[4], o.wq[5], o.wq[6], o.wq[7]);  // + 128 bytes: second K half
+                    *reinterpret_cast<float2*>(sm + p.s_off + base + (uint32_t)(j * kM + row) * 8) =
+                        make_float2(o.a, o.b);
+                }
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // operand stores -> tensor core
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&a_ready[slot]);
+                mbar_arrive(&st_free[slot]);
+            }
+            issue(iss, gi);  // stage gs + S - 1 (its slot's previous use is stage gs - 1)
+            if (valid(iss)) {
+                iss = next(iss);
+                ++gi;
+            }
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into shared memory outlives the role
+    } else {
+        // ------------------------------------------------------ epilogue --
+        switch (p.ncol) {
+        case 16:
+            epilogue_role<8>(sm, p, jobs, full_w, a_ready, st_free, t_full, t_empty, abort_flag, tmem, warp, lane);
+            break;
+        case 32:
+            epilogue_role<16>(sm, p, jobs, full_w, a_ready, st_free, t_full, t_empty, abort_flag, tmem, warp, lane);
+            break;
+        default:
+            epilogue_role<32>(sm, p, jobs, full_w, a_ready, st_free, t_full, t_empty, abort_flag, tmem, warp, lane);
+            break;
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag && threadIdx.x == 0) {
+        // Some role gave up: let every bulk copy this CTA issued land
+        // (bounded) before its shared memory is released.
+        for (int s = 0; s < S; ++s)
+            if (misc[2 + s] > 0) mbar_wait_bounded(&full_w[s], (misc[2 + s] - 1) & 1, nullptr);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(p.tmem_cols)
+                     : "memory");
+    }
+}
+
+// ------------------------------------------------------------ host side --
+
+uint32_t seg_bytes(uint32_t type)
+{
+    return type == T_Q8_0 ? (uint32_t)kUS * 34u : (uint32_t)block_bytes(type);
+}
+
+} // namespace tc
+
+struct TcPlan {
+    int device = 0;
+    std::vector<tc::TcJob> jobs;
+    std::vector<tc::TcQTask> tasks;
+    tc::TcParams pp{};
+    tc::TcQParams qp{};
+    int grid = 0;
+    size_t smem = 0;
+    tc::TcJob* d_jobs = nullptr;
+    tc::TcQTask* d_tasks = nullptr;
+    uint8_t* d_act = nullptr;
+};
+
+int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
+{
+    using namespace tc;
+    if (!out || !in || njobs <= 0 || njobs > kTcMaxJobs) return QUANTR_ERR_BAD_ARG;
+    *out = nullptr;
+    TcPlan* P = new (std::nothrow) TcPlan();
+    if (!P) return QUANTR_ERR_OOM;
+    cudaGetDevice(&P->device);
+    // Activation tasks, one per distinct (x, ldx, d, B, element order); the
+    // operand layout depends on the weight type only through that order.
+    std::map<std::tuple<const float*, long long, int, int, int>, int> dedupe;
+    size_t act_total = 0;
+    long long blocks = 0;
+    int Nmax = 16, item = 0;
+    uint32_t segmax = 0;
+    std::vector<size_t> task_act_off;
+    std::vector<int> job_task;
+    for (int j = 0; j < njobs; ++j) {
+        const GemvJobIn& a = in[j];
+        if (!type_supported(a.type) || a.type == T_F32) {
+            delete P;
+            return QUANTR_ERR_UNSUPPORTED_TYPE;
+        }
+        if (!a.w || !a.x || !a.out || a.n <= 0 || a.B <= 0 || a.B > kMaxN || a.ldx < a.d || a.ldo < a.n ||
+            ((uintptr_t)a.w & 15) || row_bytes(a.type, a.d) <= 0) {
+            delete P;
+            return QUANTR_ERR_BAD_ARG;
+        }
+        TcJob J{};
+        J.w = a.w;
+        J.rb = row_bytes(a.type, a.d);
+        J.type = a.type;
+        J.n = (uint32_t)a.n;
+        J.U = (uint32_t)((a.d / block_elems(a.type)) * block_units(a.type));
+        J.B = (uint32_t)a.B;
+        J.N = (uint32_t)std::max(16, (a.B + 15) / 16 * 16);
+        J.nst = (J.U + kUS - 1) / kUS;
+        J.seg = seg_bytes(a.type);
+        // D s32 (bits 4-5 = 2); A unsigned 8-bit for the K-quants (0..63),
+        // signed for Q8_0 (bit 7); B signed (bit 10); K-major A and B;
+        // N >> 3 at bit 17; M >> 4 at bit 24.
+        J.idesc = (2u << 4) | ((a.type == T_Q8_0 ? 1u : 0u) << 7) | (1u << 10) | ((J.N >> 3) << 17) |
+                  ((uint32_t)(kM >> 4) << 24);
+        J.out = a.out;
+        J.ldo = a.ldo;
+        J.tiles = (a.n + kM - 1) / kM;
+        J.item0 = item;
+        item += J.tiles;
+        Nmax = std::max(Nmax, (int)J.N);
+        segmax = std::max(segmax, J.seg);
+        const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
+        auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, perm);
+        auto it = dedupe.find(key);
+        int ti;
+        if (it == dedupe.end()) {
+            TcQTask t{};
+            t.x = a.x;
+            t.ldx = a.ldx;
+            t.U = (int)J.U;
+            t.B = a.B;
+            t.N = (int)J.N;
+            t.type = (int)a.type;
+            t.blk0 = blocks;
+            blocks += (long long)a.B * J.U;
+            task_act_off.push_back(act_total);
+            act_total += ((size_t)J.U * J.N * 48 + 255) & ~size_t(255);
+            ti = (int)P->tasks.size();
+            P->tasks.push_back(t);
+            dedupe[key] = ti;
+        } else {
+            ti = it->second;
+        }
+        job_task.push_back(ti);
+        P->jobs.push_back(J);
+    }
+    // Shared memory: barriers | S slots of {packed rows | A tiles | B tiles | ds | scales} | job table.
+    // A row's staged copy is the 16-byte aligned cover of its segment: up to
+    // 15 bytes before it and 15 after, plus one word the decoder may read past.
+    const uint32_t segp = (segmax + 45) & ~15u;
+    const uint32_t wbytes = kM * segp, abytes = kUS * kATile, bbytes = kUS * (uint32_t)Nmax * 32u,
+                   dbytes = kUS * (uint32_t)Nmax * 16u, sbytes = kUS * kM * 8u;
+    const uint32_t slot = (wbytes + abytes + bbytes + dbytes + sbytes + 1023) & ~1023u;
+    const uint32_t bars = 1024, tbl = ((uint32_t)(P->jobs.size() * sizeof(TcJob)) + 127) & ~127u;
+    const int S = (int)std::min<size_t>(kMaxSlots, (kSmemMax - bars - tbl) / slot);
+    if (S < 2) {
+        delete P;
+        return QUANTR_ERR_TOO_LARGE;
+    }
+    TcParams& pp = P->pp;
+    pp.njobs = (int)P->jobs.size();
+    pp.total_items = item;
+    pp.S = (uint32_t)S;
+    pp.ncol = (uint32_t)Nmax;
+    pp.NB = (uint32_t)std::min(kMaxNB, 512 / Nmax);
+    uint32_t cols = 32;
+    while (cols < pp.NB * pp.ncol) cols <<= 1;
+    pp.tmem_cols = cols;
+    pp.segp = segp;
+    pp.slot_bytes = slot;
+    pp.w_off = bars;
+    pp.a_off = bars + wbytes;
+    pp.b_off = pp.a_off + abytes;
+    pp.d_off = pp.b_off + bbytes;
+    pp.s_off = pp.d_off + dbytes;
+    pp.jobs_off = bars + (uint32_t)S * slot;
+    P->smem = pp.jobs_off + tbl;
+    P->grid = std::min(device_sm_count(), item);
+
+    cudaError_t e = cudaMalloc((void**)&P->d_act, std::max<size_t>(act_total, 256));
+    if (e == cudaSuccess) e = cudaMemset(P->d_act, 0, std::max<size_t>(act_total, 256));  // padding tokens stay 0
+    if (e == cudaSuccess) {
+        for (size_t t = 0; t < P->tasks.size(); ++t) {
+            P->tasks[t].act = P->d_act + task_act_off[t];
+            P->tasks[t].ds = P->tasks[t].act + (size_t)P->tasks[t].U * P->tasks[t].N * 32;
+        }
+        for (size_t j = 0; j < P->jobs.size(); ++j) {
+            P->jobs[j].act = P->tasks[job_task[j]].act;
+            P->jobs[j].ds = P->tasks[job_task[j]].ds;
+        }
+    }
+    if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_jobs, P->jobs.size() * sizeof(TcJob));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(P->d_jobs, P->jobs.data(), P->jobs.size() * sizeof(TcJob), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_tasks, P->tasks.size() * sizeof(TcQTask));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(P->d_tasks, P->tasks.data(), P->tasks.size() * sizeof(TcQTask), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        const int code = e == cudaErrorMemoryAllocation ? QUANTR_ERR_OOM : QUANTR_ERR_CUDA;
+        cudaGetLastError();
+        tc_plan_destroy(P);
+        return code;
+    }
+    pp.jobs = P->d_jobs;
+    P->qp.tasks = P->d_tasks;
+    P->qp.ntasks = (int)P->tasks.size();
+    P->qp.total = blocks;
+    *out = P;
+    return QUANTR_OK;
+}
+
+cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
+{
+    using namespace tc;
+    LaunchCfg c;
+    c.stream = stream;
+    static int configured_dev = -1;
+    cudaError_t e = ensure_smem_attr(&k_tc_program, (int)kSmemMax, configured_dev);
+    if (e != cudaSuccess) return e;
+    const long long qgrid = std::max(1LL, std::min<long long>((P->qp.total + 7) / 8, 8LL * device_sm_count()));
+    e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
+    if (e != cudaSuccess) return e;
+    TcParams pp = P->pp;
+    pp.err = err;
+    return launch_ex(&k_tc_program, dim3(P->grid), dim3(kThreads), P->smem, c, pp);
+}
+
+void tc_plan_destroy(TcPlan* P)
+{
+    if (!P) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(P->device);
+    cudaDeviceSynchronize();
+    cudaFree(P->d_jobs);
+    cudaFree(P->d_tasks);
+    cudaFree(P->d_act);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete P;
+}
+
+void tc_plan_info(const TcPlan* P, int* items, int* grid, int* smem)
+{
+    if (items) *items = P->pp.total_items;
+    if (grid) *grid = P->grid;
+    if (smem) *smem = (int)P->smem;
+}
+
+} // namespace qr
