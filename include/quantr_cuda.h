@@ -174,8 +174,8 @@ int quantr_gpu_device_status(void* stream, int reset);
  * (B <= 64), with the reference's numerics (the same as matmul_q_fused per
  * token).  All pointers are device pointers; w must be 16-byte aligned and
  * readable up to the next 16-byte boundary past its last row (every cudaMalloc
- * allocation and registered range is).  Jobs of up to 8 tokens run on the dp4a
- * engine, jobs of 9..64 tokens on the tensor cores (tcgen05 kind::i8). */
+ * allocation and registered range is).  Jobs of up to 4 tokens run on the dp4a
+ * engine, jobs of 5..64 tokens on the tensor cores (tcgen05 kind::i8). */
 typedef struct {
     const void* w;
     uint32_t type;       /* QUANTR_TYPE_Q8_0 / Q4_K / Q5_K / Q6_K */

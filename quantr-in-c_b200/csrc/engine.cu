@@ -779,7 +779,7 @@ size_t engine_act_bytes(uint32_t type, int d, int B) { return eng::act_bytes_for
 // Jobs with B >= kTcMinB tokens (up to kTcMaxB) run on the tensor-core kernel
 // (tc.cu), the others on the dp4a engine above.
 #ifndef QR_TC_MIN_B
-#define QR_TC_MIN_B 9
+#define QR_TC_MIN_B 5
 #endif
 constexpr int kTcMinB = QR_TC_MIN_B;
 

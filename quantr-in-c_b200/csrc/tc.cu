@@ -18,18 +18,23 @@
 //   producer (warp 0)    per stage: two cp.async.bulk copies, the stage's
 //                        activation operand tiles and per-(unit, token) scale
 //                        records, on one mbarrier transaction count;
-//   MMA (warp 1, one     per unit: tcgen05.mma into one of NB TMEM buffers,
-//   thread)              tcgen05.commit to that buffer's barrier; after the
-//                        stage, a commit that frees the slot's operands;
-//   decoders (4 warps)   one thread per row: fetch the row's packed bytes for
-//                        the stage (16-byte cp.async of the aligned cover of
-//                        the segment, S-1 stages ahead, one async-copy group
-//                        per stage), unpack each unit's quants into the
-//                        canonical K-major no-swizzle operand layout (8x16-byte
-//                        core matrices) and the unit's scales;
-//   epilogue (8 warps)   TMEM lane quarter (warp % 4) x token half: per unit
-//                        tcgen05.ld the int32 sums, then term and running
-//                        sum per (row, token), in unit order.
+//   MMA (warp 1)         per unit: tcgen05.mma (issued by one elected lane of
+//                        the converged warp) into the stage's TMEM buffer (one
+//                        of NBS, 8 units x N columns each); after the stage,
+//                        one commit to the buffer's barrier and one that frees
+//                        the slot's operands;
+//   decoders (4 warps)   fetch the tile's packed bytes for the stage together
+//                        (16-byte cp.async of each row's aligned segment cover,
+//                        consecutive threads on consecutive chunks of a row,
+//                        S-1 stages ahead, one async-copy group per stage, a
+//                        named barrier before use), then one thread per row
+//                        unpacks each unit's quants into the canonical K-major
+//                        no-swizzle operand layout (8x16-byte core matrices)
+//                        and the unit's scales;
+//   epilogue (8 warps)   TMEM lane quarter (warp % 4) x token half: per stage
+//                        one barrier wait, tcgen05.ld of several units' int32
+//                        sums before one wait::ld, then term and running sum
+//                        per (row, token), in unit order.
 //
 // Activations are quantized by k_tc_quant (quantize_row_q8_0 per token, the
 // same kernel math as every other path) straight into operand tiles in the
@@ -37,6 +42,9 @@
 // (250 ms); on a timeout every role stops, copies in flight are drained, the
 // last MMAs are awaited and TMEM is freed before the CTA exits.  No multicast.
 #include "quantr_cuda.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "device_common.cuh"
 #include "formats.cuh"
@@ -60,7 +68,7 @@ constexpr int kEpiWarps = 8;   // 4 lane quarters x 2 token halves
 constexpr int kWarps = 2 + kDecWarps + kEpiWarps;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kMaxSlots = 3;
-constexpr int kMaxNB = 32;     // TMEM buffers
+constexpr int kMaxNB = 4;      // TMEM stage buffers
 constexpr int kMaxN = kTcMaxB; // tokens per job (MMA N after padding)
 constexpr size_t kSmemMax = 227 * 1024;
 constexpr uint32_t kATile = 4096;  // one unit's 128 x 32-byte operand tile
@@ -69,23 +77,29 @@ constexpr uint32_t kATile = 4096;  // one unit's 128 x 32-byte operand tile
 struct __align__(16) TcJob {
     const uint8_t* w;      // packed rows (16-byte aligned base)
     const uint8_t* act;    // [U] x (N x 32-byte canonical operand tile)
-    const uint8_t* ds;     // [U] x N records {float dx, float bsum, int 32*bsum, 0}
+    const uint8_t* ds;     // per unit: dx[N] | (float)bsum[N] | 32*bsum[N] (int) | unused[N]
     float* out;
     long long ldo;
     long long rb;          // packed row bytes
     uint32_t type, n, U, B;
     uint32_t N, nst, seg, idesc;  // nst stages of kUS units; seg = packed bytes of a full stage per row
-    int tiles, item0, pad0, pad1;
+    int tiles, item0;
+    int tma;  // weights fetched by one 2-D TMA copy per stage (rows 16-byte aligned: Q4_K, Q5_K)
+    int pad0;
 };
 static_assert(sizeof(TcJob) % 16 == 0, "job table is copied in 16-byte words");
 
 struct TcParams {
     const TcJob* jobs;
     int njobs, total_items;
-    uint32_t S, NB, ncol, tmem_cols;      // slots, TMEM buffers, columns per buffer, allocated columns
+    uint32_t S, NB, ncol, tmem_cols;      // slots, TMEM stage buffers, max N (columns per unit), allocated columns
     uint32_t segp;                        // staging bytes per row per slot
     uint32_t w_off, a_off, b_off, d_off, s_off, slot_bytes, jobs_off;
     int* err;
+    // Per job with tma set: rows x row-bytes uint8 view of the packed weights,
+    // box = 128 rows x one stage's bytes (passed by value: TMA reads the map
+    // from the kernel's parameter space).
+    CUtensorMap tmap[kTcMaxJobs];
 };
 
 // ------------------------------------------------------------ tcgen05 --
@@ -153,6 +167,16 @@ __device__ __forceinline__ void tmem_ld<32>(uint32_t addr, uint32_t (&v)[32])
 
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// True in exactly one lane of the (converged) warp.
+__device__ __forceinline__ bool elect_one()
+{
+    uint32_t pred = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
 // ------------------------------------------------------------- quantizer --
 
 struct TcQTask {
@@ -203,13 +227,11 @@ __global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQPar
         const int8_t q = q8_block_warp(v, h, sum);
         const int k = tc_perm(T.type, lane);
         T.act[(size_t)u * T.N * 32 + (t >> 3) * 256 + (t & 7) * 16 + (k >> 4) * 128 + (k & 15)] = (uint8_t)q;
-        if (lane == 0) {
-            float4 rec;
-            rec.x = h2f_ref(h);
-            rec.y = (float)sum;
-            rec.z = __int_as_float(32 * sum);
-            rec.w = 0.0f;
-            reinterpret_cast<float4*>(T.ds)[(size_t)u * T.N + t] = rec;
+        if (lane == 0) {  // planar per unit: dx | bsum | 32*bsum
+            float* rec = reinterpret_cast<float*>(T.ds) + (size_t)u * T.N * 4;
+            rec[t] = h2f_ref(h);
+            rec[T.N + t] = (float)sum;
+            rec[2 * T.N + t] = __int_as_float(32 * sum);
         }
     }
 }
@@ -222,83 +244,168 @@ __device__ __forceinline__ int job_of(const TcJob* jobs, int njobs, int item, in
     return jc;
 }
 
-// Epilogue of one unit for NT tokens of this warp: terms and running sums.
-template <int NT>
-__device__ __forceinline__ void epi_unit(uint32_t taddr, uint32_t type, int tok0, int B, float sc, float m,
-                                         const float4* ds, float (&acc)[NT])
+// Term and running sum of one unit for this warp's NT tokens (v = the unit's
+// int32 sums from TMEM).  Padding tokens (>= B) have zero activations and
+// records, so they are computed without branches and never stored.  Shared
+// memory is read through 32-bit shared-window addresses.
+template <uint32_t TYPE, int NT>
+__device__ __forceinline__ void epi_unit(const uint32_t (&v)[NT], uint32_t sbase, uint32_t s_off, uint32_t d_off,
+                                         int N, int j, int row, int tok0, float (&acc)[NT])
 {
-    uint32_t v[NT];
-    tmem_ld<NT>(taddr, v);
-    tmem_wait_ld();
+    const uint2 scm = lds64(sbase + s_off + (uint32_t)(j * kM + row) * 8);
+    const float sc = __uint_as_float(scm.x), m = __uint_as_float(scm.y);
+    const uint32_t rec = sbase + d_off + (uint32_t)(j * N) * 16 + (uint32_t)tok0 * 4;
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-        if (tok0 + t < B) {
-            const float4 r = ds[tok0 + t];
-            const int isum = (int)v[t];
+    for (int t4 = 0; t4 < NT; t4 += 4) {
+        const uint4 dx = lds128(rec + (uint32_t)t4 * 4);
+        uint4 aux = make_uint4(0, 0, 0, 0);
+        if (TYPE == T_Q4_K || TYPE == T_Q5_K) aux = lds128(rec + (uint32_t)(N + t4) * 4);  // bsum
+        if (TYPE == T_Q6_K) aux = lds128(rec + (uint32_t)(2 * N + t4) * 4);                // 32*bsum
+        const uint32_t dxa[4] = {dx.x, dx.y, dx.z, dx.w}, ax[4] = {aux.x, aux.y, aux.z, aux.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int isum = (int)v[t4 + q];
+            const float d = __uint_as_float(dxa[q]);
             float term;
-            if (type == T_Q8_0) term = __fmul_rn(__fmul_rn((float)isum, sc), r.x);  // src/quant.c:284
-            else if (type == T_Q6_K)
-                term = __fmul_rn(__fmul_rn(sc, (float)(isum - __float_as_int(r.z))), r.x);  // :433
-            else term = __fmul_rn(__fsub_rn(__fmul_rn(sc, (float)isum), __fmul_rn(m, r.y)), r.x);  // :399
-            acc[t] = __fadd_rn(acc[t], term);
+            if (TYPE == T_Q8_0) term = __fmul_rn(__fmul_rn((float)isum, sc), d);  // src/quant.c:284
+            else if (TYPE == T_Q6_K) term = __fmul_rn(__fmul_rn(sc, (float)(isum - (int)ax[q])), d);  // :433
+            else term = __fmul_rn(__fsub_rn(__fmul_rn(sc, (float)isum), __fmul_rn(m, __uint_as_float(ax[q]))), d);  // :399
+            acc[t4 + q] = __fadd_rn(acc[t4 + q], term);
+        }
+    }
+}
+
+// One stage of the epilogue: the TMEM load of unit j+1 is in flight while
+// unit j's terms are computed (two register buffers; one for NT = 32).
+template <uint32_t TYPE, int NT>
+__device__ __forceinline__ void epi_stage(uint32_t tbase, uint32_t sbase, uint32_t s_off, uint32_t d_off, int N,
+                                          int us, int row, int tok0, float (&acc)[NT])
+{
+    if (NT >= 32) {
+        for (int j = 0; j < us; ++j) {
+            uint32_t v[NT];
+            tmem_ld<NT>(tbase + (uint32_t)(j * N), v);
+            tmem_wait_ld();
+            epi_unit<TYPE, NT>(v, sbase, s_off, d_off, N, j, row, tok0, acc);
+        }
+        return;
+    }
+    uint32_t va[NT], vb[NT];
+    tmem_ld<NT>(tbase, va);
+    tmem_wait_ld();
+    for (int j = 0; j < us; j += 2) {
+        if (j + 1 < us) tmem_ld<NT>(tbase + (uint32_t)((j + 1) * N), vb);
+        epi_unit<TYPE, NT>(va, sbase, s_off, d_off, N, j, row, tok0, acc);
+        tmem_wait_ld();
+        if (j + 1 < us) {
+            if (j + 2 < us) tmem_ld<NT>(tbase + (uint32_t)((j + 2) * N), va);
+            epi_unit<TYPE, NT>(vb, sbase, s_off, d_off, N, j + 1, row, tok0, acc);
+            tmem_wait_ld();
         }
     }
 }
 
 template <int NT>
 __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, uint64_t* full_w,
-                              uint64_t* a_ready, uint64_t* st_free, uint64_t* t_full, uint64_t* t_empty,
-                              volatile int* abort_flag, uint32_t tmem, int warp, int lane)
+                                              uint64_t* a_ready, uint64_t* st_free, uint64_t* t_full,
+                                              uint64_t* t_empty, volatile int* abort_flag, uint32_t tmem, int warp,
+                                              int lane)
 {
     const int quarter = warp & 3, half = (warp - 2 - kDecWarps) >> 2;
     const int row = 32 * quarter + lane;
     const int S = (int)p.S, NB = (int)p.NB;
-    int gs = 0, gu = 0, jc = 0;
+    const uint32_t smb = sptr(sm);
+    int gs = 0, jc = 0;
     bool ok = true;
     for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
         jc = job_of(jobs, p.njobs, i, jc);
         const TcJob& J = jobs[jc];
         const int r0 = (i - J.item0) * kM;
         const int rows = min(kM, (int)J.n - r0);
+        const int B = (int)J.B, N = (int)J.N, U = (int)J.U, nst = (int)J.nst;
+        const uint32_t type = J.type;
+        float* out = J.out;
+        const long long ldo = J.ldo;
         const int tok0 = half * NT;
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-        for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-            const int slot = gs % S, use = gs / S;
+        for (int st = 0; st < nst; ++st, ++gs) {
+            const int slot = gs % S, use = gs / S, sb = gs % NB;
             if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
-                !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag)) {
+                !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag) ||
+                !mbar_wait_bounded(&t_full[sb], (gs / NB) & 1, p.err, abort_flag)) {
                 ok = false;
                 break;
             }
-            const uint32_t base = p.slot_bytes * (uint32_t)slot;
-            const int us = min(kUS, (int)J.U - kUS * st);
-            for (int j = 0; j < us; ++j, ++gu) {
-                const int b = gu % NB;
-                if (!mbar_wait_bounded(&t_full[b], (gu / NB) & 1, p.err, abort_flag)) {
-                    ok = false;
-                    break;
+            tc_fence_after();
+            const uint32_t sbase = smb + p.slot_bytes * (uint32_t)slot;
+            const int us = min(kUS, U - kUS * st);
+            const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(sb * kUS * (int)p.ncol + tok0);
+            if (tok0 < B) {
+                switch (type) {
+                case T_Q4_K: epi_stage<T_Q4_K, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
+                case T_Q5_K: epi_stage<T_Q5_K, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
+                case T_Q6_K: epi_stage<T_Q6_K, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
+                default: epi_stage<T_Q8_0, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
                 }
-                tc_fence_after();
-                const float2 scm =
-                    *reinterpret_cast<const float2*>(sm + p.s_off + base + (uint32_t)(j * kM + row) * 8);
-                const float4* ds =
-                    reinterpret_cast<const float4*>(sm + p.d_off + base + (uint32_t)(j * (int)J.N) * 16);
-                const uint32_t taddr = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(b * (int)p.ncol + tok0);
-                if (tok0 < (int)J.B) epi_unit<NT>(taddr, J.type, tok0, (int)J.B, scm.x, scm.y, ds, acc);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&t_empty[b]);
             }
-            if (!ok) break;
+            tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&st_free[slot]);
+            if (lane == 0) {
+                mbar_arrive(&t_empty[sb]);
+                mbar_arrive(&st_free[slot]);
+            }
         }
         if (!ok) break;
         if (row < rows)
 #pragma unroll
             for (int t = 0; t < NT; ++t)
-                if (tok0 + t < (int)J.B) J.out[(long long)(tok0 + t) * J.ldo + r0 + row] = acc[t];
+                if (tok0 + t < B) out[(long long)(tok0 + t) * ldo + r0 + row] = acc[t];
+    }
+}
+
+// A 16-byte aligned Q4_K/Q5_K super-block (shared-memory offset sb) into the
+// stage's 8 operand tiles (row offset arow) and scales (srow): the element
+// order of quant_decode.cuh decode_unit, read with 128-bit loads.
+template <uint32_t TYPE>
+__device__ __forceinline__ void decode_k45_aligned(uint8_t* sm, uint32_t sb, uint32_t arow, uint32_t srow)
+{
+    const uint4 hdr = *reinterpret_cast<const uint4*>(sm + sb);
+    const float d = h2f_ref(hdr.x & 0xFFFFu), dmin = h2f_ref(hdr.x >> 16);
+    uint4 qh0 = make_uint4(0, 0, 0, 0), qh1 = qh0;
+    if (TYPE == T_Q5_K) {
+        qh0 = *reinterpret_cast<const uint4*>(sm + sb + 16);
+        qh1 = *reinterpret_cast<const uint4*>(sm + sb + 32);
+    }
+    const uint32_t qs = sb + (TYPE == T_Q4_K ? 16u : 48u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t scb = ((j < 4 ? hdr.y : hdr.z) >> (8 * (j & 3))) & 0xFFu;
+        const float sc = __fmul_rn((float)(scb & 63u), d);   // src/quant.c:385
+        const float m = __fmul_rn((float)(scb >> 6), dmin);  // src/quant.c:386
+        const uint4 q = *reinterpret_cast<const uint4*>(sm + qs + 16 * j);
+        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        uint32_t wq[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            wq[2 * i] = qw[i] & 0x0F0F0F0Fu;
+            wq[2 * i + 1] = (qw[i] >> 4) & 0x0F0F0F0Fu;
+        }
+        if (TYPE == T_Q5_K) {
+            const uint32_t H = (j < 4) ? (j == 0 ? qh0.x : j == 1 ? qh0.y : j == 2 ? qh0.z : qh0.w)
+                                       : (j == 4 ? qh1.x : j == 5 ? qh1.y : j == 6 ? qh1.z : qh1.w);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t hb = (H >> (8 * i)) & 0xFFu;
+                wq[2 * i] |= spread_even_bits_to_b4(hb);
+                wq[2 * i + 1] |= spread_even_bits_to_b4(hb >> 1);
+            }
+        }
+        uint4* at = reinterpret_cast<uint4*>(sm + arow + (uint32_t)j * kATile);
+        at[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
+        at[8] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
+        *reinterpret_cast<float2*>(sm + srow + (uint32_t)j * kM * 8) = make_float2(sc, m);
     }
 }
 
@@ -364,10 +471,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 }
                 const int us = min(kUS, (int)J.U - kUS * st);
                 const uint32_t abytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
+                const uint32_t wbytes = J.tma ? J.seg * (uint32_t)kM : 0u;
                 const uint32_t base = p.slot_bytes * (uint32_t)slot;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(&full_w[slot], abytes + dbytes);
+                    mbar_arrive_expect_tx(&full_w[slot], abytes + dbytes + wbytes);
                     misc[2 + slot] += 1;
+                    if (J.tma) {  // box (x = byte offset in the row, y = first row); x is a multiple of 16
+                        const int x = st * (int)J.seg, y = (i - J.item0) * kM;
+                        asm volatile(
+                            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
+                            "[%0], [%1, {%2, %3}], [%4];" ::"r"(sptr(sm + p.w_off + base)),
+                            "l"(reinterpret_cast<uint64_t>(&p.tmap[jc])), "r"(x), "r"(y), "r"(sptr(&full_w[slot]))
+                            : "memory");
+                    }
                     bulk_g2s(sm + p.b_off + base, J.act + (size_t)kUS * st * J.N * 32, abytes, &full_w[slot]);
                     bulk_g2s(sm + p.d_off + base, J.ds + (size_t)kUS * st * J.N * 16, dbytes, &full_w[slot]);
                 }
@@ -377,45 +493,40 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         }
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
-        if (lane == 0) {
-            int gs = 0, gu = 0, jc = 0, last_b = -1, last_ph = 0;
-            bool ok = true;
-            for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
-                jc = job_of(jobs, p.njobs, i, jc);
-                const TcJob& J = jobs[jc];
-                for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-                    const int slot = gs % S, use = gs / S;
-                    if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
-                        !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    const uint32_t base = p.slot_bytes * (uint32_t)slot;
-                    const int us = min(kUS, (int)J.U - kUS * st);
-                    for (int j = 0; j < us; ++j, ++gu) {
-                        const int b = gu % NB;
-                        if (gu >= NB) {
-                            if (!mbar_wait_bounded(&t_empty[b], ((gu / NB) - 1) & 1, p.err, abort_flag)) {
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                        }
+        // The whole warp walks the stages (converged); one elected lane issues.
+        int gs = 0, jc = 0, last_sb = -1, last_ph = 0;
+        bool ok = true;
+        for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
+            jc = job_of(jobs, p.njobs, i, jc);
+            const TcJob& J = jobs[jc];
+            for (int st = 0; st < (int)J.nst; ++st, ++gs) {
+                const int slot = gs % S, use = gs / S, sb = gs % NB;
+                if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
+                    !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag) ||
+                    (gs >= NB && !mbar_wait_bounded(&t_empty[sb], ((gs / NB) - 1) & 1, p.err, abort_flag))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                __syncwarp();
+                const uint32_t base = p.slot_bytes * (uint32_t)slot;
+                const int us = min(kUS, (int)J.U - kUS * st);
+                if (elect_one()) {
+                    for (int j = 0; j < us; ++j) {
                         const uint64_t ad = smem_desc(sptr(sm + p.a_off + base + (uint32_t)j * kATile));
                         const uint64_t bd = smem_desc(sptr(sm + p.b_off + base + (uint32_t)(j * (int)J.N) * 32u));
-                        tc_mma(tmem + (uint32_t)(b * (int)p.ncol), ad, bd, J.idesc);
-                        tc_commit(&t_full[b]);
-                        last_b = b;
-                        last_ph = (gu / NB) & 1;
+                        tc_mma(tmem + (uint32_t)(sb * kUS * (int)p.ncol + j * (int)J.N), ad, bd, J.idesc);
                     }
-                    if (!ok) break;
+                    tc_commit(&t_full[sb]);
                     tc_commit(&st_free[slot]);
                 }
+                __syncwarp();
+                last_sb = sb;
+                last_ph = (gs / NB) & 1;
             }
-            // The MMAs issued last complete before TMEM is released.
-            if (last_b >= 0) mbar_wait_bounded(&t_full[last_b], (uint32_t)last_ph, nullptr);
         }
+        // The MMAs issued last complete before TMEM is released.
+        if (last_sb >= 0) mbar_wait_bounded(&t_full[last_sb], (uint32_t)last_ph, nullptr);
         __syncwarp();
     } else if (warp < 2 + kDecWarps) {
         // ------------------------------------------------------ decoders --
@@ -439,8 +550,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         if (valid(first)) first.jc = job_of(jobs, p.njobs, first.i, 0);
         bool ok = true;
         // Issues stage g (at position q): after the slot's previous use is
-        // released, 16-byte async copies of this row's aligned segment cover;
-        // one commit group per stage (empty when there is nothing to fetch).
+        // released, 16-byte async copies of every row's aligned segment cover,
+        // the 128 decoder threads walking (row, chunk) pairs chunk-fastest so
+        // a warp instruction reads a few rows' contiguous bytes; one commit
+        // group per stage (empty when there is nothing to fetch).
+        const int dtid = (warp - 2) * 32 + lane;
         auto issue = [&](const Pos& q, int g) {
             if (valid(q)) {
                 const int slot = g % S, use = g / S;
@@ -448,14 +562,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 const TcJob& J = jobs[q.jc];
                 const int r0 = (q.i - J.item0) * kM;
                 const int rows = min(kM, (int)J.n - r0);
-                if (ok && row < rows) {
-                    const int us = min(kUS, (int)J.U - kUS * q.st);
-                    const uint32_t segb = J.type == T_Q8_0 ? (uint32_t)us * 34u : J.seg;
-                    const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)q.st * J.seg);
+                const int us = min(kUS, (int)J.U - kUS * q.st);
+                const uint32_t segb = J.type == T_Q8_0 ? (uint32_t)us * 34u : J.seg;
+                const int cpr = (int)((segb + 30) >> 4);  // chunk slots per row (>= any row's cover)
+                const uint32_t dst0 = sptr(sm + p.w_off + p.slot_bytes * (uint32_t)slot);
+                const uint8_t* src0 = J.w + (long long)r0 * J.rb + (long long)q.st * J.seg;
+                for (int f = dtid; ok && !J.tma && f < rows * cpr; f += kDecWarps * 32) {
+                    const int r = f / cpr, c = f - r * cpr;
+                    const uintptr_t a = (uintptr_t)(src0 + (long long)r * J.rb);
                     const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + segb + 15) & ~(uintptr_t)15;
-                    const uint32_t dst = sptr(sm + p.w_off + p.slot_bytes * (uint32_t)slot + (uint32_t)row * p.segp);
-                    for (uintptr_t off = a0; off < a1; off += 16)
-                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + (uint32_t)(off - a0)),
+                    const uintptr_t off = a0 + 16 * (uintptr_t)c;
+                    if (off < a1)
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst0 + (uint32_t)r * p.segp +
+                                                                                       16u * (uint32_t)c),
                                      "l"(off)
                                      : "memory");
                 }
@@ -472,10 +591,24 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             }
         }
         int gs = 0;
-        for (Pos cur = first; ok && valid(cur); cur = next(cur), ++gs) {
+        for (Pos cur = first; valid(cur); cur = next(cur), ++gs) {
             // This stage's group is the oldest not yet waited for.
             if (S == 3) asm volatile("cp.async.wait_group 1;" ::: "memory");
             else asm volatile("cp.async.wait_group 0;" ::: "memory");
+            // TMA-fetched weights arrive on the slot's full barrier.
+            if (jobs[cur.jc].tma && ok && !mbar_wait_bounded(&full_w[gs % S], (gs / S) & 1, p.err, abort_flag))
+                ok = false;
+            // Every decoder thread's copies of this stage have landed; the
+            // decoders stop together if any of them gave up on a wait.
+            uint32_t all_ok;
+            asm volatile(
+                "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\t"
+                "bar.red.and.pred b, 1, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}\n"
+                : "=r"(all_ok)
+                : "r"(ok ? 1u : 0u)
+                : "memory");
+            static_assert(kDecWarps * 32 == 128, "named barrier 1 counts the decoder threads");
+            if (!all_ok) break;
             const TcJob& J = jobs[cur.jc];
             const int slot = gs % S;
             const uint32_t base = p.slot_bytes * (uint32_t)slot;
@@ -484,9 +617,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             const int us = min(kUS, (int)J.U - kUS * cur.st);
             if (row < rows) {
                 const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
-                const uint32_t seg0 = p.w_off + base + (uint32_t)row * p.segp + (uint32_t)(a & 15);
+                const uint32_t seg0 = J.tma ? p.w_off + base + (uint32_t)row * J.seg
+                                            : p.w_off + base + (uint32_t)row * p.segp + (uint32_t)(a & 15);
                 const uint32_t arow = p.a_off + base + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
-                for (int j = 0; j < us; ++j) {
+                const uint32_t srow = p.s_off + base + (uint32_t)row * 8;
+                if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
+                else if (J.type == T_Q5_K && (a & 15) == 0) decode_k45_aligned<T_Q5_K>(sm, seg0, arow, srow);
+                else for (int j = 0; j < us; ++j) {
                     Unit o;
                     switch (J.type) {
                     case T_Q4_K: decode_unit<T_Q4_K>(s32, sm, seg0, j, o); break;
@@ -660,9 +797,9 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.total_items = item;
     pp.S = (uint32_t)S;
     pp.ncol = (uint32_t)Nmax;
-    pp.NB = (uint32_t)std::min(kMaxNB, 512 / Nmax);
+    pp.NB = (uint32_t)std::min(kMaxNB, 512 / (kUS * Nmax));  // 4, 2 or 1 stage buffers for N = 16, 32, 64
     uint32_t cols = 32;
-    while (cols < pp.NB * pp.ncol) cols <<= 1;
+    while (cols < pp.NB * kUS * pp.ncol) cols <<= 1;
     pp.tmem_cols = cols;
     pp.segp = segp;
     pp.slot_bytes = slot;
@@ -700,6 +837,41 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         return code;
     }
     pp.jobs = P->d_jobs;
+    // 2-D TMA maps for the jobs whose rows are 16-byte aligned (Q4_K, Q5_K);
+    // the others (and all jobs, if the driver entry point is unavailable)
+    // keep the per-thread async copies.
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static bool looked_up = false;
+    if (!looked_up) {
+        looked_up = true;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&encode, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            encode = nullptr;
+        cudaGetLastError();
+    }
+    bool any_tma = false;
+    for (size_t j = 0; j < P->jobs.size(); ++j) {
+        TcJob& J = P->jobs[j];
+        J.tma = 0;
+        if (!encode || (J.type != T_Q4_K && J.type != T_Q5_K) || (J.rb % 16) != 0) continue;
+        const cuuint64_t dims[2] = {(cuuint64_t)J.rb, (cuuint64_t)J.n};
+        const cuuint64_t strides[1] = {(cuuint64_t)J.rb};
+        const cuuint32_t box[2] = {J.seg, (cuuint32_t)kM};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&pp.tmap[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(J.w), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+            J.tma = 1;
+            any_tma = true;
+        }
+    }
+    if (any_tma && cudaMemcpy(P->d_jobs, P->jobs.data(), P->jobs.size() * sizeof(TcJob), cudaMemcpyHostToDevice) !=
+                       cudaSuccess) {
+        cudaGetLastError();
+        tc_plan_destroy(P);
+        return QUANTR_ERR_CUDA;
+    }
     P->qp.tasks = P->d_tasks;
     P->qp.ntasks = (int)P->tasks.size();
     P->qp.total = blocks;

@@ -1,4 +1,4 @@
-"""GPU: programs of 9..64-token GEMVs, which run on the tensor cores
+"""GPU: programs of 5..64-token GEMVs, which run on the tensor cores
 (tcgen05.mma kind::i8 per 32-element unit, exact terms and running sums from
 TMEM), against the oracle.  Bit-identical to the reference's scalar build, like
 every other path (the north-star tolerance 1e-5 rel / 1e-6 abs is asserted too).
@@ -55,7 +55,7 @@ def run(prog):
 
 @pytest.mark.parametrize("type_,n,d", [(Q4_K, 257, 2048), (Q5_K, 130, 2048), (Q6_K, 200, 1408), (Q8_0, 129, 288),
                                        (Q8_0, 300, 2048), (Q6_K, 64, 256)])
-@pytest.mark.parametrize("B", [9, 16, 33, 64])
+@pytest.mark.parametrize("B", [5, 9, 16, 33, 64])
 def test_tc_types_and_batches(qr_gpu, orc, type_, n, d, B):
     """Ragged row tiles (n not a multiple of 128), Q6_K/Q8_0 rows that are
     not 16-byte aligned, a partial last stage (Q8_0 d=288: 9 blocks)."""
