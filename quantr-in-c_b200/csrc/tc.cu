@@ -13,21 +13,27 @@
 // A launch runs a list of GEMV jobs (B <= 64 tokens each, N = B rounded up
 // to 16 columns) cut into 128-row tiles, dealt round-robin to one persistent
 // CTA per SM.  A tile's K dimension streams in stages of 8 units (one K-quant
-// super-block, or 8 Q8_0 blocks) through S shared-memory slots:
+// super-block, or 8 Q8_0 blocks) through two shared-memory rings: SW slots of
+// packed weights (deep, so that fetch latency hides behind several stages) and
+// SO slots of MMA operands (unpacked weight tiles, scales, activation tiles):
 //
-//   producer (warp 0)    per stage: two cp.async.bulk copies, the stage's
-//                        activation operand tiles and per-(unit, token) scale
-//                        records, on one mbarrier transaction count;
+//   producer (warp 0)    lane 0, per stage: one 2-D TMA copy of the tile's
+//                        packed weights (128 rows x one stage of bytes) for
+//                        jobs whose rows are 16-byte aligned (Q4_K, Q5_K);
+//                        lane 1, per stage: two cp.async.bulk copies, the
+//                        stage's activation operand tiles and per-(unit,
+//                        token) scale records;
 //   MMA (warp 1)         per unit: tcgen05.mma (issued by one elected lane of
 //                        the converged warp) into the stage's TMEM buffer (one
 //                        of NBS, 8 units x N columns each); after the stage,
 //                        one commit to the buffer's barrier and one that frees
 //                        the slot's operands;
-//   decoders (4 warps)   fetch the tile's packed bytes for the stage together
-//                        (16-byte cp.async of each row's aligned segment cover,
-//                        consecutive threads on consecutive chunks of a row,
-//                        S-1 stages ahead, one async-copy group per stage, a
-//                        named barrier before use), then one thread per row
+//   decoders (4 warps)   for the other jobs, fetch the tile's packed bytes for
+//                        the stage together (16-byte cp.async of each row's
+//                        aligned segment cover, consecutive threads on
+//                        consecutive chunks of a row, SW-1 stages ahead, one
+//                        async-copy group per stage, a named barrier before
+//                        use); then one thread per row
 //                        unpacks each unit's quants into the canonical K-major
 //                        no-swizzle operand layout (8x16-byte core matrices)
 //                        and the unit's scales;
@@ -67,7 +73,8 @@ constexpr int kDecWarps = 4;   // one decoder thread per tile row
 constexpr int kEpiWarps = 8;   // 4 lane quarters x 2 token halves
 constexpr int kWarps = 2 + kDecWarps + kEpiWarps;
 constexpr int kThreads = 32 * kWarps;
-constexpr int kMaxSlots = 3;
+constexpr int kMaxSW = 8;      // packed-weight slots
+constexpr int kMaxSO = 2;      // operand slots
 constexpr int kMaxNB = 4;      // TMEM stage buffers
 constexpr int kMaxN = kTcMaxB; // tokens per job (MMA N after padding)
 constexpr size_t kSmemMax = 227 * 1024;
@@ -92,9 +99,12 @@ static_assert(sizeof(TcJob) % 16 == 0, "job table is copied in 16-byte words");
 struct TcParams {
     const TcJob* jobs;
     int njobs, total_items;
-    uint32_t S, NB, ncol, tmem_cols;      // slots, TMEM stage buffers, max N (columns per unit), allocated columns
-    uint32_t segp;                        // staging bytes per row per slot
-    uint32_t w_off, a_off, b_off, d_off, s_off, slot_bytes, jobs_off;
+    uint32_t SW, SO, NB, ncol, tmem_cols;  // weight slots, operand slots, TMEM stage buffers, max N, TMEM columns
+    uint32_t segp;                         // staging bytes per row of a weight slot (cp.async jobs)
+    uint32_t w_off, w_slot;                // weight ring: first slot, bytes per slot
+    uint32_t o_off, o_slot;                // operand ring: first slot, bytes per slot
+    uint32_t a_rel, b_rel, d_rel, s_rel;   // A tiles, B tiles, records, scales within an operand slot
+    uint32_t jobs_off;
     int* err;
     // Per job with tma set: rows x row-bytes uint8 view of the packed weights,
     // box = 128 rows x one stage's bytes (passed by value: TMA reads the map
@@ -305,15 +315,17 @@ __device__ __forceinline__ void epi_stage(uint32_t tbase, uint32_t sbase, uint32
     }
 }
 
+struct Bars {
+    uint64_t *wfull, *wempty, *bfull, *afull, *ofree, *t_full, *t_empty;
+};
+
 template <int NT>
-__device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, uint64_t* full_w,
-                                              uint64_t* a_ready, uint64_t* st_free, uint64_t* t_full,
-                                              uint64_t* t_empty, volatile int* abort_flag, uint32_t tmem, int warp,
-                                              int lane)
+__device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, const Bars& br,
+                              volatile int* abort_flag, uint32_t tmem, int warp, int lane)
 {
     const int quarter = warp & 3, half = (warp - 2 - kDecWarps) >> 2;
     const int row = 32 * quarter + lane;
-    const int S = (int)p.S, NB = (int)p.NB;
+    const int SO = (int)p.SO, NB = (int)p.NB;
     const uint32_t smb = sptr(sm);
     int gs = 0, jc = 0;
     bool ok = true;
@@ -331,30 +343,30 @@ __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs,
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
         for (int st = 0; st < nst; ++st, ++gs) {
-            const int slot = gs % S, use = gs / S, sb = gs % NB;
-            if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
-                !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag) ||
-                !mbar_wait_bounded(&t_full[sb], (gs / NB) & 1, p.err, abort_flag)) {
+            const int os = gs % SO, ou = gs / SO, sb = gs % NB;
+            if (!mbar_wait_bounded(&br.bfull[os], ou & 1, p.err, abort_flag) ||
+                !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag) ||
+                !mbar_wait_bounded(&br.t_full[sb], (gs / NB) & 1, p.err, abort_flag)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t sbase = smb + p.slot_bytes * (uint32_t)slot;
+            const uint32_t obase = smb + p.o_off + p.o_slot * (uint32_t)os;
             const int us = min(kUS, U - kUS * st);
             const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(sb * kUS * (int)p.ncol + tok0);
             if (tok0 < B) {
                 switch (type) {
-                case T_Q4_K: epi_stage<T_Q4_K, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
-                case T_Q5_K: epi_stage<T_Q5_K, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
-                case T_Q6_K: epi_stage<T_Q6_K, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
-                default: epi_stage<T_Q8_0, NT>(tbase, sbase, p.s_off, p.d_off, N, us, row, tok0, acc); break;
+                case T_Q4_K: epi_stage<T_Q4_K, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
+                case T_Q5_K: epi_stage<T_Q5_K, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
+                case T_Q6_K: epi_stage<T_Q6_K, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
+                default: epi_stage<T_Q8_0, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&t_empty[sb]);
-                mbar_arrive(&st_free[slot]);
+                mbar_arrive(&br.t_empty[sb]);
+                mbar_arrive(&br.ofree[os]);
             }
         }
         if (!ok) break;
@@ -409,29 +421,54 @@ __device__ __forceinline__ void decode_k45_aligned(uint8_t* sm, uint32_t sb, uin
     }
 }
 
+// cp.async.wait_group with the immediate n = SW - 2 (all but the newest
+// SW - 2 groups complete).
+__device__ __forceinline__ void wait_groups_but(int n)
+{
+    switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    }
+}
+
 __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constant__ TcParams p)
 {
     extern __shared__ __align__(1024) uint8_t sm[];
-    uint64_t* full_w = reinterpret_cast<uint64_t*>(sm);
-    uint64_t* a_ready = full_w + kMaxSlots;
-    uint64_t* st_free = a_ready + kMaxSlots;
-    uint64_t* t_full = st_free + kMaxSlots;
-    uint64_t* t_empty = t_full + kMaxNB;
-    uint32_t* misc = reinterpret_cast<uint32_t*>(t_empty + kMaxNB);  // [0] TMEM base, [1] abort, [2..] fills
+    Bars br;
+    br.wfull = reinterpret_cast<uint64_t*>(sm);
+    br.wempty = br.wfull + kMaxSW;
+    br.bfull = br.wempty + kMaxSW;
+    br.afull = br.bfull + kMaxSO;
+    br.ofree = br.afull + kMaxSO;
+    br.t_full = br.ofree + kMaxSO;
+    br.t_empty = br.t_full + kMaxNB;
+    // [0] TMEM base, [1] abort, [2..2+kMaxSW) TMA fills per weight slot,
+    // [2+kMaxSW..) bulk fills per operand slot.
+    uint32_t* misc = reinterpret_cast<uint32_t*>(br.t_empty + kMaxNB);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int S = (int)p.S, NB = (int)p.NB;
+    const int SW = (int)p.SW, SO = (int)p.SO, NB = (int)p.NB;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; ++s) {
-            mbar_init(&full_w[s], 1);
-            mbar_init(&a_ready[s], kDecWarps);
-            mbar_init(&st_free[s], 1 + kDecWarps + kEpiWarps);
+        for (int s = 0; s < SW; ++s) {
+            mbar_init(&br.wfull[s], 1);
+            mbar_init(&br.wempty[s], kDecWarps);
             misc[2 + s] = 0;
         }
+        for (int s = 0; s < SO; ++s) {
+            mbar_init(&br.bfull[s], 1);
+            mbar_init(&br.afull[s], kDecWarps);
+            mbar_init(&br.ofree[s], 1 + kEpiWarps);
+            misc[2 + kMaxSW + s] = 0;
+        }
         for (int b = 0; b < NB; ++b) {
-            mbar_init(&t_full[b], 1);
-            mbar_init(&t_empty[b], kEpiWarps);
+            mbar_init(&br.t_full[b], 1);
+            mbar_init(&br.t_empty[b], kEpiWarps);
         }
         misc[1] = 0;
         mbar_fence_init();
@@ -457,40 +494,60 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
 
     if (warp == 0) {
         // ------------------------------------------------------ producer --
-        pdl_wait();  // activations come from the quantizer grid
-        int gs = 0, jc = 0;
-        for (int i = blockIdx.x; i < p.total_items; i += gridDim.x) {
-            jc = job_of(jobs, p.njobs, i, jc);
-            const TcJob& J = jobs[jc];
-            bool stop = false;
-            for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-                const int slot = gs % S, use = gs / S;
-                if (use > 0 && !mbar_wait_bounded(&st_free[slot], (use - 1) & 1, p.err, abort_flag)) {
-                    stop = true;
-                    break;
-                }
-                const int us = min(kUS, (int)J.U - kUS * st);
-                const uint32_t abytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
-                const uint32_t wbytes = J.tma ? J.seg * (uint32_t)kM : 0u;
-                const uint32_t base = p.slot_bytes * (uint32_t)slot;
-                if (lane == 0) {
-                    mbar_arrive_expect_tx(&full_w[slot], abytes + dbytes + wbytes);
-                    misc[2 + slot] += 1;
-                    if (J.tma) {  // box (x = byte offset in the row, y = first row); x is a multiple of 16
+        if (lane == 0) {
+            // Weight ring: waits for every stage's slot (so it never runs more
+            // than SW stages ahead of the decoders), copies the TMA jobs'.
+            // Weights do not depend on the previous grid: no PDL wait.
+            int gs = 0, jc = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
+                jc = job_of(jobs, p.njobs, i, jc);
+                const TcJob& J = jobs[jc];
+                for (int st = 0; st < (int)J.nst; ++st, ++gs) {
+                    const int ws = gs % SW, wu = gs / SW;
+                    if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    misc[2 + ws] += 1;  // one arrival per use keeps the slot's phases = its uses
+                    if (!J.tma) {
+                        mbar_arrive(&br.wfull[ws]);  // the decoders fetch this stage themselves
+                    } else {  // box (x = byte offset in the row, a multiple of 16; y = first row)
+                        mbar_arrive_expect_tx(&br.wfull[ws], J.seg * (uint32_t)kM);
                         const int x = st * (int)J.seg, y = (i - J.item0) * kM;
                         asm volatile(
                             "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes "
-                            "[%0], [%1, {%2, %3}], [%4];" ::"r"(sptr(sm + p.w_off + base)),
-                            "l"(reinterpret_cast<uint64_t>(&p.tmap[jc])), "r"(x), "r"(y), "r"(sptr(&full_w[slot]))
+                            "[%0], [%1, {%2, %3}], [%4];" ::"r"(sptr(sm + p.w_off + p.w_slot * (uint32_t)ws)),
+                            "l"(reinterpret_cast<uint64_t>(&p.tmap[jc])), "r"(x), "r"(y), "r"(sptr(&br.wfull[ws]))
                             : "memory");
                     }
-                    bulk_g2s(sm + p.b_off + base, J.act + (size_t)kUS * st * J.N * 32, abytes, &full_w[slot]);
-                    bulk_g2s(sm + p.d_off + base, J.ds + (size_t)kUS * st * J.N * 16, dbytes, &full_w[slot]);
                 }
-                __syncwarp();
             }
-            if (stop) break;
+        } else if (lane == 1) {
+            // Operand ring: activation tiles and records of each stage.
+            pdl_wait();  // activations come from the quantizer grid
+            int gs = 0, jc = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
+                jc = job_of(jobs, p.njobs, i, jc);
+                const TcJob& J = jobs[jc];
+                for (int st = 0; st < (int)J.nst; ++st, ++gs) {
+                    const int os = gs % SO, ou = gs / SO;
+                    if (ou > 0 && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const int us = min(kUS, (int)J.U - kUS * st);
+                    const uint32_t abytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
+                    uint8_t* obase = sm + p.o_off + p.o_slot * (uint32_t)os;
+                    mbar_arrive_expect_tx(&br.bfull[os], abytes + dbytes);
+                    misc[2 + kMaxSW + os] += 1;
+                    bulk_g2s(obase + p.b_rel, J.act + (size_t)kUS * st * J.N * 32, abytes, &br.bfull[os]);
+                    bulk_g2s(obase + p.d_rel, J.ds + (size_t)kUS * st * J.N * 16, dbytes, &br.bfull[os]);
+                }
+            }
         }
+        __syncwarp();
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
         // The whole warp walks the stages (converged); one elected lane issues.
@@ -500,25 +557,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             jc = job_of(jobs, p.njobs, i, jc);
             const TcJob& J = jobs[jc];
             for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-                const int slot = gs % S, use = gs / S, sb = gs % NB;
-                if (!mbar_wait_bounded(&full_w[slot], use & 1, p.err, abort_flag) ||
-                    !mbar_wait_bounded(&a_ready[slot], use & 1, p.err, abort_flag) ||
-                    (gs >= NB && !mbar_wait_bounded(&t_empty[sb], ((gs / NB) - 1) & 1, p.err, abort_flag))) {
+                const int os = gs % SO, ou = gs / SO, sb = gs % NB;
+                if (!mbar_wait_bounded(&br.bfull[os], ou & 1, p.err, abort_flag) ||
+                    !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag) ||
+                    (gs >= NB && !mbar_wait_bounded(&br.t_empty[sb], ((gs / NB) - 1) & 1, p.err, abort_flag))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 __syncwarp();
-                const uint32_t base = p.slot_bytes * (uint32_t)slot;
+                const uint32_t obase = p.o_off + p.o_slot * (uint32_t)os;
                 const int us = min(kUS, (int)J.U - kUS * st);
                 if (elect_one()) {
                     for (int j = 0; j < us; ++j) {
-                        const uint64_t ad = smem_desc(sptr(sm + p.a_off + base + (uint32_t)j * kATile));
-                        const uint64_t bd = smem_desc(sptr(sm + p.b_off + base + (uint32_t)(j * (int)J.N) * 32u));
+                        const uint64_t ad = smem_desc(sptr(sm + obase + p.a_rel + (uint32_t)j * kATile));
+                        const uint64_t bd = smem_desc(sptr(sm + obase + p.b_rel + (uint32_t)(j * (int)J.N) * 32u));
                         tc_mma(tmem + (uint32_t)(sb * kUS * (int)p.ncol + j * (int)J.N), ad, bd, J.idesc);
                     }
-                    tc_commit(&t_full[sb]);
-                    tc_commit(&st_free[slot]);
+                    tc_commit(&br.t_full[sb]);
+                    tc_commit(&br.ofree[os]);
                 }
                 __syncwarp();
                 last_sb = sb;
@@ -526,14 +583,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             }
         }
         // The MMAs issued last complete before TMEM is released.
-        if (last_sb >= 0) mbar_wait_bounded(&t_full[last_sb], (uint32_t)last_ph, nullptr);
+        if (last_sb >= 0) mbar_wait_bounded(&br.t_full[last_sb], (uint32_t)last_ph, nullptr);
         __syncwarp();
     } else if (warp < 2 + kDecWarps) {
         // ------------------------------------------------------ decoders --
         const int row = (warp - 2) * 32 + lane;
         const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
         // Stage positions (item, stage within item, job) walked twice: once
-        // to issue a stage's copies S-1 stages ahead, once to decode it.
+        // to issue a stage's copies SW-1 stages ahead, once to decode it.
         struct Pos {
             int i, st, jc;
         };
@@ -549,25 +606,25 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         Pos first{(int)blockIdx.x, 0, 0};
         if (valid(first)) first.jc = job_of(jobs, p.njobs, first.i, 0);
         bool ok = true;
-        // Issues stage g (at position q): after the slot's previous use is
-        // released, 16-byte async copies of every row's aligned segment cover,
-        // the 128 decoder threads walking (row, chunk) pairs chunk-fastest so
-        // a warp instruction reads a few rows' contiguous bytes; one commit
-        // group per stage (empty when there is nothing to fetch).
+        // Issues stage g (at position q) of a job without a TMA map: after the
+        // weight slot's previous use is released, 16-byte async copies of
+        // every row's aligned segment cover, the 128 decoder threads walking
+        // (row, chunk) pairs chunk-fastest so a warp instruction reads a few
+        // rows' contiguous bytes; one commit group per stage, empty otherwise.
         const int dtid = (warp - 2) * 32 + lane;
         auto issue = [&](const Pos& q, int g) {
-            if (valid(q)) {
-                const int slot = g % S, use = g / S;
-                if (use > 0 && !mbar_wait_bounded(&st_free[slot], (use - 1) & 1, p.err, abort_flag)) ok = false;
+            if (valid(q) && !jobs[q.jc].tma) {
+                const int ws = g % SW, wu = g / SW;
+                if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag)) ok = false;
                 const TcJob& J = jobs[q.jc];
                 const int r0 = (q.i - J.item0) * kM;
                 const int rows = min(kM, (int)J.n - r0);
                 const int us = min(kUS, (int)J.U - kUS * q.st);
                 const uint32_t segb = J.type == T_Q8_0 ? (uint32_t)us * 34u : J.seg;
                 const int cpr = (int)((segb + 30) >> 4);  // chunk slots per row (>= any row's cover)
-                const uint32_t dst0 = sptr(sm + p.w_off + p.slot_bytes * (uint32_t)slot);
+                const uint32_t dst0 = sptr(sm + p.w_off + p.w_slot * (uint32_t)ws);
                 const uint8_t* src0 = J.w + (long long)r0 * J.rb + (long long)q.st * J.seg;
-                for (int f = dtid; ok && !J.tma && f < rows * cpr; f += kDecWarps * 32) {
+                for (int f = dtid; ok && f < rows * cpr; f += kDecWarps * 32) {
                     const int r = f / cpr, c = f - r * cpr;
                     const uintptr_t a = (uintptr_t)(src0 + (long long)r * J.rb);
                     const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + segb + 15) & ~(uintptr_t)15;
@@ -583,7 +640,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         };
         Pos iss = first;
         int gi = 0;
-        for (int k = 0; k < S - 1; ++k) {  // prologue: S-1 groups, real or empty
+        for (int k = 0; k < SW - 1; ++k) {  // prologue: SW-1 groups, real or empty
             issue(iss, gi);
             if (valid(iss)) {
                 iss = next(iss);
@@ -592,12 +649,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         }
         int gs = 0;
         for (Pos cur = first; valid(cur); cur = next(cur), ++gs) {
-            // This stage's group is the oldest not yet waited for.
-            if (S == 3) asm volatile("cp.async.wait_group 1;" ::: "memory");
-            else asm volatile("cp.async.wait_group 0;" ::: "memory");
-            // TMA-fetched weights arrive on the slot's full barrier.
-            if (jobs[cur.jc].tma && ok && !mbar_wait_bounded(&full_w[gs % S], (gs / S) & 1, p.err, abort_flag))
-                ok = false;
+            const TcJob& J = jobs[cur.jc];
+            const int ws = gs % SW, os = gs % SO, ou = gs / SO;
+            wait_groups_but(SW - 2);  // this stage's group is the oldest not yet waited for
+            if (J.tma && ok && !mbar_wait_bounded(&br.wfull[ws], (gs / SW) & 1, p.err, abort_flag)) ok = false;
+            // The operand slot's previous stage is consumed (MMAs done, epilogue done).
+            if (ou > 0 && ok && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag)) ok = false;
             // Every decoder thread's copies of this stage have landed; the
             // decoders stop together if any of them gave up on a wait.
             uint32_t all_ok;
@@ -609,18 +666,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 : "memory");
             static_assert(kDecWarps * 32 == 128, "named barrier 1 counts the decoder threads");
             if (!all_ok) break;
-            const TcJob& J = jobs[cur.jc];
-            const int slot = gs % S;
-            const uint32_t base = p.slot_bytes * (uint32_t)slot;
+            const uint32_t wbase = p.w_off + p.w_slot * (uint32_t)ws, obase = p.o_off + p.o_slot * (uint32_t)os;
             const int r0 = (cur.i - J.item0) * kM;
             const int rows = min(kM, (int)J.n - r0);
             const int us = min(kUS, (int)J.U - kUS * cur.st);
             if (row < rows) {
                 const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
-                const uint32_t seg0 = J.tma ? p.w_off + base + (uint32_t)row * J.seg
-                                            : p.w_off + base + (uint32_t)row * p.segp + (uint32_t)(a & 15);
-                const uint32_t arow = p.a_off + base + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
-                const uint32_t srow = p.s_off + base + (uint32_t)row * 8;
+                const uint32_t seg0 = J.tma ? wbase + (uint32_t)row * J.seg
+                                            : wbase + (uint32_t)row * p.segp + (uint32_t)(a & 15);
+                const uint32_t arow = obase + p.a_rel + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
+                const uint32_t srow = obase + p.s_rel + (uint32_t)row * 8;
                 if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
                 else if (J.type == T_Q5_K && (a & 15) == 0) decode_k45_aligned<T_Q5_K>(sm, seg0, arow, srow);
                 else for (int j = 0; j < us; ++j) {
@@ -634,17 +689,16 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                     uint4* at = reinterpret_cast<uint4*>(sm + arow + (uint32_t)j * kATile);
                     at[0] = make_uint4(o.wq[0], o.wq[1], o.wq[2], o.wq[3]);
                     at[8] = make_uint4(o.wq[4], o.wq[5], o.wq[6], o.wq[7]);  // + 128 bytes: second K half
-                    *reinterpret_cast<float2*>(sm + p.s_off + base + (uint32_t)(j * kM + row) * 8) =
-                        make_float2(o.a, o.b);
+                    *reinterpret_cast<float2*>(sm + srow + (uint32_t)j * kM * 8) = make_float2(o.a, o.b);
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // operand stores -> tensor core
             __syncwarp();
             if (lane == 0) {
-                mbar_arrive(&a_ready[slot]);
-                mbar_arrive(&st_free[slot]);
+                mbar_arrive(&br.afull[os]);
+                mbar_arrive(&br.wempty[ws]);
             }
-            issue(iss, gi);  // stage gs + S - 1 (its slot's previous use is stage gs - 1)
+            issue(iss, gi);  // stage gs + SW - 1 (its weight slot's previous use is stage gs - 1)
             if (valid(iss)) {
                 iss = next(iss);
                 ++gi;
@@ -654,25 +708,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     } else {
         // ------------------------------------------------------ epilogue --
         switch (p.ncol) {
-        case 16:
-            epilogue_role<8>(sm, p, jobs, full_w, a_ready, st_free, t_full, t_empty, abort_flag, tmem, warp, lane);
-            break;
-        case 32:
-            epilogue_role<16>(sm, p, jobs, full_w, a_ready, st_free, t_full, t_empty, abort_flag, tmem, warp, lane);
-            break;
-        default:
-            epilogue_role<32>(sm, p, jobs, full_w, a_ready, st_free, t_full, t_empty, abort_flag, tmem, warp, lane);
-            break;
+        case 16: epilogue_role<8>(sm, p, jobs, br, abort_flag, tmem, warp, lane); break;
+        case 32: epilogue_role<16>(sm, p, jobs, br, abort_flag, tmem, warp, lane); break;
+        default: epilogue_role<32>(sm, p, jobs, br, abort_flag, tmem, warp, lane); break;
         }
     }
 
     tc_fence_before();
     __syncthreads();
     if (*abort_flag && threadIdx.x == 0) {
-        // Some role gave up: let every bulk copy this CTA issued land
+        // Some role gave up: let every bulk/TMA copy this CTA issued land
         // (bounded) before its shared memory is released.
-        for (int s = 0; s < S; ++s)
-            if (misc[2 + s] > 0) mbar_wait_bounded(&full_w[s], (misc[2 + s] - 1) & 1, nullptr);
+        for (int s = 0; s < SW; ++s)
+            if (misc[2 + s] > 0) mbar_wait_bounded(&br.wfull[s], (misc[2 + s] - 1) & 1, nullptr);
+        for (int s = 0; s < SO; ++s)
+            if (misc[2 + kMaxSW + s] > 0) mbar_wait_bounded(&br.bfull[s], (misc[2 + kMaxSW + s] - 1) & 1, nullptr);
     }
     __syncthreads();
     if (warp == 1) {
@@ -779,36 +829,43 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         job_task.push_back(ti);
         P->jobs.push_back(J);
     }
-    // Shared memory: barriers | S slots of {packed rows | A tiles | B tiles | ds | scales} | job table.
-    // A row's staged copy is the 16-byte aligned cover of its segment: up to
-    // 15 bytes before it and 15 after, plus one word the decoder may read past.
+    // Shared memory: barriers | SW weight slots | SO operand slots of {A tiles
+    // | B tiles | records | scales} | job table.  A row's staged copy (cp.async
+    // jobs) is the 16-byte aligned cover of its segment: up to 15 bytes before
+    // and 15 after, plus one word the decoder may read past.
     const uint32_t segp = (segmax + 45) & ~15u;
-    const uint32_t wbytes = kM * segp, abytes = kUS * kATile, bbytes = kUS * (uint32_t)Nmax * 32u,
-                   dbytes = kUS * (uint32_t)Nmax * 16u, sbytes = kUS * kM * 8u;
-    const uint32_t slot = (wbytes + abytes + bbytes + dbytes + sbytes + 1023) & ~1023u;
+    const uint32_t wslot = (kM * segp + 1023) & ~1023u;
+    const uint32_t abytes = kUS * kATile, bbytes = kUS * (uint32_t)Nmax * 32u, dbytes = kUS * (uint32_t)Nmax * 16u,
+                   sbytes = kUS * kM * 8u;
+    const uint32_t oslot = (abytes + bbytes + dbytes + sbytes + 1023) & ~1023u;
     const uint32_t bars = 1024, tbl = ((uint32_t)(P->jobs.size() * sizeof(TcJob)) + 127) & ~127u;
-    const int S = (int)std::min<size_t>(kMaxSlots, (kSmemMax - bars - tbl) / slot);
-    if (S < 2) {
+    const int SO = kMaxSO;
+    const long long room = (long long)kSmemMax - bars - tbl - (long long)SO * oslot;
+    const int SW = room > 0 ? (int)std::min<long long>(kMaxSW, room / wslot) : 0;
+    if (SW < 2) {
         delete P;
         return QUANTR_ERR_TOO_LARGE;
     }
     TcParams& pp = P->pp;
     pp.njobs = (int)P->jobs.size();
     pp.total_items = item;
-    pp.S = (uint32_t)S;
+    pp.SW = (uint32_t)SW;
+    pp.SO = (uint32_t)SO;
     pp.ncol = (uint32_t)Nmax;
     pp.NB = (uint32_t)std::min(kMaxNB, 512 / (kUS * Nmax));  // 4, 2 or 1 stage buffers for N = 16, 32, 64
     uint32_t cols = 32;
     while (cols < pp.NB * kUS * pp.ncol) cols <<= 1;
     pp.tmem_cols = cols;
     pp.segp = segp;
-    pp.slot_bytes = slot;
     pp.w_off = bars;
-    pp.a_off = bars + wbytes;
-    pp.b_off = pp.a_off + abytes;
-    pp.d_off = pp.b_off + bbytes;
-    pp.s_off = pp.d_off + dbytes;
-    pp.jobs_off = bars + (uint32_t)S * slot;
+    pp.w_slot = wslot;
+    pp.o_off = bars + (uint32_t)SW * wslot;
+    pp.o_slot = oslot;
+    pp.a_rel = 0;
+    pp.b_rel = abytes;
+    pp.d_rel = abytes + bbytes;
+    pp.s_rel = abytes + bbytes + dbytes;
+    pp.jobs_off = pp.o_off + (uint32_t)SO * oslot;
     P->smem = pp.jobs_off + tbl;
     P->grid = std::min(device_sm_count(), item);
 
