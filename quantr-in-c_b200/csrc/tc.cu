@@ -59,9 +59,12 @@
 #include "quant_decode.cuh"
 
 #include <algorithm>
+#include <functional>
 #include <map>
 #include <new>
+#include <queue>
 #include <tuple>
+#include <utility>
 #include <vector>
 
 namespace qr {
@@ -105,6 +108,11 @@ struct TcParams {
     uint32_t o_off, o_slot;                // operand ring: first slot, bytes per slot
     uint32_t a_rel, b_rel, d_rel, s_rel;   // A tiles, B tiles, records, scales within an operand slot
     uint32_t jobs_off;
+    // Static schedule: CTA c walks entries [sched_off[c], sched_off[c + 1]) of
+    // sched, each (job << 20) | item, copied to shared memory at sched_smem.
+    const uint32_t* sched;
+    const int* sched_off;
+    uint32_t sched_smem;
     int* err;
     // Per job with tma set: rows x row-bytes uint8 view of the packed weights,
     // box = 128 rows x one stage's bytes (passed by value: TMA reads the map
@@ -248,11 +256,13 @@ __global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQPar
 
 // ---------------------------------------------------------------- kernel --
 
-__device__ __forceinline__ int job_of(const TcJob* jobs, int njobs, int item, int jc)
-{
-    while (jc + 1 < njobs && item >= jobs[jc + 1].item0) ++jc;
-    return jc;
-}
+// This CTA's schedule: entry k = (job << 20) | item.
+struct Sched {
+    const uint32_t* list;
+    int cnt;
+    __device__ __forceinline__ int item(int k) const { return (int)(list[k] & 0xFFFFFu); }
+    __device__ __forceinline__ int job(int k) const { return (int)(list[k] >> 20); }
+};
 
 // Term and running sum of one unit for this warp's NT tokens (v = the unit's
 // int32 sums from TMEM).  Padding tokens (>= B) have zero activations and
@@ -320,18 +330,18 @@ struct Bars {
 };
 
 template <int NT>
-__device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, const Bars& br,
+__device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, const Sched& sc, const Bars& br,
                               volatile int* abort_flag, uint32_t tmem, int warp, int lane)
 {
     const int quarter = warp & 3, half = (warp - 2 - kDecWarps) >> 2;
     const int row = 32 * quarter + lane;
     const int SO = (int)p.SO, NB = (int)p.NB;
     const uint32_t smb = sptr(sm);
-    int gs = 0, jc = 0;
+    int gs = 0;
     bool ok = true;
-    for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
-        jc = job_of(jobs, p.njobs, i, jc);
-        const TcJob& J = jobs[jc];
+    for (int k = 0; ok && k < sc.cnt; ++k) {
+        const int i = sc.item(k);
+        const TcJob& J = jobs[sc.job(k)];
         const int r0 = (i - J.item0) * kM;
         const int rows = min(kM, (int)J.n - r0);
         const int B = (int)J.B, N = (int)J.N, U = (int)J.U, nst = (int)J.nst;
@@ -391,13 +401,18 @@ __device__ __forceinline__ void decode_k45_aligned(uint8_t* sm, uint32_t sb, uin
         qh1 = *reinterpret_cast<const uint4*>(sm + sb + 32);
     }
     const uint32_t qs = sb + (TYPE == T_Q4_K ? 16u : 48u);
+    // Every load before the first store: the stores go through the same
+    // shared-memory pointer, so the compiler would otherwise keep each
+    // unit's load behind the previous unit's stores.
+    uint4 q8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q8[j] = *reinterpret_cast<const uint4*>(sm + qs + 16 * j);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint32_t scb = ((j < 4 ? hdr.y : hdr.z) >> (8 * (j & 3))) & 0xFFu;
         const float sc = __fmul_rn((float)(scb & 63u), d);   // src/quant.c:385
         const float m = __fmul_rn((float)(scb >> 6), dmin);  // src/quant.c:386
-        const uint4 q = *reinterpret_cast<const uint4*>(sm + qs + 16 * j);
-        const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+        const uint32_t qw[4] = {q8[j].x, q8[j].y, q8[j].z, q8[j].w};
         uint32_t wq[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -418,6 +433,22 @@ __device__ __forceinline__ void decode_k45_aligned(uint8_t* sm, uint32_t sb, uin
         at[0] = make_uint4(wq[0], wq[1], wq[2], wq[3]);
         at[8] = make_uint4(wq[4], wq[5], wq[6], wq[7]);
         *reinterpret_cast<float2*>(sm + srow + (uint32_t)j * kM * 8) = make_float2(sc, m);
+    }
+}
+
+// The us (<= 8) units of a row segment at seg0 with the generic per-unit
+// decoder (Q6_K, Q8_0 and rows that are not 16-byte aligned).
+template <uint32_t TYPE>
+__device__ __forceinline__ void decode_units(const uint32_t* s32, uint8_t* sm, uint32_t seg0, int us, uint32_t arow,
+                                             uint32_t srow)
+{
+    for (int j = 0; j < us; ++j) {
+        Unit o;
+        decode_unit<TYPE>(s32, sm, seg0, j, o);
+        uint4* at = reinterpret_cast<uint4*>(sm + arow + (uint32_t)j * kATile);
+        at[0] = make_uint4(o.wq[0], o.wq[1], o.wq[2], o.wq[3]);
+        at[8] = make_uint4(o.wq[4], o.wq[5], o.wq[6], o.wq[7]);
+        *reinterpret_cast<float2*>(sm + srow + (uint32_t)j * kM * 8) = make_float2(o.a, o.b);
     }
 }
 
@@ -479,6 +510,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         const int words = p.njobs * (int)(sizeof(TcJob) / 16);
         for (int w = threadIdx.x; w < words; w += kThreads) dst[w] = src[w];
     }
+    Sched sc;
+    {  // this CTA's schedule -> shared memory
+        const int s0 = p.sched_off[blockIdx.x];
+        sc.cnt = p.sched_off[blockIdx.x + 1] - s0;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(sm + p.sched_smem);
+        for (int w = threadIdx.x; w < sc.cnt; w += kThreads) dst[w] = p.sched[s0 + w];
+        sc.list = dst;
+    }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sptr(&misc[0])),
                      "r"(p.tmem_cols)
@@ -498,10 +537,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             // Weight ring: waits for every stage's slot (so it never runs more
             // than SW stages ahead of the decoders), copies the TMA jobs'.
             // Weights do not depend on the previous grid: no PDL wait.
-            int gs = 0, jc = 0;
+            int gs = 0;
             bool ok = true;
-            for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
-                jc = job_of(jobs, p.njobs, i, jc);
+            for (int k = 0; ok && k < sc.cnt; ++k) {
+                const int i = sc.item(k), jc = sc.job(k);
                 const TcJob& J = jobs[jc];
                 for (int st = 0; st < (int)J.nst; ++st, ++gs) {
                     const int ws = gs % SW, wu = gs / SW;
@@ -526,11 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         } else if (lane == 1) {
             // Operand ring: activation tiles and records of each stage.
             pdl_wait();  // activations come from the quantizer grid
-            int gs = 0, jc = 0;
+            int gs = 0;
             bool ok = true;
-            for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
-                jc = job_of(jobs, p.njobs, i, jc);
-                const TcJob& J = jobs[jc];
+            for (int k = 0; ok && k < sc.cnt; ++k) {
+                const TcJob& J = jobs[sc.job(k)];
                 for (int st = 0; st < (int)J.nst; ++st, ++gs) {
                     const int os = gs % SO, ou = gs / SO;
                     if (ou > 0 && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag)) {
@@ -551,11 +589,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
         // The whole warp walks the stages (converged); one elected lane issues.
-        int gs = 0, jc = 0, last_sb = -1, last_ph = 0;
+        int gs = 0, last_sb = -1, last_ph = 0;
         bool ok = true;
-        for (int i = blockIdx.x; ok && i < p.total_items; i += gridDim.x) {
-            jc = job_of(jobs, p.njobs, i, jc);
-            const TcJob& J = jobs[jc];
+        for (int k = 0; ok && k < sc.cnt; ++k) {
+            const TcJob& J = jobs[sc.job(k)];
             for (int st = 0; st < (int)J.nst; ++st, ++gs) {
                 const int os = gs % SO, ou = gs / SO, sb = gs % NB;
                 if (!mbar_wait_bounded(&br.bfull[os], ou & 1, p.err, abort_flag) ||
@@ -589,22 +626,23 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         // ------------------------------------------------------ decoders --
         const int row = (warp - 2) * 32 + lane;
         const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
-        // Stage positions (item, stage within item, job) walked twice: once
-        // to issue a stage's copies SW-1 stages ahead, once to decode it.
+        // Stage positions (schedule entry, item, job, stage within the item)
+        // walked twice: once to issue a stage's copies SW-1 stages ahead,
+        // once to decode it.
         struct Pos {
-            int i, st, jc;
+            int k, i, jc, st;
         };
-        auto valid = [&](const Pos& q) { return q.i < p.total_items; };
-        auto next = [&](Pos q) {
-            if (++q.st >= (int)jobs[q.jc].nst) {
-                q.st = 0;
-                q.i += gridDim.x;
-                if (q.i < p.total_items) q.jc = job_of(jobs, p.njobs, q.i, q.jc);
+        auto valid = [&](const Pos& q) { return q.k < sc.cnt; };
+        auto at = [&](int k) {
+            Pos q{k, 0, 0, 0};
+            if (k < sc.cnt) {
+                q.i = sc.item(k);
+                q.jc = sc.job(k);
             }
             return q;
         };
-        Pos first{(int)blockIdx.x, 0, 0};
-        if (valid(first)) first.jc = job_of(jobs, p.njobs, first.i, 0);
+        auto next = [&](Pos q) { return ++q.st < (int)jobs[q.jc].nst ? q : at(q.k + 1); };
+        const Pos first = at(0);
         bool ok = true;
         // Issues stage g (at position q) of a job without a TMA map: after the
         // weight slot's previous use is released, 16-byte async copies of
@@ -678,19 +716,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 const uint32_t srow = obase + p.s_rel + (uint32_t)row * 8;
                 if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
                 else if (J.type == T_Q5_K && (a & 15) == 0) decode_k45_aligned<T_Q5_K>(sm, seg0, arow, srow);
-                else for (int j = 0; j < us; ++j) {
-                    Unit o;
-                    switch (J.type) {
-                    case T_Q4_K: decode_unit<T_Q4_K>(s32, sm, seg0, j, o); break;
-                    case T_Q5_K: decode_unit<T_Q5_K>(s32, sm, seg0, j, o); break;
-                    case T_Q6_K: decode_unit<T_Q6_K>(s32, sm, seg0, j, o); break;
-                    default: decode_unit<T_Q8_0>(s32, sm, seg0, j, o); break;
+                else switch (J.type) {
+                    case T_Q4_K: decode_units<T_Q4_K>(s32, sm, seg0, us, arow, srow); break;
+                    case T_Q5_K: decode_units<T_Q5_K>(s32, sm, seg0, us, arow, srow); break;
+                    case T_Q6_K: decode_units<T_Q6_K>(s32, sm, seg0, us, arow, srow); break;
+                    default: decode_units<T_Q8_0>(s32, sm, seg0, us, arow, srow); break;
                     }
-                    uint4* at = reinterpret_cast<uint4*>(sm + arow + (uint32_t)j * kATile);
-                    at[0] = make_uint4(o.wq[0], o.wq[1], o.wq[2], o.wq[3]);
-                    at[8] = make_uint4(o.wq[4], o.wq[5], o.wq[6], o.wq[7]);  // + 128 bytes: second K half
-                    *reinterpret_cast<float2*>(sm + srow + (uint32_t)j * kM * 8) = make_float2(o.a, o.b);
-                }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // operand stores -> tensor core
             __syncwarp();
@@ -708,9 +739,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     } else {
         // ------------------------------------------------------ epilogue --
         switch (p.ncol) {
-        case 16: epilogue_role<8>(sm, p, jobs, br, abort_flag, tmem, warp, lane); break;
-        case 32: epilogue_role<16>(sm, p, jobs, br, abort_flag, tmem, warp, lane); break;
-        default: epilogue_role<32>(sm, p, jobs, br, abort_flag, tmem, warp, lane); break;
+        case 16: epilogue_role<8>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
+        case 32: epilogue_role<16>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
+        default: epilogue_role<32>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
         }
     }
 
@@ -751,6 +782,8 @@ struct TcPlan {
     size_t smem = 0;
     tc::TcJob* d_jobs = nullptr;
     tc::TcQTask* d_tasks = nullptr;
+    uint32_t* d_sched = nullptr;
+    int* d_sched_off = nullptr;
     uint8_t* d_act = nullptr;
 };
 
@@ -829,8 +862,46 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         job_task.push_back(ti);
         P->jobs.push_back(J);
     }
+    if (item >= (1 << 20)) {  // schedule entries hold the item in 20 bits
+        delete P;
+        return QUANTR_ERR_TOO_LARGE;
+    }
+    // Static schedule: items (128-row tiles, J.nst stages each) dealt longest
+    // first to the least-loaded CTA (ties to the lower index), so every CTA
+    // ends within one item's stages of the others; entries (job << 20) | item.
+    const int grid = std::min(device_sm_count(), item);
+    std::vector<std::vector<uint32_t>> lists((size_t)grid);
+    {
+        std::vector<std::pair<int, uint32_t>> order;  // (-stages, entry)
+        order.reserve((size_t)item);
+        for (size_t j = 0; j < P->jobs.size(); ++j)
+            for (uint32_t t = 0; t < P->jobs[j].tiles; ++t)
+                order.push_back({-(int)P->jobs[j].nst, ((uint32_t)j << 20) | (P->jobs[j].item0 + t)});
+        std::stable_sort(order.begin(), order.end(),
+                         [](const std::pair<int, uint32_t>& a, const std::pair<int, uint32_t>& b) {
+                             return a.first < b.first;
+                         });
+        std::priority_queue<std::pair<long long, int>, std::vector<std::pair<long long, int>>,
+                            std::greater<std::pair<long long, int>>>
+            load;
+        for (int c = 0; c < grid; ++c) load.push({0LL, c});
+        for (const auto& o : order) {
+            auto top = load.top();
+            load.pop();
+            lists[(size_t)top.second].push_back(o.second);
+            load.push({top.first - o.first, top.second});
+        }
+    }
+    std::vector<uint32_t> sched;
+    std::vector<int> sched_off(1, 0);
+    size_t maxcnt = 0;
+    for (const auto& l : lists) {
+        sched.insert(sched.end(), l.begin(), l.end());
+        sched_off.push_back((int)sched.size());
+        maxcnt = std::max(maxcnt, l.size());
+    }
     // Shared memory: barriers | SW weight slots | SO operand slots of {A tiles
-    // | B tiles | records | scales} | job table.  A row's staged copy (cp.async
+    // | B tiles | records | scales} | job table | this CTA's schedule.  A row's staged copy (cp.async
     // jobs) is the 16-byte aligned cover of its segment: up to 15 bytes before
     // and 15 after, plus one word the decoder may read past.
     const uint32_t segp = (segmax + 45) & ~15u;
@@ -839,8 +910,9 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
                    sbytes = kUS * kM * 8u;
     const uint32_t oslot = (abytes + bbytes + dbytes + sbytes + 1023) & ~1023u;
     const uint32_t bars = 1024, tbl = ((uint32_t)(P->jobs.size() * sizeof(TcJob)) + 127) & ~127u;
+    const uint32_t stbl = ((uint32_t)(maxcnt * 4) + 127) & ~127u;
     const int SO = kMaxSO;
-    const long long room = (long long)kSmemMax - bars - tbl - (long long)SO * oslot;
+    const long long room = (long long)kSmemMax - bars - tbl - stbl - (long long)SO * oslot;
     const int SW = room > 0 ? (int)std::min<long long>(kMaxSW, room / wslot) : 0;
     if (SW < 2) {
         delete P;
@@ -866,8 +938,9 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.d_rel = abytes + bbytes;
     pp.s_rel = abytes + bbytes + dbytes;
     pp.jobs_off = pp.o_off + (uint32_t)SO * oslot;
-    P->smem = pp.jobs_off + tbl;
-    P->grid = std::min(device_sm_count(), item);
+    pp.sched_smem = pp.jobs_off + tbl;
+    P->smem = pp.sched_smem + stbl;
+    P->grid = grid;
 
     cudaError_t e = cudaMalloc((void**)&P->d_act, std::max<size_t>(act_total, 256));
     if (e == cudaSuccess) e = cudaMemset(P->d_act, 0, std::max<size_t>(act_total, 256));  // padding tokens stay 0
@@ -887,6 +960,12 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_tasks, P->tasks.size() * sizeof(TcQTask));
     if (e == cudaSuccess)
         e = cudaMemcpy(P->d_tasks, P->tasks.data(), P->tasks.size() * sizeof(TcQTask), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_sched, sched.size() * sizeof(uint32_t));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(P->d_sched, sched.data(), sched.size() * sizeof(uint32_t), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_sched_off, sched_off.size() * sizeof(int));
+    if (e == cudaSuccess)
+        e = cudaMemcpy(P->d_sched_off, sched_off.data(), sched_off.size() * sizeof(int), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         const int code = e == cudaErrorMemoryAllocation ? QUANTR_ERR_OOM : QUANTR_ERR_CUDA;
         cudaGetLastError();
@@ -894,6 +973,8 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         return code;
     }
     pp.jobs = P->d_jobs;
+    pp.sched = P->d_sched;
+    pp.sched_off = P->d_sched_off;
     // 2-D TMA maps for the jobs whose rows are 16-byte aligned (Q4_K, Q5_K);
     // the others (and all jobs, if the driver entry point is unavailable)
     // keep the per-thread async copies.
@@ -962,6 +1043,8 @@ void tc_plan_destroy(TcPlan* P)
     cudaFree(P->d_jobs);
     cudaFree(P->d_tasks);
     cudaFree(P->d_act);
+    cudaFree(P->d_sched);
+    cudaFree(P->d_sched_off);
     if (prev >= 0) cudaSetDevice(prev);
     delete P;
 }
