@@ -57,15 +57,32 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait that may suspend the thread for up to `ns` nanoseconds while the
+// phase is incomplete (it resumes as soon as the phase completes).
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(sptr(bar)), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Waits for the barrier phase with parity `parity`.  Gives up after kWaitNs
 // (recording DEV_ERR_WAIT_TIMEOUT in *err when given) or as soon as *abort
 // becomes non-zero (another role of the CTA gave up).  Never spins unboundedly.
+// suspend_ns > 0 lets each poll suspend the thread that long (fewer polls,
+// fewer issue slots taken from the warps that have work).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
-                                                  volatile int* abort = nullptr)
+                                                  volatile int* abort = nullptr, unsigned suspend_ns = 0)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtimer();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!(suspend_ns ? mbar_try_wait_for(bar, parity, suspend_ns) : mbar_try_wait(bar, parity))) {
         if (abort && *abort) return false;
         if (gtimer() - t0 > kWaitNs) {
             if (err) atomicExch(err, DEV_ERR_WAIT_TIMEOUT);

@@ -11,11 +11,14 @@
 // keep only the exact-term arithmetic the reference's semantics require.
 //
 // A launch runs a list of GEMV jobs (B <= 64 tokens each, N = B rounded up
-// to 16 columns) cut into 128-row tiles, dealt round-robin to one persistent
-// CTA per SM.  A tile's K dimension streams in stages of 8 units (one K-quant
-// super-block, or 8 Q8_0 blocks) through two shared-memory rings: SW slots of
-// packed weights (deep, so that fetch latency hides behind several stages) and
-// SO slots of MMA operands (unpacked weight tiles, scales, activation tiles):
+// to 16 columns) cut into 128-row tiles, dealt by a static longest-first
+// schedule to one persistent CTA per SM.  A tile's K dimension streams in
+// stages of 8 units (one K-quant super-block, or 8 Q8_0 blocks) through three
+// shared-memory rings: SW slots of packed weights (fetched ahead, so that
+// latency hides behind several stages), SO slots of MMA operands (unpacked
+// weight tiles and activation tiles, free again when the stage's MMAs are
+// done) and SE slots of epilogue data (weight scales and activation records,
+// free again when the stage's epilogue is done):
 //
 //   producer (warp 0)    lane 0, per stage: one 2-D TMA copy of the tile's
 //                        packed weights (128 rows x one stage of bytes) for
@@ -27,7 +30,7 @@
 //                        the converged warp) into the stage's TMEM buffer (one
 //                        of NBS, 8 units x N columns each); after the stage,
 //                        one commit to the buffer's barrier and one that frees
-//                        the slot's operands;
+//                        the operand slot;
 //   decoders (4 warps)   for the other jobs, fetch the tile's packed bytes for
 //                        the stage together (16-byte cp.async of each row's
 //                        aligned segment cover, consecutive threads on
@@ -37,10 +40,11 @@
 //                        unpacks each unit's quants into the canonical K-major
 //                        no-swizzle operand layout (8x16-byte core matrices)
 //                        and the unit's scales;
-//   epilogue (8 warps)   TMEM lane quarter (warp % 4) x token half: per stage
-//                        one barrier wait, tcgen05.ld of several units' int32
-//                        sums before one wait::ld, then term and running sum
-//                        per (row, token), in unit order.
+//   epilogue (16 warps)  TMEM lane quarter (warp % 4) x one of 4 token
+//                        groups: per stage, tcgen05.ld of each unit's int32
+//                        sums (the next unit's load in flight while one is
+//                        used), then term and running sum per (row, token),
+//                        in unit order.
 //
 // Activations are quantized by k_tc_quant (quantize_row_q8_0 per token, the
 // same kernel math as every other path) straight into operand tiles in the
@@ -73,11 +77,30 @@ namespace tc {
 constexpr int kM = 128;        // rows per tile (MMA M)
 constexpr int kUS = 8;         // units per stage
 constexpr int kDecWarps = 4;   // one decoder thread per tile row
-constexpr int kEpiWarps = 8;   // 4 lane quarters x 2 token halves
+// Longest suspension (ns) of one barrier poll, per role: a waiting warp
+// sleeps until its phase completes instead of spinning on issue slots.
+#ifndef QR_TC_SUSPEND_EPI
+#define QR_TC_SUSPEND_EPI 2000
+#endif
+#ifndef QR_TC_SUSPEND_MMA
+#define QR_TC_SUSPEND_MMA 1000
+#endif
+#ifndef QR_TC_SUSPEND_PROD
+#define QR_TC_SUSPEND_PROD 4000
+#endif
+#ifndef QR_TC_SUSPEND_DEC
+#define QR_TC_SUSPEND_DEC 1000
+#endif
+constexpr unsigned kSleepEpi = QR_TC_SUSPEND_EPI, kSleepMma = QR_TC_SUSPEND_MMA, kSleepProd = QR_TC_SUSPEND_PROD,
+                   kSleepDec = QR_TC_SUSPEND_DEC;
+constexpr int kEpiGroups = 4;  // token groups of the epilogue (N / 4 tokens each)
+constexpr int kEpiWarps = 4 * kEpiGroups;  // 4 TMEM lane quarters x token groups
 constexpr int kWarps = 2 + kDecWarps + kEpiWarps;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kMaxSW = 8;      // packed-weight slots
-constexpr int kMaxSO = 2;      // operand slots
+constexpr int kMaxSO = 2;      // unpacked weight tile slots (MMA A operands)
+constexpr int kMaxSB = 8;      // activation tile slots (MMA B operands)
+constexpr int kMaxSE = 4;      // epilogue slots (activation records and weight scales)
 constexpr int kMaxNB = 4;      // TMEM stage buffers
 constexpr int kMaxN = kTcMaxB; // tokens per job (MMA N after padding)
 constexpr size_t kSmemMax = 227 * 1024;
@@ -102,11 +125,14 @@ static_assert(sizeof(TcJob) % 16 == 0, "job table is copied in 16-byte words");
 struct TcParams {
     const TcJob* jobs;
     int njobs, total_items;
-    uint32_t SW, SO, NB, ncol, tmem_cols;  // weight slots, operand slots, TMEM stage buffers, max N, TMEM columns
+    uint32_t SW, SO, SB, SE, NB;           // weight, A-tile, B-tile and epilogue slots, TMEM stage buffers
+    uint32_t ncol, tmem_cols;              // max N, TMEM columns
     uint32_t segp;                         // staging bytes per row of a weight slot (cp.async jobs)
     uint32_t w_off, w_slot;                // weight ring: first slot, bytes per slot
-    uint32_t o_off, o_slot;                // operand ring: first slot, bytes per slot
-    uint32_t a_rel, b_rel, d_rel, s_rel;   // A tiles, B tiles, records, scales within an operand slot
+    uint32_t o_off, o_slot;                // A-tile ring: first slot, bytes per slot
+    uint32_t b_off, b_slot;                // B-tile ring: first slot, bytes per slot
+    uint32_t e_off, e_slot;                // epilogue ring: first slot, bytes per slot
+    uint32_t d_rel, s_rel;                 // activation records, weight scales within an epilogue slot
     uint32_t jobs_off;
     // Static schedule: CTA c walks entries [sched_off[c], sched_off[c + 1]) of
     // sched, each (job << 20) | item, copied to shared memory at sched_smem.
@@ -157,6 +183,14 @@ template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&v)[NC]);
 
 template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t addr, uint32_t (&v)[4])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                 : "r"(addr));
+}
+
+template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t addr, uint32_t (&v)[8])
 {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
@@ -202,8 +236,10 @@ struct TcQTask {
     uint8_t* act;
     uint8_t* ds;
     long long ldx;
-    long long blk0;  // first global (token, unit) index of this task
+    long long blk0;  // first global (unit, token) index of this task
     int U, B, N, type;
+    int vec;  // x rows start 16-byte aligned: 128-bit loads
+    int pad;
 };
 
 struct TcQParams {
@@ -221,36 +257,93 @@ __device__ __forceinline__ int tc_perm(int type, int e)
     return e;
 }
 
-// Reference quantize_row_q8_0 per (token, 32-element block), one warp each,
-// written into canonical operand tiles: token t, permuted element k of unit
-// u at u*N*32 + (t/8)*256 + (t%8)*16 + (k/16)*128 + k%16.
+// quantize_row_q8_0's rounding of one scaled value to the int8 it stores:
+// x86 lrintf (round to nearest even) truncated to 8 bits, where NaN and
+// out-of-range inputs give 0x8000000000000000 (low byte 0).  For |v| >= 2^31
+// every float is a multiple of 2^8, whose low byte is 0 as well.
+__device__ __forceinline__ uint32_t q8_round_byte(float v)
+{
+    return fabsf(v) < 2147483648.0f ? ((uint32_t)__float2int_rn(v) & 0xFFu) : 0u;
+}
+
+// Reference quantize_row_q8_0 (src/quant.c:143) per (token, 32-element
+// block), one thread per block, written into canonical operand tiles: token
+// t, permuted element k of unit u at u*N*32 + (t/8)*256 + (t%8)*16 +
+// (k/16)*128 + k%16.  Threads take blocks token-fastest within a unit, so a
+// warp's tile stores and record stores are contiguous.
 __global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQParams p)
 {
+    // The task table (written once, at plan time) goes to shared memory before
+    // the wait for the previous grid, so the per-block task search below reads
+    // no global memory.
+    static_assert(sizeof(TcQTask) % 8 == 0, "task table is copied in 8-byte words");
+    __shared__ TcQTask tasks[kTcMaxJobs];
     pdl_trigger();
+    {
+        const long long* src = reinterpret_cast<const long long*>(p.tasks);
+        long long* dst = reinterpret_cast<long long*>(tasks);
+        const int words = p.ntasks * (int)(sizeof(TcQTask) / 8);
+        for (int w = threadIdx.x; w < words; w += blockDim.x) dst[w] = src[w];
+    }
+    __syncthreads();
     pdl_wait();
-    const int lane = threadIdx.x & 31;
-    const long long step = (long long)gridDim.x * 8;
-    for (long long gb = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); gb < p.total; gb += step) {
-        int lo = 0, hi = p.ntasks - 1;  // last task with blk0 <= gb
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (p.tasks[mid].blk0 <= gb) lo = mid; else hi = mid - 1;
+    const long long step = (long long)gridDim.x * blockDim.x;
+    for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < p.total; g += step) {
+        int ti = 0, hi = p.ntasks - 1;  // last task with blk0 <= g
+        while (ti < hi) {
+            const int mid = (ti + hi + 1) >> 1;
+            if (tasks[mid].blk0 <= g) ti = mid; else hi = mid - 1;
         }
-        const TcQTask& T = p.tasks[lo];
-        const long long local = gb - T.blk0;
-        const int t = (int)(local / T.U), u = (int)(local - (long long)t * T.U);
-        const float v = T.x[(long long)t * T.ldx + (long long)u * 32 + lane];
-        uint32_t h;
-        int sum;
-        const int8_t q = q8_block_warp(v, h, sum);
-        const int k = tc_perm(T.type, lane);
-        T.act[(size_t)u * T.N * 32 + (t >> 3) * 256 + (t & 7) * 16 + (k >> 4) * 128 + (k & 15)] = (uint8_t)q;
-        if (lane == 0) {  // planar per unit: dx | bsum | 32*bsum
-            float* rec = reinterpret_cast<float*>(T.ds) + (size_t)u * T.N * 4;
-            rec[t] = h2f_ref(h);
-            rec[T.N + t] = (float)sum;
-            rec[2 * T.N + t] = __int_as_float(32 * sum);
+        const TcQTask& T = tasks[ti];
+        const int local = (int)(g - T.blk0);  // < B * U
+        const int u = local / T.B, t = local - u * T.B;
+        const float* src = T.x + (long long)t * T.ldx + (long long)u * 32;
+        float v[32];
+        if (T.vec) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 f = reinterpret_cast<const float4*>(src)[i];
+                v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = src[i];
         }
+        // amax = max |x| over the block, NaN ignored (src/quant.c:149-152).
+        uint32_t abits = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const float a = fabsf(v[i]);
+            abits = max(abits, (a == a) ? __float_as_uint(a) : 0u);
+        }
+        const float dd = __fdiv_rn(__uint_as_float(abits), 127.0f);
+        const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
+        uint32_t q[32];
+        int sum = 0;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            q[i] = q8_round_byte(__fmul_rn(v[i], id));
+            sum += (int)(int8_t)q[i];
+        }
+        // Element e goes to byte tc_perm(type, e) of the unit's 32 bytes.
+        uint32_t w[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (T.type == T_Q4_K || T.type == T_Q5_K) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) w[tc_perm(T_Q4_K, e) >> 2] |= q[e] << (8 * (tc_perm(T_Q4_K, e) & 3));
+        } else if (T.type == T_Q6_K) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) w[tc_perm(T_Q6_K, e) >> 2] |= q[e] << (8 * (tc_perm(T_Q6_K, e) & 3));
+        } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) w[e >> 2] |= q[e] << (8 * (e & 3));
+        }
+        uint8_t* tile = T.act + (size_t)u * T.N * 32 + (t >> 3) * 256 + (t & 7) * 16;
+        *reinterpret_cast<uint4*>(tile) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(tile + 128) = make_uint4(w[4], w[5], w[6], w[7]);
+        float* rec = reinterpret_cast<float*>(T.ds) + (size_t)u * T.N * 4;  // planar per unit: dx | bsum | 32*bsum
+        rec[t] = h2f_ref(f2h_ref(dd));
+        rec[T.N + t] = (float)sum;
+        rec[2 * T.N + t] = __int_as_float(32 * sum);
     }
 }
 
@@ -265,22 +358,22 @@ struct Sched {
 };
 
 // Term and running sum of one unit for this warp's NT tokens (v = the unit's
-// int32 sums from TMEM).  Padding tokens (>= B) have zero activations and
-// records, so they are computed without branches and never stored.  Shared
-// memory is read through 32-bit shared-window addresses.
+// int32 sums from TMEM; scale_at = this row's (scale, min) pair, rec_at = the
+// unit's activation scales for the warp's first token, aux_off = the distance
+// to its bsum or 32*bsum records).  Padding tokens (>= B) have zero
+// activations and records, so they are computed without branches and never
+// stored.  Shared memory is read through 32-bit shared-window addresses.
 template <uint32_t TYPE, int NT>
-__device__ __forceinline__ void epi_unit(const uint32_t (&v)[NT], uint32_t sbase, uint32_t s_off, uint32_t d_off,
-                                         int N, int j, int row, int tok0, float (&acc)[NT])
+__device__ __forceinline__ void epi_unit(const uint32_t (&v)[NT], uint32_t scale_at, uint32_t rec_at,
+                                         uint32_t aux_off, float (&acc)[NT])
 {
-    const uint2 scm = lds64(sbase + s_off + (uint32_t)(j * kM + row) * 8);
+    const uint2 scm = lds64(scale_at);
     const float sc = __uint_as_float(scm.x), m = __uint_as_float(scm.y);
-    const uint32_t rec = sbase + d_off + (uint32_t)(j * N) * 16 + (uint32_t)tok0 * 4;
 #pragma unroll
     for (int t4 = 0; t4 < NT; t4 += 4) {
-        const uint4 dx = lds128(rec + (uint32_t)t4 * 4);
+        const uint4 dx = lds128(rec_at + (uint32_t)t4 * 4);
         uint4 aux = make_uint4(0, 0, 0, 0);
-        if (TYPE == T_Q4_K || TYPE == T_Q5_K) aux = lds128(rec + (uint32_t)(N + t4) * 4);  // bsum
-        if (TYPE == T_Q6_K) aux = lds128(rec + (uint32_t)(2 * N + t4) * 4);                // 32*bsum
+        if (TYPE != T_Q8_0) aux = lds128(rec_at + aux_off + (uint32_t)t4 * 4);  // bsum | 32*bsum
         const uint32_t dxa[4] = {dx.x, dx.y, dx.z, dx.w}, ax[4] = {aux.x, aux.y, aux.z, aux.w};
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -295,49 +388,69 @@ __device__ __forceinline__ void epi_unit(const uint32_t (&v)[NT], uint32_t sbase
     }
 }
 
-// One stage of the epilogue: the TMEM load of unit j+1 is in flight while
-// unit j's terms are computed (two register buffers; one for NT = 32).
-template <uint32_t TYPE, int NT>
-__device__ __forceinline__ void epi_stage(uint32_t tbase, uint32_t sbase, uint32_t s_off, uint32_t d_off, int N,
-                                          int us, int row, int tok0, float (&acc)[NT])
+// One stage of the epilogue over us units (FULL: all kUS, straight-line code
+// with compile-time offsets).  The TMEM load of unit j+1 is in flight while
+// unit j's terms are computed (two register buffers; one for NT >= 16).
+// scale0 / rec0: unit 0's scale pair of this row and records of this warp's
+// first token.
+template <uint32_t TYPE, int NT, bool FULL>
+__device__ __forceinline__ void epi_stage(uint32_t tbase, uint32_t scale0, uint32_t rec0, int N, int us,
+                                          float (&acc)[NT])
 {
-    if (NT >= 32) {
+    const uint32_t aux_off = (TYPE == T_Q6_K ? 8u : 4u) * (uint32_t)N;  // records: dx[N] | bsum[N] | 32*bsum[N]
+    const uint32_t rec_step = 16u * (uint32_t)N;
+    constexpr uint32_t sc_step = kM * 8;
+    if constexpr (FULL) {
+        if constexpr (NT >= 16) {
+#pragma unroll
+            for (int j = 0; j < kUS; ++j) {
+                uint32_t v[NT];
+                tmem_ld<NT>(tbase + (uint32_t)(j * N), v);
+                tmem_wait_ld();
+                epi_unit<TYPE, NT>(v, scale0 + j * sc_step, rec0 + j * rec_step, aux_off, acc);
+            }
+        } else {
+            uint32_t v[2][NT];
+            tmem_ld<NT>(tbase, v[0]);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < kUS; ++j) {
+                if (j + 1 < kUS) tmem_ld<NT>(tbase + (uint32_t)((j + 1) * N), v[(j + 1) & 1]);
+                epi_unit<TYPE, NT>(v[j & 1], scale0 + j * sc_step, rec0 + j * rec_step, aux_off, acc);
+                if (j + 1 < kUS) tmem_wait_ld();
+            }
+        }
+    } else {
         for (int j = 0; j < us; ++j) {
             uint32_t v[NT];
             tmem_ld<NT>(tbase + (uint32_t)(j * N), v);
             tmem_wait_ld();
-            epi_unit<TYPE, NT>(v, sbase, s_off, d_off, N, j, row, tok0, acc);
-        }
-        return;
-    }
-    uint32_t va[NT], vb[NT];
-    tmem_ld<NT>(tbase, va);
-    tmem_wait_ld();
-    for (int j = 0; j < us; j += 2) {
-        if (j + 1 < us) tmem_ld<NT>(tbase + (uint32_t)((j + 1) * N), vb);
-        epi_unit<TYPE, NT>(va, sbase, s_off, d_off, N, j, row, tok0, acc);
-        tmem_wait_ld();
-        if (j + 1 < us) {
-            if (j + 2 < us) tmem_ld<NT>(tbase + (uint32_t)((j + 2) * N), va);
-            epi_unit<TYPE, NT>(vb, sbase, s_off, d_off, N, j + 1, row, tok0, acc);
-            tmem_wait_ld();
+            epi_unit<TYPE, NT>(v, scale0 + j * sc_step, rec0 + j * rec_step, aux_off, acc);
         }
     }
 }
 
 struct Bars {
-    uint64_t *wfull, *wempty, *bfull, *afull, *ofree, *t_full, *t_empty;
+    uint64_t *wfull, *wempty;         // weight ring: filled (TMA or decoders' own copies), free again
+    uint64_t *afull, *ofree;          // A-tile ring: tiles written, MMAs done
+    uint64_t *bfull, *bfree;          // B-tile ring: tiles landed, MMAs done
+    uint64_t *dfull, *sfull, *efree;  // epilogue ring: records landed, scales written, epilogue done
+    uint64_t *t_full, *t_empty;       // TMEM stage buffers: sums ready, read
 };
 
 template <int NT>
 __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, const Sched& sc, const Bars& br,
                               volatile int* abort_flag, uint32_t tmem, int warp, int lane)
 {
-    const int quarter = warp & 3, half = (warp - 2 - kDecWarps) >> 2;
+    const int quarter = warp & 3, grp = (warp - 2 - kDecWarps) >> 2;
     const int row = 32 * quarter + lane;
-    const int SO = (int)p.SO, NB = (int)p.NB;
-    const uint32_t smb = sptr(sm);
-    int gs = 0;
+    const int SE = (int)p.SE, NB = (int)p.NB;
+    const int tok0 = grp * NT;
+    const uint32_t tq = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)tok0;  // this warp's lanes and tokens
+    const uint32_t e0 = sptr(sm) + p.e_off, srow = p.s_rel + (uint32_t)row * 8, drow = p.d_rel + (uint32_t)tok0 * 4;
+    // Stage gs's epilogue slot es (used eu times before) and TMEM buffer sb
+    // (used bu times before).
+    int es = 0, eu = 0, sb = 0, bu = 0;
     bool ok = true;
     for (int k = 0; ok && k < sc.cnt; ++k) {
         const int i = sc.item(k);
@@ -348,36 +461,46 @@ __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs,
         const uint32_t type = J.type;
         float* out = J.out;
         const long long ldo = J.ldo;
-        const int tok0 = half * NT;
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-        for (int st = 0; st < nst; ++st, ++gs) {
-            const int os = gs % SO, ou = gs / SO, sb = gs % NB;
-            if (!mbar_wait_bounded(&br.bfull[os], ou & 1, p.err, abort_flag) ||
-                !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag) ||
-                !mbar_wait_bounded(&br.t_full[sb], (gs / NB) & 1, p.err, abort_flag)) {
+        for (int st = 0; st < nst; ++st) {
+            if (!mbar_wait_bounded(&br.dfull[es], eu & 1, p.err, abort_flag, kSleepEpi) ||
+                !mbar_wait_bounded(&br.sfull[es], eu & 1, p.err, abort_flag, kSleepEpi) ||
+                !mbar_wait_bounded(&br.t_full[sb], bu & 1, p.err, abort_flag, kSleepEpi)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            const uint32_t obase = smb + p.o_off + p.o_slot * (uint32_t)os;
+            const uint32_t ebase = e0 + p.e_slot * (uint32_t)es;
             const int us = min(kUS, U - kUS * st);
-            const uint32_t tbase = tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)(sb * kUS * (int)p.ncol + tok0);
+            const uint32_t tbase = tq + (uint32_t)(sb * kUS) * p.ncol;
             if (tok0 < B) {
-                switch (type) {
-                case T_Q4_K: epi_stage<T_Q4_K, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
-                case T_Q5_K: epi_stage<T_Q5_K, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
-                case T_Q6_K: epi_stage<T_Q6_K, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
-                default: epi_stage<T_Q8_0, NT>(tbase, obase, p.s_rel, p.d_rel, N, us, row, tok0, acc); break;
+                const uint32_t s0 = ebase + srow, r0b = ebase + drow;
+                if (us == kUS) {
+                    switch (type) {
+                    case T_Q4_K: epi_stage<T_Q4_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                    case T_Q5_K: epi_stage<T_Q5_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                    case T_Q6_K: epi_stage<T_Q6_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                    default: epi_stage<T_Q8_0, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                    }
+                } else {
+                    switch (type) {
+                    case T_Q4_K: epi_stage<T_Q4_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                    case T_Q5_K: epi_stage<T_Q5_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                    case T_Q6_K: epi_stage<T_Q6_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                    default: epi_stage<T_Q8_0, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                    }
                 }
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&br.t_empty[sb]);
-                mbar_arrive(&br.ofree[os]);
+                mbar_arrive(&br.efree[es]);
             }
+            if (++es == SE) es = 0, ++eu;
+            if (++sb == NB) sb = 0, ++bu;
         }
         if (!ok) break;
         if (row < rows)
@@ -473,29 +596,43 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     Bars br;
     br.wfull = reinterpret_cast<uint64_t*>(sm);
     br.wempty = br.wfull + kMaxSW;
-    br.bfull = br.wempty + kMaxSW;
-    br.afull = br.bfull + kMaxSO;
+    br.afull = br.wempty + kMaxSW;
     br.ofree = br.afull + kMaxSO;
-    br.t_full = br.ofree + kMaxSO;
+    br.bfull = br.ofree + kMaxSO;
+    br.bfree = br.bfull + kMaxSB;
+    br.dfull = br.bfree + kMaxSB;
+    br.sfull = br.dfull + kMaxSE;
+    br.efree = br.sfull + kMaxSE;
+    br.t_full = br.efree + kMaxSE;
     br.t_empty = br.t_full + kMaxNB;
-    // [0] TMEM base, [1] abort, [2..2+kMaxSW) TMA fills per weight slot,
-    // [2+kMaxSW..) bulk fills per operand slot.
+    // [0] TMEM base, [1] abort, then the bulk/TMA fills issued so far per
+    // weight slot [kFillW..), B-tile slot [kFillB..) and record slot [kFillD..).
+    constexpr int kFillW = 2, kFillB = kFillW + kMaxSW, kFillD = kFillB + kMaxSB;
     uint32_t* misc = reinterpret_cast<uint32_t*>(br.t_empty + kMaxNB);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int SW = (int)p.SW, SO = (int)p.SO, NB = (int)p.NB;
+    const int SW = (int)p.SW, SO = (int)p.SO, SB = (int)p.SB, SE = (int)p.SE, NB = (int)p.NB;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < SW; ++s) {
             mbar_init(&br.wfull[s], 1);
             mbar_init(&br.wempty[s], kDecWarps);
-            misc[2 + s] = 0;
+            misc[kFillW + s] = 0;
         }
         for (int s = 0; s < SO; ++s) {
-            mbar_init(&br.bfull[s], 1);
             mbar_init(&br.afull[s], kDecWarps);
-            mbar_init(&br.ofree[s], 1 + kEpiWarps);
-            misc[2 + kMaxSW + s] = 0;
+            mbar_init(&br.ofree[s], 1);
+        }
+        for (int s = 0; s < SB; ++s) {
+            mbar_init(&br.bfull[s], 1);
+            mbar_init(&br.bfree[s], 1);
+            misc[kFillB + s] = 0;
+        }
+        for (int s = 0; s < SE; ++s) {
+            mbar_init(&br.dfull[s], 1);
+            mbar_init(&br.sfull[s], kDecWarps);
+            mbar_init(&br.efree[s], kEpiWarps);
+            misc[kFillD + s] = 0;
         }
         for (int b = 0; b < NB; ++b) {
             mbar_init(&br.t_full[b], 1);
@@ -537,18 +674,17 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             // Weight ring: waits for every stage's slot (so it never runs more
             // than SW stages ahead of the decoders), copies the TMA jobs'.
             // Weights do not depend on the previous grid: no PDL wait.
-            int gs = 0;
+            int ws = 0, wu = 0;  // this stage's weight slot, earlier uses of it
             bool ok = true;
             for (int k = 0; ok && k < sc.cnt; ++k) {
                 const int i = sc.item(k), jc = sc.job(k);
                 const TcJob& J = jobs[jc];
-                for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-                    const int ws = gs % SW, wu = gs / SW;
-                    if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag)) {
+                for (int st = 0; st < (int)J.nst; ++st, (++ws == SW ? (ws = 0, ++wu) : 0)) {
+                    if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag, kSleepProd)) {
                         ok = false;
                         break;
                     }
-                    misc[2 + ws] += 1;  // one arrival per use keeps the slot's phases = its uses
+                    misc[kFillW + ws] += 1;  // one arrival per use keeps the slot's phases = its uses
                     if (!J.tma) {
                         mbar_arrive(&br.wfull[ws]);  // the decoders fetch this stage themselves
                     } else {  // box (x = byte offset in the row, a multiple of 16; y = first row)
@@ -565,23 +701,29 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         } else if (lane == 1) {
             // Operand ring: activation tiles and records of each stage.
             pdl_wait();  // activations come from the quantizer grid
-            int gs = 0;
+            int bs = 0, bu = 0, es = 0, eu = 0;  // this stage's slots, earlier uses of them
             bool ok = true;
             for (int k = 0; ok && k < sc.cnt; ++k) {
                 const TcJob& J = jobs[sc.job(k)];
-                for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-                    const int os = gs % SO, ou = gs / SO;
-                    if (ou > 0 && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag)) {
+                for (int st = 0; st < (int)J.nst;
+                     ++st, (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
+                    // B slot: the MMAs of its previous stage are done; record
+                    // slot: the epilogue of its previous stage is done.
+                    if ((bu > 0 && !mbar_wait_bounded(&br.bfree[bs], (bu - 1) & 1, p.err, abort_flag, kSleepProd)) ||
+                        (eu > 0 && !mbar_wait_bounded(&br.efree[es], (eu - 1) & 1, p.err, abort_flag, kSleepProd))) {
                         ok = false;
                         break;
                     }
                     const int us = min(kUS, (int)J.U - kUS * st);
-                    const uint32_t abytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
-                    uint8_t* obase = sm + p.o_off + p.o_slot * (uint32_t)os;
-                    mbar_arrive_expect_tx(&br.bfull[os], abytes + dbytes);
-                    misc[2 + kMaxSW + os] += 1;
-                    bulk_g2s(obase + p.b_rel, J.act + (size_t)kUS * st * J.N * 32, abytes, &br.bfull[os]);
-                    bulk_g2s(obase + p.d_rel, J.ds + (size_t)kUS * st * J.N * 16, dbytes, &br.bfull[os]);
+                    const uint32_t bbytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
+                    mbar_arrive_expect_tx(&br.bfull[bs], bbytes);
+                    misc[kFillB + bs] += 1;
+                    bulk_g2s(sm + p.b_off + p.b_slot * (uint32_t)bs, J.act + (size_t)kUS * st * J.N * 32, bbytes,
+                             &br.bfull[bs]);
+                    mbar_arrive_expect_tx(&br.dfull[es], dbytes);
+                    misc[kFillD + es] += 1;
+                    bulk_g2s(sm + p.e_off + p.e_slot * (uint32_t)es + p.d_rel, J.ds + (size_t)kUS * st * J.N * 16,
+                             dbytes, &br.dfull[es]);
                 }
             }
         }
@@ -589,34 +731,37 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     } else if (warp == 1) {
         // ----------------------------------------------------------- MMA --
         // The whole warp walks the stages (converged); one elected lane issues.
-        int gs = 0, last_sb = -1, last_ph = 0;
+        int last_sb = -1, last_ph = 0;
+        // This stage's A slot, B slot and TMEM buffer, and earlier uses of them.
+        int os = 0, ou = 0, bs = 0, bsu = 0, sb = 0, bu = 0;
         bool ok = true;
         for (int k = 0; ok && k < sc.cnt; ++k) {
             const TcJob& J = jobs[sc.job(k)];
-            for (int st = 0; st < (int)J.nst; ++st, ++gs) {
-                const int os = gs % SO, ou = gs / SO, sb = gs % NB;
-                if (!mbar_wait_bounded(&br.bfull[os], ou & 1, p.err, abort_flag) ||
-                    !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag) ||
-                    (gs >= NB && !mbar_wait_bounded(&br.t_empty[sb], ((gs / NB) - 1) & 1, p.err, abort_flag))) {
+            for (int st = 0; st < (int)J.nst; ++st, (++os == SO ? (os = 0, ++ou) : 0),
+                     (++bs == SB ? (bs = 0, ++bsu) : 0), (++sb == NB ? (sb = 0, ++bu) : 0)) {
+                if (!mbar_wait_bounded(&br.bfull[bs], bsu & 1, p.err, abort_flag, kSleepMma) ||
+                    !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag, kSleepMma) ||
+                    (bu > 0 && !mbar_wait_bounded(&br.t_empty[sb], (bu - 1) & 1, p.err, abort_flag, kSleepMma))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 __syncwarp();
-                const uint32_t obase = p.o_off + p.o_slot * (uint32_t)os;
+                const uint32_t abase = p.o_off + p.o_slot * (uint32_t)os, bbase = p.b_off + p.b_slot * (uint32_t)bs;
                 const int us = min(kUS, (int)J.U - kUS * st);
                 if (elect_one()) {
                     for (int j = 0; j < us; ++j) {
-                        const uint64_t ad = smem_desc(sptr(sm + obase + p.a_rel + (uint32_t)j * kATile));
-                        const uint64_t bd = smem_desc(sptr(sm + obase + p.b_rel + (uint32_t)(j * (int)J.N) * 32u));
+                        const uint64_t ad = smem_desc(sptr(sm + abase + (uint32_t)j * kATile));
+                        const uint64_t bd = smem_desc(sptr(sm + bbase + (uint32_t)(j * (int)J.N) * 32u));
                         tc_mma(tmem + (uint32_t)(sb * kUS * (int)p.ncol + j * (int)J.N), ad, bd, J.idesc);
                     }
                     tc_commit(&br.t_full[sb]);
                     tc_commit(&br.ofree[os]);
+                    tc_commit(&br.bfree[bs]);
                 }
                 __syncwarp();
                 last_sb = sb;
-                last_ph = (gs / NB) & 1;
+                last_ph = bu & 1;
             }
         }
         // The MMAs issued last complete before TMEM is released.
@@ -653,7 +798,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         auto issue = [&](const Pos& q, int g) {
             if (valid(q) && !jobs[q.jc].tma) {
                 const int ws = g % SW, wu = g / SW;
-                if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag)) ok = false;
+                if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag, kSleepDec)) ok = false;
                 const TcJob& J = jobs[q.jc];
                 const int r0 = (q.i - J.item0) * kM;
                 const int rows = min(kM, (int)J.n - r0);
@@ -685,26 +830,45 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 ++gi;
             }
         }
-        int gs = 0;
-        for (Pos cur = first; valid(cur); cur = next(cur), ++gs) {
+        // Stage gs's slot and earlier uses of that slot in each ring.
+        int gs = 0, ws = 0, wu = 0, os = 0, ou = 0, es = 0, eu = 0;
+        auto advance = [&]() {
+            ++gs;
+            if (++ws == SW) ws = 0, ++wu;
+            if (++os == SO) os = 0, ++ou;
+            if (++es == SE) es = 0, ++eu;
+        };
+        for (Pos cur = first; valid(cur); cur = next(cur), advance()) {
             const TcJob& J = jobs[cur.jc];
-            const int ws = gs % SW, os = gs % SO, ou = gs / SO;
-            wait_groups_but(SW - 2);  // this stage's group is the oldest not yet waited for
-            if (J.tma && ok && !mbar_wait_bounded(&br.wfull[ws], (gs / SW) & 1, p.err, abort_flag)) ok = false;
-            // The operand slot's previous stage is consumed (MMAs done, epilogue done).
-            if (ou > 0 && ok && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag)) ok = false;
-            // Every decoder thread's copies of this stage have landed; the
-            // decoders stop together if any of them gave up on a wait.
-            uint32_t all_ok;
-            asm volatile(
-                "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\t"
-                "bar.red.and.pred b, 1, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}\n"
-                : "=r"(all_ok)
-                : "r"(ok ? 1u : 0u)
-                : "memory");
-            static_assert(kDecWarps * 32 == 128, "named barrier 1 counts the decoder threads");
-            if (!all_ok) break;
-            const uint32_t wbase = p.w_off + p.w_slot * (uint32_t)ws, obase = p.o_off + p.o_slot * (uint32_t)os;
+            // A copied stage's group is the oldest not yet waited for (a TMA
+            // stage's group is empty).
+            if (!J.tma) wait_groups_but(SW - 2);
+            if (J.tma && ok && !mbar_wait_bounded(&br.wfull[ws], wu & 1, p.err, abort_flag, kSleepDec)) ok = false;
+            // The A slot's previous stage is consumed (its MMAs are done), and
+            // the scale slot's (its epilogue is done).
+            if (ou > 0 && ok && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag, kSleepDec)) ok = false;
+            if (eu > 0 && ok && !mbar_wait_bounded(&br.efree[es], (eu - 1) & 1, p.err, abort_flag, kSleepDec)) ok = false;
+            if (J.tma) {
+                // The stage's weights came by TMA: each warp goes on alone.  A
+                // warp that gave up keeps walking the stages without work (so
+                // it still meets the others at the barriers of copied stages).
+                ok = __all_sync(0xFFFFFFFFu, ok);
+            } else {
+                // Every decoder thread's copies of this stage have landed; the
+                // decoders stop together if any of them gave up on a wait.
+                uint32_t all_ok;
+                asm volatile(
+                    "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\t"
+                    "bar.red.and.pred b, 1, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}\n"
+                    : "=r"(all_ok)
+                    : "r"(ok ? 1u : 0u)
+                    : "memory");
+                static_assert(kDecWarps * 32 == 128, "named barrier 1 counts the decoder threads");
+                if (!all_ok) break;
+            }
+            if (!ok) continue;
+            const uint32_t wbase = p.w_off + p.w_slot * (uint32_t)ws, obase = p.o_off + p.o_slot * (uint32_t)os,
+                           ebase = p.e_off + p.e_slot * (uint32_t)es;
             const int r0 = (cur.i - J.item0) * kM;
             const int rows = min(kM, (int)J.n - r0);
             const int us = min(kUS, (int)J.U - kUS * cur.st);
@@ -712,8 +876,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
                 const uint32_t seg0 = J.tma ? wbase + (uint32_t)row * J.seg
                                             : wbase + (uint32_t)row * p.segp + (uint32_t)(a & 15);
-                const uint32_t arow = obase + p.a_rel + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
-                const uint32_t srow = obase + p.s_rel + (uint32_t)row * 8;
+                const uint32_t arow = obase + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
+                const uint32_t srow = ebase + p.s_rel + (uint32_t)row * 8;
                 if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
                 else if (J.type == T_Q5_K && (a & 15) == 0) decode_k45_aligned<T_Q5_K>(sm, seg0, arow, srow);
                 else switch (J.type) {
@@ -727,6 +891,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&br.afull[os]);
+                mbar_arrive(&br.sfull[es]);
                 mbar_arrive(&br.wempty[ws]);
             }
             issue(iss, gi);  // stage gs + SW - 1 (its weight slot's previous use is stage gs - 1)
@@ -739,9 +904,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     } else {
         // ------------------------------------------------------ epilogue --
         switch (p.ncol) {
-        case 16: epilogue_role<8>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
-        case 32: epilogue_role<16>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
-        default: epilogue_role<32>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
+        case 16: epilogue_role<16 / kEpiGroups>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
+        case 32: epilogue_role<32 / kEpiGroups>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
+        default: epilogue_role<64 / kEpiGroups>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
         }
     }
 
@@ -751,9 +916,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         // Some role gave up: let every bulk/TMA copy this CTA issued land
         // (bounded) before its shared memory is released.
         for (int s = 0; s < SW; ++s)
-            if (misc[2 + s] > 0) mbar_wait_bounded(&br.wfull[s], (misc[2 + s] - 1) & 1, nullptr);
-        for (int s = 0; s < SO; ++s)
-            if (misc[2 + kMaxSW + s] > 0) mbar_wait_bounded(&br.bfull[s], (misc[2 + kMaxSW + s] - 1) & 1, nullptr);
+            if (misc[kFillW + s] > 0) mbar_wait_bounded(&br.wfull[s], (misc[kFillW + s] - 1) & 1, nullptr);
+        for (int s = 0; s < SB; ++s)
+            if (misc[kFillB + s] > 0) mbar_wait_bounded(&br.bfull[s], (misc[kFillB + s] - 1) & 1, nullptr);
+        for (int s = 0; s < SE; ++s)
+            if (misc[kFillD + s] > 0) mbar_wait_bounded(&br.dfull[s], (misc[kFillD + s] - 1) & 1, nullptr);
     }
     __syncthreads();
     if (warp == 1) {
@@ -801,7 +968,6 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     size_t act_total = 0;
     long long blocks = 0;
     int Nmax = 16, item = 0;
-    uint32_t segmax = 0;
     std::vector<size_t> task_act_off;
     std::vector<int> job_task;
     for (int j = 0; j < njobs; ++j) {
@@ -836,7 +1002,6 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         J.item0 = item;
         item += J.tiles;
         Nmax = std::max(Nmax, (int)J.N);
-        segmax = std::max(segmax, J.seg);
         const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
         auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, perm);
         auto it = dedupe.find(key);
@@ -849,6 +1014,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
             t.B = a.B;
             t.N = (int)J.N;
             t.type = (int)a.type;
+            t.vec = ((uintptr_t)a.x % 16 == 0 && a.ldx % 4 == 0) ? 1 : 0;
             t.blk0 = blocks;
             blocks += (long long)a.B * J.U;
             task_act_off.push_back(act_total);
@@ -900,29 +1066,72 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         sched_off.push_back((int)sched.size());
         maxcnt = std::max(maxcnt, l.size());
     }
-    // Shared memory: barriers | SW weight slots | SO operand slots of {A tiles
-    // | B tiles | records | scales} | job table | this CTA's schedule.  A row's staged copy (cp.async
-    // jobs) is the 16-byte aligned cover of its segment: up to 15 bytes before
-    // and 15 after, plus one word the decoder may read past.
-    const uint32_t segp = (segmax + 45) & ~15u;
-    const uint32_t wslot = (kM * segp + 1023) & ~1023u;
+    TcParams& pp = P->pp;
+    // 2-D TMA maps for the jobs whose rows are 16-byte aligned (Q4_K, Q5_K);
+    // the others (and all jobs, if the driver entry point is unavailable)
+    // keep the per-thread async copies.
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    static bool looked_up = false;
+    if (!looked_up) {
+        looked_up = true;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&encode, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            encode = nullptr;
+        cudaGetLastError();
+    }
+    uint32_t seg_tma = 0, seg_copy = 0;  // widest stage segment of the TMA jobs and of the copied jobs
+    for (size_t j = 0; j < P->jobs.size(); ++j) {
+        TcJob& J = P->jobs[j];
+        J.tma = 0;
+        if (encode && (J.type == T_Q4_K || J.type == T_Q5_K) && (J.rb % 16) == 0) {
+            const cuuint64_t dims[2] = {(cuuint64_t)J.rb, (cuuint64_t)J.n};
+            const cuuint64_t strides[1] = {(cuuint64_t)J.rb};
+            const cuuint32_t box[2] = {J.seg, (cuuint32_t)kM};
+            const cuuint32_t estr[2] = {1, 1};
+            if (encode(&pp.tmap[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(J.w), dims, strides, box,
+                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS)
+                J.tma = 1;
+        }
+        if (J.tma) seg_tma = std::max(seg_tma, J.seg);
+        else seg_copy = std::max(seg_copy, J.seg);
+    }
+    // Shared memory: barriers | SW weight slots | SO A-tile slots | SB B-tile
+    // slots | SE epilogue slots of {records | scales} | job table | this CTA's
+    // schedule.  A TMA job's stage lands as 128 rows x seg bytes; a copied
+    // job's row is the 16-byte aligned cover of its segment (up to 15 bytes
+    // before and 15 after, plus one word the decoder may read past).
+    const uint32_t segp = seg_copy ? (seg_copy + 45) & ~15u : 16u;
+    const uint32_t wslot = (std::max(kM * (seg_copy ? segp : 0u), kM * seg_tma) + 1023) & ~1023u;
     const uint32_t abytes = kUS * kATile, bbytes = kUS * (uint32_t)Nmax * 32u, dbytes = kUS * (uint32_t)Nmax * 16u,
                    sbytes = kUS * kM * 8u;
-    const uint32_t oslot = (abytes + bbytes + dbytes + sbytes + 1023) & ~1023u;
+    const uint32_t oslot = abytes, bslot = (bbytes + 1023) & ~1023u, eslot = (dbytes + sbytes + 127) & ~127u;
     const uint32_t bars = 1024, tbl = ((uint32_t)(P->jobs.size() * sizeof(TcJob)) + 127) & ~127u;
     const uint32_t stbl = ((uint32_t)(maxcnt * 4) + 127) & ~127u;
     const int SO = kMaxSO;
-    const long long room = (long long)kSmemMax - bars - tbl - stbl - (long long)SO * oslot;
-    const int SW = room > 0 ? (int)std::min<long long>(kMaxSW, room / wslot) : 0;
+    // Deep B-tile and epilogue rings (activations are fetched that many
+    // stages ahead; the epilogue may trail the decoders by SE stages) as long
+    // as three weight slots remain; at least two of each.
+    int SB = 4, SE = kMaxSE, SW = 0;
+    for (;;) {
+        const long long room = (long long)kSmemMax - bars - tbl - stbl - (long long)SO * oslot -
+                               (long long)SB * bslot - (long long)SE * eslot;
+        SW = room > 0 ? (int)std::min<long long>(kMaxSW, room / wslot) : 0;
+        if (SW >= 3 || (SB == 2 && SE == 2)) break;
+        if (SB > 2) --SB;
+        if (SE > 2) --SE;
+    }
     if (SW < 2) {
         delete P;
         return QUANTR_ERR_TOO_LARGE;
     }
-    TcParams& pp = P->pp;
     pp.njobs = (int)P->jobs.size();
     pp.total_items = item;
     pp.SW = (uint32_t)SW;
     pp.SO = (uint32_t)SO;
+    pp.SB = (uint32_t)SB;
+    pp.SE = (uint32_t)SE;
     pp.ncol = (uint32_t)Nmax;
     pp.NB = (uint32_t)std::min(kMaxNB, 512 / (kUS * Nmax));  // 4, 2 or 1 stage buffers for N = 16, 32, 64
     uint32_t cols = 32;
@@ -933,11 +1142,13 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.w_slot = wslot;
     pp.o_off = bars + (uint32_t)SW * wslot;
     pp.o_slot = oslot;
-    pp.a_rel = 0;
-    pp.b_rel = abytes;
-    pp.d_rel = abytes + bbytes;
-    pp.s_rel = abytes + bbytes + dbytes;
-    pp.jobs_off = pp.o_off + (uint32_t)SO * oslot;
+    pp.b_off = pp.o_off + (uint32_t)SO * oslot;
+    pp.b_slot = bslot;
+    pp.e_off = pp.b_off + (uint32_t)SB * bslot;
+    pp.e_slot = eslot;
+    pp.d_rel = 0;
+    pp.s_rel = dbytes;
+    pp.jobs_off = pp.e_off + (uint32_t)SE * eslot;
     pp.sched_smem = pp.jobs_off + tbl;
     P->smem = pp.sched_smem + stbl;
     P->grid = grid;
@@ -975,41 +1186,6 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.jobs = P->d_jobs;
     pp.sched = P->d_sched;
     pp.sched_off = P->d_sched_off;
-    // 2-D TMA maps for the jobs whose rows are 16-byte aligned (Q4_K, Q5_K);
-    // the others (and all jobs, if the driver entry point is unavailable)
-    // keep the per-thread async copies.
-    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    static bool looked_up = false;
-    if (!looked_up) {
-        looked_up = true;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", (void**)&encode, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            encode = nullptr;
-        cudaGetLastError();
-    }
-    bool any_tma = false;
-    for (size_t j = 0; j < P->jobs.size(); ++j) {
-        TcJob& J = P->jobs[j];
-        J.tma = 0;
-        if (!encode || (J.type != T_Q4_K && J.type != T_Q5_K) || (J.rb % 16) != 0) continue;
-        const cuuint64_t dims[2] = {(cuuint64_t)J.rb, (cuuint64_t)J.n};
-        const cuuint64_t strides[1] = {(cuuint64_t)J.rb};
-        const cuuint32_t box[2] = {J.seg, (cuuint32_t)kM};
-        const cuuint32_t estr[2] = {1, 1};
-        if (encode(&pp.tmap[j], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(J.w), dims, strides, box, estr,
-                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
-            J.tma = 1;
-            any_tma = true;
-        }
-    }
-    if (any_tma && cudaMemcpy(P->d_jobs, P->jobs.data(), P->jobs.size() * sizeof(TcJob), cudaMemcpyHostToDevice) !=
-                       cudaSuccess) {
-        cudaGetLastError();
-        tc_plan_destroy(P);
-        return QUANTR_ERR_CUDA;
-    }
     P->qp.tasks = P->d_tasks;
     P->qp.ntasks = (int)P->tasks.size();
     P->qp.total = blocks;
@@ -1025,7 +1201,7 @@ cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
     static int configured_dev = -1;
     cudaError_t e = ensure_smem_attr(&k_tc_program, (int)kSmemMax, configured_dev);
     if (e != cudaSuccess) return e;
-    const long long qgrid = std::max(1LL, std::min<long long>((P->qp.total + 7) / 8, 8LL * device_sm_count()));
+    const long long qgrid = std::max(1LL, std::min<long long>((P->qp.total + 255) / 256, 8LL * device_sm_count()));
     e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
     if (e != cudaSuccess) return e;
     TcParams pp = P->pp;
