@@ -76,7 +76,7 @@ namespace tc {
 
 constexpr int kM = 128;        // rows per tile (MMA M)
 constexpr int kUS = 8;         // units per stage
-constexpr int kDecWarps = 4;   // one decoder thread per tile row
+constexpr int kGroupWarps = 4;  // one decoder thread per tile row in each decoder group
 // Longest suspension (ns) of one barrier poll, per role: a waiting warp
 // sleeps until its phase completes instead of spinning on issue slots.
 #ifndef QR_TC_SUSPEND_EPI
@@ -93,10 +93,15 @@ constexpr int kDecWarps = 4;   // one decoder thread per tile row
 #endif
 constexpr unsigned kSleepEpi = QR_TC_SUSPEND_EPI, kSleepMma = QR_TC_SUSPEND_MMA, kSleepProd = QR_TC_SUSPEND_PROD,
                    kSleepDec = QR_TC_SUSPEND_DEC;
-constexpr int kEpiGroups = 4;  // token groups of the epilogue (N / 4 tokens each)
-constexpr int kEpiWarps = 4 * kEpiGroups;  // 4 TMEM lane quarters x token groups
-constexpr int kWarps = 2 + kDecWarps + kEpiWarps;
-constexpr int kThreads = 32 * kWarps;
+// Warp split of a launch: DG decoder groups of four warps taking alternate
+// stages, and 4 TMEM lane quarters x EG epilogue token groups (N / EG tokens
+// each) after the producer and MMA warps.  Programs of up to 16 columns run
+// <2, 2> (decode-bound), wider ones <1, 4> (epilogue-bound).
+template <int DG, int EG>
+struct Split {
+    static constexpr int dec_warps = DG * kGroupWarps, epi_warps = 4 * EG;
+    static constexpr int threads = 32 * (2 + dec_warps + epi_warps);
+};
 constexpr int kMaxSW = 8;      // packed-weight slots
 constexpr int kMaxSO = 2;      // unpacked weight tile slots (MMA A operands)
 constexpr int kMaxSB = 8;      // activation tile slots (MMA B operands)
@@ -438,11 +443,11 @@ struct Bars {
     uint64_t *t_full, *t_empty;       // TMEM stage buffers: sums ready, read
 };
 
-template <int NT>
+template <int NT, int DW>
 __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, const Sched& sc, const Bars& br,
                               volatile int* abort_flag, uint32_t tmem, int warp, int lane)
 {
-    const int quarter = warp & 3, grp = (warp - 2 - kDecWarps) >> 2;
+    const int quarter = warp & 3, grp = (warp - 2 - DW) >> 2;
     const int row = 32 * quarter + lane;
     const int SE = (int)p.SE, NB = (int)p.NB;
     const int tok0 = grp * NT;
@@ -590,8 +595,11 @@ __device__ __forceinline__ void wait_groups_but(int n)
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constant__ TcParams p)
+template <int DG, int EG>
+__global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const __grid_constant__ TcParams p)
 {
+    constexpr int kDecWarps = Split<DG, EG>::dec_warps, kEpiWarps = Split<DG, EG>::epi_warps;
+    constexpr int kThreads = Split<DG, EG>::threads;
     extern __shared__ __align__(1024) uint8_t sm[];
     Bars br;
     br.wfull = reinterpret_cast<uint64_t*>(sm);
@@ -616,11 +624,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
     if (threadIdx.x == 0) {
         for (int s = 0; s < SW; ++s) {
             mbar_init(&br.wfull[s], 1);
-            mbar_init(&br.wempty[s], kDecWarps);
+            mbar_init(&br.wempty[s], kGroupWarps);
             misc[kFillW + s] = 0;
         }
         for (int s = 0; s < SO; ++s) {
-            mbar_init(&br.afull[s], kDecWarps);
+            mbar_init(&br.afull[s], kGroupWarps);
             mbar_init(&br.ofree[s], 1);
         }
         for (int s = 0; s < SB; ++s) {
@@ -630,7 +638,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         }
         for (int s = 0; s < SE; ++s) {
             mbar_init(&br.dfull[s], 1);
-            mbar_init(&br.sfull[s], kDecWarps);
+            mbar_init(&br.sfull[s], kGroupWarps);
             mbar_init(&br.efree[s], kEpiWarps);
             misc[kFillD + s] = 0;
         }
@@ -769,11 +777,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
         __syncwarp();
     } else if (warp < 2 + kDecWarps) {
         // ------------------------------------------------------ decoders --
-        const int row = (warp - 2) * 32 + lane;
+        // DG groups of four warps take alternate stages (group grp the stages
+        // gs with gs % DG == grp): one group's waits and decode overlap the
+        // other's.  One thread per tile row within a group.
+        static_assert(DG == 1 || (DG == 2 && kMaxSO == 2), "with two groups each keeps one A slot");
+        const int grp = (warp - 2) / kGroupWarps;
+        const int row = ((warp - 2) % kGroupWarps) * 32 + lane;
+        const uint32_t bar_id = 1 + (uint32_t)grp;  // named barrier of the group's 128 threads
         const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
-        // Stage positions (schedule entry, item, job, stage within the item)
-        // walked twice: once to issue a stage's copies SW-1 stages ahead,
-        // once to decode it.
+        // Stage positions (schedule entry, item, job, stage within the item).
         struct Pos {
             int k, i, jc, st;
         };
@@ -787,14 +799,19 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             return q;
         };
         auto next = [&](Pos q) { return ++q.st < (int)jobs[q.jc].nst ? q : at(q.k + 1); };
+        auto next_own = [&](Pos q) {  // DG stages on
+#pragma unroll
+            for (int d = 0; d < DG; ++d)
+                if (valid(q)) q = next(q);
+            return q;
+        };
         const Pos first = at(0);
         bool ok = true;
         // Issues stage g (at position q) of a job without a TMA map: after the
         // weight slot's previous use is released, 16-byte async copies of
-        // every row's aligned segment cover, the 128 decoder threads walking
+        // every row's aligned segment cover, the group's 128 threads walking
         // (row, chunk) pairs chunk-fastest so a warp instruction reads a few
         // rows' contiguous bytes; one commit group per stage, empty otherwise.
-        const int dtid = (warp - 2) * 32 + lane;
         auto issue = [&](const Pos& q, int g) {
             if (valid(q) && !jobs[q.jc].tma) {
                 const int ws = g % SW, wu = g / SW;
@@ -807,7 +824,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
                 const int cpr = (int)((segb + 30) >> 4);  // chunk slots per row (>= any row's cover)
                 const uint32_t dst0 = sptr(sm + p.w_off + p.w_slot * (uint32_t)ws);
                 const uint8_t* src0 = J.w + (long long)r0 * J.rb + (long long)q.st * J.seg;
-                for (int f = dtid; ok && f < rows * cpr; f += kDecWarps * 32) {
+                for (int f = row; ok && f < rows * cpr; f += kGroupWarps * 32) {
                     const int r = f / cpr, c = f - r * cpr;
                     const uintptr_t a = (uintptr_t)(src0 + (long long)r * J.rb);
                     const uintptr_t a0 = a & ~(uintptr_t)15, a1 = (a + segb + 15) & ~(uintptr_t)15;
@@ -821,15 +838,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             }
             asm volatile("cp.async.commit_group;" ::: "memory");
         };
-        Pos iss = first;
-        int gi = 0;
-        for (int k = 0; k < SW - 1; ++k) {  // prologue: SW-1 groups, real or empty
-            issue(iss, gi);
-            if (valid(iss)) {
-                iss = next(iss);
-                ++gi;
-            }
-        }
+        issue(grp == 0 ? first : (valid(first) ? next(first) : first), grp);  // the group's first stage
+        static_assert(DG <= 2, "a group's first stage is stage 0 or 1");
         // Stage gs's slot and earlier uses of that slot in each ring.
         int gs = 0, ws = 0, wu = 0, os = 0, ou = 0, es = 0, eu = 0;
         auto advance = [&]() {
@@ -839,10 +849,10 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             if (++es == SE) es = 0, ++eu;
         };
         for (Pos cur = first; valid(cur); cur = next(cur), advance()) {
+            if (gs % DG != grp) continue;  // the other group's stage
             const TcJob& J = jobs[cur.jc];
-            // A copied stage's group is the oldest not yet waited for (a TMA
-            // stage's group is empty).
-            if (!J.tma) wait_groups_but(SW - 2);
+            // A copied stage's group is the only one in flight.
+            if (!J.tma) asm volatile("cp.async.wait_group 0;" ::: "memory");
             if (J.tma && ok && !mbar_wait_bounded(&br.wfull[ws], wu & 1, p.err, abort_flag, kSleepDec)) ok = false;
             // The A slot's previous stage is consumed (its MMAs are done), and
             // the scale slot's (its epilogue is done).
@@ -851,62 +861,60 @@ __global__ void __launch_bounds__(kThreads, 1) k_tc_program(const __grid_constan
             if (J.tma) {
                 // The stage's weights came by TMA: each warp goes on alone.  A
                 // warp that gave up keeps walking the stages without work (so
-                // it still meets the others at the barriers of copied stages).
+                // it still meets its group at the barriers of copied stages).
                 ok = __all_sync(0xFFFFFFFFu, ok);
             } else {
-                // Every decoder thread's copies of this stage have landed; the
-                // decoders stop together if any of them gave up on a wait.
+                // Every thread of the group has its copies of this stage; the
+                // group stops together if any of them gave up on a wait.
                 uint32_t all_ok;
                 asm volatile(
                     "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\t"
-                    "bar.red.and.pred b, 1, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}\n"
+                    "bar.red.and.pred b, %2, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}\n"
                     : "=r"(all_ok)
-                    : "r"(ok ? 1u : 0u)
+                    : "r"(ok ? 1u : 0u), "r"(bar_id)
                     : "memory");
-                static_assert(kDecWarps * 32 == 128, "named barrier 1 counts the decoder threads");
+                static_assert(kGroupWarps * 32 == 128, "a group's named barrier counts 128 threads");
                 if (!all_ok) break;
             }
-            if (!ok) continue;
-            const uint32_t wbase = p.w_off + p.w_slot * (uint32_t)ws, obase = p.o_off + p.o_slot * (uint32_t)os,
-                           ebase = p.e_off + p.e_slot * (uint32_t)es;
-            const int r0 = (cur.i - J.item0) * kM;
-            const int rows = min(kM, (int)J.n - r0);
-            const int us = min(kUS, (int)J.U - kUS * cur.st);
-            if (row < rows) {
-                const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
-                const uint32_t seg0 = J.tma ? wbase + (uint32_t)row * J.seg
-                                            : wbase + (uint32_t)row * p.segp + (uint32_t)(a & 15);
-                const uint32_t arow = obase + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
-                const uint32_t srow = ebase + p.s_rel + (uint32_t)row * 8;
-                if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
-                else if (J.type == T_Q5_K && (a & 15) == 0) decode_k45_aligned<T_Q5_K>(sm, seg0, arow, srow);
-                else switch (J.type) {
-                    case T_Q4_K: decode_units<T_Q4_K>(s32, sm, seg0, us, arow, srow); break;
-                    case T_Q5_K: decode_units<T_Q5_K>(s32, sm, seg0, us, arow, srow); break;
-                    case T_Q6_K: decode_units<T_Q6_K>(s32, sm, seg0, us, arow, srow); break;
-                    default: decode_units<T_Q8_0>(s32, sm, seg0, us, arow, srow); break;
-                    }
+            if (ok) {
+                const uint32_t wbase = p.w_off + p.w_slot * (uint32_t)ws, obase = p.o_off + p.o_slot * (uint32_t)os,
+                               ebase = p.e_off + p.e_slot * (uint32_t)es;
+                const int r0 = (cur.i - J.item0) * kM;
+                const int rows = min(kM, (int)J.n - r0);
+                const int us = min(kUS, (int)J.U - kUS * cur.st);
+                if (row < rows) {
+                    const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
+                    const uint32_t seg0 = J.tma ? wbase + (uint32_t)row * J.seg
+                                                : wbase + (uint32_t)row * p.segp + (uint32_t)(a & 15);
+                    const uint32_t arow = obase + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
+                    const uint32_t srow = ebase + p.s_rel + (uint32_t)row * 8;
+                    if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
+                    else if (J.type == T_Q5_K && (a & 15) == 0) decode_k45_aligned<T_Q5_K>(sm, seg0, arow, srow);
+                    else switch (J.type) {
+                        case T_Q4_K: decode_units<T_Q4_K>(s32, sm, seg0, us, arow, srow); break;
+                        case T_Q5_K: decode_units<T_Q5_K>(s32, sm, seg0, us, arow, srow); break;
+                        case T_Q6_K: decode_units<T_Q6_K>(s32, sm, seg0, us, arow, srow); break;
+                        default: decode_units<T_Q8_0>(s32, sm, seg0, us, arow, srow); break;
+                        }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // operand stores -> tensor core
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&br.afull[os]);
+                    mbar_arrive(&br.sfull[es]);
+                    mbar_arrive(&br.wempty[ws]);
+                }
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // operand stores -> tensor core
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&br.afull[os]);
-                mbar_arrive(&br.sfull[es]);
-                mbar_arrive(&br.wempty[ws]);
-            }
-            issue(iss, gi);  // stage gs + SW - 1 (its weight slot's previous use is stage gs - 1)
-            if (valid(iss)) {
-                iss = next(iss);
-                ++gi;
-            }
+            issue(next_own(cur), gs + DG);  // the group's next stage
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into shared memory outlives the role
     } else {
         // ------------------------------------------------------ epilogue --
-        switch (p.ncol) {
-        case 16: epilogue_role<16 / kEpiGroups>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
-        case 32: epilogue_role<32 / kEpiGroups>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
-        default: epilogue_role<64 / kEpiGroups>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane); break;
+        if constexpr (EG == 2) {
+            epilogue_role<16 / EG, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
+        } else {
+            if (p.ncol == 32) epilogue_role<32 / EG, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
+            else epilogue_role<64 / EG, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
         }
     }
 
@@ -1198,15 +1206,18 @@ cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
     using namespace tc;
     LaunchCfg c;
     c.stream = stream;
-    static int configured_dev = -1;
-    cudaError_t e = ensure_smem_attr(&k_tc_program, (int)kSmemMax, configured_dev);
+    static int configured_narrow = -1, configured_wide = -1;
+    const bool narrow = P->pp.ncol <= 16;  // see Split
+    cudaError_t e = narrow ? ensure_smem_attr(&k_tc_program<2, 2>, (int)kSmemMax, configured_narrow)
+                           : ensure_smem_attr(&k_tc_program<1, 4>, (int)kSmemMax, configured_wide);
     if (e != cudaSuccess) return e;
     const long long qgrid = std::max(1LL, std::min<long long>((P->qp.total + 255) / 256, 8LL * device_sm_count()));
     e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
     if (e != cudaSuccess) return e;
     TcParams pp = P->pp;
     pp.err = err;
-    return launch_ex(&k_tc_program, dim3(P->grid), dim3(kThreads), P->smem, c, pp);
+    if (narrow) return launch_ex(&k_tc_program<2, 2>, dim3(P->grid), dim3(Split<2, 2>::threads), P->smem, c, pp);
+    return launch_ex(&k_tc_program<1, 4>, dim3(P->grid), dim3(Split<1, 4>::threads), P->smem, c, pp);
 }
 
 void tc_plan_destroy(TcPlan* P)
