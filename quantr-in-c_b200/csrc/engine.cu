@@ -51,15 +51,30 @@
 namespace qr {
 namespace eng {
 
-constexpr int kConsumerWarps = 12;
-constexpr int kChainWarps = 2;
+#ifndef QR_ENG_CONSUMER_WARPS
+#define QR_ENG_CONSUMER_WARPS 12
+#endif
+#ifndef QR_ENG_CHAIN_WARPS
+#define QR_ENG_CHAIN_WARPS 2
+#endif
+constexpr int kConsumerWarps = QR_ENG_CONSUMER_WARPS;
+constexpr int kChainWarps = QR_ENG_CHAIN_WARPS;
 constexpr int kWarps = 1 + kConsumerWarps + kChainWarps;
 constexpr int kThreads = 32 * kWarps;
 constexpr int kConsumerThreads = 32 * kConsumerWarps;
 // Ring depths: 3 weight slots of ~44 KB measured best on B200 for the c2
 // shapes (fewer, larger tiles amortise the per-tile hand-off across the 12
 // consumer warps; 3 x 44 KB in flight per SM still saturates HBM).
-constexpr int kMaxS = 3, kMaxT = 4;
+#ifndef QR_ENG_SLOTS
+#define QR_ENG_SLOTS 3
+#endif
+#ifndef QR_ENG_SLOT_KB
+#define QR_ENG_SLOT_KB 44
+#endif
+#ifndef QR_ENG_TERMS
+#define QR_ENG_TERMS 4
+#endif
+constexpr int kMaxS = QR_ENG_SLOTS, kMaxT = QR_ENG_TERMS;
 constexpr int kMaxB = 16;
 constexpr size_t kSmemMax = 227 * 1024;
 constexpr uint32_t kBulkChunk = 32768;
@@ -82,7 +97,7 @@ static_assert(sizeof(ItemHdr) == 64, "item header is copied as four 16-byte word
 struct __align__(16) JobDesc {
     ItemHdr hdr;         // template of every tile's header (out = job base, rows = R)
     const uint8_t* w;    // 16-byte aligned packed rows
-    const uint8_t* act;  // quantized activations: q[B][U][32] | ds[B][U] (fp32 scale, int32 sum)
+    const uint8_t* act;  // quantized activations: q[B][U][32] | ds[B][U] (fp32 scale, quant sum as fp32)
     long long rb;
     uint32_t act_bytes;
     int n, U, R, tiles, item0, pad_[4];
@@ -131,6 +146,17 @@ __device__ __forceinline__ int perm_pos(uint32_t type, int e)
     return e;
 }
 
+// Integer -> float conversions of the consumers.  Every converted value is an
+// integer of magnitude below 2^22, so adding it to the bit pattern of
+// 1.5 * 2^23 (whose ulp is 1) and subtracting 1.5 * 2^23 in fp32 gives the
+// same float as a conversion, exactly, on the full-rate add pipe.  The
+// activation records carry the block's quant sum as a float for the same
+// reason (|sum| <= 32 * 127).
+constexpr int kCvtBias = 0x4B400000;
+constexpr float kCvtBiasF = 12582912.0f;
+// float(v) for 0 <= v < 2^23 (scale codes)
+__device__ __forceinline__ float small_u2f(uint32_t v) { return __fsub_rn(__uint_as_float(0x4B000000u | v), 8388608.0f); }
+
 // Reference quantize_row_q8_0 (src/quant.c:143-158), one warp per block,
 // writing the engine's compact layout for the consuming job's weight type.
 constexpr int kMaxTasksInSmem = 256;
@@ -174,7 +200,7 @@ __global__ void __launch_bounds__(256) k_quant_tasks(const __grid_constant__ QPa
         T.act[((long long)t * T.U + u) * 32 + perm_pos(T.type, lane)] = (uint8_t)qq;
         if (lane == 0)
             reinterpret_cast<uint2*>(T.act + T.ds_off)[t * T.U + u] =
-                make_uint2(__float_as_uint(h2f_ref(f2h_ref(dd))), (uint32_t)sum);
+                make_uint2(__float_as_uint(h2f_ref(f2h_ref(dd))), __float_as_uint((float)sum));
     }
 }
 
@@ -208,13 +234,14 @@ __device__ __forceinline__ void put_terms(uint8_t* sm, const Item& it, int g, in
         const uint4 xa = *reinterpret_cast<const uint4*>(sm + xo);
         const uint4 xb = *reinterpret_cast<const uint4*>(sm + xo + 16);
         const uint2 ds = *reinterpret_cast<const uint2*>(sm + it.ds + (uint32_t)((t * it.U + xu) * 8));
-        int isum = dot8(wq, xa, xb);
-        const int bsum = (int)ds.y;
         const float dx = __uint_as_float(ds.x);
         float term;
-        if (KIND == 0) term = unit_term<T_Q8_0>(a, b, isum, bsum, dx);
-        else if (KIND == 2) term = unit_term<T_Q6_K>(a, b, isum - 32 * bsum, bsum, dx);
-        else term = unit_term<T_Q4_K>(a, b, isum, bsum, dx);
+        // The reference's term (src/quant.c:284, :433, :399) on exactly converted operands.
+        const float isf = __fsub_rn(__int_as_float(dot8_from(wq, xa, xb, kCvtBias)), kCvtBiasF);
+        const float bsf = __uint_as_float(ds.y);
+        if (KIND == 0) term = __fmul_rn(__fmul_rn(isf, a), dx);
+        else if (KIND == 2) term = __fmul_rn(__fmul_rn(a, __fsub_rn(isf, __fmul_rn(32.0f, bsf))), dx);
+        else term = __fmul_rn(__fsub_rn(__fmul_rn(a, isf), __fmul_rn(b, bsf)), dx);
         *reinterpret_cast<float*>(sm + it.terms + (uint32_t)((tu * it.TS + g * nb + t) * 4)) = term;
     }
 }
@@ -238,8 +265,8 @@ __device__ __forceinline__ void consume_k45(uint8_t* sm, const Item& it, int g, 
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint32_t scb = ((j < 4 ? hdr.y : hdr.z) >> (8 * (j & 3))) & 0xFFu;
-        const float sc = __fmul_rn((float)(scb & 63u), d);    // src/quant.c:385
-        const float m = __fmul_rn((float)(scb >> 6), dmin);   // src/quant.c:386
+        const float sc = __fmul_rn(small_u2f(scb & 63u), d);    // src/quant.c:385
+        const float m = __fmul_rn(small_u2f(scb >> 6), dmin);   // src/quant.c:386
         const uint4 q = *reinterpret_cast<const uint4*>(sm + qs + 16 * j);
         const int tu = 8 * s + j, xu = j * it.nblk + s;
         if (TYPE == T_Q4_K) {
@@ -252,7 +279,7 @@ __device__ __forceinline__ void consume_k45(uint8_t* sm, const Item& it, int g, 
                 const uint4 xa = *reinterpret_cast<const uint4*>(sm + xo);
                 const uint4 xb = *reinterpret_cast<const uint4*>(sm + xo + 16);
                 const uint2 ds = *reinterpret_cast<const uint2*>(sm + it.ds + (uint32_t)((t * it.U + xu) * 8));
-                int lo = __dp4a((int)l0, (int)xa.x, 0);
+                int lo = __dp4a((int)l0, (int)xa.x, kCvtBias);
                 lo = __dp4a((int)l1, (int)xa.z, lo);
                 lo = __dp4a((int)l2, (int)xb.x, lo);
                 lo = __dp4a((int)l3, (int)xb.z, lo);
@@ -261,7 +288,10 @@ __device__ __forceinline__ void consume_k45(uint8_t* sm, const Item& it, int g, 
                 hi = dp4a_us(h2, (int)xb.y, hi);
                 hi = dp4a_us(h3, (int)xb.w, hi);
                 const int isum = lo + (hi >> 4);
-                const float term = unit_term<T_Q4_K>(sc, m, isum, (int)ds.y, __uint_as_float(ds.x));
+                // src/quant.c:399 on exactly converted operands
+                const float term = __fmul_rn(__fsub_rn(__fmul_rn(sc, __fsub_rn(__int_as_float(isum), kCvtBiasF)),
+                                                       __fmul_rn(m, __uint_as_float(ds.y))),
+                                             __uint_as_float(ds.x));
                 *reinterpret_cast<float*>(sm + it.terms + (uint32_t)((tu * it.TS + g * nb + t) * 4)) = term;
             }
         } else {
@@ -551,7 +581,7 @@ struct JobIn {
 
 int units_of(uint32_t type, int d) { return (d / block_elems(type)) * block_units(type); }
 
-// Activation region of one input: q[B][U][32] then 8-byte (scale, sum) pairs.
+// Activation region of one input: q[B][U][32] then 8-byte (scale, quant sum as fp32) pairs.
 size_t act_ds_off(uint32_t type, int d, int B) { return (size_t)B * units_of(type, d) * 32; }
 size_t act_bytes_for(uint32_t type, int d, int B)
 {
@@ -633,7 +663,7 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
     pl = Plan{};
     if (njobs <= 0) return QUANTR_ERR_BAD_ARG;
     std::map<std::tuple<const float*, long long, int, int, int, int>, int> dedupe;  // x,ldx,d,B,U,perm -> task
-    constexpr size_t kSlotW = 44 * 1024, kTermMax = 16 * 1024;
+    constexpr size_t kSlotW = QR_ENG_SLOT_KB * 1024, kTermMax = 16 * 1024;
     std::vector<JobDesc> all;
     for (int j = 0; j < njobs; ++j) {
         const JobIn& a = in[j];
@@ -779,7 +809,7 @@ size_t engine_act_bytes(uint32_t type, int d, int B) { return eng::act_bytes_for
 // Jobs with B >= kTcMinB tokens (up to kTcMaxB) run on the tensor-core kernel
 // (tc.cu), the others on the dp4a engine above.
 #ifndef QR_TC_MIN_B
-#define QR_TC_MIN_B 5
+#define QR_TC_MIN_B 2
 #endif
 constexpr int kTcMinB = QR_TC_MIN_B;
 

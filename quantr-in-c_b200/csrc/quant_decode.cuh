@@ -115,9 +115,8 @@ __device__ __forceinline__ void decode_unit(const uint32_t* s32, const uint8_t* 
     }
 }
 
-__device__ __forceinline__ int dot8(const uint32_t* wq, uint4 xa, uint4 xb)
+__device__ __forceinline__ int dot8_from(const uint32_t* wq, uint4 xa, uint4 xb, int s)
 {
-    int s = 0;
     s = __dp4a((int)wq[0], (int)xa.x, s);
     s = __dp4a((int)wq[1], (int)xa.y, s);
     s = __dp4a((int)wq[2], (int)xa.z, s);
@@ -128,6 +127,8 @@ __device__ __forceinline__ int dot8(const uint32_t* wq, uint4 xa, uint4 xb)
     s = __dp4a((int)wq[7], (int)xb.w, s);
     return s;
 }
+
+__device__ __forceinline__ int dot8(const uint32_t* wq, uint4 xa, uint4 xb) { return dot8_from(wq, xa, xb, 0); }
 
 // One Q8_0 block per warp, lane = element: reference quantize_row_q8_0
 // (src/quant.c:143-158) with IEEE division, the fp32 reciprocal of the

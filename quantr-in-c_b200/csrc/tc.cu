@@ -20,12 +20,13 @@
 // done) and SE slots of epilogue data (weight scales and activation records,
 // free again when the stage's epilogue is done):
 //
-//   producer (warp 0)    lane 0, per stage: one 2-D TMA copy of the tile's
+//   weights (warp 0)     lane 0, per stage: one 2-D TMA copy of the tile's
 //                        packed weights (128 rows x one stage of bytes) for
 //                        jobs whose rows are 16-byte aligned (Q4_K, Q5_K);
-//                        lane 1, per stage: two cp.async.bulk copies, the
-//                        stage's activation operand tiles and per-(unit,
-//                        token) scale records;
+//   activations (last    lane 0, per stage: two cp.async.bulk copies, the
+//     warp)              stage's activation operand tiles and per-(unit,
+//                        token) scale records (a warp of its own: one lane
+//                        waiting on a barrier would stall the other's path);
 //   MMA (warp 1)         per unit: tcgen05.mma (issued by one elected lane of
 //                        the converged warp) into the stage's TMEM buffer (one
 //                        of NBS, 8 units x N columns each); after the stage,
@@ -40,11 +41,13 @@
 //                        unpacks each unit's quants into the canonical K-major
 //                        no-swizzle operand layout (8x16-byte core matrices)
 //                        and the unit's scales;
-//   epilogue (16 warps)  TMEM lane quarter (warp % 4) x one of 4 token
-//                        groups: per stage, tcgen05.ld of each unit's int32
-//                        sums (the next unit's load in flight while one is
-//                        used), then term and running sum per (row, token),
-//                        in unit order.
+//   epilogue (4 x EG     TMEM lane quarter (warp % 4) x one of EG token
+//     warps)             groups of NT tokens: per stage, tcgen05.ld of each
+//                        unit's int32 sums for the group's live tokens (the
+//                        next unit's load in flight while one is used), then
+//                        term and running sum per (row, token), in unit
+//                        order.  NT follows the launch's largest job (1, 2,
+//                        4 or 8 tokens; 8 or 16 for wider jobs).
 //
 // Activations are quantized by k_tc_quant (quantize_row_q8_0 per token, the
 // same kernel math as every other path) straight into operand tiles in the
@@ -94,13 +97,19 @@ constexpr int kGroupWarps = 4;  // one decoder thread per tile row in each decod
 constexpr unsigned kSleepEpi = QR_TC_SUSPEND_EPI, kSleepMma = QR_TC_SUSPEND_MMA, kSleepProd = QR_TC_SUSPEND_PROD,
                    kSleepDec = QR_TC_SUSPEND_DEC;
 // Warp split of a launch: DG decoder groups of four warps taking alternate
-// stages, and 4 TMEM lane quarters x EG epilogue token groups (N / EG tokens
-// each) after the producer and MMA warps.  Programs of up to 16 columns run
-// <2, 2> (decode-bound), wider ones <1, 4> (epilogue-bound).
+// stages, and 4 TMEM lane quarters x EG epilogue token groups (NT tokens
+// each) after the producer and MMA warps.  Launches whose jobs have at most 8
+// tokens run <2, 1> with NT = the token count rounded up to a power of two
+// (the MMA still computes N = 16 columns; the epilogue reads and evaluates
+// only the live ones), up to 16 tokens <2, 2> with NT = 8, wider ones <1, 4>
+// (epilogue-bound).
 template <int DG, int EG>
 struct Split {
     static constexpr int dec_warps = DG * kGroupWarps, epi_warps = 4 * EG;
-    static constexpr int threads = 32 * (2 + dec_warps + epi_warps);
+    // + weight producer, MMA warp and (last) activation producer.  The two
+    // producers are separate warps: lanes of one diverged warp that wait on
+    // different barriers would hold each other up.
+    static constexpr int threads = 32 * (3 + dec_warps + epi_warps);
 };
 constexpr int kMaxSW = 8;      // packed-weight slots
 constexpr int kMaxSO = 2;      // unpacked weight tile slots (MMA A operands)
@@ -186,6 +195,18 @@ __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::
 
 template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t addr, uint32_t (&v)[NC]);
+
+template <>
+__device__ __forceinline__ void tmem_ld<1>(uint32_t addr, uint32_t (&v)[1])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n" : "=r"(v[0]) : "r"(addr));
+}
+
+template <>
+__device__ __forceinline__ void tmem_ld<2>(uint32_t addr, uint32_t (&v)[2])
+{
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];\n" : "=r"(v[0]), "=r"(v[1]) : "r"(addr));
+}
 
 template <>
 __device__ __forceinline__ void tmem_ld<4>(uint32_t addr, uint32_t (&v)[4])
@@ -374,6 +395,20 @@ __device__ __forceinline__ void epi_unit(const uint32_t (&v)[NT], uint32_t scale
 {
     const uint2 scm = lds64(scale_at);
     const float sc = __uint_as_float(scm.x), m = __uint_as_float(scm.y);
+    if constexpr (NT < 4) {  // one or two tokens: word loads of the records
+#pragma unroll
+        for (int q = 0; q < NT; ++q) {
+            const int isum = (int)v[q];
+            const float d = __uint_as_float(lds32(rec_at + (uint32_t)q * 4));
+            const uint32_t ax = TYPE != T_Q8_0 ? lds32(rec_at + aux_off + (uint32_t)q * 4) : 0u;
+            float term;
+            if (TYPE == T_Q8_0) term = __fmul_rn(__fmul_rn((float)isum, sc), d);  // src/quant.c:284
+            else if (TYPE == T_Q6_K) term = __fmul_rn(__fmul_rn(sc, (float)(isum - (int)ax)), d);  // :433
+            else term = __fmul_rn(__fsub_rn(__fmul_rn(sc, (float)isum), __fmul_rn(m, __uint_as_float(ax))), d);  // :399
+            acc[q] = __fadd_rn(acc[q], term);
+        }
+        return;
+    }
 #pragma unroll
     for (int t4 = 0; t4 < NT; t4 += 4) {
         const uint4 dx = lds128(rec_at + (uint32_t)t4 * 4);
@@ -595,7 +630,7 @@ __device__ __forceinline__ void wait_groups_but(int n)
     }
 }
 
-template <int DG, int EG>
+template <int DG, int EG, int NT>
 __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const __grid_constant__ TcParams p)
 {
     constexpr int kDecWarps = Split<DG, EG>::dec_warps, kEpiWarps = Split<DG, EG>::epi_warps;
@@ -677,7 +712,7 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
     pdl_trigger();
 
     if (warp == 0) {
-        // ------------------------------------------------------ producer --
+        // ----------------------------------------------- weight producer --
         if (lane == 0) {
             // Weight ring: waits for every stage's slot (so it never runs more
             // than SW stages ahead of the decoders), copies the TMA jobs'.
@@ -704,34 +739,6 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
                             "l"(reinterpret_cast<uint64_t>(&p.tmap[jc])), "r"(x), "r"(y), "r"(sptr(&br.wfull[ws]))
                             : "memory");
                     }
-                }
-            }
-        } else if (lane == 1) {
-            // Operand ring: activation tiles and records of each stage.
-            pdl_wait();  // activations come from the quantizer grid
-            int bs = 0, bu = 0, es = 0, eu = 0;  // this stage's slots, earlier uses of them
-            bool ok = true;
-            for (int k = 0; ok && k < sc.cnt; ++k) {
-                const TcJob& J = jobs[sc.job(k)];
-                for (int st = 0; st < (int)J.nst;
-                     ++st, (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
-                    // B slot: the MMAs of its previous stage are done; record
-                    // slot: the epilogue of its previous stage is done.
-                    if ((bu > 0 && !mbar_wait_bounded(&br.bfree[bs], (bu - 1) & 1, p.err, abort_flag, kSleepProd)) ||
-                        (eu > 0 && !mbar_wait_bounded(&br.efree[es], (eu - 1) & 1, p.err, abort_flag, kSleepProd))) {
-                        ok = false;
-                        break;
-                    }
-                    const int us = min(kUS, (int)J.U - kUS * st);
-                    const uint32_t bbytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
-                    mbar_arrive_expect_tx(&br.bfull[bs], bbytes);
-                    misc[kFillB + bs] += 1;
-                    bulk_g2s(sm + p.b_off + p.b_slot * (uint32_t)bs, J.act + (size_t)kUS * st * J.N * 32, bbytes,
-                             &br.bfull[bs]);
-                    mbar_arrive_expect_tx(&br.dfull[es], dbytes);
-                    misc[kFillD + es] += 1;
-                    bulk_g2s(sm + p.e_off + p.e_slot * (uint32_t)es + p.d_rel, J.ds + (size_t)kUS * st * J.N * 16,
-                             dbytes, &br.dfull[es]);
                 }
             }
         }
@@ -908,14 +915,41 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
             issue(next_own(cur), gs + DG);  // the group's next stage
         }
         asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into shared memory outlives the role
-    } else {
+    } else if (warp < 2 + kDecWarps + kEpiWarps) {
         // ------------------------------------------------------ epilogue --
-        if constexpr (EG == 2) {
-            epilogue_role<16 / EG, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
-        } else {
-            if (p.ncol == 32) epilogue_role<32 / EG, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
-            else epilogue_role<64 / EG, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
+        epilogue_role<NT, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
+    } else {
+        // ------------------------------------------ activation producer --
+        if (lane == 0) {
+            // Operand ring: activation tiles and records of each stage.
+            pdl_wait();  // activations come from the quantizer grid
+            int bs = 0, bu = 0, es = 0, eu = 0;  // this stage's slots, earlier uses of them
+            bool ok = true;
+            for (int k = 0; ok && k < sc.cnt; ++k) {
+                const TcJob& J = jobs[sc.job(k)];
+                for (int st = 0; st < (int)J.nst;
+                     ++st, (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
+                    // B slot: the MMAs of its previous stage are done; record
+                    // slot: the epilogue of its previous stage is done.
+                    if ((bu > 0 && !mbar_wait_bounded(&br.bfree[bs], (bu - 1) & 1, p.err, abort_flag, kSleepProd)) ||
+                        (eu > 0 && !mbar_wait_bounded(&br.efree[es], (eu - 1) & 1, p.err, abort_flag, kSleepProd))) {
+                        ok = false;
+                        break;
+                    }
+                    const int us = min(kUS, (int)J.U - kUS * st);
+                    const uint32_t bbytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
+                    mbar_arrive_expect_tx(&br.bfull[bs], bbytes);
+                    misc[kFillB + bs] += 1;
+                    bulk_g2s(sm + p.b_off + p.b_slot * (uint32_t)bs, J.act + (size_t)kUS * st * J.N * 32, bbytes,
+                             &br.bfull[bs]);
+                    mbar_arrive_expect_tx(&br.dfull[es], dbytes);
+                    misc[kFillD + es] += 1;
+                    bulk_g2s(sm + p.e_off + p.e_slot * (uint32_t)es + p.d_rel, J.ds + (size_t)kUS * st * J.N * 16,
+                             dbytes, &br.dfull[es]);
+                }
+            }
         }
+        __syncwarp();
     }
 
     tc_fence_before();
@@ -960,6 +994,7 @@ struct TcPlan {
     uint32_t* d_sched = nullptr;
     int* d_sched_off = nullptr;
     uint8_t* d_act = nullptr;
+    int bmax = 1;  // most tokens of any job: selects the epilogue's tokens per thread
 };
 
 int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
@@ -975,7 +1010,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     std::map<std::tuple<const float*, long long, int, int, int>, int> dedupe;
     size_t act_total = 0;
     long long blocks = 0;
-    int Nmax = 16, item = 0;
+    int Nmax = 16, Bmax = 1, item = 0;
     std::vector<size_t> task_act_off;
     std::vector<int> job_task;
     for (int j = 0; j < njobs; ++j) {
@@ -1010,6 +1045,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         J.item0 = item;
         item += J.tiles;
         Nmax = std::max(Nmax, (int)J.N);
+        Bmax = std::max(Bmax, a.B);
         const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
         auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, perm);
         auto it = dedupe.find(key);
@@ -1141,6 +1177,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.SB = (uint32_t)SB;
     pp.SE = (uint32_t)SE;
     pp.ncol = (uint32_t)Nmax;
+    P->bmax = Bmax;
     pp.NB = (uint32_t)std::min(kMaxNB, 512 / (kUS * Nmax));  // 4, 2 or 1 stage buffers for N = 16, 32, 64
     uint32_t cols = 32;
     while (cols < pp.NB * kUS * pp.ncol) cols <<= 1;
@@ -1201,23 +1238,37 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     return QUANTR_OK;
 }
 
+namespace tc {
+
+template <int DG, int EG, int NT>
+cudaError_t launch_tc(const TcPlan* P, const TcParams& pp, const LaunchCfg& c)
+{
+    static int configured = -1;
+    cudaError_t e = ensure_smem_attr(&k_tc_program<DG, EG, NT>, (int)kSmemMax, configured);
+    if (e != cudaSuccess) return e;
+    return launch_ex(&k_tc_program<DG, EG, NT>, dim3(P->grid), dim3(Split<DG, EG>::threads), P->smem, c, pp);
+}
+
+} // namespace tc
+
 cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
 {
     using namespace tc;
     LaunchCfg c;
     c.stream = stream;
-    static int configured_narrow = -1, configured_wide = -1;
-    const bool narrow = P->pp.ncol <= 16;  // see Split
-    cudaError_t e = narrow ? ensure_smem_attr(&k_tc_program<2, 2>, (int)kSmemMax, configured_narrow)
-                           : ensure_smem_attr(&k_tc_program<1, 4>, (int)kSmemMax, configured_wide);
-    if (e != cudaSuccess) return e;
     const long long qgrid = std::max(1LL, std::min<long long>((P->qp.total + 255) / 256, 8LL * device_sm_count()));
-    e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
+    cudaError_t e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
     if (e != cudaSuccess) return e;
     TcParams pp = P->pp;
     pp.err = err;
-    if (narrow) return launch_ex(&k_tc_program<2, 2>, dim3(P->grid), dim3(Split<2, 2>::threads), P->smem, c, pp);
-    return launch_ex(&k_tc_program<1, 4>, dim3(P->grid), dim3(Split<1, 4>::threads), P->smem, c, pp);
+    // The split and the epilogue's tokens per thread (see Split).
+    if (P->bmax <= 1) return launch_tc<2, 1, 1>(P, pp, c);
+    if (P->bmax <= 2) return launch_tc<2, 1, 2>(P, pp, c);
+    if (P->bmax <= 4) return launch_tc<2, 1, 4>(P, pp, c);
+    if (P->bmax <= 8) return launch_tc<2, 1, 8>(P, pp, c);
+    if (pp.ncol <= 16) return launch_tc<2, 2, 8>(P, pp, c);
+    if (pp.ncol == 32) return launch_tc<1, 4, 8>(P, pp, c);
+    return launch_tc<1, 4, 16>(P, pp, c);
 }
 
 void tc_plan_destroy(TcPlan* P)
