@@ -12,7 +12,7 @@
 //                        mbarrier transaction counts signal "slot full".  It
 //                        runs up to S items ahead, so HBM streaming never waits
 //                        for compute.
-//   consumers (12 warps) decode one row x super-block (or Q8_0 block) per
+//   consumers (16 warps) decode one row x super-block (or Q8_0 block) per
 //                        thread and evaluate the reference's exact per-unit
 //                        terms (dp4a integer sums, explicitly rounded fp32
 //                        ops) into one of T term buffers.  Work is dealt
@@ -52,7 +52,7 @@ namespace qr {
 namespace eng {
 
 #ifndef QR_ENG_CONSUMER_WARPS
-#define QR_ENG_CONSUMER_WARPS 12
+#define QR_ENG_CONSUMER_WARPS 16
 #endif
 #ifndef QR_ENG_CHAIN_WARPS
 #define QR_ENG_CHAIN_WARPS 2

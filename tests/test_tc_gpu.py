@@ -1,4 +1,4 @@
-"""GPU: programs of 5..64-token GEMVs, which run on the tensor cores
+"""GPU: programs of 2..64-token GEMVs, which run on the tensor cores
 (tcgen05.mma kind::i8 per 32-element unit, exact terms and running sums from
 TMEM), against the oracle.  Bit-identical to the reference's scalar build, like
 every other path (the north-star tolerance 1e-5 rel / 1e-6 abs is asserted too).
@@ -55,7 +55,7 @@ def run(prog):
 
 @pytest.mark.parametrize("type_,n,d", [(Q4_K, 257, 2048), (Q5_K, 130, 2048), (Q6_K, 200, 1408), (Q8_0, 129, 288),
                                        (Q8_0, 300, 2048), (Q6_K, 64, 256)])
-@pytest.mark.parametrize("B", [5, 9, 16, 33, 64])
+@pytest.mark.parametrize("B", [2, 3, 4, 5, 9, 16, 33, 64])
 def test_tc_types_and_batches(qr_gpu, orc, type_, n, d, B):
     """Ragged row tiles (n not a multiple of 128), Q6_K/Q8_0 rows that are
     not 16-byte aligned, a partial last stage (Q8_0 d=288: 9 blocks)."""
@@ -105,3 +105,28 @@ def test_tc_rerun_new_inputs_and_graph(qr_gpu, orc):
     torch.cuda.synchronize()
     check(orc, new)
     del g
+
+
+@pytest.mark.parametrize("B", [2, 3, 4])
+def test_tc_small_batches_strided_x(qr_gpu, orc, B):
+    """Few-token jobs on the tensor cores with rows of x that are not 16-byte
+    aligned (ldx = d + 1: the quantizer's scalar loads), and jobs of different
+    token counts (and epilogue widths) sharing one launch."""
+    rng = synth.rng_for(300 + B)
+    specs = [(Q4_K, 300, 1024, B), (Q6_K, 130, 512, 1 + (B % 2)), (Q8_0, 200, 320, B), (Q5_K, 64, 256, 2)]
+    jobs, keep, host = [], [], []
+    for type_, n, d, b in specs:
+        w = synth.matrix(rng, type_, n, d)
+        x = synth.activations(rng, b, d)
+        xs = np.zeros((b, d + 1), np.float32)
+        xs[:, :d] = x
+        xd = torch.from_numpy(xs).cuda()
+        wd = torch.from_numpy(np.ascontiguousarray(w)).cuda()
+        out = torch.full((b, n), float("nan"), device="cuda")
+        keep += [wd, xd, out]
+        host.append((w, x, type_, n, d, out))
+        jobs.append((wd.data_ptr(), type_, n, d, b, xd.data_ptr(), d + 1, out.data_ptr(), n))
+    prog = qr_gpu.Program(jobs)
+    run(prog)
+    check(orc, host)
+    assert qr_gpu.device_status() == 0
