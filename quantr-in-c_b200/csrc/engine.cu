@@ -18,7 +18,7 @@
 //                        ops) into one of T term buffers.  Work is dealt
 //                        round-robin over the concatenation of all items, so a
 //                        thread idle at the end of one tile starts the next.
-//   chain (2 warps)      sum each (row, token)'s terms left to right - the
+//   chain (3 warps)      sum each (row, token)'s terms left to right - the
 //                        reference's accumulation order, src/quant.c:279-285,
 //                        :384-401, :422-435 - and store the fp32 outputs,
 //                        while the consumers already work on later items.
@@ -55,7 +55,7 @@ namespace eng {
 #define QR_ENG_CONSUMER_WARPS 16
 #endif
 #ifndef QR_ENG_CHAIN_WARPS
-#define QR_ENG_CHAIN_WARPS 2
+#define QR_ENG_CHAIN_WARPS 3
 #endif
 constexpr int kConsumerWarps = QR_ENG_CONSUMER_WARPS;
 constexpr int kChainWarps = QR_ENG_CHAIN_WARPS;
@@ -71,6 +71,13 @@ constexpr int kConsumerThreads = 32 * kConsumerWarps;
 #ifndef QR_ENG_SLOT_KB
 #define QR_ENG_SLOT_KB 44
 #endif
+// Longest suspension (ns) of one barrier poll: a waiting warp sleeps until
+// the phase completes (or this long) instead of spinning on issue slots the
+// working warps need.
+#ifndef QR_ENG_SUSPEND_NS
+#define QR_ENG_SUSPEND_NS 1000
+#endif
+constexpr unsigned kSuspendNs = QR_ENG_SUSPEND_NS;
 #ifndef QR_ENG_TERMS
 #define QR_ENG_TERMS 4
 #endif
@@ -470,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
             for (; i < p.total_items; ++k, i += P) {
                 jc = job_of(jobs, p.njobs, i, jc);
                 const int slot = k % S;
-                if (!mbar_wait_bounded(&wempty[slot], ((k / S) - 1) & 1, p.err, abort_flag)) break;
+                if (!mbar_wait_bounded(&wempty[slot], ((k / S) - 1) & 1, p.err, abort_flag, kSuspendNs)) break;
                 issue_w(jobs[jc], i, slot);
                 issue_x(jobs[jc], slot);
             }
@@ -481,8 +488,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
         int rot = 0;  // sum of earlier items' work, mod kConsumerThreads
         for (int k = 0, i = c; i < p.total_items; ++k, i += P) {
             const int slot = k % S, tb = k % T;
-            if (!mbar_wait_bounded(&wfull[slot], (k / S) & 1, p.err, abort_flag)) break;
-            if (k >= T && !mbar_wait_bounded(&tempty[tb], ((k / T) - 1) & 1, p.err, abort_flag)) break;
+            if (!mbar_wait_bounded(&wfull[slot], (k / S) & 1, p.err, abort_flag, kSuspendNs)) break;
+            if (k >= T && !mbar_wait_bounded(&tempty[tb], ((k / T) - 1) & 1, p.err, abort_flag, kSuspendNs)) break;
             const uint32_t base = p.slot_off + (uint32_t)slot * p.slot_bytes;
             const ItemHdr h = *reinterpret_cast<const ItemHdr*>(sm + base);
             Item it;
@@ -517,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
         const int ch = warp - 1 - kConsumerWarps;
         for (int k = ch, i = c + ch * P; i < p.total_items; k += kChainWarps, i += kChainWarps * P) {
             const int tb = k % T;
-            if (!mbar_wait_bounded(&tfull[tb], (k / T) & 1, p.err, abort_flag)) break;
+            if (!mbar_wait_bounded(&tfull[tb], (k / T) & 1, p.err, abort_flag, kSuspendNs)) break;
             const uint32_t tbase = p.term_off + (uint32_t)tb * p.term_bytes;
             const ItemHdr h = *reinterpret_cast<const ItemHdr*>(sm + tbase);
             const float* terms = reinterpret_cast<const float*>(sm + tbase + kHdr);

@@ -94,6 +94,18 @@ constexpr int kGroupWarps = 4;  // one decoder thread per tile row in each decod
 #ifndef QR_TC_SUSPEND_DEC
 #define QR_TC_SUSPEND_DEC 1000
 #endif
+#ifndef QR_TC_N16_EG
+#define QR_TC_N16_EG 2
+#endif
+#ifndef QR_TC_B8_EG
+#define QR_TC_B8_EG 2
+#endif
+#ifndef QR_TC_B4_EG
+#define QR_TC_B4_EG 1
+#endif
+#ifndef QR_TC_N16_DG
+#define QR_TC_N16_DG 2
+#endif
 constexpr unsigned kSleepEpi = QR_TC_SUSPEND_EPI, kSleepMma = QR_TC_SUSPEND_MMA, kSleepProd = QR_TC_SUSPEND_PROD,
                    kSleepDec = QR_TC_SUSPEND_DEC;
 // Warp split of a launch: DG decoder groups of four warps taking alternate
@@ -1263,10 +1275,10 @@ cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
     pp.err = err;
     // The split and the epilogue's tokens per thread (see Split).
     if (P->bmax <= 1) return launch_tc<2, 1, 1>(P, pp, c);
-    if (P->bmax <= 2) return launch_tc<2, 1, 2>(P, pp, c);
-    if (P->bmax <= 4) return launch_tc<2, 1, 4>(P, pp, c);
-    if (P->bmax <= 8) return launch_tc<2, 1, 8>(P, pp, c);
-    if (pp.ncol <= 16) return launch_tc<2, 2, 8>(P, pp, c);
+    if (P->bmax <= 2) return launch_tc<2, QR_TC_B4_EG, 2 / QR_TC_B4_EG>(P, pp, c);
+    if (P->bmax <= 4) return launch_tc<2, QR_TC_B4_EG, 4 / QR_TC_B4_EG>(P, pp, c);
+    if (P->bmax <= 8) return launch_tc<2, QR_TC_B8_EG, 8 / QR_TC_B8_EG>(P, pp, c);
+    if (pp.ncol <= 16) return launch_tc<QR_TC_N16_DG, QR_TC_N16_EG, 16 / QR_TC_N16_EG>(P, pp, c);
     if (pp.ncol == 32) return launch_tc<1, 4, 8>(P, pp, c);
     return launch_tc<1, 4, 16>(P, pp, c);
 }
