@@ -20,6 +20,9 @@ value  : whole-job GB/s of algorithmic bytes (packed weights + fp32 x + fp32
 e2e    : the same metric through the reference-facing C ABI
          (matmul_q_fused_batch with HOST arrays; weights registered once, like
          the reference's load-time mmap), host<->device copies inside.
+batch_sweep : the rest of the c2 sweep (batch 4 and 16 by default, --sweep)
+         on the same weights, timed like `value`; jobs of 2+ tokens run on
+         the tensor-core kernel.
 N > 1  : every rank runs its own replica of the step on its GPU (the GEMV
          metric shards by independent work; no collective on the data path),
          so scaling is weak.
@@ -49,10 +52,10 @@ Q4_K = 12
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one k_program launch of the c2 step, from the
-# ncu capture summarised in profiles/k_program_c2_full.md: 159,996,160 read +
-# 5,175,552 written (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB
+# ncu capture summarised in profiles/k_program_c2_full.md: 159,993,600 read +
+# 4,826,624 written (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB
 # out per step).
-NCU_TRAFFIC_PER_STEP = 165171712
+NCU_TRAFFIC_PER_STEP = 164820224
 
 
 def row_bytes(t, d):
@@ -316,6 +319,40 @@ def ours_arm(args):
     torch.cuda.synchronize()
     per_call_gbs = nbytes * args.steps / (ev2.elapsed_time(ev3) / 1e3) / 1e9
 
+    # The rest of the c2 batch sweep (batch 1, 4 and 16): the same 72 weights
+    # at the other batch sizes, device-resident inputs, CUDA-graph replays
+    # timed with CUDA events like `value` (rank-local; reported per GPU).
+    sweep = {}
+    for Bs in args.sweep:
+        if Bs == B:
+            continue
+        xs = [torch.from_numpy(synth.activations(rng, Bs, d)).to(dev) for _, _, d, _ in shapes]
+        os_ = [torch.empty(Bs, n, device=dev) for _, n, _, _ in shapes]
+        pr = quantr.Program([(w.data_ptr(), t, n, d, Bs, x.data_ptr(), d, o.data_ptr(), n)
+                             for (t, n, d, _), w, x, o in zip(shapes, dev_w, xs, os_)])
+        with torch.cuda.stream(s):
+            pr.run(s.cuda_stream)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                pr.run(s.cuda_stream)
+            for _ in range(args.warmup):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(args.steps):
+                g.replay()
+            e1.record(s)
+        torch.cuda.synchronize()
+        assert quantr.device_status(0) == 0
+        t_ms = e0.elapsed_time(e1) / args.steps
+        nb = sum(gemv_bytes(t, n, d, Bs) for t, n, d, _ in shapes)
+        sweep[str(Bs)] = {"GB/s": round(nb / (t_ms / 1e3) / 1e9, 2), "ms_per_step": round(t_ms, 5),
+                          "tok_per_s": round(Bs / (t_ms / 1e3), 1),
+                          "path": "tensor cores (tcgen05.mma kind::i8)" if Bs >= 2 else "dp4a engine"}
+        del g
+        pr.close()
+
     # End to end with HOST buffers, (a) through the C-ABI program call: every
     # step copies all 72 inputs from pinned host memory to the device, runs
     # the program, and copies all outputs back; CUDA events bracket the copies.
@@ -404,6 +441,7 @@ def ours_arm(args):
             "e2e_dropin": {"value": round(e2e_dropin_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                            "d2h_bytes_per_step": d2h,
                            "api": "72 synchronous matmul_q_fused_batch calls per step with host arrays"},
+            "batch_sweep": sweep,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
@@ -425,6 +463,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", type=lambda v: [int(b) for b in v.split(",") if b], default=[4, 16],
+                    help="other batch sizes timed on the same weights (comma list; empty to skip)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
