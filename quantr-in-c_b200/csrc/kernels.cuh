@@ -93,6 +93,20 @@ struct GemvJobIn {
     long long ldx;
     float* out;
     long long ldo;
+    // Gathered job (the pairs routed to one MoE expert; tensor-core path
+    // only): counts[e] live columns (a device value an earlier launch
+    // writes), processed B = 16 at a time; column i stands for the pair
+    // list[offsets[e] + i], its output row.  Its activations are operand
+    // tiles (act/ds), one set of U units per 16 columns.  Null counts: all B
+    // columns live, output row = column.
+    const int* g_counts = nullptr;
+    const int* g_offsets = nullptr;
+    const int* g_list = nullptr;
+    int g_e = 0;
+    // Activations already quantized into operand tiles ([U] x N x 32 bytes)
+    // and records ([U] x N x 16 bytes, tensor-core layout): x is unused.
+    const uint8_t* act = nullptr;
+    const uint8_t* ds = nullptr;
 };
 
 // Plans a tensor-core program (B <= kTcMaxB per job, at most kTcMaxJobs

@@ -23,6 +23,11 @@
 //            chose are never read); silu(h1)*h3 fused with the Q8_0
 //            quantization of hb per pair; grouped GEMV for W2 -> o per pair;
 //   combine: out = sum over slots in selection order of o*ew, from +0.0.
+// From kMoeTcMinT tokens on, the experts stage runs on the tensor cores
+// instead: each local pair's xb (and later hb) is quantized into its expert's
+// operand tiles (16 pairs per chunk), and every (expert, matrix) is one
+// gathered tcgen05 GEMV job over its pairs (tc.cu; counts and pair lists stay
+// on the device).
 // Every GEMV output is bit-identical to the reference's matmul_q_fused for
 // that (row, pair).  expf is evaluated correctly rounded (through double
 // precision), which differs from glibc's expf in rare last-bit cases.
@@ -34,6 +39,10 @@
 
 #include <algorithm>
 #include <cuda_runtime.h>
+#include <map>
+#include <mutex>
+#include <tuple>
+#include <vector>
 
 namespace qr {
 namespace {
@@ -111,7 +120,7 @@ __global__ void __launch_bounds__(128)
 // per local expert in pair order (warp ballots), with counts and offsets.
 __global__ void __launch_bounds__(1024)
     k_moe_group(const int* __restrict__ sel, int P, int e0, int El, int* __restrict__ counts,
-                int* __restrict__ offsets, int* __restrict__ list)
+                int* __restrict__ offsets, int* __restrict__ list, int* __restrict__ pos)
 {
     __shared__ int cnt[kMoeMaxExperts];
     __shared__ int off[kMoeMaxExperts + 1];
@@ -146,7 +155,11 @@ __global__ void __launch_bounds__(1024)
             const int q = p0 + lane;
             const bool hit = q < P && sel[q] == e0 + e;
             const unsigned mk = __ballot_sync(0xffffffffu, hit);
-            if (hit) list[o + __popc(mk & ((1u << lane) - 1u))] = q;
+            if (hit) {
+                const int r = o + __popc(mk & ((1u << lane) - 1u));
+                list[r] = q;
+                pos[q] = r - off[e];  // the pair's place among its expert's pairs
+            }
             o += __popc(mk);
         }
     }
@@ -306,6 +319,91 @@ __global__ void __launch_bounds__(kThreads)
     }
 }
 
+// Position of element e (0..31) of a unit in the tensor-core operand row for
+// a weight type (the element order its decoder produces).
+__device__ __forceinline__ int tc_elem_pos(uint32_t type, int e)
+{
+    if (type == T_Q4_K || type == T_Q5_K) return (e & ~7) + ((e & 1) << 2) + ((e & 7) >> 1);
+    if (type == T_Q6_K) return (e & ~15) + ((e & 3) << 2) + ((e & 15) >> 2);
+    return e;
+}
+
+// Tensor-core operand tiles of the pairs routed to each local expert: the
+// pairs of local expert e, in list order (pos[p] = place of pair p), in chunks
+// of 16 columns; chunk c of expert e holds U units of 16 x 32 quant bytes at
+// tiles + ((e*nch + c)*U + u)*512 (column i%16 at (i/8)*256 + (i%8)*16 + (k/16)*128
+// + k%16 for element order position k) and records (dx | bsum | 32*bsum, 16
+// floats each) at recs + ((e*nch + c)*U + u)*256.
+__device__ __forceinline__ void put_tile_block(uint8_t* tiles, uint8_t* recs, int e, int nch, int U, int u, int i,
+                                               int kk, int lane, int8_t qq, uint32_t h, int sum)
+{
+    const long long unit = ((long long)e * nch + (i >> 4)) * U + u;
+    const int c = i & 15;
+    tiles[unit * 512 + (c >> 3) * 256 + (c & 7) * 16 + (kk >> 4) * 128 + (kk & 15)] = (uint8_t)qq;
+    if (lane == 0) {
+        float* rec = reinterpret_cast<float*>(recs + unit * 256);
+        rec[c] = h2f_ref(h);
+        rec[16 + c] = (float)sum;
+        rec[32 + c] = __int_as_float(32 * sum);
+    }
+}
+
+// xb of each local pair's token, quantized (quantize_row_q8_0, as every path)
+// into W1's operand tiles and, when W3's element order or unit count differ,
+// W3's.
+__global__ void __launch_bounds__(kThreads)
+    k_moe_x_tc(const float* __restrict__ xb, long long ldx, int P, int k, const int* __restrict__ sel,
+               const int* __restrict__ pos, int e0, int El, int nch, int U1, uint32_t type1, uint8_t* tiles1,
+               uint8_t* recs1, int U3, uint32_t type3, uint8_t* tiles3, uint8_t* recs3)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int Um = max(U1, tiles3 ? U3 : 0);
+    const long long total = (long long)P * Um;
+    const long long step = (long long)gridDim.x * (kThreads / 32);
+    const int k1 = tc_elem_pos(type1, lane), k3 = tc_elem_pos(type3, lane);
+    for (long long wb = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); wb < total; wb += step) {
+        const int pr = (int)(wb / Um);
+        const int b = (int)(wb - (long long)pr * Um);
+        const int se = sel[pr];
+        if (se < e0 || se >= e0 + El) continue;  // not a local pair (warp-uniform)
+        const float v = xb[(long long)(pr / k) * ldx + b * 32 + lane];
+        uint32_t h;
+        int sum;
+        const int8_t qq = q8_block_warp(v, h, sum);
+        if (b < U1) put_tile_block(tiles1, recs1, se - e0, nch, U1, b, pos[pr], k1, lane, qq, h, sum);
+        if (tiles3 && b < U3) put_tile_block(tiles3, recs3, se - e0, nch, U3, b, pos[pr], k3, lane, qq, h, sum);
+    }
+}
+
+// hb = silu(h1)*h3 per local pair (src/runtime.c:254-256), quantized (the
+// same arithmetic as k_moe_act) into W2's operand tiles.
+__global__ void __launch_bounds__(kThreads)
+    k_moe_act_tc(const float* __restrict__ h1, const float* __restrict__ h3, int hidden, int P,
+                 const int* __restrict__ sel, const int* __restrict__ pos, int e0, int El, int nch, int U2,
+                 uint32_t type2, uint8_t* __restrict__ tiles, uint8_t* __restrict__ recs)
+{
+    pdl_trigger();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const long long total = (long long)P * U2;
+    const long long step = (long long)gridDim.x * (kThreads / 32);
+    const int kk = tc_elem_pos(type2, lane);
+    for (long long wb = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); wb < total; wb += step) {
+        const int pr = (int)(wb / U2);
+        const int b = (int)(wb - (long long)pr * U2);
+        const int se = sel[pr];
+        if (se < e0 || se >= e0 + El) continue;  // not a local pair (warp-uniform)
+        const long long x = (long long)pr * hidden + b * 32 + lane;
+        const float v = __fmul_rn(silu_ref(h1[x]), h3[x]);
+        uint32_t h;
+        int sum;
+        const int8_t qq = q8_block_warp(v, h, sum);
+        put_tile_block(tiles, recs, se - e0, nch, U2, b, pos[pr], kk, lane, qq, h, sum);
+    }
+}
+
 // out[t][i] = ((0 + o[t,0][i]*w[t,0]) + o[t,1][i]*w[t,1]) + ... in selection
 // order (src/runtime.c:241, 262-264).
 __global__ void __launch_bounds__(kThreads)
@@ -349,8 +447,12 @@ __global__ void __launch_bounds__(kThreads)
 // Workspace: probs (route) | counts | offsets | list | xb quants | h1 | h3 |
 // hb quants (experts).  One layout serves every stage.
 struct MoeWs {
-    size_t probs, counts, offsets, list, actx, h1, h3, acth, total;
+    size_t probs, counts, offsets, list, pos, actx, h1, h3, acth, t1, r1, t3, r3, t2, r2, total;
 };
+
+// Chunks of 16 pairs per local expert on the tensor-core path (an expert has
+// at most T pairs: a token picks an expert once; the path takes T <= kTcMaxB).
+int moe_tc_chunks(int T) { return (T + 15) / 16; }
 
 size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -368,10 +470,21 @@ MoeWs moe_layout(int T, int E, int k, int dim, int hidden)
     w.counts = take((size_t)E * 4);
     w.offsets = take((size_t)(E + 1) * 4);
     w.list = take(P * 4);
+    w.pos = take(P * 4);
     w.actx = take(actq_bytes(dim, T));
     w.h1 = take(P * hidden * 4);
     w.h3 = take(P * hidden * 4);
     w.acth = take(actq_bytes(hidden, (int)P));
+    // Operand tiles per local expert for the tensor-core path (W1, W3 when its
+    // element order differs, W2): up to d/32 units x 16 columns x (32 quant +
+    // 16 record bytes) per chunk.
+    const size_t ch = T <= kTcMaxB ? (size_t)E * moe_tc_chunks(T) : 0;
+    w.t1 = take(ch * (dim / 32) * 512);
+    w.r1 = take(ch * (dim / 32) * 256);
+    w.t3 = take(ch * (dim / 32) * 512);
+    w.r3 = take(ch * (dim / 32) * 256);
+    w.t2 = take(ch * (hidden / 32) * 512);
+    w.r2 = take(ch * (hidden / 32) * 256);
     w.total = off;
     return w;
 }
@@ -479,6 +592,147 @@ cudaError_t launch_moe_route(const MoeRoute& r, const LaunchCfg& c)
     return e;
 }
 
+namespace {
+
+// Tensor-core path of the experts stage: the W1/W3 GEMVs of every local
+// expert as gathered jobs over all T tokens' quantized xb (each expert's live
+// columns = the tokens of its pairs, outputs to the pairs' rows of h1/h3), and
+// W2 as gathered jobs over per-expert operand tiles of hb (k_moe_act_tc).
+struct MoeTcPlans {
+    std::vector<TcPlan*> a, b;
+};
+
+// Fewest tokens for the tensor-core path.  Measured on B200 (us per layer,
+// tensor cores / dp4a): c4 shapes T = 16: 266 / 212, T = 32: 328 / 302,
+// T = 64: 341 / 433; c5 T = 16: 300 / 252, T = 64: 389 / 501.  With a few
+// pairs per expert the dp4a kernel, which stages each chosen expert's rows
+// once with no pipeline to fill, is faster.
+#ifndef QR_MOE_TC_MIN_T
+#define QR_MOE_TC_MIN_T 48
+#endif
+constexpr int kMoeTcMinT = QR_MOE_TC_MIN_T;
+
+bool tc_type(uint32_t t) { return t == T_Q8_0 || t == T_Q4_K || t == T_Q5_K || t == T_Q6_K; }
+
+// 32-element units of a row of d columns (whole blocks only, src/quant.c:477-484).
+int units_of_type(uint32_t t, int d) { return (d / block_elems(t)) * block_units(t); }
+
+// Device pointers of the local experts' matrices (a pointer table is read
+// once, here).
+bool expert_ptrs(const ExpertMats& m, int El, std::vector<const uint8_t*>& out)
+{
+    out.resize((size_t)El);
+    if (m.table) {
+        if (cudaMemcpy(out.data(), m.table, sizeof(void*) * (size_t)El, cudaMemcpyDeviceToHost) != cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
+    } else {
+        for (int e = 0; e < El; ++e) out[(size_t)e] = m.base + (long long)e * m.stride;
+    }
+    for (auto* q : out)
+        if (!q || ((uintptr_t)q & 15)) return false;
+    return true;
+}
+
+void destroy_plans(MoeTcPlans& P)
+{
+    for (auto* t : P.a) tc_plan_destroy(t);
+    for (auto* t : P.b) tc_plan_destroy(t);
+    P.a.clear();
+    P.b.clear();
+}
+
+// Plans (cached per configuration and buffers) or nullptr when the tensor-core
+// path does not take this configuration.
+// W3 needs operand tiles of its own when its element order or its unit count
+// differs from W1's.
+bool w3_own_tiles(const MoeExperts& a)
+{
+    auto perm = [](uint32_t t) { return t == T_Q8_0 ? 0 : (t == T_Q6_K ? 2 : 1); };
+    return perm(a.w1.type) != perm(a.w3.type) || units_of_type(a.w1.type, a.dim) != units_of_type(a.w3.type, a.dim);
+}
+
+const MoeTcPlans* moe_tc_plans(const MoeExperts& a, const MoeWs& L)
+{
+    if (a.T < kMoeTcMinT || a.T > kTcMaxB || !tc_type(a.w1.type) || !tc_type(a.w3.type) || !tc_type(a.w2.type) ||
+        row_bytes(a.w1.type, a.dim) <= 0 || row_bytes(a.w3.type, a.dim) <= 0 || row_bytes(a.w2.type, a.hidden) <= 0 ||
+        ((uintptr_t)a.xb & 3))
+        return nullptr;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    using MKey = std::tuple<const uint8_t*, long long, const uint8_t* const*, uint32_t>;
+    auto mk = [](const ExpertMats& m) { return MKey{m.base, m.stride, m.table, m.type}; };
+    using Key = std::tuple<int, int, int, int, int, int, int, MKey, MKey, MKey, const float*, long long, void*, float*>;
+    const Key key{dev, a.T, a.k, a.e0, a.El, a.dim, a.hidden, mk(a.w1), mk(a.w3), mk(a.w2), a.xb, a.ldx, a.ws, a.o};
+    static std::mutex mu;
+    static std::map<Key, MoeTcPlans> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second.a.empty() ? nullptr : &it->second;
+    MoeTcPlans P;
+    std::vector<const uint8_t*> p1, p3, p2;
+    uint8_t* ws = static_cast<uint8_t*>(a.ws);
+    const int* counts = reinterpret_cast<const int*>(ws + L.counts);
+    const int* offsets = reinterpret_cast<const int*>(ws + L.offsets);
+    const int* list = reinterpret_cast<const int*>(ws + L.list);
+    float* h1 = reinterpret_cast<float*>(ws + L.h1);
+    float* h3 = reinterpret_cast<float*>(ws + L.h3);
+    const int nch = moe_tc_chunks(a.T);
+    const int U1 = units_of_type(a.w1.type, a.dim), U3 = units_of_type(a.w3.type, a.dim);
+    const int U2 = units_of_type(a.w2.type, a.hidden);
+    const bool own3 = w3_own_tiles(a);
+    bool ok = expert_ptrs(a.w1, a.El, p1) && expert_ptrs(a.w3, a.El, p3) && expert_ptrs(a.w2, a.El, p2);
+    std::vector<GemvJobIn> ja, jb;
+    // One gathered job per (expert, matrix): 16 of the expert's pairs per pass.
+    auto job = [&](const uint8_t* w, uint32_t type, int n, int d, size_t t_off, size_t r_off, int U, int e,
+                   float* out) {
+        GemvJobIn j{};
+        j.w = w;
+        j.type = type;
+        j.n = n;
+        j.d = d;
+        j.B = 16;
+        j.act = ws + t_off + (size_t)e * nch * U * 512;
+        j.ds = ws + r_off + (size_t)e * nch * U * 256;
+        j.out = out;
+        j.ldo = n;
+        j.g_counts = counts;
+        j.g_offsets = offsets;
+        j.g_list = list;
+        j.g_e = e;
+        return j;
+    };
+    for (int e = 0; ok && e < a.El; ++e) {
+        ja.push_back(job(p1[(size_t)e], a.w1.type, a.hidden, a.dim, L.t1, L.r1, U1, e, h1));
+        ja.push_back(own3 ? job(p3[(size_t)e], a.w3.type, a.hidden, a.dim, L.t3, L.r3, U3, e, h3)
+                          : job(p3[(size_t)e], a.w3.type, a.hidden, a.dim, L.t1, L.r1, U1, e, h3));
+        jb.push_back(job(p2[(size_t)e], a.w2.type, a.dim, a.hidden, L.t2, L.r2, U2, e, a.o));
+    }
+    auto plan = [&](std::vector<GemvJobIn>& jobs, std::vector<TcPlan*>& out) {
+        for (size_t j0 = 0; ok && j0 < jobs.size(); j0 += kTcMaxJobs) {
+            TcPlan* t = nullptr;
+            if (tc_plan_create(jobs.data() + j0, (int)std::min<size_t>(kTcMaxJobs, jobs.size() - j0), &t) != 0) {
+                ok = false;
+                break;
+            }
+            out.push_back(t);
+        }
+    };
+    plan(ja, P.a);
+    plan(jb, P.b);
+    if (!ok) destroy_plans(P);  // an empty entry: this configuration takes the dp4a path
+    if (cache.size() >= 64) {
+        for (auto& kv : cache) destroy_plans(kv.second);
+        cache.clear();
+    }
+    auto& slot = cache[key];
+    slot = P;
+    return slot.a.empty() ? nullptr : &slot;
+}
+
+} // namespace
+
 cudaError_t launch_moe_experts(const MoeExperts& a, const LaunchCfg& c)
 {
     if (a.T <= 0 || a.El <= 0) return cudaSuccess;
@@ -494,8 +748,32 @@ cudaError_t launch_moe_experts(const MoeExperts& a, const LaunchCfg& c)
     const int P = a.T * a.k;
     ActQ ah = actq_carve(ws + L.acth, a.hidden, P);
 
-    cudaError_t e = launch_ex(&k_moe_group, dim3(1), dim3(1024), 0, c, a.sel, P, a.e0, a.El, counts, offsets, list);
-    if (e == cudaSuccess) e = launch_quantize(a.xb, a.ldx, a.dim, a.T, ax, nullptr, nullptr, c);
+    int* pos = reinterpret_cast<int*>(ws + L.pos);
+
+    cudaError_t e =
+        launch_ex(&k_moe_group, dim3(1), dim3(1024), 0, c, a.sel, P, a.e0, a.El, counts, offsets, list, pos);
+    if (e != cudaSuccess) return e;
+    if (const MoeTcPlans* tp = moe_tc_plans(a, L)) {
+        // Tensor cores: each pair's xb into its expert's W1 (and W3) operand
+        // tiles, W1/W3 over each expert's pairs, hb into W2's tiles, W2.
+        const int nch = moe_tc_chunks(a.T);
+        const int U1 = units_of_type(a.w1.type, a.dim), U3 = units_of_type(a.w3.type, a.dim);
+        const int U2 = units_of_type(a.w2.type, a.hidden);
+        const bool own3 = w3_own_tiles(a);
+        e = launch_ex(&k_moe_x_tc, dim3(grid_for((long long)P * std::max(U1, U3), kThreads / 32)), dim3(kThreads), 0,
+                      c, a.xb, a.ldx, P, a.k, a.sel, (const int*)pos, a.e0, a.El, nch, U1, a.w1.type, ws + L.t1,
+                      ws + L.r1, U3, a.w3.type, own3 ? ws + L.t3 : nullptr, own3 ? ws + L.r3 : nullptr);
+        for (auto* t : tp->a)
+            if (e == cudaSuccess) e = tc_plan_run(t, a.err, c.stream);
+        if (e == cudaSuccess)
+            e = launch_ex(&k_moe_act_tc, dim3(grid_for((long long)P * U2, kThreads / 32)), dim3(kThreads), 0, c,
+                          (const float*)h1, (const float*)h3, a.hidden, P, a.sel, (const int*)pos, a.e0, a.El, nch, U2,
+                          a.w2.type, ws + L.t2, ws + L.r2);
+        for (auto* t : tp->b)
+            if (e == cudaSuccess) e = tc_plan_run(t, a.err, c.stream);
+        return e;
+    }
+    e = launch_quantize(a.xb, a.ldx, a.dim, a.T, ax, nullptr, nullptr, c);
     if (e != cudaSuccess) return e;
 
     auto grouped = [&](const ExpertMats* m, int nmat, float* const* outs, int n, int d, ActQ x, int in_div,

@@ -145,6 +145,11 @@ struct __align__(16) TcJob {
     int tiles, item0;
     int tma;  // weights fetched by one 2-D TMA copy per stage (rows 16-byte aligned: Q4_K, Q5_K)
     int pad0;
+    // Gathered job (GemvJobIn): gc[ge] live columns, column i = pair gl[go[ge] + i].
+    const int* gc;
+    const int* go;
+    const int* gl;
+    int ge, pad1;
 };
 static_assert(sizeof(TcJob) % 16 == 0, "job table is copied in 16-byte words");
 
@@ -165,6 +170,7 @@ struct TcParams {
     const uint32_t* sched;
     const int* sched_off;
     uint32_t sched_smem;
+    int gathered;  // some job's live columns come from an earlier launch: every role waits for it
     int* err;
     // Per job with tma set: rows x row-bytes uint8 view of the packed weights,
     // box = 128 rows x one stage's bytes (passed by value: TMA reads the map
@@ -387,6 +393,20 @@ __global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQPar
 
 // ---------------------------------------------------------------- kernel --
 
+// Passes of an item over its K stages: 1 for a dense job; for a gathered job
+// (the pairs routed to one MoE expert, count written by an earlier launch and
+// read after the dependency wait) one per N live columns, 0 when it has none.
+// Every role derives the same value, so all of them walk the same stages.
+__device__ __forceinline__ int job_passes(const TcJob& J)
+{
+    return J.gc ? (J.gc[J.ge] + (int)J.N - 1) / (int)J.N : 1;
+}
+// Live columns of pass `pass`.
+__device__ __forceinline__ int pass_live(const TcJob& J, int pass)
+{
+    return J.gc ? min((int)J.N, J.gc[J.ge] - pass * (int)J.N) : (int)J.B;
+}
+
 // This CTA's schedule: entry k = (job << 20) | item.
 struct Sched {
     const uint32_t* list;
@@ -509,56 +529,65 @@ __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs,
         const TcJob& J = jobs[sc.job(k)];
         const int r0 = (i - J.item0) * kM;
         const int rows = min(kM, (int)J.n - r0);
-        const int B = (int)J.B, N = (int)J.N, U = (int)J.U, nst = (int)J.nst;
+        const int N = (int)J.N, U = (int)J.U, nst = (int)J.nst;
         const uint32_t type = J.type;
         float* out = J.out;
         const long long ldo = J.ldo;
-        float acc[NT];
+        const int npass = job_passes(J);
+        for (int pass = 0; ok && pass < npass; ++pass) {
+            const int B = pass_live(J, pass);  // live columns of this pass
+            float acc[NT];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
-        for (int st = 0; st < nst; ++st) {
-            if (!mbar_wait_bounded(&br.dfull[es], eu & 1, p.err, abort_flag, kSleepEpi) ||
-                !mbar_wait_bounded(&br.sfull[es], eu & 1, p.err, abort_flag, kSleepEpi) ||
-                !mbar_wait_bounded(&br.t_full[sb], bu & 1, p.err, abort_flag, kSleepEpi)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t ebase = e0 + p.e_slot * (uint32_t)es;
-            const int us = min(kUS, U - kUS * st);
-            const uint32_t tbase = tq + (uint32_t)(sb * kUS) * p.ncol;
-            if (tok0 < B) {
-                const uint32_t s0 = ebase + srow, r0b = ebase + drow;
-                if (us == kUS) {
-                    switch (type) {
-                    case T_Q4_K: epi_stage<T_Q4_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
-                    case T_Q5_K: epi_stage<T_Q5_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
-                    case T_Q6_K: epi_stage<T_Q6_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
-                    default: epi_stage<T_Q8_0, NT, true>(tbase, s0, r0b, N, us, acc); break;
-                    }
-                } else {
-                    switch (type) {
-                    case T_Q4_K: epi_stage<T_Q4_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
-                    case T_Q5_K: epi_stage<T_Q5_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
-                    case T_Q6_K: epi_stage<T_Q6_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
-                    default: epi_stage<T_Q8_0, NT, false>(tbase, s0, r0b, N, us, acc); break;
+            for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
+            for (int st = 0; st < nst; ++st) {
+                if (!mbar_wait_bounded(&br.dfull[es], eu & 1, p.err, abort_flag, kSleepEpi) ||
+                    !mbar_wait_bounded(&br.sfull[es], eu & 1, p.err, abort_flag, kSleepEpi) ||
+                    !mbar_wait_bounded(&br.t_full[sb], bu & 1, p.err, abort_flag, kSleepEpi)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t ebase = e0 + p.e_slot * (uint32_t)es;
+                const int us = min(kUS, U - kUS * st);
+                const uint32_t tbase = tq + (uint32_t)(sb * kUS) * p.ncol;
+                if (tok0 < B) {
+                    const uint32_t s0 = ebase + srow, r0b = ebase + drow;
+                    if (us == kUS) {
+                        switch (type) {
+                        case T_Q4_K: epi_stage<T_Q4_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                        case T_Q5_K: epi_stage<T_Q5_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                        case T_Q6_K: epi_stage<T_Q6_K, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                        default: epi_stage<T_Q8_0, NT, true>(tbase, s0, r0b, N, us, acc); break;
+                        }
+                    } else {
+                        switch (type) {
+                        case T_Q4_K: epi_stage<T_Q4_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                        case T_Q5_K: epi_stage<T_Q5_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                        case T_Q6_K: epi_stage<T_Q6_K, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                        default: epi_stage<T_Q8_0, NT, false>(tbase, s0, r0b, N, us, acc); break;
+                        }
                     }
                 }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&br.t_empty[sb]);
+                    mbar_arrive(&br.efree[es]);
+                }
+                if (++es == SE) es = 0, ++eu;
+                if (++sb == NB) sb = 0, ++bu;
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&br.t_empty[sb]);
-                mbar_arrive(&br.efree[es]);
-            }
-            if (++es == SE) es = 0, ++eu;
-            if (++sb == NB) sb = 0, ++bu;
-        }
-        if (!ok) break;
-        if (row < rows)
+            if (!ok) break;
+            if (row < rows) {
+                // Output row of column t: the token (dense job) or the pair
+                // the gathered column stands for.
+                const int* lst = J.gc ? J.gl + J.go[J.ge] + pass * N : nullptr;
 #pragma unroll
-            for (int t = 0; t < NT; ++t)
-                if (tok0 + t < B) out[(long long)(tok0 + t) * ldo + r0 + row] = acc[t];
+                for (int t = 0; t < NT; ++t)
+                    if (tok0 + t < B)
+                        out[(long long)(lst ? lst[tok0 + t] : tok0 + t) * ldo + r0 + row] = acc[t];
+            }
+        }
     }
 }
 
@@ -722,6 +751,9 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
     const uint32_t tmem = misc[0];
     const TcJob* jobs = reinterpret_cast<const TcJob*>(sm + p.jobs_off);
     pdl_trigger();
+    // Gathered jobs' live-column counts come from an earlier launch: every role
+    // needs them to skip the same items.
+    if (p.gathered) pdl_wait();
 
     if (warp == 0) {
         // ----------------------------------------------- weight producer --
@@ -734,7 +766,9 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
             for (int k = 0; ok && k < sc.cnt; ++k) {
                 const int i = sc.item(k), jc = sc.job(k);
                 const TcJob& J = jobs[jc];
-                for (int st = 0; st < (int)J.nst; ++st, (++ws == SW ? (ws = 0, ++wu) : 0)) {
+                const int nps = job_passes(J) * (int)J.nst;  // (pass, stage) steps; each pass re-reads the tile
+                for (int ps = 0; ps < nps; ++ps, (++ws == SW ? (ws = 0, ++wu) : 0)) {
+                    const int st = ps % (int)J.nst;
                     if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag, kSleepProd)) {
                         ok = false;
                         break;
@@ -764,7 +798,8 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         bool ok = true;
         for (int k = 0; ok && k < sc.cnt; ++k) {
             const TcJob& J = jobs[sc.job(k)];
-            for (int st = 0; st < (int)J.nst; ++st, (++os == SO ? (os = 0, ++ou) : 0),
+            const int nps = job_passes(J) * (int)J.nst;
+            for (int ps = 0; ps < nps; ++ps, (++os == SO ? (os = 0, ++ou) : 0),
                      (++bs == SB ? (bs = 0, ++bsu) : 0), (++sb == NB ? (sb = 0, ++bu) : 0)) {
                 if (!mbar_wait_bounded(&br.bfull[bs], bsu & 1, p.err, abort_flag, kSleepMma) ||
                     !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag, kSleepMma) ||
@@ -775,7 +810,7 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
                 tc_fence_after();
                 __syncwarp();
                 const uint32_t abase = p.o_off + p.o_slot * (uint32_t)os, bbase = p.b_off + p.b_slot * (uint32_t)bs;
-                const int us = min(kUS, (int)J.U - kUS * st);
+                const int us = min(kUS, (int)J.U - kUS * (ps % (int)J.nst));
                 if (elect_one()) {
                     for (int j = 0; j < us; ++j) {
                         const uint64_t ad = smem_desc(sptr(sm + abase + (uint32_t)j * kATile));
@@ -804,20 +839,27 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         const int row = ((warp - 2) % kGroupWarps) * 32 + lane;
         const uint32_t bar_id = 1 + (uint32_t)grp;  // named barrier of the group's 128 threads
         const uint32_t* s32 = reinterpret_cast<const uint32_t*>(sm);
-        // Stage positions (schedule entry, item, job, stage within the item).
+        // Stage positions (schedule entry, item, job, stage within the item,
+        // pass over the item and the item's passes).
         struct Pos {
-            int k, i, jc, st;
+            int k, i, jc, st, pass, np;
         };
         auto valid = [&](const Pos& q) { return q.k < sc.cnt; };
         auto at = [&](int k) {
-            Pos q{k, 0, 0, 0};
-            if (k < sc.cnt) {
-                q.i = sc.item(k);
-                q.jc = sc.job(k);
+            Pos q{k, 0, 0, 0, 0, 0};
+            for (; q.k < sc.cnt; ++q.k) {  // items of gathered jobs without live columns: skipped by every role
+                q.jc = sc.job(q.k);
+                q.np = job_passes(jobs[q.jc]);
+                if (q.np > 0) break;
             }
+            if (q.k < sc.cnt) q.i = sc.item(q.k);
             return q;
         };
-        auto next = [&](Pos q) { return ++q.st < (int)jobs[q.jc].nst ? q : at(q.k + 1); };
+        auto next = [&](Pos q) {
+            if (++q.st < (int)jobs[q.jc].nst) return q;
+            q.st = 0;
+            return ++q.pass < q.np ? q : at(q.k + 1);
+        };
         auto next_own = [&](Pos q) {  // DG stages on
 #pragma unroll
             for (int d = 0; d < DG; ++d)
@@ -939,8 +981,12 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
             bool ok = true;
             for (int k = 0; ok && k < sc.cnt; ++k) {
                 const TcJob& J = jobs[sc.job(k)];
-                for (int st = 0; st < (int)J.nst;
-                     ++st, (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
+                const int nps = job_passes(J) * (int)J.nst;
+                for (int ps = 0; ps < nps;
+                     ++ps, (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
+                    // Pass `pass` of a gathered job reads the operand tiles of
+                    // its live columns [pass*N, pass*N + N): U units each.
+                    const int st = ps % (int)J.nst, pass = ps / (int)J.nst;
                     // B slot: the MMAs of its previous stage are done; record
                     // slot: the epilogue of its previous stage is done.
                     if ((bu > 0 && !mbar_wait_bounded(&br.bfree[bs], (bu - 1) & 1, p.err, abort_flag, kSleepProd)) ||
@@ -952,12 +998,12 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
                     const uint32_t bbytes = (uint32_t)us * J.N * 32u, dbytes = (uint32_t)us * J.N * 16u;
                     mbar_arrive_expect_tx(&br.bfull[bs], bbytes);
                     misc[kFillB + bs] += 1;
-                    bulk_g2s(sm + p.b_off + p.b_slot * (uint32_t)bs, J.act + (size_t)kUS * st * J.N * 32, bbytes,
-                             &br.bfull[bs]);
+                    const size_t u0 = (size_t)pass * J.U + (size_t)kUS * st;  // first unit tile of the stage
+                    bulk_g2s(sm + p.b_off + p.b_slot * (uint32_t)bs, J.act + u0 * J.N * 32, bbytes, &br.bfull[bs]);
                     mbar_arrive_expect_tx(&br.dfull[es], dbytes);
                     misc[kFillD + es] += 1;
-                    bulk_g2s(sm + p.e_off + p.e_slot * (uint32_t)es + p.d_rel, J.ds + (size_t)kUS * st * J.N * 16,
-                             dbytes, &br.dfull[es]);
+                    bulk_g2s(sm + p.e_off + p.e_slot * (uint32_t)es + p.d_rel, J.ds + u0 * J.N * 16, dbytes,
+                             &br.dfull[es]);
                 }
             }
         }
@@ -1023,6 +1069,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     size_t act_total = 0;
     long long blocks = 0;
     int Nmax = 16, Bmax = 1, item = 0;
+    bool gathered = false;
     std::vector<size_t> task_act_off;
     std::vector<int> job_task;
     for (int j = 0; j < njobs; ++j) {
@@ -1031,7 +1078,10 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
             delete P;
             return QUANTR_ERR_UNSUPPORTED_TYPE;
         }
-        if (!a.w || !a.x || !a.out || a.n <= 0 || a.B <= 0 || a.B > kMaxN || a.ldx < a.d || a.ldo < a.n ||
+        const bool pre = a.act != nullptr;  // activations given as operand tiles
+        if (!a.w || (!pre && (!a.x || a.ldx < a.d)) || (pre && !a.ds) ||
+            (a.g_counts && (!a.g_offsets || !a.g_list || a.g_e < 0 || !pre || a.B != 16)) || !a.out || a.n <= 0 ||
+            a.B <= 0 || a.B > kMaxN || a.ldo < a.n ||
             ((uintptr_t)a.w & 15) || row_bytes(a.type, a.d) <= 0) {
             delete P;
             return QUANTR_ERR_BAD_ARG;
@@ -1058,6 +1108,18 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         item += J.tiles;
         Nmax = std::max(Nmax, (int)J.N);
         Bmax = std::max(Bmax, a.B);
+        J.gc = a.g_counts;
+        J.go = a.g_offsets;
+        J.gl = a.g_list;
+        J.ge = a.g_e;
+        if (a.g_counts) gathered = true;
+        if (pre) {
+            J.act = a.act;
+            J.ds = a.ds;
+            job_task.push_back(-1);
+            P->jobs.push_back(J);
+            continue;
+        }
         const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
         auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, perm);
         auto it = dedupe.find(key);
@@ -1189,6 +1251,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.SB = (uint32_t)SB;
     pp.SE = (uint32_t)SE;
     pp.ncol = (uint32_t)Nmax;
+    pp.gathered = gathered ? 1 : 0;
     P->bmax = Bmax;
     pp.NB = (uint32_t)std::min(kMaxNB, 512 / (kUS * Nmax));  // 4, 2 or 1 stage buffers for N = 16, 32, 64
     uint32_t cols = 32;
@@ -1218,6 +1281,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
             P->tasks[t].ds = P->tasks[t].act + (size_t)P->tasks[t].U * P->tasks[t].N * 32;
         }
         for (size_t j = 0; j < P->jobs.size(); ++j) {
+            if (job_task[j] < 0) continue;  // operand tiles given
             P->jobs[j].act = P->tasks[job_task[j]].act;
             P->jobs[j].ds = P->tasks[job_task[j]].ds;
         }
@@ -1268,9 +1332,12 @@ cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
     using namespace tc;
     LaunchCfg c;
     c.stream = stream;
-    const long long qgrid = std::max(1LL, std::min<long long>((P->qp.total + 255) / 256, 8LL * device_sm_count()));
-    cudaError_t e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
-    if (e != cudaSuccess) return e;
+    if (P->qp.total > 0) {  // no quantizer when every job came with operand tiles
+        const long long qgrid =
+            std::max(1LL, std::min<long long>((P->qp.total + 255) / 256, 8LL * device_sm_count()));
+        const cudaError_t e = launch_ex(&k_tc_quant, dim3((unsigned)qgrid), dim3(256), 0, c, P->qp);
+        if (e != cudaSuccess) return e;
+    }
     TcParams pp = P->pp;
     pp.err = err;
     // The split and the epilogue's tokens per thread (see Split).

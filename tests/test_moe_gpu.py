@@ -256,14 +256,15 @@ def test_moe_layer_host_api(qr_gpu, orc):
     assert rc == 10 and np.all(o == 0.0)
 
 
-def test_moe_stages_emulate_expert_parallel(qr_gpu, orc):
+@pytest.mark.parametrize("T", [9, 56])
+def test_moe_stages_emulate_expert_parallel(qr_gpu, orc, T):
     """route once, run the experts stage on two disjoint expert ranges into
     zeroed buffers (what two expert-parallel ranks compute), add them (each row
     has one non-zero contributor, so the sum is exact), combine: bit-identical
-    to quantr_moe_dev."""
-    c = make_case(13, T=9, E=10, k=3, dim=512, hidden=256, t1=Q5_K, t3=Q5_K, t2=Q6_K)
+    to quantr_moe_dev.  T = 56 takes the tensor-core experts stage."""
+    c = make_case(13, T=T, E=10, k=3, dim=512, hidden=256, t1=Q5_K, t3=Q5_K, t2=Q6_K)
     full = run_dev(qr_gpu, c)
-    T, E, k, dim, hidden = 9, 10, 3, 512, 256
+    E, k, dim, hidden = 10, 3, 512, 256
     s = torch.cuda.current_stream().cuda_stream
     xb = _dev(c["xb"])
     lg = _dev(c["logits"])
@@ -291,3 +292,69 @@ def test_moe_stages_emulate_expert_parallel(qr_gpu, orc):
     np.testing.assert_array_equal(sel.cpu().numpy(), full[1])
     np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), full[2].view(np.uint32))
     np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), full[0].view(np.uint32))
+
+
+# Tensor-core experts stage (T >= 48 tokens: gathered tcgen05 jobs over each
+# expert's pairs) on the cases above that shape it differently.
+
+def test_moe_tc_mixed_types(qr_gpu, orc):
+    """W1 Q4_K with W3 Q8_0 (different element order and unit count: W3 gets
+    operand tiles of its own), Q6_K down projection over a ragged hidden."""
+    c = make_case(21, T=48, E=6, k=3, dim=512, hidden=320, t1=Q4_K, t3=Q8_0, t2=Q6_K)
+    check(run_dev(qr_gpu, c), oracle_case(orc, c))
+
+
+def test_moe_tc_hot_expert_four_passes(qr_gpu, orc):
+    """All 64 tokens pick expert 3 first: its job runs four 16-pair passes."""
+    c = make_case(22, T=64, E=10, k=2, dim=512, hidden=256, t1=Q5_K, t3=Q5_K, t2=Q6_K)
+    c["logits"][:, 3] += 8.0
+    got = run_dev(qr_gpu, c)
+    assert np.all(got[1][:, 0] == 3)
+    check(got, oracle_case(orc, c))
+
+
+def test_moe_tc_pointer_table_and_idle_experts(qr_gpu, orc):
+    """Experts addressed through a device pointer table (read once when the
+    launch plan is built); two experts nobody picks are skipped."""
+    c = make_case(23, T=48, E=8, k=2, dim=512, hidden=256, t1=Q5_K, t3=Q5_K, t2=Q6_K)
+    c["logits"][:, 6:] -= 50.0
+    keep = []
+
+    def tabled(ex):
+        bufs = [_dev(ex.host[e]) for e in range(ex.E)]
+        keep.extend(bufs)
+        tab = torch.tensor([b.data_ptr() for b in bufs], dtype=torch.int64, device="cuda")
+        keep.append(tab)
+        return qr_gpu.ExpertWeights(0, 0, tab.data_ptr(), ex.type)
+
+    got = run_dev(qr_gpu, c, tabled(c["w1"]), tabled(c["w3"]), tabled(c["w2"]))
+    assert not np.isin(got[1], [6, 7]).any()
+    check(got, oracle_case(orc, c))
+    got2 = run_dev(qr_gpu, c, tabled(c["w1"]), tabled(c["w3"]), tabled(c["w2"]))  # new tables: a new plan
+    np.testing.assert_array_equal(got2[0].view(np.uint32), got[0].view(np.uint32))
+
+
+def test_moe_tc_repeat_call_new_tokens(qr_gpu, orc):
+    """The cached launch plan reused with new inputs in the same buffers."""
+    c = make_case(24, T=64, E=8, k=2, dim=512, hidden=256, t1=Q4_K, t3=Q4_K, t2=Q4_K)
+    T, E, k, dim, hidden = 64, 8, 2, 512, 256
+    xb = _dev(c["xb"])
+    lg = _dev(c["logits"])
+    out = torch.empty(T, dim, device="cuda")
+    ws_bytes = qr_gpu.moe_workspace_bytes(T, E, k, dim, hidden)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    w = [c[key].weights(qr_gpu) for key in ("w1", "w3", "w2")]
+    s = torch.cuda.current_stream().cuda_stream
+    rng = synth.rng_for(25)
+    for it in range(2):
+        if it:
+            c["xb"] = synth.activations(rng, T, dim)
+            c["logits"] = rng.standard_normal((T, E), dtype=np.float32)
+            xb.copy_(torch.from_numpy(c["xb"]))
+            lg.copy_(torch.from_numpy(c["logits"]))
+        sel = torch.empty(T, k, dtype=torch.int32, device="cuda")
+        wts = torch.empty(T, k, device="cuda")
+        qr_gpu.moe_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, E, k, *w, dim, hidden, ws.data_ptr(), ws_bytes,
+                       logits=lg.data_ptr(), ldl=E, sel=sel.data_ptr(), wts=wts.data_ptr(), stream=s)
+        torch.cuda.synchronize()
+        check((out.cpu().numpy(), sel.cpu().numpy(), wts.cpu().numpy()), oracle_case(orc, c))
