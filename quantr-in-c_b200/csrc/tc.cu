@@ -144,14 +144,10 @@ struct __align__(16) TcJob {
     uint32_t N, nst, seg, idesc;  // nst stages of kUS units; seg = packed bytes of a full stage per row
     int tiles, item0;
     int tma;  // weights fetched by one 2-D TMA copy per stage (rows 16-byte aligned: Q4_K, Q5_K)
-    int pad0;
-    // Gathered job (GemvJobIn): gc[ge] live columns, column i = pair gl[go[ge] + i].
-    const int* gc;
-    const int* go;
-    const int* gl;
-    int ge, pad1;
+    int ge;   // gathered job (GemvJobIn): expert index into the launch's pair counts/lists; -1: dense
 };
 static_assert(sizeof(TcJob) % 16 == 0, "job table is copied in 16-byte words");
+static_assert(sizeof(TcJob) == 96, "the job table lives in shared memory: keep it small");
 
 struct TcParams {
     const TcJob* jobs;
@@ -171,6 +167,10 @@ struct TcParams {
     const int* sched_off;
     uint32_t sched_smem;
     int gathered;  // some job's live columns come from an earlier launch: every role waits for it
+    // Gathered jobs' pair counts, list offsets and pair lists (one set per launch).
+    const int* gcounts;
+    const int* goffsets;
+    const int* glist;
     int* err;
     // Per job with tma set: rows x row-bytes uint8 view of the packed weights,
     // box = 128 rows x one stage's bytes (passed by value: TMA reads the map
@@ -391,20 +391,24 @@ __global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQPar
     }
 }
 
-// ---------------------------------------------------------------- kernel --
-
 // Passes of an item over its K stages: 1 for a dense job; for a gathered job
 // (the pairs routed to one MoE expert, count written by an earlier launch and
 // read after the dependency wait) one per N live columns, 0 when it has none.
 // Every role derives the same value, so all of them walk the same stages.
-__device__ __forceinline__ int job_passes(const TcJob& J)
+// GAT: the launch has gathered jobs (a separate kernel instantiation, so that
+// dense launches keep single-pass loops).
+template <bool GAT>
+__device__ __forceinline__ int job_passes(const TcParams& p, const TcJob& J)
 {
-    return J.gc ? (J.gc[J.ge] + (int)J.N - 1) / (int)J.N : 1;
+    if constexpr (!GAT) return 1;
+    return J.ge >= 0 ? (p.gcounts[J.ge] + (int)J.N - 1) / (int)J.N : 1;
 }
 // Live columns of pass `pass`.
-__device__ __forceinline__ int pass_live(const TcJob& J, int pass)
+template <bool GAT>
+__device__ __forceinline__ int pass_live(const TcParams& p, const TcJob& J, int pass)
 {
-    return J.gc ? min((int)J.N, J.gc[J.ge] - pass * (int)J.N) : (int)J.B;
+    if constexpr (!GAT) return (int)J.B;
+    return J.ge >= 0 ? min((int)J.N, p.gcounts[J.ge] - pass * (int)J.N) : (int)J.B;
 }
 
 // This CTA's schedule: entry k = (job << 20) | item.
@@ -510,7 +514,7 @@ struct Bars {
     uint64_t *t_full, *t_empty;       // TMEM stage buffers: sums ready, read
 };
 
-template <int NT, int DW>
+template <int NT, int DW, bool GAT>
 __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs, const Sched& sc, const Bars& br,
                               volatile int* abort_flag, uint32_t tmem, int warp, int lane)
 {
@@ -533,9 +537,9 @@ __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs,
         const uint32_t type = J.type;
         float* out = J.out;
         const long long ldo = J.ldo;
-        const int npass = job_passes(J);
+        const int npass = job_passes<GAT>(p, J);
         for (int pass = 0; ok && pass < npass; ++pass) {
-            const int B = pass_live(J, pass);  // live columns of this pass
+            const int B = pass_live<GAT>(p, J, pass);  // live columns of this pass
             float acc[NT];
 #pragma unroll
             for (int t = 0; t < NT; ++t) acc[t] = 0.0f;
@@ -581,7 +585,7 @@ __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs,
             if (row < rows) {
                 // Output row of column t: the token (dense job) or the pair
                 // the gathered column stands for.
-                const int* lst = J.gc ? J.gl + J.go[J.ge] + pass * N : nullptr;
+                const int* lst = GAT && J.ge >= 0 ? p.glist + p.goffsets[J.ge] + pass * N : nullptr;
 #pragma unroll
                 for (int t = 0; t < NT; ++t)
                     if (tok0 + t < B)
@@ -671,7 +675,7 @@ __device__ __forceinline__ void wait_groups_but(int n)
     }
 }
 
-template <int DG, int EG, int NT>
+template <int DG, int EG, int NT, bool GAT>
 __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const __grid_constant__ TcParams p)
 {
     constexpr int kDecWarps = Split<DG, EG>::dec_warps, kEpiWarps = Split<DG, EG>::epi_warps;
@@ -753,7 +757,7 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
     pdl_trigger();
     // Gathered jobs' live-column counts come from an earlier launch: every role
     // needs them to skip the same items.
-    if (p.gathered) pdl_wait();
+    if (GAT) pdl_wait();
 
     if (warp == 0) {
         // ----------------------------------------------- weight producer --
@@ -766,9 +770,10 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
             for (int k = 0; ok && k < sc.cnt; ++k) {
                 const int i = sc.item(k), jc = sc.job(k);
                 const TcJob& J = jobs[jc];
-                const int nps = job_passes(J) * (int)J.nst;  // (pass, stage) steps; each pass re-reads the tile
-                for (int ps = 0; ps < nps; ++ps, (++ws == SW ? (ws = 0, ++wu) : 0)) {
-                    const int st = ps % (int)J.nst;
+                const int nps = job_passes<GAT>(p, J) * (int)J.nst;  // (pass, stage) steps; each pass re-reads the tile
+                // Counters, not divisions: this single thread is on every stage's critical path.
+                for (int ps = 0, st = 0; ps < nps;
+                     ++ps, (++st == (int)J.nst ? st = 0 : 0), (++ws == SW ? (ws = 0, ++wu) : 0)) {
                     if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag, kSleepProd)) {
                         ok = false;
                         break;
@@ -798,8 +803,8 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         bool ok = true;
         for (int k = 0; ok && k < sc.cnt; ++k) {
             const TcJob& J = jobs[sc.job(k)];
-            const int nps = job_passes(J) * (int)J.nst;
-            for (int ps = 0; ps < nps; ++ps, (++os == SO ? (os = 0, ++ou) : 0),
+            const int nps = job_passes<GAT>(p, J) * (int)J.nst;
+            for (int ps = 0, st = 0; ps < nps; ++ps, (++st == (int)J.nst ? st = 0 : 0), (++os == SO ? (os = 0, ++ou) : 0),
                      (++bs == SB ? (bs = 0, ++bsu) : 0), (++sb == NB ? (sb = 0, ++bu) : 0)) {
                 if (!mbar_wait_bounded(&br.bfull[bs], bsu & 1, p.err, abort_flag, kSleepMma) ||
                     !mbar_wait_bounded(&br.afull[os], ou & 1, p.err, abort_flag, kSleepMma) ||
@@ -810,7 +815,7 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
                 tc_fence_after();
                 __syncwarp();
                 const uint32_t abase = p.o_off + p.o_slot * (uint32_t)os, bbase = p.b_off + p.b_slot * (uint32_t)bs;
-                const int us = min(kUS, (int)J.U - kUS * (ps % (int)J.nst));
+                const int us = min(kUS, (int)J.U - kUS * st);
                 if (elect_one()) {
                     for (int j = 0; j < us; ++j) {
                         const uint64_t ad = smem_desc(sptr(sm + abase + (uint32_t)j * kATile));
@@ -846,17 +851,23 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         };
         auto valid = [&](const Pos& q) { return q.k < sc.cnt; };
         auto at = [&](int k) {
-            Pos q{k, 0, 0, 0, 0, 0};
-            for (; q.k < sc.cnt; ++q.k) {  // items of gathered jobs without live columns: skipped by every role
-                q.jc = sc.job(q.k);
-                q.np = job_passes(jobs[q.jc]);
-                if (q.np > 0) break;
+            Pos q{k, 0, 0, 0, 0, 1};
+            if constexpr (GAT) {
+                for (; q.k < sc.cnt; ++q.k) {  // items of gathered jobs without live columns: skipped by every role
+                    q.jc = sc.job(q.k);
+                    q.np = job_passes<GAT>(p, jobs[q.jc]);
+                    if (q.np > 0) break;
+                }
+                if (q.k < sc.cnt) q.i = sc.item(q.k);
+            } else if (k < sc.cnt) {
+                q.i = sc.item(k);
+                q.jc = sc.job(k);
             }
-            if (q.k < sc.cnt) q.i = sc.item(q.k);
             return q;
         };
         auto next = [&](Pos q) {
             if (++q.st < (int)jobs[q.jc].nst) return q;
+            if constexpr (!GAT) return at(q.k + 1);
             q.st = 0;
             return ++q.pass < q.np ? q : at(q.k + 1);
         };
@@ -971,7 +982,7 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         asm volatile("cp.async.wait_all;" ::: "memory");  // no copy into shared memory outlives the role
     } else if (warp < 2 + kDecWarps + kEpiWarps) {
         // ------------------------------------------------------ epilogue --
-        epilogue_role<NT, kDecWarps>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
+        epilogue_role<NT, kDecWarps, GAT>(sm, p, jobs, sc, br, abort_flag, tmem, warp, lane);
     } else {
         // ------------------------------------------ activation producer --
         if (lane == 0) {
@@ -981,12 +992,11 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
             bool ok = true;
             for (int k = 0; ok && k < sc.cnt; ++k) {
                 const TcJob& J = jobs[sc.job(k)];
-                const int nps = job_passes(J) * (int)J.nst;
-                for (int ps = 0; ps < nps;
-                     ++ps, (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
-                    // Pass `pass` of a gathered job reads the operand tiles of
-                    // its live columns [pass*N, pass*N + N): U units each.
-                    const int st = ps % (int)J.nst, pass = ps / (int)J.nst;
+                const int nps = job_passes<GAT>(p, J) * (int)J.nst;
+                // Pass `pass` of a gathered job reads the operand tiles of its
+                // live columns [pass*N, pass*N + N): U units each.
+                for (int ps = 0, st = 0, pass = 0; ps < nps; ++ps, (++st == (int)J.nst ? (st = 0, ++pass) : 0),
+                         (++bs == SB ? (bs = 0, ++bu) : 0), (++es == SE ? (es = 0, ++eu) : 0)) {
                     // B slot: the MMAs of its previous stage are done; record
                     // slot: the epilogue of its previous stage is done.
                     if ((bu > 0 && !mbar_wait_bounded(&br.bfree[bs], (bu - 1) & 1, p.err, abort_flag, kSleepProd)) ||
@@ -1108,11 +1118,19 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
         item += J.tiles;
         Nmax = std::max(Nmax, (int)J.N);
         Bmax = std::max(Bmax, a.B);
-        J.gc = a.g_counts;
-        J.go = a.g_offsets;
-        J.gl = a.g_list;
-        J.ge = a.g_e;
-        if (a.g_counts) gathered = true;
+        J.ge = -1;
+        if (a.g_counts) {  // every gathered job of a launch shares one set of counts and lists
+            TcParams& q = P->pp;
+            if (gathered && (a.g_counts != q.gcounts || a.g_offsets != q.goffsets || a.g_list != q.glist)) {
+                delete P;
+                return QUANTR_ERR_BAD_ARG;
+            }
+            gathered = true;
+            q.gcounts = a.g_counts;
+            q.goffsets = a.g_offsets;
+            q.glist = a.g_list;
+            J.ge = a.g_e;
+        }
         if (pre) {
             J.act = a.act;
             J.ds = a.ds;
@@ -1316,13 +1334,19 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
 
 namespace tc {
 
+template <int DG, int EG, int NT, bool GAT>
+cudaError_t launch_tc_k(const TcPlan* P, const TcParams& pp, const LaunchCfg& c)
+{
+    static int configured = -1;
+    cudaError_t e = ensure_smem_attr(&k_tc_program<DG, EG, NT, GAT>, (int)kSmemMax, configured);
+    if (e != cudaSuccess) return e;
+    return launch_ex(&k_tc_program<DG, EG, NT, GAT>, dim3(P->grid), dim3(Split<DG, EG>::threads), P->smem, c, pp);
+}
+
 template <int DG, int EG, int NT>
 cudaError_t launch_tc(const TcPlan* P, const TcParams& pp, const LaunchCfg& c)
 {
-    static int configured = -1;
-    cudaError_t e = ensure_smem_attr(&k_tc_program<DG, EG, NT>, (int)kSmemMax, configured);
-    if (e != cudaSuccess) return e;
-    return launch_ex(&k_tc_program<DG, EG, NT>, dim3(P->grid), dim3(Split<DG, EG>::threads), P->smem, c, pp);
+    return pp.gathered ? launch_tc_k<DG, EG, NT, true>(P, pp, c) : launch_tc_k<DG, EG, NT, false>(P, pp, c);
 }
 
 } // namespace tc
