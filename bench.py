@@ -48,7 +48,7 @@ import synth  # noqa: E402
 
 METRIC = "quantized GEMV HBM GB/s (% of 8 TB/s); decode tok/s at 1/2/4/8 B200 vs host CPU"
 HIDDEN, FFN, LAYERS = 896, 4864, 24
-Q4_K = 12
+Q8_0, Q4_K = 8, 12
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one k_program launch of the c2 step, from the
@@ -322,14 +322,12 @@ def ours_arm(args):
     # The rest of the c2 batch sweep (batch 1, 4 and 16): the same 72 weights
     # at the other batch sizes, device-resident inputs, CUDA-graph replays
     # timed with CUDA events like `value` (rank-local; reported per GPU).
-    sweep = {}
-    for Bs in args.sweep:
-        if Bs == B:
-            continue
-        xs = [torch.from_numpy(synth.activations(rng, Bs, d)).to(dev) for _, _, d, _ in shapes]
-        os_ = [torch.empty(Bs, n, device=dev) for _, n, _, _ in shapes]
+    def time_program(shp, ws_dev, Bs):
+        """ms per replay of one program over (type, n, d) shapes and weights."""
+        xs = [torch.from_numpy(synth.activations(rng, Bs, d)).to(dev) for _, _, d, *_ in shp]
+        os_ = [torch.empty(Bs, n, device=dev) for _, n, _, *_ in shp]
         pr = quantr.Program([(w.data_ptr(), t, n, d, Bs, x.data_ptr(), d, o.data_ptr(), n)
-                             for (t, n, d, _), w, x, o in zip(shapes, dev_w, xs, os_)])
+                             for (t, n, d, *_), w, x, o in zip(shp, ws_dev, xs, os_)])
         with torch.cuda.stream(s):
             pr.run(s.cuda_stream)
             s.synchronize()
@@ -345,13 +343,34 @@ def ours_arm(args):
             e1.record(s)
         torch.cuda.synchronize()
         assert quantr.device_status(0) == 0
-        t_ms = e0.elapsed_time(e1) / args.steps
+        del g
+        pr.close()
+        return e0.elapsed_time(e1) / args.steps
+
+    sweep = {}
+    for Bs in args.sweep:
+        if Bs == B:
+            continue
+        t_ms = time_program(shapes, dev_w, Bs)
         nb = sum(gemv_bytes(t, n, d, Bs) for t, n, d, _ in shapes)
         sweep[str(Bs)] = {"GB/s": round(nb / (t_ms / 1e3) / 1e9, 2), "ms_per_step": round(t_ms, 5),
                           "tok_per_s": round(Bs / (t_ms / 1e3), 1),
                           "path": "tensor cores (tcgen05.mma kind::i8)" if Bs >= 2 else "dp4a engine"}
-        del g
-        pr.close()
+
+    # BASELINE config c1: the Q8_0 GEMV at the TinyLlama FFN shape (5632 x
+    # 2048, quants uniform in [-127, 127], scale max|w|/127 of w ~ N(0, 0.02)),
+    # batch 1; 16 distinct copies per replay (196 MB, above L2) as one program.
+    c1 = None
+    if not args.no_c1:
+        c1_shapes = [(Q8_0, 5632, 2048)] * 16
+        w1 = torch.from_numpy(synth.q8_0_matrix(rng, 5632, 2048)).to(dev)
+        c1_w = [w1.clone() for _ in c1_shapes]  # distinct addresses: every replay streams 196 MB
+        t_ms = time_program(c1_shapes, c1_w, 1)
+        nb = sum(gemv_bytes(t, n, d, 1) for t, n, d in c1_shapes)
+        c1 = {"GB/s": round(nb / (t_ms / 1e3) / 1e9, 2), "us_per_gemv": round(t_ms * 1e3 / len(c1_shapes), 3),
+              "frac_of_peak": round(nb / (t_ms / 1e3) / 1e9 / load_peaks()[0], 4),
+              "workload": "c1: 16 distinct Q8_0 5632x2048 GEMVs per replay (196 MB > L2), batch 1"}
+        del c1_w
 
     # End to end with HOST buffers, (a) through the C-ABI program call: every
     # step copies all 72 inputs from pinned host memory to the device, runs
@@ -442,6 +461,7 @@ def ours_arm(args):
                            "d2h_bytes_per_step": d2h,
                            "api": "72 synchronous matmul_q_fused_batch calls per step with host arrays"},
             "batch_sweep": sweep,
+            "c1_q8_0": c1,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
         }
@@ -463,6 +483,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c1", action="store_true", help="skip the c1 Q8_0 GEMV line")
     ap.add_argument("--sweep", type=lambda v: [int(b) for b in v.split(",") if b], default=[4, 16],
                     help="other batch sizes timed on the same weights (comma list; empty to skip)")
     args = ap.parse_args()
