@@ -174,8 +174,8 @@ int quantr_gpu_device_status(void* stream, int reset);
  * (B <= 64), with the reference's numerics (the same as matmul_q_fused per
  * token).  All pointers are device pointers; w must be 16-byte aligned and
  * readable up to the next 16-byte boundary past its last row (every cudaMalloc
- * allocation and registered range is).  Jobs of up to 4 tokens run on the dp4a
- * engine, jobs of 5..64 tokens on the tensor cores (tcgen05 kind::i8). */
+ * allocation and registered range is).  Jobs of one token run on the dp4a
+ * engine, jobs of 2..64 tokens on the tensor cores (tcgen05 kind::i8). */
 typedef struct {
     const void* w;
     uint32_t type;       /* QUANTR_TYPE_Q8_0 / Q4_K / Q5_K / Q6_K */
@@ -197,8 +197,9 @@ typedef struct quantr_program quantr_program;
  * matmul_q_fused per GEMV (src/runtime.c:124-287); a program is the batched
  * device form of such a sequence. */
 int quantr_program_create(quantr_program** prog, const quantr_gemv_job* jobs, int njobs);
-/* Runs the program on `stream` (two launches: activation quantizer, then the
- * persistent GEMV engine; programmatic dependent launch between them). */
+/* Runs the program on `stream` (per kernel kind used: an activation quantizer
+ * launch, then the persistent GEMV kernel; programmatic dependent launch
+ * between them). */
 int quantr_program_run(quantr_program* prog, void* stream);
 void quantr_program_destroy(quantr_program* prog);
 /* Work items (row tiles), persistent CTAs and shared memory per CTA. */
@@ -236,7 +237,12 @@ size_t quantr_moe_workspace_bytes(int T, int E, int k, int dim, int hidden);
  * differ from glibc's expf in the last bit.  A token whose probabilities are
  * not finite (NaN logits) gets no experts and out = 0, and the device status
  * reports QUANTR_ERR_ROUTING.  The workspace must be 256-byte aligned.
- * Asynchronous on `stream`. */
+ * Asynchronous on `stream`.  From 48 tokens on the expert GEMVs run on the
+ * tensor cores: the first call with a given configuration (shapes, weight
+ * descriptors, xb, workspace and output pointers) plans those launches, which
+ * allocates their job tables and, for a pointer table of experts, reads the
+ * table once; make that first call before any stream capture.  Later calls
+ * with the same configuration allocate nothing. */
 int quantr_moe_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* router,
                    const float* logits, long long ldl, int E, int k, const quantr_expert_weights* w1,
                    const quantr_expert_weights* w3, const quantr_expert_weights* w2, int dim, int hidden, int* sel,
