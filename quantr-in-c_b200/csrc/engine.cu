@@ -383,16 +383,20 @@ __device__ __forceinline__ void consume_range(uint8_t* sm, const Item& it, int f
     }
 }
 
-template <uint32_t TYPE>
+template <uint32_t TYPE, bool ONE_ONLY>
 __device__ __forceinline__ void consume_typed(uint8_t* sm, const Item& it, int first, int total, const ItemHdr& h)
 {
     const bool gfast = (TYPE == T_Q4_K || TYPE == T_Q5_K) && h.gfast;
-    if (it.B == 1) consume_range<TYPE, true>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
+    if (ONE_ONLY || it.B == 1) consume_range<TYPE, true>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
     else consume_range<TYPE, false>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
 }
 
 // ---------------------------------------------------------------- kernel --
 
+// TY: the weight type every job of the launch shares (only its consumer code
+// is built in), or -1 for launches that mix types; ONE: every job has one
+// token (programs send wider jobs to the tensor cores).
+template <int TY, bool ONE>
 __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__ ProgParams p)
 {
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -505,11 +509,15 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
             const int total = (int)h.rows * it.nblk;
             const int first = ctid >= rot ? ctid - rot : ctid - rot + kConsumerThreads;
             rot = (int)(((unsigned)rot + (unsigned)total) % (unsigned)kConsumerThreads);
-            switch (h.type) {
-            case T_Q4_K: consume_typed<T_Q4_K>(sm, it, first, total, h); break;
-            case T_Q5_K: consume_typed<T_Q5_K>(sm, it, first, total, h); break;
-            case T_Q6_K: consume_typed<T_Q6_K>(sm, it, first, total, h); break;
-            default: consume_typed<T_Q8_0>(sm, it, first, total, h); break;
+            if constexpr (TY >= 0) {
+                consume_typed<(uint32_t)TY, ONE>(sm, it, first, total, h);
+            } else {
+                switch (h.type) {
+                case T_Q4_K: consume_typed<T_Q4_K, ONE>(sm, it, first, total, h); break;
+                case T_Q5_K: consume_typed<T_Q5_K, ONE>(sm, it, first, total, h); break;
+                case T_Q6_K: consume_typed<T_Q6_K, ONE>(sm, it, first, total, h); break;
+                default: consume_typed<T_Q8_0, ONE>(sm, it, first, total, h); break;
+                }
             }
             if (ctid == 0)  // forward the header to the chain warps
                 *reinterpret_cast<ItemHdr*>(sm + p.term_off + (uint32_t)tb * p.term_bytes) = h;
@@ -566,6 +574,8 @@ struct SubPlan {
     int grid = 0;
     size_t smem = 0;
     JobDesc* d_jobs = nullptr;  // device job table; null for a single inline job
+    int ty = -1;                // the weight type all jobs share, -1 if mixed
+    bool one = false;           // every job has one token
 };
 
 struct Plan {
@@ -737,11 +747,43 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
         if (!tables && sp.jobs.size() != 1) return QUANTR_ERR_BAD_ARG;
         const int rc = layout_sub(sp, sms, tables);
         if (rc) return rc;
+        sp.ty = (int)sp.jobs[0].hdr.type;
+        sp.one = true;
+        for (const auto& J : sp.jobs) {
+            if ((int)J.hdr.type != sp.ty) sp.ty = -1;
+            if (J.hdr.B != 1) sp.one = false;
+        }
         pl.subs.push_back(std::move(sp));
     }
     pl.qp.ntasks = (int)pl.tasks.size();
     pl.qp.total_blocks = pl.total_blocks;
     return QUANTR_OK;
+}
+
+template <int TY, bool ONE>
+cudaError_t launch_program_k(const SubPlan& sp, const ProgParams& pp, const LaunchCfg& c)
+{
+    static int configured_dev = -1;
+    cudaError_t e = ensure_smem_attr(&k_program<TY, ONE>, (int)kSmemMax, configured_dev);
+    if (e != cudaSuccess) return e;
+    return launch_ex(&k_program<TY, ONE>, dim3(sp.grid), dim3(kThreads), sp.smem, c, pp);
+}
+
+template <int TY>
+cudaError_t launch_program_t(const SubPlan& sp, const ProgParams& pp, const LaunchCfg& c)
+{
+    return sp.one ? launch_program_k<TY, true>(sp, pp, c) : launch_program_k<TY, false>(sp, pp, c);
+}
+
+cudaError_t launch_program(const SubPlan& sp, const ProgParams& pp, const LaunchCfg& c)
+{
+    switch (sp.ty) {
+    case T_Q4_K: return launch_program_t<T_Q4_K>(sp, pp, c);
+    case T_Q5_K: return launch_program_t<T_Q5_K>(sp, pp, c);
+    case T_Q6_K: return launch_program_t<T_Q6_K>(sp, pp, c);
+    case T_Q8_0: return launch_program_t<T_Q8_0>(sp, pp, c);
+    default: return launch_program_t<-1>(sp, pp, c);
+    }
 }
 
 // Launches the quantizer over every task, then one engine launch per
@@ -750,9 +792,7 @@ cudaError_t launch_plan(Plan& pl, const QTask* d_tasks, int* err, cudaStream_t s
 {
     LaunchCfg c;
     c.stream = stream;
-    static int configured_dev = -1;
-    cudaError_t e = ensure_smem_attr(&k_program, (int)kSmemMax, configured_dev);
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
     QParams qp = pl.qp;
     qp.tasks = d_tasks;
     if (!d_tasks) qp.inline_task = pl.tasks[0];
@@ -764,7 +804,7 @@ cudaError_t launch_plan(Plan& pl, const QTask* d_tasks, int* err, cudaStream_t s
         pp.jobs = sp.d_jobs;
         if (!sp.d_jobs) pp.inline_job = sp.jobs[0];
         pp.err = err;
-        e = launch_ex(&k_program, dim3(sp.grid), dim3(kThreads), sp.smem, c, pp);
+        e = launch_program(sp, pp, c);
     }
     return e;
 }
