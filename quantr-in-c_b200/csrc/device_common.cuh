@@ -77,10 +77,11 @@ __device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t parity
 // becomes non-zero (another role of the CTA gave up).  Never spins unboundedly.
 // suspend_ns > 0 lets each poll suspend the thread that long (fewer polls,
 // fewer issue slots taken from the warps that have work).
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
-                                                  volatile int* abort = nullptr, unsigned suspend_ns = 0)
+// The polling loop is out of line: every wait site's fast path (the phase is
+// already complete) stays a single instruction in the caller's hot code.
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, int* err, volatile int* abort,
+                                            unsigned suspend_ns)
 {
-    if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = gtimer();
     while (!(suspend_ns ? mbar_try_wait_for(bar, parity, suspend_ns) : mbar_try_wait(bar, parity))) {
         if (abort && *abort) return false;
@@ -91,6 +92,13 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
         }
     }
     return true;
+}
+
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
+                                                  volatile int* abort = nullptr, unsigned suspend_ns = 0)
+{
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, err, abort, suspend_ns);
 }
 
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar)
