@@ -556,7 +556,10 @@ __device__ void epilogue_role(uint8_t* sm, const TcParams& p, const TcJob* jobs,
                 const uint32_t tbase = tq + (uint32_t)(sb * kUS) * p.ncol;
                 if (tok0 < B) {
                     const uint32_t s0 = ebase + srow, r0b = ebase + drow;
-                    if constexpr (TY >= 0) {  // one weight type in the launch: its code only
+                    if constexpr (TY == T_Q4_K || TY == T_Q5_K || TY == T_Q6_K) {
+                        // One K-quant type: a row is whole super-blocks, every stage is full.
+                        epi_stage<(uint32_t)TY, NT, true>(tbase, s0, r0b, N, us, acc);
+                    } else if constexpr (TY >= 0) {  // one weight type in the launch: its code only
                         if (us == kUS) epi_stage<(uint32_t)TY, NT, true>(tbase, s0, r0b, N, us, acc);
                         else epi_stage<(uint32_t)TY, NT, false>(tbase, s0, r0b, N, us, acc);
                     } else if (us == kUS) {
@@ -889,7 +892,11 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         // every row's aligned segment cover, the group's 128 threads walking
         // (row, chunk) pairs chunk-fastest so a warp instruction reads a few
         // rows' contiguous bytes; one commit group per stage, empty otherwise.
+        // Q4_K / Q5_K launches fetch every stage by TMA (the host builds
+        // them only when every job has a tensor map): no copy path.
+        constexpr bool kAllTma = TY == T_Q4_K || TY == T_Q5_K;
         auto issue = [&](const Pos& q, int g) {
+            if constexpr (kAllTma) return;
             if (valid(q) && !jobs[q.jc].tma) {
                 const int ws = g % SW, wu = g / SW;
                 if (wu > 0 && !mbar_wait_bounded(&br.wempty[ws], (wu - 1) & 1, p.err, abort_flag, kSleepDec)) ok = false;
@@ -928,14 +935,15 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
         for (Pos cur = first; valid(cur); cur = next(cur), advance()) {
             if (gs % DG != grp) continue;  // the other group's stage
             const TcJob& J = jobs[cur.jc];
+            const bool tma = kAllTma || J.tma;
             // A copied stage's group is the only one in flight.
-            if (!J.tma) asm volatile("cp.async.wait_group 0;" ::: "memory");
-            if (J.tma && ok && !mbar_wait_bounded(&br.wfull[ws], wu & 1, p.err, abort_flag, kSleepDec)) ok = false;
+            if (!tma) asm volatile("cp.async.wait_group 0;" ::: "memory");
+            if (tma && ok && !mbar_wait_bounded(&br.wfull[ws], wu & 1, p.err, abort_flag, kSleepDec)) ok = false;
             // The A slot's previous stage is consumed (its MMAs are done), and
             // the scale slot's (its epilogue is done).
             if (ou > 0 && ok && !mbar_wait_bounded(&br.ofree[os], (ou - 1) & 1, p.err, abort_flag, kSleepDec)) ok = false;
             if (eu > 0 && ok && !mbar_wait_bounded(&br.efree[es], (eu - 1) & 1, p.err, abort_flag, kSleepDec)) ok = false;
-            if (J.tma) {
+            if (tma) {
                 // The stage's weights came by TMA: each warp goes on alone.  A
                 // warp that gave up keeps walking the stages without work (so
                 // it still meets its group at the barriers of copied stages).
@@ -961,13 +969,12 @@ __global__ void __launch_bounds__(Split<DG, EG>::threads, 1) k_tc_program(const 
                 const int us = min(kUS, (int)J.U - kUS * cur.st);
                 if (row < rows) {
                     const uintptr_t a = (uintptr_t)(J.w + (long long)(r0 + row) * J.rb + (long long)cur.st * J.seg);
-                    const uint32_t seg0 = J.tma ? wbase + (uint32_t)row * J.seg
+                    const uint32_t seg0 = tma ? wbase + (uint32_t)row * J.seg
                                                 : wbase + (uint32_t)row * p.segp + (uint32_t)(a & 15);
                     const uint32_t arow = obase + (uint32_t)((row >> 3) * 256 + (row & 7) * 16);
                     const uint32_t srow = ebase + p.s_rel + (uint32_t)row * 8;
-                    if constexpr (TY == T_Q4_K || TY == T_Q5_K) {
-                        if ((a & 15) == 0) decode_k45_aligned<(uint32_t)TY>(sm, seg0, arow, srow);
-                        else decode_units<(uint32_t)TY>(s32, sm, seg0, us, arow, srow);
+                    if constexpr (kAllTma) {  // TMA-fetched rows are 16-byte aligned
+                        decode_k45_aligned<(uint32_t)TY>(sm, seg0, arow, srow);
                     } else if constexpr (TY >= 0) {
                         decode_units<(uint32_t)TY>(s32, sm, seg0, us, arow, srow);
                     } else if (J.type == T_Q4_K && (a & 15) == 0) decode_k45_aligned<T_Q4_K>(sm, seg0, arow, srow);
@@ -1283,8 +1290,8 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     pp.gathered = gathered ? 1 : 0;
     P->bmax = Bmax;
     P->ty = (int)P->jobs[0].type;
-    for (const auto& J : P->jobs)
-        if ((int)J.type != P->ty) P->ty = -1;
+    for (const auto& J : P->jobs)  // a Q4_K/Q5_K kernel assumes every job has a tensor map
+        if ((int)J.type != P->ty || ((J.type == T_Q4_K || J.type == T_Q5_K) && !J.tma)) P->ty = -1;
     pp.NB = (uint32_t)std::min(kMaxNB, 512 / (kUS * Nmax));  // 4, 2 or 1 stage buffers for N = 16, 32, 64
     uint32_t cols = 32;
     while (cols < pp.NB * kUS * pp.ncol) cols <<= 1;
