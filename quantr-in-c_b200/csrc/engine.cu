@@ -383,10 +383,10 @@ __device__ __forceinline__ void consume_range(uint8_t* sm, const Item& it, int f
     }
 }
 
-template <uint32_t TYPE, bool ONE_ONLY>
+template <uint32_t TYPE, bool ONE_ONLY, bool GFAST_ALL>
 __device__ __forceinline__ void consume_typed(uint8_t* sm, const Item& it, int first, int total, const ItemHdr& h)
 {
-    const bool gfast = (TYPE == T_Q4_K || TYPE == T_Q5_K) && h.gfast;
+    const bool gfast = (TYPE == T_Q4_K || TYPE == T_Q5_K) && (GFAST_ALL || h.gfast);
     if (ONE_ONLY || it.B == 1) consume_range<TYPE, true>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
     else consume_range<TYPE, false>(sm, it, first, total, h.magic, (int)h.rows, h.inv_rows, gfast);
 }
@@ -395,8 +395,9 @@ __device__ __forceinline__ void consume_typed(uint8_t* sm, const Item& it, int f
 
 // TY: the weight type every job of the launch shares (only its consumer code
 // is built in), or -1 for launches that mix types; ONE: every job has one
-// token (programs send wider jobs to the tensor cores).
-template <int TY, bool ONE>
+// token (programs send wider jobs to the tensor cores); GF: every job takes
+// the row-fastest work order.
+template <int TY, bool ONE, bool GF>
 __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__ ProgParams p)
 {
     extern __shared__ __align__(1024) uint8_t sm[];
@@ -510,13 +511,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
             const int first = ctid >= rot ? ctid - rot : ctid - rot + kConsumerThreads;
             rot = (int)(((unsigned)rot + (unsigned)total) % (unsigned)kConsumerThreads);
             if constexpr (TY >= 0) {
-                consume_typed<(uint32_t)TY, ONE>(sm, it, first, total, h);
+                consume_typed<(uint32_t)TY, ONE, GF>(sm, it, first, total, h);
             } else {
                 switch (h.type) {
-                case T_Q4_K: consume_typed<T_Q4_K, ONE>(sm, it, first, total, h); break;
-                case T_Q5_K: consume_typed<T_Q5_K, ONE>(sm, it, first, total, h); break;
-                case T_Q6_K: consume_typed<T_Q6_K, ONE>(sm, it, first, total, h); break;
-                default: consume_typed<T_Q8_0, ONE>(sm, it, first, total, h); break;
+                case T_Q4_K: consume_typed<T_Q4_K, ONE, false>(sm, it, first, total, h); break;
+                case T_Q5_K: consume_typed<T_Q5_K, ONE, false>(sm, it, first, total, h); break;
+                case T_Q6_K: consume_typed<T_Q6_K, ONE, false>(sm, it, first, total, h); break;
+                default: consume_typed<T_Q8_0, ONE, false>(sm, it, first, total, h); break;
                 }
             }
             if (ctid == 0)  // forward the header to the chain warps
@@ -540,7 +541,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_program(const __grid_constant__
             float* out = h.out;
             const long long ldo = h.ldo;
             for (int q = lane; q < rows * B; q += 32) {
-                const int g = q / B, t = q - g * B;
+                const int g = ONE ? q : q / B, t = ONE ? 0 : q - g * B;
                 const float* tp = terms + q;
                 float acc = 0.0f;
 #pragma unroll 8
@@ -576,6 +577,7 @@ struct SubPlan {
     JobDesc* d_jobs = nullptr;  // device job table; null for a single inline job
     int ty = -1;                // the weight type all jobs share, -1 if mixed
     bool one = false;           // every job has one token
+    bool gfast = false;         // every job takes the row-fastest work order
 };
 
 struct Plan {
@@ -748,10 +750,11 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
         const int rc = layout_sub(sp, sms, tables);
         if (rc) return rc;
         sp.ty = (int)sp.jobs[0].hdr.type;
-        sp.one = true;
+        sp.one = sp.gfast = true;
         for (const auto& J : sp.jobs) {
             if ((int)J.hdr.type != sp.ty) sp.ty = -1;
             if (J.hdr.B != 1) sp.one = false;
+            if (!J.hdr.gfast) sp.gfast = false;
         }
         pl.subs.push_back(std::move(sp));
     }
@@ -760,19 +763,22 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
     return QUANTR_OK;
 }
 
-template <int TY, bool ONE>
+template <int TY, bool ONE, bool GF>
 cudaError_t launch_program_k(const SubPlan& sp, const ProgParams& pp, const LaunchCfg& c)
 {
     static int configured_dev = -1;
-    cudaError_t e = ensure_smem_attr(&k_program<TY, ONE>, (int)kSmemMax, configured_dev);
+    cudaError_t e = ensure_smem_attr(&k_program<TY, ONE, GF>, (int)kSmemMax, configured_dev);
     if (e != cudaSuccess) return e;
-    return launch_ex(&k_program<TY, ONE>, dim3(sp.grid), dim3(kThreads), sp.smem, c, pp);
+    return launch_ex(&k_program<TY, ONE, GF>, dim3(sp.grid), dim3(kThreads), sp.smem, c, pp);
 }
 
 template <int TY>
 cudaError_t launch_program_t(const SubPlan& sp, const ProgParams& pp, const LaunchCfg& c)
 {
-    return sp.one ? launch_program_k<TY, true>(sp, pp, c) : launch_program_k<TY, false>(sp, pp, c);
+    if constexpr (TY == T_Q4_K || TY == T_Q5_K) {  // the row-fastest order applies to these
+        if (sp.one && sp.gfast) return launch_program_k<TY, true, true>(sp, pp, c);
+    }
+    return sp.one ? launch_program_k<TY, true, false>(sp, pp, c) : launch_program_k<TY, false, false>(sp, pp, c);
 }
 
 cudaError_t launch_program(const SubPlan& sp, const ProgParams& pp, const LaunchCfg& c)
