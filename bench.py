@@ -58,10 +58,10 @@ Q8_0, Q4_K = 8, 12
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one k_program launch of the c2 step, from the
-# ncu capture summarised in profiles/k_program_c2_full.md: 159,993,600 read +
-# 4,826,624 written (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB
+# ncu capture summarised in profiles/k_program_c2_full.md: 159,962,112 read +
+# 4,132,864 written (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB
 # out per step).
-NCU_TRAFFIC_PER_STEP = 164820224
+NCU_TRAFFIC_PER_STEP = 164094976
 
 
 def row_bytes(t, d):
