@@ -237,7 +237,7 @@ size_t quantr_moe_workspace_bytes(int T, int E, int k, int dim, int hidden);
  * differ from glibc's expf in the last bit.  A token whose probabilities are
  * not finite (NaN logits) gets no experts and out = 0, and the device status
  * reports QUANTR_ERR_ROUTING.  The workspace must be 256-byte aligned.
- * Asynchronous on `stream`.  From 48 tokens on the expert GEMVs run on the
+ * Asynchronous on `stream`.  From 16 tokens on the expert GEMVs run on the
  * tensor cores: the first call with a given configuration (shapes, weight
  * descriptors, xb, workspace and output pointers) plans those launches, which
  * allocates their job tables and, for a pointer table of experts, reads the

@@ -603,12 +603,12 @@ struct MoeTcPlans {
 };
 
 // Fewest tokens for the tensor-core path.  Measured on B200 (us per layer,
-// tensor cores / dp4a): c4 shapes T = 16: 266 / 212, T = 32: 328 / 302,
-// T = 64: 341 / 433; c5 T = 16: 300 / 252, T = 64: 389 / 501.  With a few
-// pairs per expert the dp4a kernel, which stages each chosen expert's rows
-// once with no pipeline to fill, is faster.
+// tensor cores / dp4a): c4 shapes T = 1: 83 / 57, T = 16: 212 / 212, T = 32:
+// 250 / 302, T = 64: 261 / 433; c5 T = 8: 187 / 163, T = 16: 234 / 252,
+// T = 64: 303 / 501.  With about one pair per expert the dp4a kernel, which
+// stages each chosen expert's rows once with no pipeline to fill, is faster.
 #ifndef QR_MOE_TC_MIN_T
-#define QR_MOE_TC_MIN_T 48
+#define QR_MOE_TC_MIN_T 16
 #endif
 constexpr int kMoeTcMinT = QR_MOE_TC_MIN_T;
 

@@ -294,7 +294,7 @@ def test_moe_stages_emulate_expert_parallel(qr_gpu, orc, T):
     np.testing.assert_array_equal(out.cpu().numpy().view(np.uint32), full[0].view(np.uint32))
 
 
-# Tensor-core experts stage (T >= 48 tokens: gathered tcgen05 jobs over each
+# Tensor-core experts stage (T >= 16 tokens: gathered tcgen05 jobs over each
 # expert's pairs) on the cases above that shape it differently.
 
 def test_moe_tc_mixed_types(qr_gpu, orc):
