@@ -30,7 +30,10 @@
 // reference's quantize_row_q8_0 per input) in the compact, weight-type
 // permuted layout the consumers read; the program kernel issues its first
 // weight copies before griddepcontrol.wait, so under programmatic dependent
-// launch the weight stream overlaps the quantizer.
+// launch the weight stream overlaps the quantizer.  Each launch runs a kernel
+// built for its weight type when all jobs share one, for one-token jobs and
+// for the row-fastest work order (smaller code: fewer instruction-fetch
+// stalls).
 #include "quantr_cuda.h"
 
 #include "device_common.cuh"

@@ -51,7 +51,13 @@
 //
 // Activations are quantized by k_tc_quant (quantize_row_q8_0 per token, the
 // same kernel math as every other path) straight into operand tiles in the
-// element order each weight type's decode produces.  All waits are bounded
+// element order each weight type's decode produces, or arrive as operand
+// tiles (gathered jobs: the pairs routed to one MoE expert, whose count and
+// pair list an earlier launch writes; every role reads the count, skips
+// experts nobody chose and runs one pass over the tile per 16 pairs).  Each
+// launch runs a kernel built for its split, for whether it has gathered jobs,
+// and for its weight type when all jobs share one (smaller code: instruction
+// fetch was a leading stall of the generic kernel).  All waits are bounded
 // (250 ms); on a timeout every role stops, copies in flight are drained, the
 // last MMAs are awaited and TMEM is freed before the CTA exits.  No multicast.
 #include "quantr_cuda.h"
