@@ -167,3 +167,24 @@ def test_program_rejects_bad_jobs(qr_gpu):
     with pytest.raises(qr_gpu.QuantrError):  # misaligned weights on the tensor-core path
         qr_gpu.Program([(w.data_ptr() + 1, 12, 4, 256, 16, x.data_ptr(), 256, o.data_ptr(), 4)])
     assert ctypes is not None
+
+
+@pytest.mark.parametrize("type_,d", [(12, 512), (12, 768), (13, 512), (13, 768), (14, 1024), (8, 2048), (8, 288)])
+def test_program_single_type_one_token(qr_gpu, orc, type_, d):
+    """Programs whose one-token jobs share one weight type run the engine
+    kernel built for that type (and, for Q4_K/Q5_K rows of an odd number of
+    16-byte units - d = 768 - for the row-fastest order only; d = 512 gives an
+    even number and the other order).  A second run sees new inputs."""
+    specs = [(type_, 300, d, 1), (type_, 129, d, 1), (type_, 64, d, 1)]
+    prog, host, keep = build_program(qr_gpu, specs, 40 + type_)
+    prog.run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    check_outputs(orc, host, keep)
+    rng = synth.rng_for(99)
+    for k, (w, x, t, n, dd) in enumerate(host):
+        x2 = synth.activations(rng, 1, dd)
+        keep[3 * k + 1].copy_(torch.from_numpy(x2))
+        host[k] = (w, x2, t, n, dd)
+    prog.run(torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    check_outputs(orc, host, keep)
