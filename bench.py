@@ -505,6 +505,30 @@ def ours_arm(args):
         dist.destroy_process_group()
 
 
+def int8_peak(device=0):
+    """Dense int8 tensor throughput of this GPU (TOP/s): torch._int_mm (a cuBLASLt
+    int8 x int8 -> int32 GEMM) of 8192^3, best of 20 after warm-up, CUDA events.
+    The denominator for tensor-pipe fractions of int8 work."""
+    import torch
+    dev = torch.device("cuda", device)
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(20):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    return 2.0 * n ** 3 / (best / 1e3) / 1e12
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -516,11 +540,17 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c1", action="store_true", help="skip the c1 Q8_0 GEMV line")
+    ap.add_argument("--int8-peak", action="store_true",
+                    help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")
     ap.add_argument("--sweep", type=lambda v: [int(b) for b in v.split(",") if b], default=[4, 16],
                     help="other batch sizes timed on the same weights (comma list; empty to skip)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.int8_peak:
+        print(json.dumps({"int8_dense_tops": round(int8_peak(), 1),
+                          "how": "torch._int_mm 8192^3 int8 GEMM (cuBLASLt), best of 20, CUDA events"}))
+        return
     if args.impl == "reference":
         reference_arm(args)
     else:
