@@ -59,42 +59,61 @@ __device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_
 
 // ------------------------------------------------------- route and group --
 
-// Thread t routes token t, working on its row of `probs` (T x E in the
-// workspace; logits may alias it).
+// Warp w routes token w, working on its row of `probs` (T x E in the
+// workspace; logits may alias it): lane l takes experts l, l+32, ...  Every
+// value is computed as the reference computes it; only the independent
+// per-expert steps run in parallel, and the two left-to-right sums (softmax
+// denominator, renormalisation) stay sequential in one lane.
 __global__ void __launch_bounds__(128)
     k_moe_route(const float* logits, long long ldl, float* probs, int T, int E, int k, int* __restrict__ sel,
                 float* __restrict__ wts, int* err)
 {
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= T) return;
+    const int lane = threadIdx.x & 31;
+    const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (t >= T) return;  // warp-uniform
     float* p = probs + (long long)t * E;
     const float* lg = logits + (long long)t * ldl;
-    // softmax_ref (src/kernels.c:191-207)
-    float m = lg[0];
-    for (int e = 1; e < E; ++e)
-        if (lg[e] > m) m = lg[e];
+    // softmax_ref (src/kernels.c:191-207).  The running maximum with a strict
+    // '>' from lg[0] is lg[0] when that is NaN, else the largest non-NaN value
+    // (which of +0/-0 it keeps does not change lg[e] - m).
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, lg[e]);  // fmaxf skips NaN
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float l0 = lg[0];
+    if (l0 != l0) m = l0;
+    for (int e = lane; e < E; e += 32) p[e] = expf_cr(__fsub_rn(lg[e], m));
+    __syncwarp();
     float sum = 0.0f;
-    for (int e = 0; e < E; ++e) {
-        const float v = expf_cr(__fsub_rn(lg[e], m));
-        p[e] = v;
-        sum = __fadd_rn(sum, v);
-    }
-    const float inv = __fdiv_rn(1.0f, sum);
-    for (int e = 0; e < E; ++e) p[e] = __fmul_rn(p[e], inv);
-    // top-k (src/runtime.c:208-221)
+    if (lane == 0)
+        for (int e = 0; e < E; ++e) sum = __fadd_rn(sum, p[e]);
+    const float inv = __fdiv_rn(1.0f, __shfl_sync(0xffffffffu, sum, 0));
+    for (int e = lane; e < E; e += 32) p[e] = __fmul_rn(p[e], inv);
+    __syncwarp();
+    // top-k (src/runtime.c:208-221): k passes of the first strict maximum
+    // above -1e9 (the lowest index among equal values), then masked to -1e9.
     float w[kMoeMaxK];
     int s_[kMoeMaxK];
     bool bad = false;
     for (int s = 0; s < k; ++s) {
         float best = -1e9f;
         int arg = -1;
-        for (int e = 0; e < E; ++e) {
+        for (int e = lane; e < E; e += 32) {
             const float v = p[e];
             if (v > best) {
                 best = v;
                 arg = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+            const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oa = __shfl_xor_sync(0xffffffffu, arg, o);
+            if (oa >= 0 && (arg < 0 || ob > best || (ob == best && oa < arg))) {
+                best = ob;
+                arg = oa;
             }
         }
         if (arg < 0) {  // non-finite probabilities: the reference would index [-1]
@@ -103,8 +122,10 @@ __global__ void __launch_bounds__(128)
         }
         s_[s] = arg;
         w[s] = best;
-        p[arg] = -1e9f;
+        if (lane == (arg & 31)) p[arg] = -1e9f;
+        __syncwarp();
     }
+    if (lane != 0) return;
     // renormalisation (src/runtime.c:223-229)
     float tot = 0.0f;
     if (!bad)
@@ -587,7 +608,7 @@ cudaError_t launch_moe_route(const MoeRoute& r, const LaunchCfg& c)
         ldl = r.E;
     }
     if (e == cudaSuccess)
-        e = launch_ex(&k_moe_route, dim3((r.T + 127) / 128), dim3(128), 0, c, lg, ldl, probs, r.T, r.E, r.k, r.sel,
+        e = launch_ex(&k_moe_route, dim3((r.T + 3) / 4), dim3(128), 0, c, lg, ldl, probs, r.T, r.E, r.k, r.sel,
                       r.wts, r.err);
     return e;
 }
