@@ -1334,8 +1334,9 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_jobs, P->jobs.size() * sizeof(TcJob));
     if (e == cudaSuccess)
         e = cudaMemcpy(P->d_jobs, P->jobs.data(), P->jobs.size() * sizeof(TcJob), cudaMemcpyHostToDevice);
-    if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_tasks, P->tasks.size() * sizeof(TcQTask));
-    if (e == cudaSuccess)
+    if (e == cudaSuccess && !P->tasks.empty())  // none when every job came with operand tiles
+        e = cudaMalloc((void**)&P->d_tasks, P->tasks.size() * sizeof(TcQTask));
+    if (e == cudaSuccess && !P->tasks.empty())
         e = cudaMemcpy(P->d_tasks, P->tasks.data(), P->tasks.size() * sizeof(TcQTask), cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaMalloc((void**)&P->d_sched, sched.size() * sizeof(uint32_t));
     if (e == cudaSuccess)
