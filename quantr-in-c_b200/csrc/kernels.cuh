@@ -115,7 +115,7 @@ struct GemvJobIn {
 // nothing.
 struct TcPlan;
 constexpr int kTcMaxB = 64;
-constexpr int kTcMaxJobs = 96;
+constexpr int kTcMaxJobs = 128;
 int tc_plan_create(const GemvJobIn* jobs, int njobs, TcPlan** out);
 cudaError_t tc_plan_run(TcPlan* plan, int* err, cudaStream_t stream);
 void tc_plan_destroy(TcPlan* plan);
