@@ -170,12 +170,12 @@ int quantr_gpu_device_status(void* stream, int reset);
 
 /* ---- GEMV programs: many independent GEMVs per launch ------------------ */
 
-/* One GEMV of a program: out[t*ldo + r] = row_r(w) . x[t*ldx ...] for t < B
- * (B <= 64), with the reference's numerics (the same as matmul_q_fused per
- * token).  All pointers are device pointers; w must be 16-byte aligned and
+/* One GEMV of a program: out[t*ldo + r] = row_r(w) . x[t*ldx ...] for t < B,
+ * with the reference's numerics (the same as matmul_q_fused per token).  All pointers are device pointers; w must be 16-byte aligned and
  * readable up to the next 16-byte boundary past its last row (every cudaMalloc
  * allocation and registered range is).  Jobs of one token run on the dp4a
- * engine, jobs of 2..64 tokens on the tensor cores (tcgen05 kind::i8). */
+ * engine, jobs of 2..64 tokens on the tensor cores (tcgen05 kind::i8), wider
+ * jobs (a prefill chunk) as 64-token slices on the tensor cores. */
 typedef struct {
     const void* w;
     uint32_t type;       /* QUANTR_TYPE_Q8_0 / Q4_K / Q5_K / Q6_K */

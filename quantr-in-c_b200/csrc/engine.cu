@@ -889,7 +889,14 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     std::vector<GemvJobIn> tcj;
     for (int j = 0; j < njobs; ++j) {
         const quantr_gemv_job& J = jobs[j];
-        if (J.B >= kTcMinB && J.B <= kTcMaxB && J.type != T_F32)
+        if (J.B > kTcMaxB && J.type != T_F32 && J.x && J.out && J.ldx >= J.d && J.ldo >= J.n) {
+            // Wider jobs (a prefill chunk) run as kTcMaxB-token slices of the
+            // same weights: tokens [b0, b0 + Bs) of x and out.
+            for (int b0 = 0; b0 < J.B; b0 += kTcMaxB)
+                tcj.push_back(GemvJobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d,
+                                        std::min(kTcMaxB, J.B - b0), J.x + (long long)b0 * J.ldx, J.ldx,
+                                        J.out + (long long)b0 * J.ldo, J.ldo});
+        } else if (J.B >= kTcMinB && J.B <= kTcMaxB && J.type != T_F32)
             tcj.push_back(GemvJobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out,
                                     J.ldo});
         else

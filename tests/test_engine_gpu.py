@@ -162,8 +162,10 @@ def test_program_rejects_bad_jobs(qr_gpu):
         qr_gpu.Program([(w.data_ptr() + 1, 12, 4, 256, 1, x.data_ptr(), 256, o.data_ptr(), 4)])
     with pytest.raises(qr_gpu.QuantrError):  # unsupported type
         qr_gpu.Program([(w.data_ptr(), 2, 4, 256, 1, x.data_ptr(), 256, o.data_ptr(), 4)])
-    with pytest.raises(qr_gpu.QuantrError):  # B above 64
-        qr_gpu.Program([(w.data_ptr(), 12, 4, 256, 65, x.data_ptr(), 256, o.data_ptr(), 4)])
+    with pytest.raises(qr_gpu.QuantrError):  # no tokens
+        qr_gpu.Program([(w.data_ptr(), 12, 4, 256, 0, x.data_ptr(), 256, o.data_ptr(), 4)])
+    with pytest.raises(qr_gpu.QuantrError):  # output rows overlap (ldo < n), sliced wide job
+        qr_gpu.Program([(w.data_ptr(), 12, 4, 256, 65, x.data_ptr(), 256, o.data_ptr(), 3)])
     with pytest.raises(qr_gpu.QuantrError):  # misaligned weights on the tensor-core path
         qr_gpu.Program([(w.data_ptr() + 1, 12, 4, 256, 16, x.data_ptr(), 256, o.data_ptr(), 4)])
     assert ctypes is not None

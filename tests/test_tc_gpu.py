@@ -130,3 +130,13 @@ def test_tc_small_batches_strided_x(qr_gpu, orc, B):
     run(prog)
     check(orc, host)
     assert qr_gpu.device_status() == 0
+
+
+@pytest.mark.parametrize("type_,B", [(Q4_K, 150), (Q6_K, 65), (Q8_0, 128)])
+def test_tc_wide_jobs_as_slices(qr_gpu, orc, type_, B):
+    """A job wider than 64 tokens (a prefill chunk) runs as 64-token slices of
+    the same weights; every token's outputs are the reference's."""
+    prog, host, keep = build(qr_gpu, [(type_, 200, 512, B), (Q4_K, 128, 256, 3)], 200 + B)
+    run(prog)
+    check(orc, host)
+    assert qr_gpu.device_status() == 0
