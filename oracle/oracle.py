@@ -9,8 +9,9 @@ never part of the product path.
                       build and pinned by tests/golden/.
   RefLib(variant)  -> _ref/libquantr_ref_<variant>.so, the reference's own
                       src/quant.c compiled by oracle/Makefile (scalar, avx2,
-                      avx512).  Present wherever it was built (it travels with
-                      the tree; /root/reference itself does not).
+                      avx512).  Present wherever it was built (the built
+                      libraries travel with the tree; the reference's sources
+                      are needed only to build them).
 """
 import ctypes
 import os
