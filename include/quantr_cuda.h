@@ -165,7 +165,9 @@ int quantr_gemv_partials_dev(float* out, int32_t* isum, int32_t* bsum, const flo
                              void* stream);
 
 /* Device error word of the current device (DEVICE_TIMEOUT if any bounded
- * in-kernel wait gave up since the last reset); synchronises `stream`. */
+ * in-kernel wait gave up since the last reset, including waits of
+ * quantr_gemv_noalloc_dev calls); synchronises `stream`.  reset != 0 clears
+ * the recorded error. */
 int quantr_gpu_device_status(void* stream, int reset);
 
 /* ---- GEMV programs: many independent GEMVs per launch ------------------ */
@@ -294,7 +296,16 @@ int quantr_moe_layer(float* out, const float* xb, int T, const float* router, co
  * first call on each device looks up the scratch address (cudaGetSymbolAddress)
  * with that device current; make that first call before any stream capture.
  * All calls on a device share the one array: calls that overlap on the GPU
- * (different streams, or other threads) race, so serialise them. */
+ * (different streams, or other threads) race, so serialise them.  The call is
+ * asynchronous and returns QUANTR_OK once its launches are queued; a bounded
+ * in-kernel wait that gave up is recorded in the array's error word and stays
+ * recorded until quantr_gpu_device_status(stream, 1) reports and clears it
+ * (QUANTR_ERR_DEVICE_TIMEOUT), as for quantr_gemv_dev.  The cached scratch
+ * address belongs to the device's primary context: do not call this entry
+ * point after cudaDeviceReset in the same process.  It always runs the
+ * one-launch-per-GEMV kernel (the persistent engine that quantr_gemv_dev uses
+ * for aligned decode shapes keeps a cached plan in allocated memory), so it is
+ * slower than quantr_gemv_dev at batch 1-16, with identical results. */
 #define QUANTR_NOALLOC_SCRATCH_BYTES (1u << 20)
 int quantr_gemv_noalloc_dev(float* out, long long ldo, const float* x, long long ldx, const void* w,
                             uint32_t type, int n, int d, int B, void* stream);

@@ -30,10 +30,15 @@ def _p(a):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
 
+def ref_root():
+    """The reference checkout: $REF, else ../reference beside this repository."""
+    return os.environ.get("REF") or os.path.abspath(os.path.join(HERE, "..", "..", "reference"))
+
+
 def build(ref=True):
     """Builds the restatement (and, if the reference sources exist, _ref)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref and os.path.isdir(os.environ.get("REF", "/root/reference") + "/src"):
+    if ref and os.path.isdir(os.path.join(ref_root(), "src")):
         subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
 
 

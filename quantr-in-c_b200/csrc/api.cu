@@ -957,6 +957,10 @@ int quantr_gpu_device_status(void* stream, int reset)
     }
     if (cudaMemcpy(&v, w, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return QUANTR_ERR_CUDA;
     if (reset) cudaMemset(w, 0, 4);
+    // The allocation-free GEMV keeps its own word in the library's static
+    // scratch array; a timeout recorded there is reported here too.
+    const int na = noalloc_device_error(reset);
+    if (v == DEV_OK) v = na;
     return dev_code(v);
 }
 

@@ -931,7 +931,8 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     }
     if (cudaMalloc((void**)&p->d_act, std::max<size_t>(sizing.act_total, 256)) != cudaSuccess) {
         cudaGetLastError();
-        delete p;
+        p->d_act = nullptr;
+        quantr_program_destroy(p);
         return QUANTR_ERR_OOM;
     }
     rc = eng::make_plan(in.data(), (int)in.size(), p->d_act, sms, true, p->plan);

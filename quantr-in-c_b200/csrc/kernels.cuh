@@ -72,6 +72,10 @@ unsigned long long launch_count();
 // bounded-wait timeouts into (allocated on first use; api.cu).
 int* device_error_word();
 
+// Error word of the allocation-free GEMV (noalloc.cu) on the current device;
+// reset != 0 clears a recorded error.  DEV_OK if that path never ran here.
+int noalloc_device_error(int reset);
+
 // Single GEMV through the persistent engine (engine.cu): x is quantized into
 // `ws` (engine_act_bytes of it) and the engine program runs one job.  Returns
 // cudaErrorNotSupported when the engine cannot take the call (unaligned

@@ -61,6 +61,35 @@ int code_of(cudaError_t e)
 
 } // namespace
 
+// Error word of the allocation-free path on the current device, read (and
+// optionally cleared) by quantr_gpu_device_status.  Returns DEV_OK when no
+// allocation-free call has run on this device yet (the word was never looked
+// up, and the array starts zeroed).  Allocates nothing.
+int qr::noalloc_device_error(int reset)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+        cudaGetLastError();
+        return DEV_OK;
+    }
+    void* p = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_addr_mu);
+        p = g_addr[dev];
+    }
+    if (!p) return DEV_OK;
+    int v = DEV_OK;
+    if (cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        cudaGetLastError();
+        return DEV_OK;
+    }
+    if (reset && v != DEV_OK) {
+        const int zero = DEV_OK;
+        if (cudaMemcpy(p, &zero, sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) cudaGetLastError();
+    }
+    return v;
+}
+
 extern "C" int quantr_gemv_noalloc_dev(float* out, long long ldo, const float* x, long long ldx, const void* w,
                                        uint32_t type, int n, int d, int B, void* stream)
 {
@@ -75,9 +104,11 @@ extern "C" int quantr_gemv_noalloc_dev(float* out, long long ldo, const float* x
     ActQ a = actq_carve(static_cast<unsigned char*>(base) + kErrBytes, d, B);
     LaunchCfg c;
     c.stream = static_cast<cudaStream_t>(stream);
-    // The quantizer overwrites every activation byte the GEMV reads and zeroes
-    // the error word first, so nothing left by an earlier call leaks in.
-    rc = code_of(launch_quantize(x, ldx, d, B, a, nullptr, err, c));
+    // The quantizer overwrites every activation byte the GEMV reads, so
+    // nothing left by an earlier call leaks in.  The error word is NOT cleared
+    // here: a bounded wait that gave up stays recorded until
+    // quantr_gpu_device_status(stream, 1) reads and clears it.
+    rc = code_of(launch_quantize(x, ldx, d, B, a, nullptr, nullptr, c));
     if (rc) return rc;
     GemvArgs g;
     g.w = static_cast<const uint8_t*>(w);

@@ -50,6 +50,9 @@ def test_noalloc_matches_allocating_entry_point_twice():
         assert np.all(np.isfinite(g))
         assert np.all(np.abs(g - e) <= ATOL + RTOL * np.abs(e))
         assert np.array_equal(g.view(np.uint32), e.view(np.uint32))
+    # No bounded wait gave up on either path: the status call reads the
+    # allocation-free path's own error word as well and reports it clean.
+    assert L.quantr_gpu_device_status(ctypes.c_void_p(stream), 1) == 0
 
 
 def test_noalloc_rejects_oversized_shape():
