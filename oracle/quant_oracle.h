@@ -24,6 +24,7 @@
 #ifndef QUANT_ORACLE_H
 #define QUANT_ORACLE_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -82,6 +83,68 @@ int   qo_moe_token(float* out, int* sel, float* wts, const float* xb,
 /* Reference F32 kernels the MoE block uses (src/kernels.c:18-28, :191-207). */
 void  qo_matmul_f32(float* out, const float* x, const float* w, int n, int d);
 void  qo_softmax(float* x, int size);
+
+/* ---- decoder step (forward_oracle.c) ------------------------------------ */
+
+/* Model description: the reference's Config + TransformerWeights
+ * (include/types.h:19-71) as plain arrays indexed by layer (experts: per layer
+ * an array of expert_count pointers).  The fields up to exp_w3_type are laid
+ * out exactly like oracle/ref_forward.c's ref_model, so one struct drives both
+ * the restatement and the reference.  head_dim = 0 means dim / n_heads. */
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
+    float rope_freq_base;
+    int expert_count, expert_used_count;
+    int kv_type;                       /* 0 = fp32, 1 = fp16 (src/runtime.c:74-92) */
+    const void* token_embd;
+    uint32_t token_embd_type;
+    size_t token_embd_row_bytes;       /* 0: F32 table of dim floats per token */
+    const float* const* rms_att;
+    const float* const* rms_ffn;
+    const void* const* wq;
+    const void* const* wk;
+    const void* const* wv;
+    const void* const* wo;
+    const void* const* w1;
+    const void* const* w2;
+    const void* const* w3;
+    const uint32_t* wq_type;
+    const uint32_t* wk_type;
+    const uint32_t* wv_type;
+    const uint32_t* wo_type;
+    const uint32_t* w1_type;
+    const uint32_t* w2_type;
+    const uint32_t* w3_type;
+    const float* rms_final;
+    const void* wcls;
+    uint32_t wcls_type;
+    const float* const* ffn_gate_inp;  /* router, expert_count x dim F32 */
+    const void* const* const* expert_w1;
+    const void* const* const* expert_w2;
+    const void* const* const* expert_w3;
+    const uint32_t* exp_w1_type;
+    const uint32_t* exp_w2_type;
+    const uint32_t* exp_w3_type;
+    /* restatement-only extensions */
+    int head_dim;
+    int shexp_hidden_dim;              /* shared expert (0 = none) */
+    const void* const* shexp_w1;       /* gate: shexp_hidden x dim */
+    const void* const* shexp_w2;       /* down: dim x shexp_hidden */
+    const void* const* shexp_w3;       /* up:   shexp_hidden x dim */
+    const uint32_t* shexp_w1_type;
+    const uint32_t* shexp_w2_type;
+    const uint32_t* shexp_w3_type;
+    const float* const* shexp_gate;    /* dim F32 per layer */
+} qo_model;
+
+typedef struct qo_state qo_state;
+qo_state*    qo_open(const qo_model* m, int threads);
+void         qo_close(qo_state* s);
+/* forward_runtime(token, pos): returns the state's logits (vocab floats). */
+const float* qo_forward(qo_state* s, int token, int pos);
+/* src/main.c:305-317 with greedy sampling; logits optional (steps x vocab). */
+void         qo_generate(qo_state* s, const int* prompt, int n_prompt, int steps, int* out_tokens,
+                         float* logits);
 
 #ifdef __cplusplus
 }

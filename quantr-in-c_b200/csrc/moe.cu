@@ -29,12 +29,14 @@
 // gathered tcgen05 GEMV job over its pairs (tc.cu; counts and pair lists stay
 // on the device).
 // Every GEMV output is bit-identical to the reference's matmul_q_fused for
-// that (row, pair).  expf is evaluated correctly rounded (through double
-// precision), which differs from glibc's expf in rare last-bit cases.
+// that (row, pair), and expf (softmax, silu) is the host C library's own
+// method evaluated step for step (libm_ref.cuh), so the whole block is
+// bit-identical to the reference's scalar build.
 #include "device_common.cuh"
 #include "formats.cuh"
 #include "kernels.cuh"
 #include "launch_util.cuh"
+#include "libm_ref.cuh"
 #include "quant_decode.cuh"
 
 #include <algorithm>
@@ -52,10 +54,8 @@ constexpr int kBT = 8;             // pairs per pass over a staged weight tile
 constexpr uint32_t kChunk = 16384; // bytes per bulk copy
 constexpr size_t kSmemMax = 227 * 1024;
 
-__device__ __forceinline__ float expf_cr(float x) { return __double2float_rn(exp((double)x)); }
-
 // src/runtime.c:15-17: x / (1.0f + expf(-x)).
-__device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf_cr(-x))); }
+__device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, libm::expf_ref(-x))); }
 
 // ------------------------------------------------------- route and group --
 
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(128)
     for (int o = 16; o >= 1; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
     const float l0 = lg[0];
     if (l0 != l0) m = l0;
-    for (int e = lane; e < E; e += 32) p[e] = expf_cr(__fsub_rn(lg[e], m));
+    for (int e = lane; e < E; e += 32) p[e] = libm::expf_ref(__fsub_rn(lg[e], m));
     __syncwarp();
     float sum = 0.0f;
     if (lane == 0)
