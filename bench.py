@@ -505,6 +505,109 @@ def ours_arm(args):
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------- decode --
+
+def cpu_forward_run(spec, model_seed, prompt, positions, budget_s):
+    """Times the reference's own forward_runtime on this host: the unmodified
+    reference (oracle/_ref/libquantr_ref_forward_avx512.so, all host threads)
+    on the same model, feeding `prompt` at positions 0.. until `positions`
+    forward calls or `budget_s` seconds.  Returns (s per call, calls, threads,
+    kind)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    threads = os.cpu_count() or 1
+    import forward  # test infrastructure: the CPU baseline leg only
+    import model_synth as ms
+    model = ms.build(spec, seed=model_seed)
+    if forward.reference_available("avx512"):
+        r, kind = forward.Reference(model, variant="avx512", threads=threads, backend=2), "reference"
+    else:
+        r, kind = forward.Restated(model, threads=threads), "port"
+    r.forward(int(prompt[0]), 0)  # warm-up (page-in)
+    t0 = time.perf_counter()
+    done = 0
+    while done < positions and (done < 2 or time.perf_counter() - t0 < budget_s):
+        r.forward(int(prompt[done % len(prompt)]), done)
+        done += 1
+    el = time.perf_counter() - t0
+    r.close()
+    return el / done, done, threads, kind
+
+
+def decode_c3(args, dev, s):
+    """BASELINE config c3 on the device decoder: TinyLlama-1.1B shape, 512
+    prompt tokens prefilled, then greedy decode.  Decode time per token is
+    the difference of two CUDA-event-timed generate runs (512 + K and 512 + 0
+    positions), so the prefill cancels; the KV context runs 512..511+K."""
+    import torch
+
+    import model_synth as ms
+    import quantr
+    spec = ms.tinyllama()
+    t0 = time.perf_counter()
+    model = ms.build(spec, seed=1)
+    t_build = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    dec = quantr.Decoder(model)
+    torch.cuda.synchronize()
+    t_load = time.perf_counter() - t0
+    info = dec.info()
+    n_prompt, K = 512, args.decode_steps
+    prompt_h = ms.prompt(spec, n_prompt, seed=7)
+    prompt = torch.from_numpy(prompt_h).to(dev)
+    out = torch.empty(max(K, 1), 1, dtype=torch.int32, device=dev)
+
+    def timed(steps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            dec.generate_dev(prompt.data_ptr(), n_prompt, steps, out.data_ptr(), s.cuda_stream)
+            e1.record(s)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1)
+
+    timed(8)  # warm-up
+    reps = []
+    for _ in range(3):
+        t_full, t_pre = timed(K), timed(0)
+        reps.append(((t_full - t_pre) / K, t_pre / n_prompt))
+    ms_tok = statistics.median(r[0] for r in reps)
+    ms_pos_prefill = statistics.median(r[1] for r in reps)
+    assert quantr.device_status(0) == 0
+    toks_dev = out[:K, 0].cpu().numpy()
+    # End to end through the host API: prompt from host memory in, tokens out.
+    t0 = time.perf_counter()
+    toks_host = dec.generate(prompt_h, K)[0]
+    t_e2e = time.perf_counter() - t0
+    same = bool(np.array_equal(toks_dev, toks_host))
+    kv_bytes = info["kv_bytes_per_position"] * (n_prompt + (K + 1) / 2.0)  # average context
+    bytes_tok = info["weight_bytes_per_step"] + kv_bytes
+    gbs = bytes_tok / (ms_tok / 1e3) / 1e9
+    peak, peak_kind = load_peaks()
+    res = {
+        "workload": ("c3: TinyLlama-1.1B shape (22 layers, dim 2048, 32/4 heads, head_dim 64, FFN 5632, vocab "
+                     "32000, RoPE 10000), Q4_K linears, Q6_K head, Q8_0 embedding, fp32 KV; 512 prompt tokens "
+                     f"then {K} greedy tokens, batch 1; seeded random weights"),
+        "tok_per_s": round(1e3 / ms_tok, 1), "ms_per_token": round(ms_tok, 4),
+        "prefill_us_per_position": round(ms_pos_prefill * 1e3, 2),
+        "bytes_per_token": int(bytes_tok), "achieved_GBs": round(gbs, 1),
+        "hbm_frac": round(gbs / peak, 4), "pct_of_8TBs": round(100 * gbs / NOMINAL_HBM_GBS, 2),
+        "launches_per_token": info["launches_per_decode_step"],
+        "e2e": {"tok_per_s": round(K / t_e2e, 2), "positions_per_s": round((n_prompt + K) / t_e2e, 1),
+                "api": (f"quantr_decoder_generate with host prompt in / host tokens out: {n_prompt} prefill "
+                        f"positions + {K} greedy tokens in {t_e2e * 1e3:.1f} ms wall")},
+        "tokens_device_equal_host": same,
+        "model_build_s": round(t_build, 2), "decoder_create_s": round(t_load, 2),
+        "device_bytes": info["device_bytes"],
+    }
+    dec.close()
+    if not args.no_cpu_baseline:
+        sec, done, threads, kind = cpu_forward_run(spec, 1, prompt_h[0], 1000, args.cpu_seconds)
+        res["cpu_baseline"] = {"value": round(1.0 / sec, 3), "unit": "tok/s", "cores": threads, "kind": kind,
+                               "sample": (f"{done} forward_runtime calls at positions 0..{done - 1} on the same "
+                                          f"model ({sec * 1e3:.0f} ms each)")}
+    return res
+
+
 def int8_peak(device=0):
     """Dense int8 tensor throughput of this GPU (TOP/s): torch._int_mm (a cuBLASLt
     int8 x int8 -> int32 GEMM) of 8192^3, best of 20 after warm-up, CUDA events.
@@ -540,6 +643,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c1", action="store_true", help="skip the c1 Q8_0 GEMV line")
+    ap.add_argument("--no-decode", action="store_true", help="skip the c3 decode line")
+    ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")
     ap.add_argument("--sweep", type=lambda v: [int(b) for b in v.split(",") if b], default=[4, 16],

@@ -150,6 +150,14 @@ int quantr_gemv_dev(float* out, long long ldo, const float* x, long long ldx, co
  * (B * (k/32) blocks), bit-identical to the reference quantize_row_q8_0. */
 int quantr_quantize_q8_0_dev(block_q8_0* y, const float* x, long long ldx, int k, int B, void* stream);
 
+/* dequantize_row (src/quant.c:160-240) of `rows` packed rows of n elements,
+ * row r at src + r*src_stride bytes, into out[r*ldo ...]; elements past the
+ * last whole block are left untouched, as in the reference.  Q8_0/Q4_K/Q5_K/
+ * Q6_K.  (The expert-parallel MoE dequantizes the Q8_0 activation rows it
+ * receives with it; re-quantizing them reproduces the sender's blocks.) */
+int quantr_dequantize_rows_dev(float* out, long long ldo, const void* src, long long src_stride, uint32_t type, int n,
+                               int rows, void* stream);
+
 /* GEMV over already-quantized activations given as packed block_q8_0 rows
  * (B rows of d/32 blocks): the device counterpart of B vec_dot calls per row. */
 int quantr_gemv_q8act_dev(float* out, long long ldo, const block_q8_0* xq, const void* w, uint32_t type,
@@ -280,6 +288,126 @@ int quantr_moe_combine_dev(float* out, long long ldo, const float* o, const int*
 int quantr_moe_layer(float* out, const float* xb, int T, const float* router, const float* logits, int E, int k,
                      const void* const* w1, uint32_t t1, const void* const* w3, uint32_t t3, const void* const* w2,
                      uint32_t t2, int dim, int hidden, int* sel, float* wts);
+
+/* ---- device-resident decoder (forward_runtime on the GPU) -------------- */
+
+/* A decoder model: the reference's Config and TransformerWeights
+ * (include/types.h:19-71) flattened into per-layer arrays.  Every tensor
+ * pointer is a HOST address inside a range registered with
+ * quantr_gpu_register_weights (the GGUF mapping, the normal case: resolved to
+ * the device copy), a device address, or any other host address (uploaded
+ * once into memory the decoder owns).  Weight tensors must be 16-byte aligned
+ * (GGUF aligns tensors to 32 bytes, src/gguf.c:130-140).  Types are GGML ids;
+ * linears may be Q8_0/Q4_K/Q5_K/Q6_K, the router and norms F32, the embedding
+ * any type dequantize_row reads (row bytes token_embd_row_bytes; 0 = an F32
+ * table).  The reference's fields come first in its own order; head_dim and
+ * the shared expert are additions with no counterpart in the reference:
+ *   head_dim          0 = dim / n_heads (src/runtime.c:102); otherwise the
+ *                     query has n_heads*head_dim elements (Wq is that x dim,
+ *                     Wo dim x that) and RoPE runs over all of them;
+ *   shexp_*           a shared expert after the routed ones (Qwen1.5-MoE):
+ *                     xb2 += (Ws2.(silu(Ws1.xb) * Ws3.xb)) * sigmoid(gate.xb),
+ *                     Ws1 the gate projection like the dense FFN's W1. */
+typedef struct {
+    int dim, hidden_dim, n_layers, n_heads, n_kv_heads, vocab_size, seq_len;
+    float rope_freq_base;                   /* <= 0: 10000 (src/runtime.c:24) */
+    int expert_count, expert_used_count;    /* 0 experts: dense SwiGLU FFN */
+    int kv_type;                            /* 0 = fp32 KV cache, 1 = fp16 (src/runtime.c:74-92) */
+    const void* token_embd;
+    uint32_t token_embd_type;
+    size_t token_embd_row_bytes;
+    const float* const* rms_att;
+    const float* const* rms_ffn;
+    const void* const* wq;
+    const void* const* wk;
+    const void* const* wv;
+    const void* const* wo;
+    const void* const* w1;                  /* dense FFN gate (SiLU side) */
+    const void* const* w2;                  /* dense FFN down */
+    const void* const* w3;                  /* dense FFN up */
+    const uint32_t* wq_type;
+    const uint32_t* wk_type;
+    const uint32_t* wv_type;
+    const uint32_t* wo_type;
+    const uint32_t* w1_type;
+    const uint32_t* w2_type;
+    const uint32_t* w3_type;
+    const float* rms_final;
+    const void* wcls;
+    uint32_t wcls_type;
+    const float* const* ffn_gate_inp;       /* router, expert_count x dim F32 */
+    const void* const* const* expert_w1;    /* [layer][expert]: the loader's ffn_up (SiLU side) */
+    const void* const* const* expert_w2;
+    const void* const* const* expert_w3;
+    const uint32_t* exp_w1_type;
+    const uint32_t* exp_w2_type;
+    const uint32_t* exp_w3_type;
+    int head_dim;
+    int shexp_hidden_dim;                   /* 0 = no shared expert */
+    const void* const* shexp_w1;
+    const void* const* shexp_w2;
+    const void* const* shexp_w3;
+    const uint32_t* shexp_w1_type;
+    const uint32_t* shexp_w2_type;
+    const uint32_t* shexp_w3_type;
+    const float* const* shexp_gate;         /* dim F32 per layer */
+} quantr_model;
+
+typedef struct quantr_decoder quantr_decoder;
+
+/* Builds a decoder for `batch` independent sequences on the current device:
+ * resolves or uploads every weight, allocates the KV caches
+ * (n_layers x batch x seq_len x n_kv_heads*head_dim, fp32 or fp16) and the
+ * activations, plans every GEMV, computes the RoPE cos/sin table with the
+ * host C library's powf/cosf/sinf exactly as src/runtime.c:19-41 does per
+ * call, and captures one decode step and one prefill step as CUDA graphs.
+ * Every later call allocates nothing.  No counterpart in the reference (its
+ * RunState is malloc_run_state, src/model.c:101-150). */
+int quantr_decoder_create(quantr_decoder** dec, const quantr_model* m, int batch);
+void quantr_decoder_destroy(quantr_decoder* dec);
+
+/* forward_runtime (src/runtime.c:94-289) for every sequence b < batch:
+ * token tokens[b] at position pos[b] (0 <= pos < seq_len; the KV cache of
+ * sequence b), logits[b*ldl + v] (may be NULL) and the greedy next token
+ * next[b] (src/sampling.c:125-131; may be NULL).  Device pointers,
+ * asynchronous on `stream`.  Results are bit-identical to the reference's
+ * scalar build. */
+int quantr_decoder_step_dev(quantr_decoder* dec, const int* tokens, const int* pos, float* logits, long long ldl,
+                            int* next, void* stream);
+
+/* The reference CLI's generation loop (src/main.c:305-317) for every sequence
+ * at once, on the device: sequential prefill of the n_prompt prompt tokens
+ * (prompt[b*n_prompt + i]; src/runtime.c:294-304), then the last prompt token
+ * again at position n_prompt and `steps` greedy tokens (out[b*steps + i]),
+ * positions wrapping at seq_len.  Host arrays; synchronous.  One CUDA-graph
+ * replay per position, no host round trip between steps. */
+int quantr_decoder_generate(quantr_decoder* dec, const int* prompt, int n_prompt, int steps, int* out);
+
+/* quantr_decoder_generate with device arrays, asynchronous on `stream`:
+ * prompt is batch x n_prompt, out receives the greedy tokens step-major
+ * (out[i*batch + b]); steps <= max(seq_len, 4096). */
+int quantr_decoder_generate_dev(quantr_decoder* dec, const int* prompt, int n_prompt, int steps, int* out,
+                                void* stream);
+/* Kernel launches (graph nodes) of one decode step and one prefill step. */
+int quantr_decoder_launches(const quantr_decoder* dec, int* decode_step, int* prefill_step);
+
+/* Drop-in shapes of the reference's runtime calls for sequence 0 (host
+ * values, synchronous): forward_runtime's logits (vocab floats, valid until
+ * the next call) and prefill_runtime. */
+const float* quantr_forward_runtime(quantr_decoder* dec, int token, int pos);
+void quantr_prefill_runtime(quantr_decoder* dec, const int* tokens, int n_tokens);
+
+/* Bytes the decode step reads that do not depend on the position (weights of
+ * one token: every linear, the head, the norms, one embedding row) and the
+ * KV-cache bytes it reads per position, per sequence. */
+int quantr_decoder_info(const quantr_decoder* dec, size_t* weight_bytes_per_step, size_t* kv_bytes_per_position,
+                        size_t* device_bytes);
+
+/* Test hook: out[i] = the device's expf (the C library's method, used by the
+ * decoder's softmax and silu and by the MoE block) of the float whose bit
+ * pattern is first + i, for i < n.  Lets a test compare it with the host C
+ * library's expf over every float.  Asynchronous on `stream`. */
+int quantr_debug_expf_dev(float* out, uint32_t first, long long n, void* stream);
 
 /* Allocation-free quantized GEMV.  No counterpart in the reference: an
  * addition for callers that cannot call cudaMalloc - embedders whose own

@@ -126,6 +126,8 @@ class Oracle(_QuantLib):
         L.qo_softmax.argtypes = [_vp, _i]
         L.qo_matmul_f32.restype = None
         L.qo_matmul_f32.argtypes = [_vp, _vp, _vp, _i, _i]
+        L.qo_expf_mismatches.restype = _l
+        L.qo_expf_mismatches.argtypes = [_vp, _u32, _l]
         L.qo_moe_token.restype = _i
         L.qo_moe_token.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _u32, _l, _vp, _u32, _l,
                                    _vp, _u32, _l, _i, _i]
@@ -135,6 +137,12 @@ class Oracle(_QuantLib):
 
     def fp32_to_fp16(self, f):
         return int(self.L.qo_fp32_to_fp16(float(f)))
+
+    def expf_mismatches(self, got, first):
+        """Entries of got (float32[n]) that differ from the C library's expf
+        of the floats with bit patterns first, first + 1, ..."""
+        got = np.ascontiguousarray(got, np.float32)
+        return int(self.L.qo_expf_mismatches(_p(got), first, got.size))
 
     def unit_partials(self, w, type_, n, d, xq):
         units = (d // 32) if type_ == 8 else 8 * (d // 256)

@@ -263,7 +263,6 @@ static float row_dot(const uint8_t* row, const qo_block_q8_0* xq, uint32_t type,
 void qo_matmul_q_fused(float* out, const float* x, const void* w, uint32_t type,
                        int n, int d, int threads)
 {
-    (void)threads;
     if (!w) { memset(out, 0, (size_t)n * sizeof(float)); return; }
     if (type == QO_F32) {
         const float* wf = (const float*)w;
@@ -281,6 +280,14 @@ void qo_matmul_q_fused(float* out, const float* x, const void* w, uint32_t type,
     long rb = qo_row_bytes(type, d);
     int known = type == QO_Q8_0 || type == QO_Q4_K || type == QO_Q5_K || type == QO_Q6_K;
     float* tmp = known ? NULL : (float*)malloc((size_t)d * sizeof(float));
+    if (known && threads > 1) {
+        /* rows are independent (the reference's OpenMP row loop, src/quant.c:489) */
+        int r;
+#pragma omp parallel for num_threads(threads) schedule(static)
+        for (r = 0; r < n; r++) out[r] = row_dot((const uint8_t*)w + (size_t)r * (size_t)rb, xq, type, d);
+        free(xq);
+        return;
+    }
     for (int r = 0; r < n; r++) {
         const uint8_t* row = (const uint8_t*)w + (size_t)r * (size_t)rb;
         if (known) {
@@ -396,4 +403,24 @@ int qo_moe_token(float* out, int* sel, float* wts, const float* xb,
     }
     free(hb); free(hb2); free(o);
     return 0;
+}
+
+/* Number of i < n where got[i] differs from the C library's expf of the float
+ * with bit pattern first + i (NaN results compare equal to any NaN).  Used to
+ * check the device's exponential over every float. */
+long qo_expf_mismatches(const float* got, uint32_t first, long n)
+{
+    long bad = 0;
+    long i;
+#pragma omp parallel for schedule(static) reduction(+ : bad)
+    for (i = 0; i < n; i++) {
+        uint32_t u = first + (uint32_t)i, ua, ub;
+        float x, a;
+        memcpy(&x, &u, 4);
+        a = expf(x);
+        memcpy(&ua, &a, 4);
+        memcpy(&ub, &got[i], 4);
+        if (ua != ub && !(a != a && got[i] != got[i])) bad++;
+    }
+    return bad;
 }

@@ -84,6 +84,9 @@ int   qo_moe_token(float* out, int* sel, float* wts, const float* xb,
 void  qo_matmul_f32(float* out, const float* x, const float* w, int n, int d);
 void  qo_softmax(float* x, int size);
 
+/* Mismatches of got[i] against the C library's expf(bits first + i). */
+long  qo_expf_mismatches(const float* got, uint32_t first, long n);
+
 /* ---- decoder step (forward_oracle.c) ------------------------------------ */
 
 /* Model description: the reference's Config + TransformerWeights

@@ -946,6 +946,17 @@ int quantr_moe_layer(float* out, const float* xb, int T, const float* router, co
     return QUANTR_OK;
 }
 
+int quantr_dequantize_rows_dev(float* out, long long ldo, const void* src, long long src_stride, uint32_t type, int n,
+                               int rows, void* stream)
+{
+    if (n <= 0 || rows <= 0) return QUANTR_OK;
+    if (!out || !src || ldo < n || src_stride < row_bytes(type, n)) return QUANTR_ERR_BAD_ARG;
+    if (!type_supported(type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
+    LaunchCfg c;
+    c.stream = (cudaStream_t)stream;
+    return code_of(launch_dequantize_rows(out, ldo, (const uint8_t*)src, src_stride, type, n, rows, c));
+}
+
 int quantr_gpu_device_status(void* stream, int reset)
 {
     int* w = device_error_word();

@@ -1,0 +1,1190 @@
+// decode.cu -- the reference's decoder step, forward_runtime
+// (src/runtime.c:94-289), resident on the device, for `batch` independent
+// sequences, and its generation loop (src/main.c:305-317).
+//
+// One step is a fixed sequence of stream-ordered launches, captured once as a
+// CUDA graph and replayed per position; token ids, positions and the step
+// counters live in device memory, so prefill and greedy decoding run without
+// a host round trip between positions.  Per layer:
+//   rmsnorm       x += delta (the previous residual branch), xb = rmsnorm(x)
+//                 (src/kernels.c:179-189: sequential sum of squares)
+//   Q/K/V         one GEMV program over xb (csrc/engine.cu for one token,
+//                 csrc/tc.cu tensor cores for 2-64)
+//   rope + store  adjacent-pair rotation from a cos/sin table, K/V rows into
+//                 the cache (src/runtime.c:19-41, 74-92, 129-132)
+//   scores        q.k per (head, position), * 1/sqrt(head_dim) (:139-157)
+//   softmax + V   per KV head: max, expf, sequential sum, normalise, value
+//                 rows accumulated position by position (:159-194)
+//   O             GEMV program -> delta; rmsnorm (x += delta)
+//   FFN           dense: W1/W3 program, silu(h1)*h3, W2 program -> delta
+//                 (:270-284); MoE: route/experts/combine stages
+//                 (csrc/moe.cu, :202-269), plus the optional shared expert
+// then the final rmsnorm, the head GEMV (:286-287) and the greedy pick
+// (src/sampling.c:125-131).  Every floating-point operation is the
+// reference's, in its order and rounding (explicit __f*_rn intrinsics; expf
+// from libm_ref.cuh), so the logits are bit-identical to its scalar build.
+//
+// The RoPE cos/sin values depend only on (position, index): they are
+// computed once per decoder on the host with the C library's powf/cosf/sinf,
+// the functions the reference calls per token, and read from a table.
+#include "quantr_cuda.h"
+
+#include "device_common.cuh"
+#include "formats.cuh"
+#include "kernels.cuh"
+#include "launch_util.cuh"
+#include "libm_ref.cuh"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+namespace qr {
+namespace dec {
+
+constexpr int kMaxBatch = 1024;
+constexpr size_t kSmemMax = 227 * 1024;
+
+enum : int { MODE_EXPLICIT = 0, MODE_PREFILL = 1, MODE_DECODE = 2 };
+
+// Device control block: what the feed kernel at the start of each step does.
+struct Ctl {
+    int mode;
+    int n_prompt;
+    int step;   // next prefill position
+    int dstep;  // decode steps taken
+    int ring;   // capacity (steps) of the output ring
+};
+
+struct Dims {
+    int B, dim, q_dim, kv_dim, hd, n_heads, n_kv, kv_mul, seq_len, hidden, vocab, kv_type;
+    float inv_sqrt;
+};
+
+// ------------------------------------------------------------- kernels --
+
+// Token and position of every sequence for this step (src/main.c:305-317).
+__global__ void k_feed(Ctl* ctl, int* tok, int* pos, const int* prompt, const int* next, int B, int seq_len)
+{
+    pdl_wait();
+    const int b = threadIdx.x;
+    const int mode = ctl->mode, n = ctl->n_prompt;
+    const int s = ctl->step, i = ctl->dstep;
+    if (b < B) {
+        if (mode == MODE_PREFILL) {
+            tok[b] = prompt[(long long)b * n + s];
+            pos[b] = s % seq_len;
+        } else if (mode == MODE_DECODE) {
+            tok[b] = i == 0 ? prompt[(long long)b * n + n - 1] : next[b];
+            pos[b] = (n + i) % seq_len;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (mode == MODE_PREFILL) ctl->step = s + 1;
+        if (mode == MODE_DECODE) ctl->dstep = i + 1;
+    }
+    pdl_trigger();
+}
+
+// x[b] = row tok[b] of the embedding table (src/runtime.c:108-113).  A token
+// outside [0, vocab) reads row 0 (the reference would read out of bounds).
+__global__ void k_embed(float* __restrict__ x, const int* __restrict__ tok, const uint8_t* __restrict__ table,
+                        uint32_t type, long long row_bytes, int dim, int vocab)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.y;
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (e >= dim) return;
+    int t = tok[b];
+    if (t < 0 || t >= vocab) t = 0;
+    if (row_bytes == 0) {
+        x[(long long)b * dim + e] = reinterpret_cast<const float*>(table)[(long long)t * dim + e];
+    } else if (e < dequant_extent(type, dim)) {
+        x[(long long)b * dim + e] = dequant_elem(table + (long long)t * row_bytes, type, e);
+    }
+}
+
+// x += delta (if given), out = rmsnorm(x) * w, per sequence (one CTA each).
+// src/kernels.c:179-189: ss accumulated left to right, ss/size + 1e-5,
+// 1/sqrtf, o = w * (x * scale).
+__global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const float* __restrict__ delta,
+                                                 const float* __restrict__ w, float* __restrict__ out, int dim)
+{
+    extern __shared__ float4 sq4[];
+    float* sq = reinterpret_cast<float*>(sq4);
+    __shared__ float s_scale;
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x;
+    float* xr = x + (long long)b * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
+        float v = xr[i];
+        if (delta) {
+            v = __fadd_rn(v, delta[(long long)b * dim + i]);
+            xr[i] = v;
+        }
+        sq[i] = __fmul_rn(v, v);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float ss = 0.0f;
+        int i = 0;
+        for (; i + 4 <= dim; i += 4) {
+            const float4 v = sq4[i >> 2];
+            ss = __fadd_rn(ss, v.x);
+            ss = __fadd_rn(ss, v.y);
+            ss = __fadd_rn(ss, v.z);
+            ss = __fadd_rn(ss, v.w);
+        }
+        for (; i < dim; ++i) ss = __fadd_rn(ss, sq[i]);
+        ss = __fadd_rn(__fdiv_rn(ss, (float)dim), 1e-5f);
+        s_scale = __fdiv_rn(1.0f, __fsqrt_rn(ss));
+    }
+    __syncthreads();
+    const float sc = s_scale;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x)
+        out[(long long)b * dim + i] = __fmul_rn(w[i], __fmul_rn(xr[i], sc));
+}
+
+__device__ __forceinline__ void kv_put(void* cache, int kv_type, long long idx, float v)
+{
+    if (kv_type == 1)
+        reinterpret_cast<uint16_t*>(cache)[idx] = (uint16_t)f2h_ref(v);
+    else
+        reinterpret_cast<float*>(cache)[idx] = v;
+}
+__device__ __forceinline__ float kv_get(const void* cache, int kv_type, long long idx)
+{
+    return kv_type == 1 ? h2f_ref(reinterpret_cast<const uint16_t*>(cache)[idx])
+                        : reinterpret_cast<const float*>(cache)[idx];
+}
+
+// RoPE on q (all q_dim elements) and k (the first kv_dim), then k and v into
+// the cache at the sequence's position (src/runtime.c:19-41, 129-132).
+__global__ void k_rope_store(float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                             const int* __restrict__ pos, const float2* __restrict__ rope, void* kcache,
+                             void* vcache, long long layer_off, Dims D)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;  // pair index
+    if (2 * j >= D.q_dim) return;
+    const int i = 2 * j;
+    const int p = pos[b];
+    const float2 cs = rope[(long long)p * (D.q_dim / 2) + j];
+    float* qr = q + (long long)b * D.q_dim;
+    const float q0 = qr[i], q1 = qr[i + 1];
+    qr[i] = __fsub_rn(__fmul_rn(q0, cs.x), __fmul_rn(q1, cs.y));
+    qr[i + 1] = __fadd_rn(__fmul_rn(q0, cs.y), __fmul_rn(q1, cs.x));
+    if (i < D.kv_dim) {
+        const float k0 = kc[(long long)b * D.kv_dim + i], k1 = kc[(long long)b * D.kv_dim + i + 1];
+        const long long row = layer_off + ((long long)b * D.seq_len + p) * D.kv_dim;
+        kv_put(kcache, D.kv_type, row + i, __fsub_rn(__fmul_rn(k0, cs.x), __fmul_rn(k1, cs.y)));
+        kv_put(kcache, D.kv_type, row + i + 1, __fadd_rn(__fmul_rn(k0, cs.y), __fmul_rn(k1, cs.x)));
+        kv_put(vcache, D.kv_type, row + i, vc[(long long)b * D.kv_dim + i]);
+        kv_put(vcache, D.kv_type, row + i + 1, vc[(long long)b * D.kv_dim + i + 1]);
+    }
+}
+
+constexpr int kScoreTile = 32;  // positions per CTA
+
+// att[b][h][t] = dot_ref(q_h, k_t) * (1/sqrt(head_dim)) for the kv_mul query
+// heads of one KV head and 32 positions (src/runtime.c:139-157).  Threads:
+// x = position in the tile, y = query head of the group.
+__global__ void k_att_scores(const float* __restrict__ q, const void* __restrict__ kcache, long long layer_off,
+                             const int* __restrict__ pos, float* __restrict__ att, Dims D)
+{
+    extern __shared__ float sm[];
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x / D.n_kv, kh = blockIdx.x % D.n_kv;
+    const int t0 = blockIdx.y * kScoreTile;
+    const int p = pos[b];
+    if (t0 > p) return;
+    const int hd = D.hd, ld = hd + 1;  // padded rows: lanes read one column of different rows
+    float* Ks = sm;
+    float* Qs = sm + kScoreTile * ld;
+    const int nthr = blockDim.x * blockDim.y, tid = threadIdx.y * blockDim.x + threadIdx.x;
+    const int nt = min(kScoreTile, p - t0 + 1);
+    for (int e = tid; e < nt * hd; e += nthr) {
+        const int tt = e / hd, i = e % hd;
+        Ks[tt * ld + i] = kv_get(kcache, D.kv_type,
+                                 layer_off + ((long long)b * D.seq_len + t0 + tt) * D.kv_dim + (long long)kh * hd + i);
+    }
+    for (int e = tid; e < D.kv_mul * hd; e += nthr)
+        Qs[e] = q[(long long)b * D.q_dim + (long long)kh * D.kv_mul * hd + e];
+    __syncthreads();
+    const int tt = threadIdx.x, m = threadIdx.y;
+    if (tt < nt && m < D.kv_mul) {
+        const float* kr = Ks + tt * ld;
+        const float* qh = Qs + m * hd;
+        float s = 0.0f;
+        for (int i = 0; i < hd; ++i) s = __fadd_rn(s, __fmul_rn(qh[i], kr[i]));
+        const int h = kh * D.kv_mul + m;
+        att[((long long)b * D.n_heads + h) * D.seq_len + t0 + tt] = __fmul_rn(s, D.inv_sqrt);
+    }
+}
+
+constexpr int kVTile = 32;    // value rows per pipeline stage
+constexpr int kVStages = 3;   // stages in flight
+
+// Per (sequence, KV head): softmax_ref of each query head's scores
+// (src/kernels.c:191-207) and out_h[i] = sum over positions, in order, of
+// att_h[t] * v_t[i] from 0 (src/runtime.c:171-194).  The kv_mul heads share
+// the value rows, which stream through a ring of shared-memory stages by
+// bulk copies (one per row, mbarrier completion; the first stages are in
+// flight while the softmax runs), so each running sum reads shared memory
+// and the rows are read from memory once per KV head.
+template <int KVT>
+__global__ void k_att_softmax_v(const float* __restrict__ att, const void* __restrict__ vcache, long long layer_off,
+                                const int* __restrict__ pos, float* __restrict__ xa, int* err, Dims D)
+{
+    extern __shared__ __align__(16) unsigned char smraw[];
+    __shared__ __align__(8) uint64_t bars[kVStages];
+    __shared__ int s_abort;
+    constexpr int ES = KVT ? 2 : 4;
+    const int hd = D.hd;
+    const int row_bytes = hd * ES;
+    const int stage_bytes = kVTile * row_bytes;
+    unsigned char* vring = smraw;                                        // [kVStages][kVTile][hd]
+    float* S = reinterpret_cast<float*>(smraw + kVStages * stage_bytes);  // [kv_mul][seq_len]
+    const int b = blockIdx.x / D.n_kv, kh = blockIdx.x % D.n_kv;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    if (tid == 0) {
+        for (int i = 0; i < kVStages; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int p = pos[b], np = p + 1;
+    const int ntiles = (np + kVTile - 1) / kVTile;
+    const unsigned char* vrow0 = static_cast<const unsigned char*>(vcache) +
+                                 (layer_off + (long long)b * D.seq_len * D.kv_dim + (long long)kh * hd) * ES;
+    const long long vstride = (long long)D.kv_dim * ES;
+    auto issue = [&](int j) {  // one thread: tile j's rows into stage j % kVStages
+        const int st = j % kVStages, t0 = j * kVTile, nt = min(kVTile, np - t0);
+        mbar_arrive_expect_tx(&bars[st], (uint32_t)(nt * row_bytes));
+        for (int r = 0; r < nt; ++r)
+            bulk_g2s(vring + st * stage_bytes + r * row_bytes, vrow0 + (long long)(t0 + r) * vstride,
+                     (uint32_t)row_bytes, &bars[st]);
+    };
+    if (tid == 0)
+        for (int j = 0; j < min(kVStages, ntiles); ++j) issue(j);
+
+    for (int e = tid; e < D.kv_mul * np; e += blockDim.x) {
+        const int m = e / np, t = e % np;
+        S[m * D.seq_len + t] = att[((long long)b * D.n_heads + kh * D.kv_mul + m) * D.seq_len + t];
+    }
+    __syncthreads();
+    for (int m = warp; m < D.kv_mul; m += nwarps) {
+        float* s = S + m * D.seq_len;
+        // max: x[0], then any strictly greater value (a NaN at 0 sticks).
+        float mx = s[0];
+        const bool nan0 = mx != mx;
+        for (int t = lane; t < np; t += 32) mx = fmaxf(mx, s[t]);
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (nan0) mx = s[0];
+        for (int t = lane; t < np; t += 32) s[t] = libm::expf_ref(__fsub_rn(s[t], mx));
+        __syncwarp();
+        float inv = 0.0f;
+        if (lane == 0) {
+            float sum = 0.0f;
+            for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, s[t]);
+            inv = __fdiv_rn(1.0f, sum);
+        }
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (int t = lane; t < np; t += 32) s[t] = __fmul_rn(s[t], inv);
+    }
+    __syncthreads();
+
+    // Running sums: thread (m, i) for e = tid; kv_mul * hd <= 2 * blockDim.
+    const int nout = D.kv_mul * hd;
+    const int e0 = tid, e1 = tid + blockDim.x;
+    const int m0 = e0 / hd, i0 = e0 % hd, m1 = e1 / hd, i1 = e1 % hd;
+    float acc0 = 0.0f, acc1 = 0.0f;
+    int issued = min(kVStages, ntiles);  // meaningful in thread 0
+    int j = 0;
+    for (; j < ntiles; ++j) {
+        const int st = j % kVStages;
+        // Every thread waits on the same stage; a wait that gives up (250 ms)
+        // raises the CTA's abort flag, which the barrier makes uniform.
+        if (!mbar_wait_bounded(&bars[st], (uint32_t)((j / kVStages) & 1), err, &s_abort)) s_abort = 1;
+        __syncthreads();
+        if (s_abort) break;
+        const int t0 = j * kVTile, nt = min(kVTile, np - t0);
+        const unsigned char* vt = vring + st * stage_bytes;
+        if (e0 < nout) {
+            const float* sp = S + m0 * D.seq_len + t0;
+            for (int r = 0; r < nt; ++r) {
+                const float v = KVT ? h2f_ref(reinterpret_cast<const uint16_t*>(vt + r * row_bytes)[i0])
+                                    : reinterpret_cast<const float*>(vt + r * row_bytes)[i0];
+                acc0 = __fadd_rn(acc0, __fmul_rn(sp[r], v));
+            }
+        }
+        if (e1 < nout) {
+            const float* sp = S + m1 * D.seq_len + t0;
+            for (int r = 0; r < nt; ++r) {
+                const float v = KVT ? h2f_ref(reinterpret_cast<const uint16_t*>(vt + r * row_bytes)[i1])
+                                    : reinterpret_cast<const float*>(vt + r * row_bytes)[i1];
+                acc1 = __fadd_rn(acc1, __fmul_rn(sp[r], v));
+            }
+        }
+        __syncthreads();  // stage st is free again
+        if (tid == 0 && j + kVStages < ntiles) {
+            issue(j + kVStages);
+            issued = j + kVStages + 1;
+        }
+    }
+    if (j < ntiles) {
+        // Gave up: drain this CTA's copies still in flight (bounded) before
+        // its shared memory is released; the output is not written.
+        if (tid == 0)
+            for (int jj = j; jj < issued; ++jj)
+                mbar_wait_bounded(&bars[jj % kVStages], (uint32_t)((jj / kVStages) & 1), err, nullptr);
+        return;
+    }
+    if (e0 < nout) xa[(long long)b * D.q_dim + (long long)(kh * D.kv_mul + m0) * hd + i0] = acc0;
+    if (e1 < nout) xa[(long long)b * D.q_dim + (long long)(kh * D.kv_mul + m1) * hd + i1] = acc1;
+}
+
+// h1 = silu(h1) * h3 (src/runtime.c:15-17, 277-279).
+__global__ void k_silu_mul(float* __restrict__ h1, const float* __restrict__ h3, long long n)
+{
+    pdl_wait();
+    pdl_trigger();
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float v = h1[i];
+        h1[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, libm::expf_ref(-v))), h3[i]);
+    }
+}
+
+// delta += sh * sigmoid(g) per sequence (the shared expert's gated add).
+__global__ void k_shexp_add(float* __restrict__ delta, const float* __restrict__ sh, const float* __restrict__ g,
+                            int dim)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= dim) return;
+    const float gv = __fdiv_rn(1.0f, __fadd_rn(1.0f, libm::expf_ref(-g[b])));
+    delta[(long long)b * dim + i] = __fadd_rn(delta[(long long)b * dim + i], __fmul_rn(sh[(long long)b * dim + i], gv));
+}
+
+// Greedy pick (src/sampling.c:125-131): best = 0, then every later index whose
+// logit is strictly greater.  So: the first maximum among non-NaN logits,
+// and 0 when logits[0] is NaN.  Records the token in the decode ring.
+__global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logits, long long ldl, int vocab,
+                                                 int* __restrict__ next, const Ctl* __restrict__ ctl,
+                                                 int* __restrict__ ring, int B)
+{
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x;
+    const float* l = logits + (long long)b * ldl;
+    float bv = 0.0f;
+    int bi = -1;
+    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
+        const float v = l[i];
+        if (v == v && (bi < 0 || v > bv)) {
+            bv = v;
+            bi = i;
+        }
+    }
+    auto better = [](float v2, int i2, float v1, int i1) {
+        if (i2 < 0) return false;
+        if (i1 < 0) return true;
+        if (v2 > v1) return true;
+        if (v1 > v2) return false;
+        return i2 < i1;
+    };
+    for (int o = 16; o; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(v2, i2, bv, bi)) {
+            bv = v2;
+            bi = i2;
+        }
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : 0.0f;
+        bi = lane < nw ? si[lane] : -1;
+        for (int o = 16; o; o >>= 1) {
+            const float v2 = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(v2, i2, bv, bi)) {
+                bv = v2;
+                bi = i2;
+            }
+        }
+        if (lane == 0) {
+            const float l0 = l[0];
+            const int pick = (l0 != l0 || bi < 0) ? 0 : bi;
+            next[b] = pick;
+            if (ctl->mode == MODE_DECODE && ctl->dstep >= 1)
+                ring[(long long)((ctl->dstep - 1) % ctl->ring) * B + b] = pick;
+        }
+    }
+}
+
+// Test hook: out[i] = expf_ref of the float with bit pattern first + i.
+__global__ void k_debug_expf(float* __restrict__ out, uint32_t first, long long n)
+{
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        out[i] = libm::expf_ref(__uint_as_float(first + (uint32_t)i));
+}
+
+__global__ void k_ctl_set(Ctl* ctl, int mode, int n_prompt, int ring)
+{
+    ctl->mode = mode;
+    ctl->n_prompt = n_prompt;
+    ctl->step = 0;
+    ctl->dstep = 0;
+    ctl->ring = ring;
+}
+
+} // namespace dec
+} // namespace qr
+
+using namespace qr;
+using namespace qr::dec;
+
+struct quantr_decoder {
+    int device = 0;
+    Dims D{};
+    int n_layers = 0, E = 0, K = 0, shexp = 0;
+    float rope_base = 10000.0f;
+    // resolved device pointers
+    const uint8_t* embd = nullptr;
+    uint32_t embd_type = 0;
+    long long embd_rb = 0;
+    std::vector<const float*> rms_att, rms_ffn, router, sh_gate;
+    const float* rms_final = nullptr;
+    std::vector<ExpertMats> ew1, ew2, ew3;  // per layer
+    // owned device memory
+    std::vector<void*> owned;
+    uint8_t* arena = nullptr;
+    float *x = nullptr, *xb = nullptr, *xa = nullptr, *q = nullptr, *kc = nullptr, *vc = nullptr, *att = nullptr;
+    float *hb = nullptr, *hb2 = nullptr, *delta = nullptr, *logits = nullptr, *sh = nullptr, *gdot = nullptr;
+    float *moe_o = nullptr, *wts = nullptr;
+    int* sel = nullptr;
+    void *kcache = nullptr, *vcache = nullptr;
+    float2* rope = nullptr;
+    int *tok = nullptr, *pos = nullptr, *next = nullptr, *prompt = nullptr, *ring = nullptr;
+    int prompt_cap = 0, ring_cap = 0;
+    Ctl* ctl = nullptr;
+    void* moe_ws = nullptr;
+    size_t moe_ws_bytes = 0;
+    // plans
+    std::vector<quantr_program*> p_qkv, p_o, p_ffn13, p_w2, p_sh13, p_sh2;
+    quantr_program* p_head = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
+    int nodes_decode = 0, nodes_prefill = 0;
+    float* host_logits = nullptr;  // pinned, forward_runtime's return
+    size_t weight_bytes = 0, kv_pos_bytes = 0, device_bytes = 0;
+    double load_ms = 0.0;
+};
+
+namespace {
+
+int code_of(cudaError_t e)
+{
+    if (e == cudaSuccess) return QUANTR_OK;
+    cudaGetLastError();
+    return e == cudaErrorMemoryAllocation ? QUANTR_ERR_OOM : QUANTR_ERR_CUDA;
+}
+
+template <typename T>
+cudaError_t dev_alloc(quantr_decoder* d, T** p, size_t count)
+{
+    void* v = nullptr;
+    const size_t bytes = std::max<size_t>(count * sizeof(T), 16);
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess) return e;
+    d->owned.push_back(v);
+    d->device_bytes += bytes;
+    *p = static_cast<T*>(v);
+    return cudaMemset(v, 0, bytes);
+}
+
+// Device address of a model tensor: a registered host range's copy, a device
+// pointer as is, or (other host memory) a copy in the decoder's arena.
+struct Resolver {
+    struct Up {
+        const void* host;
+        size_t bytes;
+        size_t off;
+    };
+    std::vector<Up> ups;
+    size_t arena_bytes = 0;
+    const uint8_t* arena = nullptr;
+    bool planning = true;
+
+    const uint8_t* get(const void* p, size_t bytes)
+    {
+        if (!p) return nullptr;
+        if (void* r = quantr_gpu_device_ptr(p)) return static_cast<const uint8_t*>(r);
+        cudaPointerAttributes a{};
+        if (cudaPointerGetAttributes(&a, p) == cudaSuccess &&
+            (a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged))
+            return static_cast<const uint8_t*>(p);
+        cudaGetLastError();
+        for (const Up& u : ups)
+            if (u.host == p) return planning ? nullptr : arena + u.off;
+        if (!planning) return nullptr;
+        ups.push_back(Up{p, bytes, arena_bytes});
+        arena_bytes += (bytes + 255) / 256 * 256 + 256;  // +16 readable bytes past each tensor, 256-aligned
+        return nullptr;
+    }
+};
+
+size_t tensor_bytes(uint32_t type, long long rows, int cols)
+{
+    return (size_t)(rows * row_bytes(type, cols));
+}
+
+struct ProgJob {
+    const void* w;
+    uint32_t type;
+    int n, d;
+    const float* x;
+    long long ldx;
+    float* out;
+    long long ldo;
+};
+
+// Threads of the softmax/value kernel: each owns one or two running sums.
+int att_v_threads(const Dims& D)
+{
+    const int nout = D.kv_mul * D.hd;
+    return std::min(1024, std::max(128, ((nout + 1) / 2 + 31) / 32 * 32));
+}
+size_t att_v_smem(const Dims& D)
+{
+    return (size_t)kVStages * kVTile * D.hd * (D.kv_type ? 2 : 4) + (size_t)D.kv_mul * D.seq_len * 4;
+}
+
+int make_program(quantr_decoder* d, const std::vector<ProgJob>& js, quantr_program** out)
+{
+    std::vector<quantr_gemv_job> jobs;
+    for (const ProgJob& j : js)
+        jobs.push_back(quantr_gemv_job{j.w, j.type, j.n, j.d, d->D.B, j.x, j.ldx, j.out, j.ldo});
+    return quantr_program_create(out, jobs.data(), (int)jobs.size());
+}
+
+// Enqueues one step on `s`.  with_head: final norm, head GEMV and greedy pick.
+int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
+{
+    const Dims& D = d->D;
+    LaunchCfg c;
+    c.stream = s;
+    cudaError_t e = launch_ex(&k_feed, dim3(1), dim3(std::max(32, (D.B + 31) / 32 * 32)), 0, c, d->ctl, d->tok,
+                              d->pos, (const int*)d->prompt, (const int*)d->next, D.B, D.seq_len);
+    if (e == cudaSuccess)
+        e = launch_ex(&k_embed, dim3((D.dim + 255) / 256, D.B), dim3(256), 0, c, d->x, (const int*)d->tok, d->embd,
+                      d->embd_type, d->embd_rb, D.dim, D.vocab);
+    const size_t norm_smem = (size_t)(D.dim + 4) * sizeof(float);
+    const long long layer_kv = (long long)D.B * D.seq_len * D.kv_dim;
+    for (int l = 0; l < d->n_layers && e == cudaSuccess; ++l) {
+        const long long loff = (long long)l * layer_kv;
+        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)(l ? d->delta : nullptr),
+                      d->rms_att[l], d->xb, D.dim);
+        if (e != cudaSuccess) break;
+        if (quantr_program_run(d->p_qkv[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+        e = launch_ex(&k_rope_store, dim3((D.q_dim / 2 + 127) / 128, D.B), dim3(128), 0, c, d->q,
+                      (const float*)d->kc, (const float*)d->vc, (const int*)d->pos, (const float2*)d->rope,
+                      d->kcache, d->vcache, loff, D);
+        if (e != cudaSuccess) break;
+        const size_t ssm = (size_t)(kScoreTile * (D.hd + 1) + D.kv_mul * D.hd) * sizeof(float);
+        e = launch_ex(&k_att_scores, dim3(D.B * D.n_kv, (D.seq_len + kScoreTile - 1) / kScoreTile),
+                      dim3(kScoreTile, D.kv_mul), ssm, c, (const float*)d->q, (const void*)d->kcache, loff,
+                      (const int*)d->pos, d->att, D);
+        if (e != cudaSuccess) break;
+        e = launch_ex(D.kv_type ? &k_att_softmax_v<1> : &k_att_softmax_v<0>, dim3(D.B * D.n_kv),
+                      dim3(att_v_threads(D)), att_v_smem(D), c, (const float*)d->att, (const void*)d->vcache, loff,
+                      (const int*)d->pos, d->xa, device_error_word(), D);
+        if (e != cudaSuccess) break;
+        if (quantr_program_run(d->p_o[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)d->delta, d->rms_ffn[l],
+                      d->xb, D.dim);
+        if (e != cudaSuccess) break;
+        if (d->E == 0) {
+            if (quantr_program_run(d->p_ffn13[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+            const long long n = (long long)D.B * D.hidden;
+            e = launch_ex(&k_silu_mul, dim3((unsigned)std::min<long long>((n + 255) / 256, 4096)), dim3(256), 0, c,
+                          d->hb, (const float*)d->hb2, n);
+            if (e != cudaSuccess) break;
+            if (quantr_program_run(d->p_w2[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+        } else {
+            int* err = device_error_word();
+            MoeRoute r;
+            r.sel = d->sel;
+            r.wts = d->wts;
+            r.xb = d->xb;
+            r.ldx = D.dim;
+            r.T = D.B;
+            r.router = d->router[l];
+            r.E = d->E;
+            r.k = d->K;
+            r.dim = D.dim;
+            r.ws = d->moe_ws;
+            r.ws_bytes = d->moe_ws_bytes;
+            r.err = err;
+            e = launch_moe_route(r, c);
+            if (e != cudaSuccess) break;
+            MoeExperts a;
+            a.o = d->moe_o;
+            a.xb = d->xb;
+            a.ldx = D.dim;
+            a.T = D.B;
+            a.sel = d->sel;
+            a.k = d->K;
+            a.e0 = 0;
+            a.El = d->E;
+            a.dim = D.dim;
+            a.hidden = D.hidden;
+            a.w1 = d->ew1[l];
+            a.w3 = d->ew3[l];
+            a.w2 = d->ew2[l];
+            a.ws = d->moe_ws;
+            a.ws_bytes = d->moe_ws_bytes;
+            a.err = err;
+            e = launch_moe_experts(a, c);
+            if (e != cudaSuccess) break;
+            e = launch_moe_combine(d->delta, D.dim, d->moe_o, d->sel, d->wts, D.B, d->K, D.dim, c);
+            if (e != cudaSuccess) break;
+            if (d->shexp) {
+                if (quantr_program_run(d->p_sh13[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+                const long long n = (long long)D.B * d->shexp;
+                e = launch_ex(&k_silu_mul, dim3((unsigned)std::min<long long>((n + 255) / 256, 4096)), dim3(256), 0,
+                              c, d->hb, (const float*)d->hb2, n);
+                if (e != cudaSuccess) break;
+                if (quantr_program_run(d->p_sh2[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+                e = launch_gemv_f32(d->sh_gate[l], d->xb, D.dim, d->gdot, 1, 1, D.dim, D.B, c);
+                if (e != cudaSuccess) break;
+                e = launch_ex(&k_shexp_add, dim3((D.dim + 255) / 256, D.B), dim3(256), 0, c, d->delta,
+                              (const float*)d->sh, (const float*)d->gdot, D.dim);
+                if (e != cudaSuccess) break;
+            }
+        }
+    }
+    if (e == cudaSuccess && with_head) {
+        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)d->delta, d->rms_final,
+                      d->xb, D.dim);
+        if (e == cudaSuccess && quantr_program_run(d->p_head, s) != QUANTR_OK) return QUANTR_ERR_CUDA;
+        if (e == cudaSuccess)
+            e = launch_ex(&k_argmax, dim3(D.B), dim3(1024), 0, c, (const float*)d->logits, (long long)D.vocab,
+                          D.vocab, d->next, (const Ctl*)d->ctl, d->ring, D.B);
+    }
+    // A prefill step stops after the last layer: the reference's x there only
+    // feeds the head, and the next position's embedding overwrites it.
+    return code_of(e);
+}
+
+int capture(quantr_decoder* d, bool with_head, cudaGraphExec_t* out, int* nodes)
+{
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamBeginCapture(d->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return code_of(e);
+    const int rc = enqueue_step(d, d->stream, with_head);
+    e = cudaStreamEndCapture(d->stream, &g);
+    if (rc != QUANTR_OK || e != cudaSuccess) {
+        if (g) cudaGraphDestroy(g);
+        cudaGetLastError();
+        return rc != QUANTR_OK ? rc : code_of(e);
+    }
+    size_t n = 0;
+    cudaGraphGetNodes(g, nullptr, &n);
+    *nodes = (int)n;
+    e = cudaGraphInstantiate(out, g, 0);
+    cudaGraphDestroy(g);
+    return code_of(e);
+}
+
+void destroy(quantr_decoder* d)
+{
+    if (!d) return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(d->device);
+    if (d->stream) cudaStreamSynchronize(d->stream);
+    if (d->g_decode) cudaGraphExecDestroy(d->g_decode);
+    if (d->g_prefill) cudaGraphExecDestroy(d->g_prefill);
+    for (auto* v : {&d->p_qkv, &d->p_o, &d->p_ffn13, &d->p_w2, &d->p_sh13, &d->p_sh2})
+        for (quantr_program* p : *v) quantr_program_destroy(p);
+    quantr_program_destroy(d->p_head);
+    for (void* p : d->owned) cudaFree(p);
+    if (d->host_logits) cudaFreeHost(d->host_logits);
+    if (d->stream) cudaStreamDestroy(d->stream);
+    if (prev >= 0) cudaSetDevice(prev);
+    delete d;
+}
+
+// RoPE table: (cos, sin) of theta = pos * powf(base, -(i/head_dim)) for every
+// position and even index i < q_dim, with the C library's functions
+// (src/runtime.c:24-29).
+void rope_table(std::vector<float2>& t, int seq_len, int q_dim, int head_dim, float base_in)
+{
+    const float base = base_in > 0.0f ? base_in : 10000.0f;
+    const int half = q_dim / 2;
+    std::vector<float> freq(half);
+    for (int j = 0; j < half; ++j) freq[j] = ::powf(base, -((float)(2 * j) / (float)head_dim));
+    t.resize((size_t)seq_len * half);
+    for (int p = 0; p < seq_len; ++p)
+        for (int j = 0; j < half; ++j) {
+            volatile float theta = (float)p * freq[j];
+            const float th = theta;
+            t[(size_t)p * half + j] = make_float2(::cosf(th), ::sinf(th));
+        }
+}
+
+} // namespace
+
+extern "C" {
+
+int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch)
+{
+    if (!out || !m) return QUANTR_ERR_BAD_ARG;
+    *out = nullptr;
+    if (batch < 1 || batch > kMaxBatch || m->dim <= 0 || m->n_layers <= 0 || m->n_heads <= 0 ||
+        m->n_kv_heads <= 0 || m->vocab_size <= 0 || m->seq_len <= 0 || m->hidden_dim < 0)
+        return QUANTR_ERR_BAD_ARG;
+    const int hd = m->head_dim > 0 ? m->head_dim : m->dim / m->n_heads;
+    if (hd <= 0 || (hd & 1) || m->n_heads % m->n_kv_heads) return QUANTR_ERR_BAD_ARG;
+    if (m->expert_count < 0 || m->expert_count > kMoeMaxExperts || m->expert_used_count > kMoeMaxK ||
+        (m->expert_count > 0 && (m->expert_used_count < 1 || m->expert_used_count > m->expert_count)))
+        return QUANTR_ERR_BAD_ARG;
+    const auto t0 = std::chrono::steady_clock::now();
+    quantr_decoder* d = new (std::nothrow) quantr_decoder();
+    if (!d) return QUANTR_ERR_OOM;
+    cudaGetDevice(&d->device);
+    Dims& D = d->D;
+    D.B = batch;
+    D.dim = m->dim;
+    D.hd = hd;
+    D.n_heads = m->n_heads;
+    D.n_kv = m->n_kv_heads;
+    D.kv_mul = m->n_heads / m->n_kv_heads;
+    D.q_dim = m->n_heads * hd;
+    D.kv_dim = m->n_kv_heads * hd;
+    D.seq_len = m->seq_len;
+    D.hidden = m->hidden_dim;
+    D.vocab = m->vocab_size;
+    D.kv_type = m->kv_type == 1 ? 1 : 0;
+    D.inv_sqrt = 1.0f / std::sqrt((float)hd);
+    d->n_layers = m->n_layers;
+    d->E = m->expert_count;
+    d->K = m->expert_used_count;
+    d->shexp = m->expert_count > 0 && m->shexp_w1 ? m->shexp_hidden_dim : 0;
+    if (D.kv_mul > 32 || att_v_smem(D) > kSmemMax || D.kv_mul * hd > 2048 || (hd * (D.kv_type ? 2 : 4)) % 16 ||
+        (size_t)(kScoreTile * (hd + 1) + D.kv_mul * hd) * 4 > kSmemMax || (size_t)(D.dim + 4) * 4 > 48 * 1024) {
+        delete d;
+        return QUANTR_ERR_TOO_LARGE;
+    }
+    auto fail = [&](int rc) {
+        destroy(d);
+        return rc;
+    };
+    if (cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking) != cudaSuccess) return fail(QUANTR_ERR_CUDA);
+
+    // ---- weights: resolve (registered / device / upload), two passes ----
+    const int L = m->n_layers;
+    const int hid = m->hidden_dim;
+    Resolver R;
+    auto lin = [&](const void* const* arr, const uint32_t* ty, int l, int rows, int cols) -> const uint8_t* {
+        if (!arr || !ty || !arr[l]) return nullptr;
+        return R.get(arr[l], tensor_bytes(ty[l], rows, cols));
+    };
+    std::vector<const uint8_t*> wq(L), wk(L), wv(L), wo(L), w1(L), w2(L), w3(L), s1(L), s2(L), s3(L);
+    std::vector<std::vector<const uint8_t*>> e1(L), e2(L), e3(L);
+    const uint8_t* wcls = nullptr;
+    for (int pass = 0; pass < 2; ++pass) {
+        if (pass == 1) {
+            if (R.arena_bytes) {
+                uint8_t* a = nullptr;
+                if (dev_alloc(d, &a, R.arena_bytes) != cudaSuccess) return fail(QUANTR_ERR_OOM);
+                R.arena = a;
+                for (const auto& u : R.ups)
+                    if (cudaMemcpy(a + u.off, u.host, u.bytes, cudaMemcpyHostToDevice) != cudaSuccess)
+                        return fail(QUANTR_ERR_CUDA);
+            }
+            R.planning = false;
+        }
+        const size_t erb = m->token_embd_row_bytes;
+        d->embd = R.get(m->token_embd, erb ? erb * m->vocab_size : (size_t)m->vocab_size * m->dim * 4);
+        d->embd_type = m->token_embd_type;
+        d->embd_rb = (long long)erb;
+        d->rms_att.assign(L, nullptr);
+        d->rms_ffn.assign(L, nullptr);
+        d->router.assign(L, nullptr);
+        d->sh_gate.assign(L, nullptr);
+        for (int l = 0; l < L; ++l) {
+            d->rms_att[l] = (const float*)R.get(m->rms_att ? m->rms_att[l] : nullptr, (size_t)m->dim * 4);
+            d->rms_ffn[l] = (const float*)R.get(m->rms_ffn ? m->rms_ffn[l] : nullptr, (size_t)m->dim * 4);
+            wq[l] = lin(m->wq, m->wq_type, l, D.q_dim, m->dim);
+            wk[l] = lin(m->wk, m->wk_type, l, D.kv_dim, m->dim);
+            wv[l] = lin(m->wv, m->wv_type, l, D.kv_dim, m->dim);
+            wo[l] = lin(m->wo, m->wo_type, l, m->dim, D.q_dim);
+            if (d->E == 0) {
+                w1[l] = lin(m->w1, m->w1_type, l, hid, m->dim);
+                w3[l] = lin(m->w3, m->w3_type, l, hid, m->dim);
+                w2[l] = lin(m->w2, m->w2_type, l, m->dim, hid);
+            } else {
+                d->router[l] = (const float*)R.get(m->ffn_gate_inp ? m->ffn_gate_inp[l] : nullptr,
+                                                   (size_t)d->E * m->dim * 4);
+                e1[l].assign(d->E, nullptr);
+                e2[l].assign(d->E, nullptr);
+                e3[l].assign(d->E, nullptr);
+                for (int x = 0; x < d->E; ++x) {
+                    e1[l][x] = R.get(m->expert_w1[l][x], tensor_bytes(m->exp_w1_type[l], hid, m->dim));
+                    e3[l][x] = R.get(m->expert_w3[l][x], tensor_bytes(m->exp_w3_type[l], hid, m->dim));
+                    e2[l][x] = R.get(m->expert_w2[l][x], tensor_bytes(m->exp_w2_type[l], m->dim, hid));
+                }
+                if (d->shexp) {
+                    s1[l] = lin(m->shexp_w1, m->shexp_w1_type, l, d->shexp, m->dim);
+                    s3[l] = lin(m->shexp_w3, m->shexp_w3_type, l, d->shexp, m->dim);
+                    s2[l] = lin(m->shexp_w2, m->shexp_w2_type, l, m->dim, d->shexp);
+                    d->sh_gate[l] = (const float*)R.get(m->shexp_gate ? m->shexp_gate[l] : nullptr, (size_t)m->dim * 4);
+                }
+            }
+        }
+        d->rms_final = (const float*)R.get(m->rms_final, (size_t)m->dim * 4);
+        wcls = R.get(m->wcls, tensor_bytes(m->wcls_type, m->vocab_size, m->dim));
+    }
+    // Everything the step reads must exist (the reference would crash on a
+    // NULL norm; a NULL linear there gives zeros, which this decoder rejects).
+    bool ok = d->embd && d->rms_final && wcls;
+    for (int l = 0; l < L && ok; ++l) {
+        ok = d->rms_att[l] && d->rms_ffn[l] && wq[l] && wk[l] && wv[l] && wo[l];
+        if (d->E == 0) ok = ok && w1[l] && w2[l] && w3[l];
+        else {
+            ok = ok && d->router[l];
+            for (int x = 0; x < d->E && ok; ++x) ok = e1[l][x] && e2[l][x] && e3[l][x];
+            if (d->shexp) ok = ok && s1[l] && s2[l] && s3[l] && d->sh_gate[l];
+        }
+    }
+    if (!ok) return fail(QUANTR_ERR_BAD_ARG);
+
+    // ---- activations, caches, tables ----
+    const int B = batch;
+    const int wide = std::max(D.q_dim, m->dim);
+    const int hmax = std::max(hid, d->shexp);
+    cudaError_t e = cudaSuccess;
+    auto A = [&](auto** p, size_t n) {
+        if (e == cudaSuccess) e = dev_alloc(d, p, n);
+    };
+    A(&d->x, (size_t)B * m->dim);
+    A(&d->xb, (size_t)B * wide);
+    A(&d->xa, (size_t)B * D.q_dim);
+    A(&d->q, (size_t)B * D.q_dim);
+    A(&d->kc, (size_t)B * D.kv_dim);
+    A(&d->vc, (size_t)B * D.kv_dim);
+    A(&d->att, (size_t)B * D.n_heads * D.seq_len);
+    A(&d->hb, (size_t)B * std::max(hmax, 1));
+    A(&d->hb2, (size_t)B * std::max(hmax, 1));
+    A(&d->delta, (size_t)B * m->dim);
+    A(&d->logits, (size_t)B * D.vocab);
+    A(&d->tok, (size_t)B);
+    A(&d->pos, (size_t)B);
+    A(&d->next, (size_t)B);
+    d->prompt_cap = D.seq_len;
+    A(&d->prompt, (size_t)B * d->prompt_cap);
+    d->ring_cap = std::max(D.seq_len, 4096);
+    A(&d->ring, (size_t)B * d->ring_cap);
+    A(&d->ctl, 1);
+    const size_t kv_elems = (size_t)L * B * D.seq_len * D.kv_dim;
+    uint8_t *kcb = nullptr, *vcb = nullptr;
+    A(&kcb, kv_elems * (D.kv_type ? 2 : 4));
+    A(&vcb, kv_elems * (D.kv_type ? 2 : 4));
+    d->kcache = kcb;
+    d->vcache = vcb;
+    if (d->E) {
+        A(&d->moe_o, (size_t)B * d->K * m->dim);
+        A(&d->sel, (size_t)B * d->K);
+        A(&d->wts, (size_t)B * d->K);
+        d->moe_ws_bytes = moe_workspace_bytes(B, d->E, d->K, m->dim, hid);
+        uint8_t* ws = nullptr;
+        A(&ws, d->moe_ws_bytes);
+        d->moe_ws = ws;
+        if (d->shexp) {
+            A(&d->sh, (size_t)B * m->dim);
+            A(&d->gdot, (size_t)B);
+        }
+    }
+    std::vector<float2> rt;
+    rope_table(rt, D.seq_len, D.q_dim, hd, m->rope_freq_base);
+    A(&d->rope, rt.size());
+    if (e == cudaSuccess) e = cudaMemcpy(d->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&d->host_logits, (size_t)D.vocab * 4);
+    if (e != cudaSuccess) return fail(code_of(e));
+    // Expert pointer tables (device arrays of device pointers).
+    if (d->E) {
+        d->ew1.resize(L);
+        d->ew2.resize(L);
+        d->ew3.resize(L);
+        for (int l = 0; l < L; ++l) {
+            const uint8_t** tb = nullptr;
+            A(&tb, (size_t)3 * d->E);
+            if (e != cudaSuccess) return fail(code_of(e));
+            std::vector<const uint8_t*> h(3 * (size_t)d->E);
+            for (int x = 0; x < d->E; ++x) {
+                h[x] = e1[l][x];
+                h[d->E + x] = e3[l][x];
+                h[2 * d->E + x] = e2[l][x];
+            }
+            e = cudaMemcpy(tb, h.data(), h.size() * sizeof(void*), cudaMemcpyHostToDevice);
+            if (e != cudaSuccess) return fail(code_of(e));
+            d->ew1[l] = ExpertMats{nullptr, 0, tb, m->exp_w1_type[l]};
+            d->ew3[l] = ExpertMats{nullptr, 0, tb + d->E, m->exp_w3_type[l]};
+            d->ew2[l] = ExpertMats{nullptr, 0, tb + 2 * d->E, m->exp_w2_type[l]};
+        }
+    }
+
+    // ---- GEMV programs ----
+    for (int l = 0; l < L; ++l) {
+        quantr_program* p = nullptr;
+        int rc = make_program(d, {{wq[l], m->wq_type[l], D.q_dim, m->dim, d->xb, m->dim, d->q, D.q_dim},
+                                  {wk[l], m->wk_type[l], D.kv_dim, m->dim, d->xb, m->dim, d->kc, D.kv_dim},
+                                  {wv[l], m->wv_type[l], D.kv_dim, m->dim, d->xb, m->dim, d->vc, D.kv_dim}},
+                              &p);
+        if (rc) return fail(rc);
+        d->p_qkv.push_back(p);
+        rc = make_program(d, {{wo[l], m->wo_type[l], m->dim, D.q_dim, d->xa, D.q_dim, d->delta, m->dim}}, &p);
+        if (rc) return fail(rc);
+        d->p_o.push_back(p);
+        if (d->E == 0) {
+            rc = make_program(d, {{w1[l], m->w1_type[l], hid, m->dim, d->xb, m->dim, d->hb, hid},
+                                  {w3[l], m->w3_type[l], hid, m->dim, d->xb, m->dim, d->hb2, hid}},
+                              &p);
+            if (rc) return fail(rc);
+            d->p_ffn13.push_back(p);
+            rc = make_program(d, {{w2[l], m->w2_type[l], m->dim, hid, d->hb, hid, d->delta, m->dim}}, &p);
+            if (rc) return fail(rc);
+            d->p_w2.push_back(p);
+        } else if (d->shexp) {
+            const int sh = d->shexp;
+            rc = make_program(d, {{s1[l], m->shexp_w1_type[l], sh, m->dim, d->xb, m->dim, d->hb, sh},
+                                  {s3[l], m->shexp_w3_type[l], sh, m->dim, d->xb, m->dim, d->hb2, sh}},
+                              &p);
+            if (rc) return fail(rc);
+            d->p_sh13.push_back(p);
+            rc = make_program(d, {{s2[l], m->shexp_w2_type[l], m->dim, sh, d->hb, sh, d->sh, m->dim}}, &p);
+            if (rc) return fail(rc);
+            d->p_sh2.push_back(p);
+        }
+    }
+    {
+        int rc = make_program(d, {{wcls, m->wcls_type, D.vocab, m->dim, d->xb, m->dim, d->logits, D.vocab}},
+                              &d->p_head);
+        if (rc) return fail(rc);
+    }
+    // Per-step bytes: every linear once, norms, one embedding row per sequence.
+    size_t wb = 0;
+    for (int l = 0; l < L; ++l) {
+        wb += tensor_bytes(m->wq_type[l], D.q_dim, m->dim) + tensor_bytes(m->wk_type[l], D.kv_dim, m->dim) +
+              tensor_bytes(m->wv_type[l], D.kv_dim, m->dim) + tensor_bytes(m->wo_type[l], m->dim, D.q_dim) +
+              (size_t)2 * m->dim * 4;
+        if (d->E == 0)
+            wb += tensor_bytes(m->w1_type[l], hid, m->dim) + tensor_bytes(m->w3_type[l], hid, m->dim) +
+                  tensor_bytes(m->w2_type[l], m->dim, hid);
+    }
+    wb += tensor_bytes(m->wcls_type, D.vocab, m->dim) + (size_t)m->dim * 4 +
+          (size_t)B * (m->token_embd_row_bytes ? m->token_embd_row_bytes : (size_t)m->dim * 4);
+    d->weight_bytes = wb;
+    d->kv_pos_bytes = (size_t)L * 2 * D.kv_dim * (D.kv_type ? 2 : 4);
+
+    // Dynamic shared memory of the attention kernels beyond the default 48 KB.
+    {
+        const int ssm = (kScoreTile * (hd + 1) + D.kv_mul * hd) * 4;
+        const int vsm = (int)att_v_smem(D);
+        if (cudaFuncSetAttribute(k_att_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) != cudaSuccess ||
+            cudaFuncSetAttribute(k_att_softmax_v<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_att_softmax_v<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) != cudaSuccess)
+            return fail(QUANTR_ERR_CUDA);
+    }
+
+    // ---- warm-up (MoE tensor-core plans are made on their first call), then
+    // clean caches and the two graphs ----
+    k_ctl_set<<<1, 1, 0, d->stream>>>(d->ctl, MODE_EXPLICIT, 0, d->ring_cap);
+    int rc = enqueue_step(d, d->stream, true);
+    if (rc) return fail(rc);
+    if (cudaStreamSynchronize(d->stream) != cudaSuccess) return fail(QUANTR_ERR_CUDA);
+    if (cudaMemsetAsync(d->kcache, 0, kv_elems * (D.kv_type ? 2 : 4), d->stream) != cudaSuccess ||
+        cudaMemsetAsync(d->vcache, 0, kv_elems * (D.kv_type ? 2 : 4), d->stream) != cudaSuccess)
+        return fail(QUANTR_ERR_CUDA);
+    rc = capture(d, true, &d->g_decode, &d->nodes_decode);
+    if (!rc) rc = capture(d, false, &d->g_prefill, &d->nodes_prefill);
+    if (rc) return fail(rc);
+    if (cudaStreamSynchronize(d->stream) != cudaSuccess) return fail(QUANTR_ERR_CUDA);
+    d->load_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+    *out = d;
+    return QUANTR_OK;
+}
+
+void quantr_decoder_destroy(quantr_decoder* d) { destroy(d); }
+
+int quantr_decoder_step_dev(quantr_decoder* d, const int* tokens, const int* pos, float* logits, long long ldl,
+                            int* next, void* stream)
+{
+    if (!d || !tokens || !pos || (logits && ldl < d->D.vocab)) return QUANTR_ERR_BAD_ARG;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t nb = (size_t)d->D.B * sizeof(int);
+    cudaError_t e = cudaMemcpyAsync(d->tok, tokens, nb, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->pos, pos, nb, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_EXPLICIT, 0, d->ring_cap);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaGraphLaunch(d->g_decode, s);
+    if (e == cudaSuccess && logits)
+        e = cudaMemcpy2DAsync(logits, (size_t)ldl * 4, d->logits, (size_t)d->D.vocab * 4, (size_t)d->D.vocab * 4,
+                              d->D.B, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess && next) e = cudaMemcpyAsync(next, d->next, nb, cudaMemcpyDeviceToDevice, s);
+    return code_of(e);
+}
+
+int quantr_decoder_generate(quantr_decoder* d, const int* prompt, int n_prompt, int steps, int* out)
+{
+    if (!d || !prompt || n_prompt < 1 || n_prompt > d->prompt_cap || steps < 0 || (steps && !out))
+        return QUANTR_ERR_BAD_ARG;
+    const int B = d->D.B;
+    for (long long i = 0; i < (long long)B * n_prompt; ++i)
+        if (prompt[i] < 0 || prompt[i] >= d->D.vocab) return QUANTR_ERR_BAD_ARG;
+    cudaStream_t s = d->stream;
+    cudaError_t e = cudaMemcpyAsync(d->prompt, prompt, (size_t)B * n_prompt * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n_prompt, d->ring_cap);
+        e = cudaGetLastError();
+    }
+    for (int i = 0; i < n_prompt && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    if (e == cudaSuccess) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_DECODE, n_prompt, d->ring_cap);
+        e = cudaGetLastError();
+    }
+    std::vector<int> ring;
+    for (int done = 0; done < steps && e == cudaSuccess;) {
+        const int chunk = std::min(steps - done, d->ring_cap);
+        for (int i = 0; i < chunk && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_decode, s);
+        ring.resize((size_t)chunk * B);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(ring.data(), d->ring + (size_t)(done % d->ring_cap) * B, ring.size() * 4,
+                                cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        for (int i = 0; i < chunk && e == cudaSuccess; ++i)
+            for (int b = 0; b < B; ++b) out[(size_t)b * steps + done + i] = ring[(size_t)i * B + b];
+        done += chunk;
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    const int rc = code_of(e);
+    if (rc) return rc;
+    const int dv = quantr_gpu_device_status(s, 0);
+    return dv == QUANTR_ERR_ROUTING ? QUANTR_OK : dv;
+}
+
+int quantr_decoder_generate_dev(quantr_decoder* d, const int* prompt, int n_prompt, int steps, int* out, void* stream)
+{
+    if (!d || !prompt || n_prompt < 1 || n_prompt > d->prompt_cap || steps < 0 || steps > d->ring_cap ||
+        (steps && !out))
+        return QUANTR_ERR_BAD_ARG;
+    const int B = d->D.B;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(d->prompt, prompt, (size_t)B * n_prompt * 4, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n_prompt, d->ring_cap);
+        e = cudaGetLastError();
+    }
+    for (int i = 0; i < n_prompt && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    if (e == cudaSuccess && steps) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_DECODE, n_prompt, d->ring_cap);
+        e = cudaGetLastError();
+        for (int i = 0; i < steps && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_decode, s);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(out, d->ring, (size_t)steps * B * 4, cudaMemcpyDeviceToDevice, s);
+    }
+    return code_of(e);
+}
+
+int quantr_decoder_launches(const quantr_decoder* d, int* decode_step, int* prefill_step)
+{
+    if (!d) return QUANTR_ERR_BAD_ARG;
+    if (decode_step) *decode_step = d->nodes_decode;
+    if (prefill_step) *prefill_step = d->nodes_prefill;
+    return QUANTR_OK;
+}
+
+const float* quantr_forward_runtime(quantr_decoder* d, int token, int pos)
+{
+    if (!d || d->D.B != 1 || token < 0 || token >= d->D.vocab || pos < 0 || pos >= d->D.seq_len) return nullptr;
+    cudaStream_t s = d->stream;
+    const int tp[2] = {token, pos};
+    cudaError_t e = cudaMemcpyAsync(d->tok, &tp[0], 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d->pos, &tp[1], 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_EXPLICIT, 0, d->ring_cap);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaGraphLaunch(d->g_decode, s);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(d->host_logits, d->logits, (size_t)d->D.vocab * 4, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return nullptr;
+    }
+    return d->host_logits;
+}
+
+void quantr_prefill_runtime(quantr_decoder* d, const int* tokens, int n)
+{
+    if (!d || d->D.B != 1 || !tokens || n <= 0 || n > d->prompt_cap) return;
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= d->D.vocab) return;
+    cudaStream_t s = d->stream;
+    cudaError_t e = cudaMemcpyAsync(d->prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) {
+        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n, d->ring_cap);
+        e = cudaGetLastError();
+    }
+    for (int i = 0; i < n && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) cudaGetLastError();
+}
+
+int quantr_debug_expf_dev(float* out, uint32_t first, long long n, void* stream)
+{
+    if (!out || n < 0) return QUANTR_ERR_BAD_ARG;
+    if (n == 0) return QUANTR_OK;
+    k_debug_expf<<<(unsigned)std::min<long long>((n + 255) / 256, 148 * 64), 256, 0,
+                   static_cast<cudaStream_t>(stream)>>>(out, first, n);
+    return code_of(cudaGetLastError());
+}
+
+int quantr_decoder_info(const quantr_decoder* d, size_t* weight_bytes, size_t* kv_bytes_per_position,
+                        size_t* device_bytes)
+{
+    if (!d) return QUANTR_ERR_BAD_ARG;
+    if (weight_bytes) *weight_bytes = d->weight_bytes;
+    if (kv_bytes_per_position) *kv_bytes_per_position = d->kv_pos_bytes;
+    if (device_bytes) *device_bytes = d->device_bytes;
+    return QUANTR_OK;
+}
+
+} // extern "C"

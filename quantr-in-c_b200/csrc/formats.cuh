@@ -73,4 +73,39 @@ __host__ __device__ __forceinline__ uint32_t f2h_ref(float f)
     return s | ((uint32_t)e << 10) | ((x >> 13) & 0x3FFu);
 }
 
+#ifdef __CUDACC__
+// Element e of a packed row, decoded as the reference's dequantize_row does
+// (src/quant.c:160-240): Q8_0 q*d; K types q*sc - m (Q4_K/Q5_K) or
+// (q-32)*(scale*d) (Q6_K), every product explicitly rounded.  Only elements
+// below dequant_extent(type, n) are defined (whole blocks; the reference
+// leaves a ragged tail untouched).
+__device__ __forceinline__ int dequant_extent(uint32_t type, int n)
+{
+    return type == T_Q8_0 ? (n / 32) * 32 : (type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) ? (n / 256) * 256 : 0;
+}
+__device__ __forceinline__ float dequant_elem(const uint8_t* __restrict__ src, uint32_t type, int e)
+{
+    auto rd16 = [&](long long off) { return (uint32_t)src[off] | ((uint32_t)src[off + 1] << 8); };
+    if (type == T_Q8_0) {
+        const long long blk = 34LL * (e / 32);
+        return __fmul_rn((float)(int8_t)src[blk + 2 + (e & 31)], h2f_ref(rd16(blk)));
+    }
+    const int l = e & 255, j = l >> 5;
+    const long long sb = (long long)block_bytes(type) * (e >> 8);
+    if (type == T_Q6_K) {
+        const int lo = (src[sb + l / 2] >> ((l & 1) * 4)) & 0xF;
+        const int hi = (src[sb + 128 + l / 4] >> ((l % 4) * 2)) & 3;
+        const float sc = __fmul_rn((float)(int8_t)src[sb + 192 + j], h2f_ref(rd16(sb + 208)));
+        return __fmul_rn((float)((lo | (hi << 4)) - 32), sc);
+    }
+    const uint32_t sc8 = src[sb + 4 + j];
+    const float sc = __fmul_rn((float)(sc8 & 63u), h2f_ref(rd16(sb)));
+    const float m = __fmul_rn((float)(sc8 >> 6), h2f_ref(rd16(sb + 2)));
+    const long long qs = sb + (type == T_Q4_K ? 16 : 48);
+    int q = (src[qs + l / 2] >> ((l & 1) * 4)) & 0xF;
+    if (type == T_Q5_K) q |= ((src[sb + 16 + l / 8] >> (l % 8)) & 1) << 4;
+    return __fsub_rn(__fmul_rn((float)q, sc), m);
+}
+#endif
+
 } // namespace qr

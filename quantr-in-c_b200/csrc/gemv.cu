@@ -255,30 +255,18 @@ __global__ void __launch_bounds__(RT * TT)
 __global__ void k_dequantize(float* __restrict__ out, const uint8_t* __restrict__ src, uint32_t type, int n)
 {
     const int e = blockIdx.x * blockDim.x + threadIdx.x;
-    auto rd16 = [&](long long off) { return (uint32_t)src[off] | ((uint32_t)src[off + 1] << 8); };
-    if (type == T_Q8_0) {
-        if (e >= (n / 32) * 32) return;
-        const long long blk = 34LL * (e / 32);
-        out[e] = __fmul_rn((float)(int8_t)src[blk + 2 + (e & 31)], h2f_ref(rd16(blk)));
-    } else if (type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) {
-        if (e >= (n / 256) * 256) return;
-        const int l = e & 255, j = l >> 5;
-        const long long sb = (long long)block_bytes(type) * (e >> 8);
-        if (type == T_Q6_K) {
-            const int lo = (src[sb + l / 2] >> ((l & 1) * 4)) & 0xF;
-            const int hi = (src[sb + 128 + l / 4] >> ((l % 4) * 2)) & 3;
-            const float sc = __fmul_rn((float)(int8_t)src[sb + 192 + j], h2f_ref(rd16(sb + 208)));
-            out[e] = __fmul_rn((float)((lo | (hi << 4)) - 32), sc);
-        } else {
-            const uint32_t sc8 = src[sb + 4 + j];
-            const float sc = __fmul_rn((float)(sc8 & 63u), h2f_ref(rd16(sb)));
-            const float m = __fmul_rn((float)(sc8 >> 6), h2f_ref(rd16(sb + 2)));
-            const long long qs = sb + (type == T_Q4_K ? 16 : 48);
-            int q = (src[qs + l / 2] >> ((l & 1) * 4)) & 0xF;
-            if (type == T_Q5_K) q |= ((src[sb + 16 + l / 8] >> (l % 8)) & 1) << 4;
-            out[e] = __fsub_rn(__fmul_rn((float)q, sc), m);
-        }
-    }
+    if (e < dequant_extent(type, n)) out[e] = dequant_elem(src, type, e);
+}
+
+// dequantize_row of `rows` rows: out[r*ldo + e] from src + r*src_stride.
+__global__ void k_dequantize_rows(float* __restrict__ out, long long ldo, const uint8_t* __restrict__ src,
+                                  long long src_stride, uint32_t type, int n, int rows)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int r = blockIdx.y;
+    const int e = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < rows && e < dequant_extent(type, n)) out[(long long)r * ldo + e] = dequant_elem(src + r * src_stride, type, e);
 }
 
 int grid_for_warps(long long warps)
@@ -452,6 +440,14 @@ cudaError_t launch_gemv_f32(const float* w, const float* x, long long ldx, float
         return launch_ex(&k_gemv_f32<128, 1>, dim3((n + 127) / 128), dim3(128), 0, c, w, x, ldx, out, ldo, n, d, B);
     return launch_ex(&k_gemv_f32<32, 4>, dim3((n + 31) / 32, (B + 3) / 4), dim3(128), 0, c, w, x, ldx, out, ldo, n,
                      d, B);
+}
+
+cudaError_t launch_dequantize_rows(float* out, long long ldo, const uint8_t* src, long long src_stride, uint32_t type,
+                                   int n, int rows, const LaunchCfg& c)
+{
+    if (n <= 0 || rows <= 0) return cudaSuccess;
+    return launch_ex(&k_dequantize_rows, dim3((n + 255) / 256, rows), dim3(256), 0, c, out, ldo, src, src_stride,
+                     type, n, rows);
 }
 
 cudaError_t launch_dequantize(float* out, const uint8_t* src, uint32_t type, int n, const LaunchCfg& c)

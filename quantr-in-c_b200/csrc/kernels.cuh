@@ -63,6 +63,11 @@ cudaError_t launch_gemv_f32(const float* w, const float* x, long long ldx, float
 cudaError_t launch_dequantize(float* out, const uint8_t* src, uint32_t type, int n,
                               const LaunchCfg& c);
 
+// dequantize_row of `rows` packed rows (row r at src + r*src_stride) into
+// out[r*ldo ...] (elements past the last whole block are left untouched).
+cudaError_t launch_dequantize_rows(float* out, long long ldo, const uint8_t* src, long long src_stride, uint32_t type,
+                                   int n, int rows, const LaunchCfg& c);
+
 int device_sm_count();
 
 // Kernel launches issued by this library since load.

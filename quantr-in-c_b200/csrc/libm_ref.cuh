@@ -38,22 +38,23 @@
 namespace qr {
 namespace libm {
 
-// RN(2^(i/32)) as IEEE-754 bits, minus i << 47.  Global (not __constant__)
-// memory on the device: lanes index it divergently, which the constant cache
-// would serialise.
-#ifdef __CUDACC__
-__device__
-#endif
-static const uint64_t kExp2Tab[32] = {
-    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
-    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
-    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
-    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
-    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
-    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
-    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+// RN(2^(i/32)) as IEEE-754 bits, minus i << 47.  The device copy lives in
+// global (not __constant__) memory: lanes index it divergently, which the
+// constant cache would serialise.
+#define QR_EXP2_TAB_VALUES \
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull, \
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull, \
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull, \
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull, \
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull, \
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull, \
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull, \
     0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
-};
+static const uint64_t kExp2TabHost[32] = {QR_EXP2_TAB_VALUES};
+#ifdef __CUDACC__
+__device__ static const uint64_t kExp2TabDev[32] = {QR_EXP2_TAB_VALUES};
+#endif
+#undef QR_EXP2_TAB_VALUES
 
 // Cubic for 2^(r/32), r in [-1/2, 1/2]: coefficients of r^3, r^2, r (the
 // method's 2^t polynomial, t = r/32, pre-scaled by 32^-3, 32^-2, 32^-1).
@@ -155,9 +156,9 @@ QR_HD float expf_ref(float x)
     kd = dadd(kd, -kRoundShift);
     const double r = dfma(kInvLn2x32, xd, -kd);
 #ifdef __CUDA_ARCH__
-    const uint64_t t = __ldg(&kExp2Tab[ki & 31u]) + (ki << 47);
+    const uint64_t t = __ldg(&kExp2TabDev[ki & 31u]) + (ki << 47);
 #else
-    const uint64_t t = kExp2Tab[ki & 31u] + (ki << 47);
+    const uint64_t t = kExp2TabHost[ki & 31u] + (ki << 47);
 #endif
     const double s = u2d(t);
     const double p = dfma(kC0, r, kC1);

@@ -64,6 +64,17 @@ SIGNATURES = {
     "quantr_moe_experts_dev": (_i, [_vp, _vp, _ll, _i, _vp, _i, _i, _i, _vp, _vp, _vp, _i, _i, _vp, _sz, _vp]),
     "quantr_moe_combine_dev": (_i, [_vp, _ll, _vp, _vp, _vp, _i, _i, _i, _vp]),
     "quantr_moe_layer": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i, _vp, _u32, _vp, _u32, _vp, _u32, _i, _i, _vp, _vp]),
+    "quantr_decoder_create": (_i, [_c.POINTER(_vp), _vp, _i]),
+    "quantr_decoder_destroy": (None, [_vp]),
+    "quantr_decoder_step_dev": (_i, [_vp, _vp, _vp, _vp, _ll, _vp, _vp]),
+    "quantr_decoder_generate": (_i, [_vp, _vp, _i, _i, _vp]),
+    "quantr_forward_runtime": (_c.POINTER(_f), [_vp, _i, _i]),
+    "quantr_prefill_runtime": (None, [_vp, _vp, _i]),
+    "quantr_decoder_info": (_i, [_vp, _c.POINTER(_sz), _c.POINTER(_sz), _c.POINTER(_sz)]),
+    "quantr_debug_expf_dev": (_i, [_vp, _u32, _ll, _vp]),
+    "quantr_dequantize_rows_dev": (_i, [_vp, _ll, _vp, _ll, _u32, _i, _i, _vp]),
+    "quantr_decoder_generate_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
+    "quantr_decoder_launches": (_i, [_vp, _c.POINTER(_i), _c.POINTER(_i)]),
 }
 
 
@@ -214,6 +225,12 @@ def quantize_q8_0_dev(y, x, ldx, k, B, stream=0):
         raise QuantrError(rc, "quantr_quantize_q8_0_dev")
 
 
+def dequantize_rows_dev(out, ldo, src, src_stride, type_, n, rows, stream=0):
+    rc = lib().quantr_dequantize_rows_dev(out, ldo, src, src_stride, type_, n, rows, stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_dequantize_rows_dev")
+
+
 def gemv_partials_dev(out, isum, bsum, x, w, type_, n, d, B, ws, ws_bytes, stream=0):
     rc = lib().quantr_gemv_partials_dev(out, isum, bsum, x, w, type_, n, d, B, ws, ws_bytes, stream or None)
     if rc:
@@ -320,3 +337,156 @@ def moe_layer(xb, E, k, w1, t1, w3, t3, w2, t2, dim, hidden, router=None, logits
 
 def device_status(stream=0, reset=True):
     return int(lib().quantr_gpu_device_status(stream or None, 1 if reset else 0))
+
+
+# --------------------------------------------------------------- decoder --
+
+_P = ctypes.POINTER
+
+
+class Model(ctypes.Structure):
+    """quantr_model (include/quantr_cuda.h)."""
+    _fields_ = [("dim", _i), ("hidden_dim", _i), ("n_layers", _i), ("n_heads", _i), ("n_kv_heads", _i),
+                ("vocab_size", _i), ("seq_len", _i), ("rope_freq_base", _f), ("expert_count", _i),
+                ("expert_used_count", _i), ("kv_type", _i), ("token_embd", _vp), ("token_embd_type", _u32),
+                ("token_embd_row_bytes", _sz)] + \
+        [(n, _P(_vp)) for n in ("rms_att", "rms_ffn", "wq", "wk", "wv", "wo", "w1", "w2", "w3")] + \
+        [(n, _P(_u32)) for n in ("wq_type", "wk_type", "wv_type", "wo_type", "w1_type", "w2_type", "w3_type")] + \
+        [("rms_final", _vp), ("wcls", _vp), ("wcls_type", _u32), ("ffn_gate_inp", _P(_vp)),
+         ("expert_w1", _P(_P(_vp))), ("expert_w2", _P(_P(_vp))), ("expert_w3", _P(_P(_vp))),
+         ("exp_w1_type", _P(_u32)), ("exp_w2_type", _P(_u32)), ("exp_w3_type", _P(_u32)),
+         ("head_dim", _i), ("shexp_hidden_dim", _i), ("shexp_w1", _P(_vp)), ("shexp_w2", _P(_vp)),
+         ("shexp_w3", _P(_vp)), ("shexp_w1_type", _P(_u32)), ("shexp_w2_type", _P(_u32)),
+         ("shexp_w3_type", _P(_u32)), ("shexp_gate", _P(_vp))]
+
+
+def describe_model(model):
+    """quantr_model over a model_synth.Model's host buffer (host pointers into
+    one mapping, as the reference's TransformerWeights are).  Returns the
+    struct and the pointer arrays it references (keep both alive)."""
+    s = model.spec
+    L = s.n_layers
+    keep = []
+
+    def arr(ctype, vals):
+        a = (ctype * max(len(vals), 1))(*vals)
+        keep.append(a)
+        return ctypes.cast(a, _P(ctype))
+
+    def ptrs(names):
+        return arr(_vp, [model.ptr(n) if n in model.off else None for n in names])
+
+    def types(names):
+        return arr(_u32, [model.type_of(n) if n in model.off else 0 for n in names])
+
+    m = Model()
+    m.dim, m.hidden_dim, m.n_layers, m.n_heads = s.dim, s.hidden_dim, L, s.n_heads
+    m.n_kv_heads, m.vocab_size, m.seq_len, m.rope_freq_base = s.n_kv_heads, s.vocab_size, s.seq_len, s.rope_freq_base
+    m.expert_count, m.expert_used_count, m.kv_type = s.expert_count, s.expert_used_count, s.kv_type
+    m.token_embd = model.ptr("token_embd")
+    m.token_embd_type = model.type_of("token_embd")
+    m.token_embd_row_bytes = 0 if s.embd_type == F32 else row_bytes(s.embd_type, s.dim)
+    m.rms_att = ptrs([f"rms_att.{l}" for l in range(L)])
+    m.rms_ffn = ptrs([f"rms_ffn.{l}" for l in range(L)])
+    for w in ("wq", "wk", "wv", "wo", "w1", "w2", "w3"):
+        setattr(m, w, ptrs([f"{w}.{l}" for l in range(L)]))
+        setattr(m, w + "_type", types([f"{w}.{l}" for l in range(L)]))
+    m.rms_final = model.ptr("rms_final")
+    m.wcls = model.ptr("wcls")
+    m.wcls_type = model.type_of("wcls")
+    if s.expert_count:
+        m.ffn_gate_inp = ptrs([f"router.{l}" for l in range(L)])
+        for w in ("exp_w1", "exp_w2", "exp_w3"):
+            per_layer = [ptrs([f"{w}.{l}.{e}" for e in range(s.expert_count)]) for l in range(L)]
+            setattr(m, "expert_" + w[4:], arr(_P(_vp), per_layer))
+            setattr(m, w + "_type", types([f"{w}.{l}.0" for l in range(L)]))
+    m.head_dim = s.head_dim
+    if s.shexp_hidden_dim:
+        m.shexp_hidden_dim = s.shexp_hidden_dim
+        for w in ("shexp_w1", "shexp_w2", "shexp_w3"):
+            setattr(m, w, ptrs([f"{w}.{l}" for l in range(L)]))
+            setattr(m, w + "_type", types([f"{w}.{l}" for l in range(L)]))
+        m.shexp_gate = ptrs([f"shexp_gate.{l}" for l in range(L)])
+    return m, keep
+
+
+class Decoder:
+    """The device-resident decoder (quantr_decoder_*) over a model_synth.Model.
+
+    The model's host buffer (its "GGUF mapping") is registered once with
+    quantr_gpu_register_weights and the decoder is handed host pointers into
+    it, the way the reference's runtime would drive it."""
+
+    def __init__(self, model, batch=1, register=True):
+        self.model = model
+        self.batch = batch
+        self._registered = False
+        if register:
+            register_weights(model.buf)
+            self._registered = True
+        self._m, self._keep = describe_model(model)
+        h = ctypes.c_void_p()
+        rc = lib().quantr_decoder_create(ctypes.byref(h), ctypes.byref(self._m), batch)
+        if rc:
+            self._unregister()
+            raise QuantrError(rc, "quantr_decoder_create")
+        self._h = h
+
+    def generate(self, prompt, steps):
+        """src/main.c:305-317 for every sequence: prompt int32[batch, n] ->
+        int32[batch, steps] greedy tokens."""
+        p = np.ascontiguousarray(np.asarray(prompt, np.int32).reshape(self.batch, -1))
+        out = np.zeros((self.batch, steps), np.int32)
+        rc = lib().quantr_decoder_generate(self._h, _ptr(p), p.shape[1], steps, _ptr(out))
+        if rc:
+            raise QuantrError(rc, "quantr_decoder_generate")
+        return out
+
+    def forward_runtime(self, token, pos):
+        r = lib().quantr_forward_runtime(self._h, int(token), int(pos))
+        if not r:
+            raise QuantrError(QUANTR_ERR_BAD_ARG, "quantr_forward_runtime")
+        return np.ctypeslib.as_array(r, shape=(self.model.spec.vocab_size,)).copy()
+
+    def prefill_runtime(self, tokens):
+        t = np.ascontiguousarray(tokens, np.int32)
+        lib().quantr_prefill_runtime(self._h, _ptr(t), t.size)
+
+    def step_dev(self, tokens, pos, logits=None, ldl=0, next_=None, stream=0):
+        rc = lib().quantr_decoder_step_dev(self._h, tokens, pos, logits, ldl, next_, stream or None)
+        if rc:
+            raise QuantrError(rc, "quantr_decoder_step_dev")
+
+    def generate_dev(self, prompt, n_prompt, steps, out, stream=0):
+        """Device arrays, asynchronous: out is steps x batch (step-major)."""
+        rc = lib().quantr_decoder_generate_dev(self._h, prompt, n_prompt, steps, out, stream or None)
+        if rc:
+            raise QuantrError(rc, "quantr_decoder_generate_dev")
+
+    def info(self):
+        a, b, c = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        lib().quantr_decoder_info(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+        x, y = ctypes.c_int(), ctypes.c_int()
+        lib().quantr_decoder_launches(self._h, ctypes.byref(x), ctypes.byref(y))
+        return {"weight_bytes_per_step": a.value, "kv_bytes_per_position": b.value, "device_bytes": c.value,
+                "launches_per_decode_step": x.value, "launches_per_prefill_step": y.value}
+
+    def _unregister(self):
+        if self._registered:
+            unregister_weights(self.model.buf)
+            self._registered = False
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().quantr_decoder_destroy(self._h)
+            self._h = None
+        self._unregister()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+QUANTR_ERR_BAD_ARG = 3

@@ -1,5 +1,5 @@
 """Multi-GPU forms of the hot path: one process per GPU, torch.distributed
-(NCCL over NVLink/NVSwitch) for the one exchange step each form has.
+(NCCL over NVLink/NVSwitch) for the exchange steps each form has.
 
 Row-sharded (tensor-parallel) GEMV.  Every packed block lies inside one row
 (src/quant.c:491-492), so a contiguous range of rows is a contiguous byte range
@@ -9,18 +9,29 @@ kernel, so the activation blocks are bit-identical on every rank, and each
 output row is exactly what one GPU computes for it.  One all-gather of the
 np-row shards assembles out.
 
-Expert-parallel MoE (src/runtime.c:202-269).  Rank r owns experts
-[E*r/P, E*(r+1)/P).  Every rank routes every token with the same kernel on the
-same inputs (identical sel/wts), runs its own experts on the (token, slot)
-pairs routed to them, writing those rows of a zeroed (T*k) x dim buffer, and
-one all-reduce (sum) assembles it: each row has exactly one non-zero
-contributor and x + 0.0 == x, so the sum is exact whatever order the
-collective adds in (a -0.0 row becomes +0.0, which the combine's
-0.0f + o*ew cannot tell apart).  Every rank then combines in selection order.
+Expert-parallel MoE (src/runtime.c:202-269), tokens and experts both split.
+Rank r holds its own tokens and owns experts [E*r/P, E*(r+1)/P).  Each rank
+routes its tokens (the router is per token), then:
+  1. counts: every rank tells every other how many (token, slot) pairs it
+     will send it (all_to_all_single of P counts);
+  2. dispatch: each pair's activation row goes to the owner of its expert as
+     the reference's own Q8_0 blocks (quantize_row_q8_0 of xb, 34 bytes per
+     32 elements, 3.8x fewer bytes than fp32) with the expert id
+     (all_to_all_single).  The reference quantizes the same xb identically
+     for every expert call (src/runtime.c:252-253 -> src/quant.c:474), and
+     re-quantizing the exact dequantization of such blocks reproduces them,
+     so the owner's GEMVs see the very activations one GPU would;
+  3. the owner runs its experts on the received pairs (one slot each);
+  4. return: every pair's output row goes back to its token's rank
+     (all_to_all_single), which combines in selection order
+     (src/runtime.c:262-264).
+Every per-pair output is computed by the same kernels on the same bytes as
+on one GPU, so the block output is bit-identical to the unsharded one.
 
 Compute goes through a backend object with the library's stage calls
 (`CudaBackend`, the product path on the C ABI); the host logic here (shard
-ranges, padding, reassembly, exchange, combine order) is backend-agnostic.
+ranges, padding, reassembly, dispatch plans, exchanges, combine order) is
+backend-agnostic.
 """
 import numpy as np
 import torch
@@ -101,6 +112,22 @@ class CudaBackend:
                                stream=self.stream())
         return out
 
+    def quantize_q8_0(self, x):
+        """T x d fp32 -> T x (d/32*34) uint8 packed block_q8_0 rows."""
+        T, d = x.shape
+        y = torch.empty(T, (d // 32) * 34, dtype=torch.uint8, device=self.device)
+        if T:
+            quantr.quantize_q8_0_dev(y.data_ptr(), x.data_ptr(), x.stride(0), d, T, self.stream())
+        return y
+
+    def dequantize_q8_0(self, y, d):
+        """Packed block_q8_0 rows -> T x d fp32 (dequantize_row per row)."""
+        T = y.shape[0]
+        x = torch.zeros(T, d, dtype=torch.float32, device=self.device)
+        if T:
+            quantr.dequantize_rows_dev(x.data_ptr(), d, y.data_ptr(), y.stride(0), 8, d, T, self.stream())
+        return x
+
 
 class RowShardedGemv:
     """out = W.x for a packed n x d matrix whose rows are split over the group.
@@ -130,13 +157,14 @@ class RowShardedGemv:
 
 
 class ExpertShardedMoE:
-    """The routed MoE block with experts split over the group.
+    """The routed MoE block with tokens and experts split over the group.
 
     w1/w3: uint8[E, hidden, row_bytes(t, dim)], w2: uint8[E, dim,
     row_bytes(t2, hidden)] (the merged *_exps tensors, src/model.c:409-419);
     each rank uploads its experts only.  router: E x dim F32 on this rank's
-    device, or None with logits given per call.  __call__ returns (out, sel,
-    wts) on every rank."""
+    device, or None with logits given per call.  __call__(xb) takes THIS
+    rank's tokens (T_r x dim) and returns (out, sel, wts) for them; `stats`
+    then holds the pairs sent/received and the bytes each exchange moved."""
 
     def __init__(self, E, k, dim, hidden, w1, t1, w3, t3, w2, t2, backend, group=None, router=None):
         self.world, self.rank = _world(group)
@@ -144,19 +172,59 @@ class ExpertShardedMoE:
         self.E, self.k, self.dim, self.hidden = E, k, dim, hidden
         self.e0, self.e1 = expert_range(E, self.rank, self.world)
         self.router = router
+        self.owner = torch.tensor([max(r for r in range(self.world) if expert_range(E, r, self.world)[0] <= e)
+                                   for e in range(E)], dtype=torch.int64)
         self.mats = []
         for w, t in ((w1, t1), (w3, t3), (w2, t2)):
             w = np.asarray(w, np.uint8)
             local = w[self.e0:self.e1]
             stride = int(np.prod(w.shape[1:])) if w.ndim > 1 else 0
             self.mats.append((backend.upload(local), stride, t))
+        self.stats = {}
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
 
     def __call__(self, xb, logits=None):
-        T = xb.shape[0]
-        sel, wts = self.backend.route(xb, self.E, self.k, router=self.router, logits=logits)
-        o = self.backend.zeros(T * self.k, self.dim)
-        if self.e1 > self.e0:
-            self.backend.experts(o, xb, sel, self.e0, self.e1 - self.e0, self.mats, self.dim, self.hidden)
-        if self.world > 1:
-            dist.all_reduce(o, op=dist.ReduceOp.SUM, group=self.group)
-        return self.backend.combine(o, sel, wts, self.dim), sel, wts
+        T, dim, k = xb.shape[0], self.dim, self.k
+        be = self.backend
+        sel, wts = be.route(xb, self.E, k, router=self.router, logits=logits)
+        # Dispatch plan: valid pairs ordered by destination rank, then pair
+        # index (plain integer bookkeeping on the host).
+        sel_h = sel.cpu().reshape(-1).to(torch.int64)
+        pair = torch.nonzero(sel_h >= 0).reshape(-1)
+        dest = self.owner[sel_h[pair]] if pair.numel() else torch.zeros(0, dtype=torch.int64)
+        order = torch.argsort(dest * (T * k + 1) + pair)
+        pair, dest = pair[order], dest[order]
+        send_counts = torch.bincount(dest, minlength=self.world).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        self._a2a(recv_counts, send_counts, None, None)  # 1. counts
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        n_send, n_recv = sum(sc), sum(rc)
+        # 2. dispatch: Q8_0 rows of the pairs' tokens, and their expert ids.
+        xq = be.quantize_q8_0(xb)
+        dev = xq.device
+        tok = (pair // k).to(dev)
+        send_q = xq.index_select(0, tok) if n_send else xq[:0]
+        recv_q = torch.empty(n_recv, xq.shape[1], dtype=torch.uint8, device=dev)
+        self._a2a(recv_q, send_q, rc, sc)
+        send_e = sel_h[pair].to(torch.int32).to(dev)
+        recv_e = torch.empty(n_recv, dtype=torch.int32, device=dev)
+        self._a2a(recv_e, send_e, rc, sc)
+        # 3. local experts on the received pairs (one slot each).
+        o_recv = be.zeros(n_recv, dim)
+        if n_recv and self.e1 > self.e0:
+            be.experts(o_recv, be.dequantize_q8_0(recv_q, dim), recv_e.view(n_recv, 1), self.e0,
+                       self.e1 - self.e0, self.mats, dim, self.hidden)
+        # 4. outputs back to the tokens' ranks, then the combine.
+        o_back = be.zeros(n_send, dim)
+        self._a2a(o_back, o_recv, sc, rc)
+        o = be.zeros(T * k, dim)
+        if n_send:
+            o.index_copy_(0, pair.to(o.device), o_back)
+        self.stats = {"pairs_sent": n_send, "pairs_received": n_recv,
+                      "dispatch_bytes": n_send * (xq.shape[1] + 4), "return_bytes": n_send * dim * 4}
+        return be.combine(o, sel, wts, dim), sel, wts

@@ -1,7 +1,7 @@
 """CPU (gloo, world_size 2): the host logic of the multi-GPU forms in
 quantr-in-c_b200/shard.py - shard ranges, padding, the all-gather reassembly of
-row shards, the expert split, the exact all-reduce of per-pair outputs and the
-selection-order combine.
+row shards, the expert and token split, the all-to-all exchanges (counts, Q8_0
+activation dispatch, per-pair output return) and the selection-order combine.
 
 The compute runs on a CPU stand-in backend built from the oracle (test
 infrastructure); the property checked is that the sharded result is
@@ -73,6 +73,16 @@ class CpuBackend:
             o[p] = torch.from_numpy(np.asarray(
                 self.orc.matmul_q_fused(hb, w2.reshape(-1)[le * s2:(le + 1) * s2], t2, dim, hidden), np.float32))
 
+    def quantize_q8_0(self, x):
+        xn = x.numpy()
+        return torch.from_numpy(np.stack([self.orc.quantize_row_q8_0(r) for r in xn]) if len(xn)
+                                else np.zeros((0, (x.shape[1] // 32) * 34), np.uint8))
+
+    def dequantize_q8_0(self, y, d):
+        yn = y.numpy()
+        return torch.from_numpy(np.stack([self.orc.dequantize_row(r, Q8_0, d) for r in yn]).astype(np.float32)
+                                if len(yn) else np.zeros((0, d), np.float32))
+
     def combine(self, o, sel, wts, dim):
         T, k = sel.shape
         out = np.zeros((T, dim), np.float32)
@@ -97,8 +107,8 @@ def _case(seed):
     c["w1"] = np.stack([synth.matrix(rng, Q5_K, hidden, dim) for _ in range(E)])
     c["w3"] = np.stack([synth.matrix(rng, Q5_K, hidden, dim) for _ in range(E)])
     c["w2"] = np.stack([synth.matrix(rng, Q6_K, dim, hidden) for _ in range(E)])
-    c["xb"] = synth.activations(rng, 5, dim)
-    c["logits"] = rng.standard_normal((5, E), dtype=np.float32)
+    c["xb"] = synth.activations(rng, 7, dim)
+    c["logits"] = rng.standard_normal((7, E), dtype=np.float32)
     return c
 
 
@@ -115,10 +125,19 @@ def _run(rank, world, port, out_dir):
             res[f"gemv{i}"] = g(torch.from_numpy(c["x"][d])).numpy().copy()
         E, k, dim, hidden = c["moe"]
         m = shard.ExpertShardedMoE(E, k, dim, hidden, c["w1"], Q5_K, c["w3"], Q5_K, c["w2"], Q6_K, be)
-        out, sel, wts = m(torch.from_numpy(c["xb"]), logits=torch.from_numpy(c["logits"]))
-        res["moe"], res["sel"], res["wts"] = out.numpy(), sel.numpy(), wts.numpy()
+        T = c["xb"].shape[0]
+        t0, t1 = T * rank // world, T * (rank + 1) // world  # this rank's tokens
+        out, sel, wts = m(torch.from_numpy(c["xb"][t0:t1]), logits=torch.from_numpy(c["logits"][t0:t1]))
+        parts = [None] * world
+        dist.all_gather_object(parts, (out.numpy(), sel.numpy(), wts.numpy(), m.stats))
+        res["moe"] = np.concatenate([p[0] for p in parts])
+        res["sel"] = np.concatenate([p[1] for p in parts])
+        res["wts"] = np.concatenate([p[2] for p in parts])
         if rank == 0:
             np.savez(os.path.join(out_dir, f"w{world}.npz"), **res)
+            sent = sum(p[3]["pairs_sent"] for p in parts)
+            recv = sum(p[3]["pairs_received"] for p in parts)
+            assert sent == recv == T * k, (sent, recv)
     finally:
         dist.destroy_process_group()
 

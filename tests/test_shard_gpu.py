@@ -1,7 +1,10 @@
-"""GPU, 2 ranks over NCCL: the row-sharded GEMV and the expert-sharded MoE of
-quantr-in-c_b200/shard.py on real devices.  The sharded GEMV must be
-bit-identical to the oracle; the sharded MoE bit-identical to the one-GPU
-quantr_moe_dev result.  Skipped on boxes with fewer than 2 GPUs."""
+"""GPU, 2 ranks over NCCL: the row-sharded GEMV (all-gather) and the
+expert-parallel MoE (tokens split, all-to-all dispatch of Q8_0 activations
+and return of per-pair outputs) of quantr-in-c_b200/shard.py on real
+devices.  The sharded GEMV must be bit-identical to the oracle; the sharded
+MoE bit-identical to the one-GPU quantr_moe_dev result.  Skipped on boxes
+with fewer than 2 GPUs (bench.py --gpus N runs the same forms on every
+GPU count and reports their parity with one GPU)."""
 import datetime
 import os
 import socket
@@ -54,9 +57,16 @@ def _rank(rank, world, port, out_dir):
             res[f"gemv{i}"] = g(torch.from_numpy(c["x"][d]).to(dev)).cpu().numpy()
         E, k, dim, hidden = c["moe"]
         m = shard.ExpertShardedMoE(E, k, dim, hidden, c["w1"], Q5_K, c["w3"], Q5_K, c["w2"], Q6_K, be)
-        out, sel, wts = m(torch.from_numpy(c["xb"]).to(dev), logits=torch.from_numpy(c["logits"]).to(dev))
+        T = c["xb"].shape[0]
+        t0, t1 = T * rank // world, T * (rank + 1) // world  # this rank's tokens
+        out, sel, wts = m(torch.from_numpy(c["xb"][t0:t1]).to(dev),
+                          logits=torch.from_numpy(c["logits"][t0:t1]).to(dev))
         torch.cuda.synchronize()
-        res["moe"], res["sel"], res["wts"] = out.cpu().numpy(), sel.cpu().numpy(), wts.cpu().numpy()
+        parts = [None] * world
+        dist.all_gather_object(parts, (out.cpu().numpy(), sel.cpu().numpy(), wts.cpu().numpy()))
+        res["moe"] = np.concatenate([p[0] for p in parts])
+        res["sel"] = np.concatenate([p[1] for p in parts])
+        res["wts"] = np.concatenate([p[2] for p in parts])
         assert quantr.device_status(0) == 0
         dist.barrier()
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **res)
