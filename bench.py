@@ -57,11 +57,13 @@ HIDDEN, FFN, LAYERS = 896, 4864, 24
 Q8_0, Q4_K = 8, 12
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
-# DRAM bytes (read + write) of one k_program launch of the c2 step, from the
-# ncu capture summarised in profiles/k_program_c2_full.md: 159,962,112 read +
-# 4,132,864 written (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB
-# out per step).
-NCU_TRAFFIC_PER_STEP = 164094976
+# DRAM bytes (read + write) of one k_program launch of the c2 step at batch 1
+# (24 layers), from the ncu --set full capture of that launch summarised under
+# profiles/ (k_program_c2_full.txt): 159,962,112 read + 4,132,864 written
+# (algorithmic: 159,694,848 weight bytes + 0.64 MB x + 1.02 MB out per step).
+# Reported only for that configuration.
+NCU_TRAFFIC_C2_B1 = 164094976
+NCU_TRAFFIC_SOURCE = "ncu --set full capture of k_program, c2 step at batch 1, 24 layers (profiles/k_program_c2_full.txt)"
 
 
 def row_bytes(t, d):
@@ -420,18 +422,21 @@ def ours_arm(args):
 
     e2e_pipe(max(2, args.warmup))
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ev4, ev5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev4.record(s_in)
-    e2e_pipe(args.steps)
-    ev5.record(s_out)
-    torch.cuda.synchronize()
+    e2e_runs = []
+    for _ in range(3):  # median of three repeats (host-copy bandwidth varies between boxes and runs)
+        if world > 1:
+            dist.barrier()
+        ev4, ev5 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev4.record(s_in)
+        e2e_pipe(args.steps)
+        ev5.record(s_out)
+        torch.cuda.synchronize()
+        te = torch.tensor([ev4.elapsed_time(ev5)], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e_runs.append(world * nbytes * args.steps / (float(te.item()) / 1e3) / 1e9)
     assert quantr.device_status(0) == 0
-    te = torch.tensor([ev4.elapsed_time(ev5)], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(te, op=dist.ReduceOp.MAX)
-    e2e_gbs = world * nbytes * args.steps / (float(te.item()) / 1e3) / 1e9
+    e2e_gbs = statistics.median(e2e_runs)
     prog2.close()
 
     # (b) through the reference's own entry point, one synchronous
@@ -468,24 +473,31 @@ def ours_arm(args):
                "sample": (f"{done} full steps ({len(shapes)} GEMVs each, {el:.1f} s) of the same workload, "
                           f"reference src/quant.c {variant} build")}
 
+    sharded = None if args.no_sharded else sharded_forms(args, dev, world, rank)
+    decode = None
+    if rank == 0 and world == 1 and not args.no_decode:
+        decode = decode_c3(args, dev, s)
+
     peak, peak_kind = load_peaks()
     if rank == 0:
+        c2_b1 = B == 1 and args.layers == LAYERS
         line = {
             "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": config_dict(args),
             "pct_of_8TBs_per_gpu": round(100.0 * per_gpu / NOMINAL_HBM_GBS, 2),
-            "tok_per_s": round(world * B * args.steps / (ms / 1e3), 1),
+            "gemv_steps_per_s": round(world * args.steps / (ms / 1e3), 1),
             "roofline": {"bound": "hbm", "achieved": round(per_gpu, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu / peak, 4), "peak_source": peak_kind,
-                         "traffic": NCU_TRAFFIC_PER_STEP,
+                         "traffic": NCU_TRAFFIC_C2_B1 if c2_b1 else None,
+                         "traffic_source": NCU_TRAFFIC_SOURCE if c2_b1 else None,
                          "kernel": "k_program (persistent GEMV engine) + k_quant_tasks, one launch pair per step"},
             "per_call_value": round(per_call_gbs, 3),
             "per_call_note": "same step as 72 quantr_gemv_dev calls (one quantizer + engine launch each)",
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
+                    "d2h_bytes_per_step": d2h, "repeats": [round(v, 1) for v in e2e_runs],
                     "api": ("quantr_program_run with all step inputs copied from pinned host memory and all "
                             "outputs copied back inside the timed region (CUDA events); steps pipelined over two "
                             "buffer sets and copy-in / compute / copy-out streams")},
@@ -496,6 +508,8 @@ def ours_arm(args):
             "c1_q8_0": c1,
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
+            "decode_c3": decode,
+            "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
     del graph, graph_pc
@@ -503,6 +517,124 @@ def ours_arm(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+# ------------------------------------------------------ sharded forms --
+
+def sharded_forms(args, dev, world, rank):
+    """The two multi-GPU forms of quantr-in-c_b200/shard.py, timed at this N
+    (at N = 1 they run without collectives) with a bit-exactness flag against
+    the one-GPU result computed on rank 0:
+      tp_head  c3's output head (32000 x 2048 Q6_K, batch 1) row-sharded, one
+               all-gather per call (strong scaling: fixed rows);
+      ep_moe   c5's MoE layer (128 experts top-8, dim 2048, I 768, Q4_K),
+               64 tokens per rank (weak scaling), experts split 128/N,
+               all-to-all dispatch of Q8_0 activations + return of per-pair
+               outputs, selection-order combine.
+    Times are CUDA events over `steps` calls after warm-up, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    import quantr
+    import shard
+    be = shard.CudaBackend(dev)
+    rng = synth.rng_for(77)
+    out = {}
+
+    def max_ms(ms_local):
+        t = torch.tensor([ms_local], device=dev, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def timed(fn, n):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return max_ms(e0.elapsed_time(e1) / n)
+
+    # --- tensor-parallel head GEMV ---
+    n, d, t = 32000, 2048, Q6_K
+    w = synth.matrix(rng, t, n, d)
+    x = torch.from_numpy(synth.activations(rng, 1, d)).to(dev)
+    g = shard.RowShardedGemv(w, t, n, d, be)
+    res = g(x)
+    ms_call = timed(lambda: g(x), args.steps)
+    ag_in = torch.zeros(g.npad, device=dev)
+    ag_out = torch.zeros(world * g.npad, device=dev)
+    ms_ag = timed(lambda: dist.all_gather_into_tensor(ag_out, ag_in) if world > 1 else None, args.steps)
+    ok = True
+    if rank == 0:
+        full = torch.zeros(1, n, device=dev)
+        wd = be.upload(w)
+        be.gemv(full, n, x, wd, t, n, d)
+        ok = bool(torch.equal(full.view(torch.int32), res.contiguous().view(torch.int32)))
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    if world > 1:
+        dist.broadcast(flag, 0)
+    wbytes = n * row_bytes(t, d)
+    out["tp_head"] = {"shape": f"{n}x{d} Q6_K, batch 1, rows split {world} ways", "us_per_call": round(ms_call * 1e3, 2),
+                      "all_gather_us": round(ms_ag * 1e3, 2) if world > 1 else 0.0,
+                      "GBs_aggregate": round(wbytes / (ms_call / 1e3) / 1e9, 1),
+                      "bit_exact_vs_1gpu": bool(flag.item()), "collective": "all_gather_into_tensor (NCCL)"}
+
+    # --- expert-parallel MoE layer ---
+    E, k, dim, hid, tq = 128, 8, 2048, 768, Q4_K
+    T_rank = 64
+    mats = [np.stack([synth.matrix(rng, tq, hid, dim) for _ in range(E)]),
+            np.stack([synth.matrix(rng, tq, hid, dim) for _ in range(E)]),
+            np.stack([synth.matrix(rng, tq, dim, hid) for _ in range(E)])]
+    xb_all = synth.activations(rng, T_rank * world, dim)
+    lg_all = rng.standard_normal((T_rank * world, E), dtype=np.float32)
+    moe = shard.ExpertShardedMoE(E, k, dim, hid, mats[0], tq, mats[1], tq, mats[2], tq, be)
+    r0 = rank * T_rank
+    xb = torch.from_numpy(xb_all[r0:r0 + T_rank]).to(dev)
+    lg = torch.from_numpy(lg_all[r0:r0 + T_rank]).to(dev)
+    mo, _, _ = moe(xb, logits=lg)
+    ms_moe = timed(lambda: moe(xb, logits=lg), max(5, args.steps // 4))
+    parts = [torch.empty_like(mo) for _ in range(world)] if world > 1 else [mo]
+    if world > 1:
+        dist.all_gather(parts, mo)
+    ok = True
+    if rank == 0:
+        full_moe = shard.ExpertShardedMoE.__new__(shard.ExpertShardedMoE)
+        # the one-GPU block on every rank's tokens: all experts here
+        xa = torch.from_numpy(xb_all).to(dev)
+        la = torch.from_numpy(lg_all).to(dev)
+        ew = [torch.from_numpy(np.ascontiguousarray(m_).reshape(-1)).to(dev) for m_ in mats]
+        ewts = [quantr.ExpertWeights(m_.data_ptr(), mats[i][0].nbytes, None, tq) for i, m_ in enumerate(ew)]
+        T_all = T_rank * world
+        ref = torch.empty(T_all, dim, device=dev)
+        wsb = quantr.moe_workspace_bytes(T_all, E, k, dim, hid)
+        ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        quantr.moe_dev(ref.data_ptr(), dim, xa.data_ptr(), dim, T_all, E, k, *ewts, dim, hid, ws.data_ptr(), wsb,
+                       logits=la.data_ptr(), ldl=E, stream=torch.cuda.current_stream(dev).cuda_stream)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(torch.cat(parts).view(torch.int32), ref.view(torch.int32)))
+        del full_moe
+    flag = torch.tensor([1 if ok else 0], device=dev)
+    if world > 1:
+        dist.broadcast(flag, 0)
+    st = moe.stats
+    ebytes = E * (2 * hid * row_bytes(tq, dim) + dim * row_bytes(tq, hid))
+    out["ep_moe"] = {"shape": f"c5 MoE layer: E={E} top-{k}, dim {dim}, I {hid}, Q4_K; {T_rank} tokens per rank, "
+                              f"experts split {world} ways",
+                     "us_per_layer": round(ms_moe * 1e3, 2),
+                     "tokens_per_s_aggregate": round(T_rank * world / (ms_moe / 1e3), 1),
+                     "expert_GBs_aggregate": round(ebytes / (ms_moe / 1e3) / 1e9, 1),
+                     "pairs_sent_rank0": st.get("pairs_sent"), "dispatch_bytes_rank0": st.get("dispatch_bytes"),
+                     "return_bytes_rank0": st.get("return_bytes"),
+                     "bit_exact_vs_1gpu": bool(flag.item()),
+                     "collective": "all_to_all_single x4 (counts, Q8_0 rows, expert ids, per-pair outputs; NCCL)"}
+    return out
 
 
 # ------------------------------------------------------------- decode --
@@ -644,6 +776,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-c1", action="store_true", help="skip the c1 Q8_0 GEMV line")
     ap.add_argument("--no-decode", action="store_true", help="skip the c3 decode line")
+    ap.add_argument("--no-sharded", action="store_true", help="skip the tensor/expert-parallel forms")
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")

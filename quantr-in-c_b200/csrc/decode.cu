@@ -10,14 +10,15 @@
 //                 (src/kernels.c:179-189: sequential sum of squares)
 //   Q/K/V         one GEMV program over xb (csrc/engine.cu for one token,
 //                 csrc/tc.cu tensor cores for 2-64)
-//   rope + store  adjacent-pair rotation from a cos/sin table, K/V rows into
-//                 the cache (src/runtime.c:19-41, 74-92, 129-132)
-//   scores        q.k per (head, position), * 1/sqrt(head_dim) (:139-157)
+//   scores        RoPE (adjacent pairs, cos/sin table; src/runtime.c:19-41)
+//                 fused with the K/V store (:74-92, 129-132) and q.k per
+//                 (head, position) * 1/sqrt(head_dim) (:139-157)
 //   softmax + V   per KV head: max, expf, sequential sum, normalise, value
 //                 rows accumulated position by position (:159-194)
 //   O             GEMV program -> delta; rmsnorm (x += delta)
-//   FFN           dense: W1/W3 program, silu(h1)*h3, W2 program -> delta
-//                 (:270-284); MoE: route/experts/combine stages
+//   FFN           dense: W1/W3 program, W2 program whose activation quantizer
+//                 forms silu(h1)*h3 -> delta (:270-284); MoE: route/experts/
+//                 combine stages
 //                 (csrc/moe.cu, :202-269), plus the optional shared expert
 // then the final rmsnorm, the head GEMV (:286-287) and the greedy pick
 // (src/sampling.c:125-131).  Every floating-point operation is the
@@ -30,6 +31,7 @@
 #include "quantr_cuda.h"
 
 #include "device_common.cuh"
+#include "engine_act.cuh"
 #include "formats.cuh"
 #include "kernels.cuh"
 #include "launch_util.cuh"
@@ -57,6 +59,22 @@ struct Ctl {
     int dstep;  // decode steps taken
     int ring;   // capacity (steps) of the output ring
 };
+
+// Up to three engine activation layouts to write an output into (one per
+// element order the next program's weight types need); n = 0: none, the next
+// program quantizes its input itself.
+struct Tgts {
+    int n;
+    ActTarget t[3];
+};
+
+// Block b (32 elements, one warp, lane = element) of token t of an output
+// that feeds a GEMV program: quantized straight into the program's layout.
+__device__ __forceinline__ void tgts_write(const Tgts& tg, int t, int b, int lane, float v)
+{
+    for (int k = 0; k < tg.n; ++k)
+        if (b < tg.t[k].U) act_write_block(tg.t[k].act, tg.t[k].ds_off, tg.t[k].U, tg.t[k].type, t, b, lane, v);
+}
 
 struct Dims {
     int B, dim, q_dim, kv_dim, hd, n_heads, n_kv, kv_mul, seq_len, hidden, vocab, kv_type;
@@ -108,46 +126,97 @@ __global__ void k_embed(float* __restrict__ x, const int* __restrict__ tok, cons
     }
 }
 
+// s = ((s + p[0]) + p[1]) + ... in fp32, left to right: the reference's
+// accumulation order.  The additions form one dependent chain; loads are
+// issued eight at a time ahead of the adds that consume them.
+__device__ __forceinline__ float chain_sum(const float* __restrict__ p, int n, float s = 0.0f)
+{
+    int i = 0;
+    for (; i + 8 <= n; i += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = p[i + k];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+    }
+    for (; i < n; ++i) s = __fadd_rn(s, p[i]);
+    return s;
+}
+
 // x += delta (if given), out = rmsnorm(x) * w, per sequence (one CTA each).
 // src/kernels.c:179-189: ss accumulated left to right, ss/size + 1e-5,
-// 1/sqrtf, o = w * (x * scale).
+// 1/sqrtf, o = w * (x * scale).  dim % 4 == 0.  Every global access is
+// issued in one round (float4, all threads) and the rest runs out of shared
+// memory: the weight vector before the dependency wait, x (+ delta) after it;
+// one thread then walks the sum of squares while the others wait.
 __global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const float* __restrict__ delta,
-                                                 const float* __restrict__ w, float* __restrict__ out, int dim)
+                                                 const float* __restrict__ w, float* __restrict__ out, int dim,
+                                                 const __grid_constant__ Tgts tg)
 {
-    extern __shared__ float4 sq4[];
-    float* sq = reinterpret_cast<float*>(sq4);
+    extern __shared__ float4 sm4[];  // xs[dim] | ws[dim]
     __shared__ float s_scale;
+    const int n4 = dim >> 2;
+    float4* xs4 = sm4;
+    float4* ws4 = sm4 + n4;
+    const float* xs = reinterpret_cast<const float*>(xs4);
+    const float* wsm = reinterpret_cast<const float*>(ws4);
+    const int b = blockIdx.x;
+    const float4* w4 = reinterpret_cast<const float4*>(w);
+#pragma unroll 4
+    for (int k = threadIdx.x; k < n4; k += blockDim.x) ws4[k] = w4[k];
     pdl_wait();
     pdl_trigger();
-    const int b = blockIdx.x;
-    float* xr = x + (long long)b * dim;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x) {
-        float v = xr[i];
+    float4* x4 = reinterpret_cast<float4*>(x + (long long)b * dim);
+    const float4* d4 = reinterpret_cast<const float4*>(delta + (long long)b * dim);
+#pragma unroll 4
+    for (int k = threadIdx.x; k < n4; k += blockDim.x) {
+        float4 v = x4[k];
         if (delta) {
-            v = __fadd_rn(v, delta[(long long)b * dim + i]);
-            xr[i] = v;
+            const float4 dv = d4[k];
+            v.x = __fadd_rn(v.x, dv.x);
+            v.y = __fadd_rn(v.y, dv.y);
+            v.z = __fadd_rn(v.z, dv.z);
+            v.w = __fadd_rn(v.w, dv.w);
+            x4[k] = v;
         }
-        sq[i] = __fmul_rn(v, v);
+        xs4[k] = v;
     }
     __syncthreads();
     if (threadIdx.x == 0) {
         float ss = 0.0f;
-        int i = 0;
-        for (; i + 4 <= dim; i += 4) {
-            const float4 v = sq4[i >> 2];
-            ss = __fadd_rn(ss, v.x);
-            ss = __fadd_rn(ss, v.y);
-            ss = __fadd_rn(ss, v.z);
-            ss = __fadd_rn(ss, v.w);
+        int k = 0;
+        for (; k + 8 <= n4; k += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) v[u] = xs4[k + u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                ss = __fadd_rn(ss, __fmul_rn(v[u].x, v[u].x));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].y, v[u].y));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].z, v[u].z));
+                ss = __fadd_rn(ss, __fmul_rn(v[u].w, v[u].w));
+            }
         }
-        for (; i < dim; ++i) ss = __fadd_rn(ss, sq[i]);
+        for (int i = 4 * k; i < dim; ++i) ss = __fadd_rn(ss, __fmul_rn(xs[i], xs[i]));
         ss = __fadd_rn(__fdiv_rn(ss, (float)dim), 1e-5f);
         s_scale = __fdiv_rn(1.0f, __fsqrt_rn(ss));
     }
     __syncthreads();
     const float sc = s_scale;
-    for (int i = threadIdx.x; i < dim; i += blockDim.x)
-        out[(long long)b * dim + i] = __fmul_rn(w[i], __fmul_rn(xr[i], sc));
+    if (tg.n == 0) {
+        for (int i = threadIdx.x; i < dim; i += blockDim.x)
+            out[(long long)b * dim + i] = __fmul_rn(wsm[i], __fmul_rn(xs[i], sc));
+        return;
+    }
+    // Warp per 32-element block: the normalised values also go, quantized,
+    // into the next program's activation layout.
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int blk = warp; blk < (dim + 31) / 32; blk += nw) {
+        const int i = blk * 32 + lane;
+        const float v = i < dim ? __fmul_rn(wsm[i], __fmul_rn(xs[i], sc)) : 0.0f;
+        if (i < dim) out[(long long)b * dim + i] = v;
+        if (blk < dim / 32) tgts_write(tg, b, blk, lane, v);
+    }
 }
 
 __device__ __forceinline__ void kv_put(void* cache, int kv_type, long long idx, float v)
@@ -157,46 +226,43 @@ __device__ __forceinline__ void kv_put(void* cache, int kv_type, long long idx, 
     else
         reinterpret_cast<float*>(cache)[idx] = v;
 }
+// The value a cache of this type returns for v (the fp16 cache stores the
+// reference's truncated half, src/runtime.c:74-92).
+__device__ __forceinline__ float kv_round(int kv_type, float v) { return kv_type == 1 ? h2f_ref(f2h_ref(v)) : v; }
 __device__ __forceinline__ float kv_get(const void* cache, int kv_type, long long idx)
 {
     return kv_type == 1 ? h2f_ref(reinterpret_cast<const uint16_t*>(cache)[idx])
                         : reinterpret_cast<const float*>(cache)[idx];
 }
 
-// RoPE on q (all q_dim elements) and k (the first kv_dim), then k and v into
-// the cache at the sequence's position (src/runtime.c:19-41, 129-132).
-__global__ void k_rope_store(float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
-                             const int* __restrict__ pos, const float2* __restrict__ rope, void* kcache,
-                             void* vcache, long long layer_off, Dims D)
-{
-    pdl_wait();
-    pdl_trigger();
-    const int b = blockIdx.y;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;  // pair index
-    if (2 * j >= D.q_dim) return;
-    const int i = 2 * j;
-    const int p = pos[b];
-    const float2 cs = rope[(long long)p * (D.q_dim / 2) + j];
-    float* qr = q + (long long)b * D.q_dim;
-    const float q0 = qr[i], q1 = qr[i + 1];
-    qr[i] = __fsub_rn(__fmul_rn(q0, cs.x), __fmul_rn(q1, cs.y));
-    qr[i + 1] = __fadd_rn(__fmul_rn(q0, cs.y), __fmul_rn(q1, cs.x));
-    if (i < D.kv_dim) {
-        const float k0 = kc[(long long)b * D.kv_dim + i], k1 = kc[(long long)b * D.kv_dim + i + 1];
-        const long long row = layer_off + ((long long)b * D.seq_len + p) * D.kv_dim;
-        kv_put(kcache, D.kv_type, row + i, __fsub_rn(__fmul_rn(k0, cs.x), __fmul_rn(k1, cs.y)));
-        kv_put(kcache, D.kv_type, row + i + 1, __fadd_rn(__fmul_rn(k0, cs.y), __fmul_rn(k1, cs.x)));
-        kv_put(vcache, D.kv_type, row + i, vc[(long long)b * D.kv_dim + i]);
-        kv_put(vcache, D.kv_type, row + i + 1, vc[(long long)b * D.kv_dim + i + 1]);
-    }
-}
-
 constexpr int kScoreTile = 32;  // positions per CTA
 
-// att[b][h][t] = dot_ref(q_h, k_t) * (1/sqrt(head_dim)) for the kv_mul query
-// heads of one KV head and 32 positions (src/runtime.c:139-157).  Threads:
-// x = position in the tile, y = query head of the group.
-__global__ void k_att_scores(const float* __restrict__ q, const void* __restrict__ kcache, long long layer_off,
+__device__ __forceinline__ void rot(float a, float b, float2 cs, float& o0, float& o1)
+{
+    o0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
+    o1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
+}
+
+// KV cache layout (head-major): element i of head kh at position t of
+// sequence b in layer l is at layer_off + ((b*n_kv + kh)*seq_len + t)*hd + i,
+// so the rows of one head are contiguous across positions (one bulk copy per
+// tile of positions).  Values match the reference's cache element for
+// element (src/runtime.c:129-132, 143, 181), only the addresses differ.
+__device__ __forceinline__ long long kv_head_base(const Dims& D, long long layer_off, int b, int kh)
+{
+    return layer_off + ((long long)b * D.n_kv + kh) * D.seq_len * D.hd;
+}
+
+// RoPE (src/runtime.c:19-41) fused with the scores (:139-157): each CTA
+// rotates the kv_mul query heads of its KV head (the whole query is rotated,
+// adjacent pairs, cos/sin from the table), loads 32 cached key rows, and the
+// CTA whose tile holds the current position rotates that position's key and
+// stores the key and value rows into the cache (:129-132).  Then
+// att[b][h][t] = dot_ref(q_h, k_t) * (1/sqrt(head_dim)).  Threads: x = position
+// in the tile, y = query head of the group.
+template <int KVT>
+__global__ void k_att_scores(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+                             const float2* __restrict__ rope, void* kcache, void* vcache, long long layer_off,
                              const int* __restrict__ pos, float* __restrict__ att, Dims D)
 {
     extern __shared__ float sm[];
@@ -211,26 +277,76 @@ __global__ void k_att_scores(const float* __restrict__ q, const void* __restrict
     float* Qs = sm + kScoreTile * ld;
     const int nthr = blockDim.x * blockDim.y, tid = threadIdx.y * blockDim.x + threadIdx.x;
     const int nt = min(kScoreTile, p - t0 + 1);
-    for (int e = tid; e < nt * hd; e += nthr) {
-        const int tt = e / hd, i = e % hd;
-        Ks[tt * ld + i] = kv_get(kcache, D.kv_type,
-                                 layer_off + ((long long)b * D.seq_len + t0 + tt) * D.kv_dim + (long long)kh * hd + i);
+    const float2* rp = rope + (long long)p * (D.q_dim / 2);
+    const long long q0 = (long long)b * D.q_dim + (long long)kh * D.kv_mul * hd;
+    const bool here = p < t0 + kScoreTile;  // this tile holds the current position
+    const long long hb = kv_head_base(D, layer_off, b, kh);
+    // Cached rows t0 .. (here ? p-1 : t0+nt-1): contiguous, 16-byte words.
+    const int ncached = nt - (here ? 1 : 0);
+    constexpr int EPW = KVT ? 8 : 4;  // elements per 16-byte word
+    const int words = ncached * hd / EPW;
+    const uint4* src = reinterpret_cast<const uint4*>(static_cast<const unsigned char*>(kcache) +
+                                                      (hb + (long long)t0 * hd) * (KVT ? 2 : 4));
+#pragma unroll 4
+    for (int wd = tid; wd < words; wd += nthr) {
+        const uint4 v = src[wd];
+        const int e = wd * EPW, tt = e / hd, i = e % hd;
+        float* dst = Ks + tt * ld + i;
+        if (KVT) {
+            const uint32_t h[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                dst[2 * k] = h2f_ref(h[k] & 0xFFFFu);
+                dst[2 * k + 1] = h2f_ref(h[k] >> 16);
+            }
+        } else {
+            dst[0] = __uint_as_float(v.x);
+            dst[1] = __uint_as_float(v.y);
+            dst[2] = __uint_as_float(v.z);
+            dst[3] = __uint_as_float(v.w);
+        }
     }
-    for (int e = tid; e < D.kv_mul * hd; e += nthr)
-        Qs[e] = q[(long long)b * D.q_dim + (long long)kh * D.kv_mul * hd + e];
+    for (int e = 2 * tid; e < D.kv_mul * hd; e += 2 * nthr) {
+        float o0, o1;
+        rot(q[q0 + e], q[q0 + e + 1], rp[(kh * D.kv_mul * hd + e) >> 1], o0, o1);
+        Qs[e] = o0;
+        Qs[e + 1] = o1;
+    }
+    if (here) {
+        const long long kb = (long long)b * D.kv_dim + (long long)kh * hd;
+        const long long row = hb + (long long)p * hd;
+        for (int i = 2 * tid; i < hd; i += 2 * nthr) {
+            float o0, o1;
+            rot(kc[kb + i], kc[kb + i + 1], rp[(kh * hd + i) >> 1], o0, o1);
+            Ks[(p - t0) * ld + i] = kv_round(KVT, o0);
+            Ks[(p - t0) * ld + i + 1] = kv_round(KVT, o1);
+            kv_put(kcache, KVT, row + i, o0);
+            kv_put(kcache, KVT, row + i + 1, o1);
+            kv_put(vcache, KVT, row + i, vc[kb + i]);
+            kv_put(vcache, KVT, row + i + 1, vc[kb + i + 1]);
+        }
+    }
     __syncthreads();
     const int tt = threadIdx.x, m = threadIdx.y;
     if (tt < nt && m < D.kv_mul) {
         const float* kr = Ks + tt * ld;
         const float* qh = Qs + m * hd;
         float s = 0.0f;
-        for (int i = 0; i < hd; ++i) s = __fadd_rn(s, __fmul_rn(qh[i], kr[i]));
+        int i = 0;
+        for (; i + 8 <= hd; i += 8) {
+            float pr[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) pr[k] = __fmul_rn(qh[i + k], kr[i + k]);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) s = __fadd_rn(s, pr[k]);
+        }
+        for (; i < hd; ++i) s = __fadd_rn(s, __fmul_rn(qh[i], kr[i]));
         const int h = kh * D.kv_mul + m;
         att[((long long)b * D.n_heads + h) * D.seq_len + t0 + tt] = __fmul_rn(s, D.inv_sqrt);
     }
 }
 
-constexpr int kVTile = 32;    // value rows per pipeline stage
+constexpr int kVTile = 64;    // value rows per pipeline stage
 constexpr int kVStages = 3;   // stages in flight
 
 // Per (sequence, KV head): softmax_ref of each query head's scores
@@ -242,7 +358,8 @@ constexpr int kVStages = 3;   // stages in flight
 // and the rows are read from memory once per KV head.
 template <int KVT>
 __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __restrict__ vcache, long long layer_off,
-                                const int* __restrict__ pos, float* __restrict__ xa, int* err, Dims D)
+                                const int* __restrict__ pos, float* __restrict__ xa, int* err, Dims D,
+                                const __grid_constant__ Tgts tg)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
     __shared__ __align__(8) uint64_t bars[kVStages];
@@ -266,19 +383,18 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
     pdl_trigger();
     const int p = pos[b], np = p + 1;
     const int ntiles = (np + kVTile - 1) / kVTile;
-    const unsigned char* vrow0 = static_cast<const unsigned char*>(vcache) +
-                                 (layer_off + (long long)b * D.seq_len * D.kv_dim + (long long)kh * hd) * ES;
-    const long long vstride = (long long)D.kv_dim * ES;
+    // The head's value rows are contiguous: one bulk copy per tile.
+    const unsigned char* vrow0 =
+        static_cast<const unsigned char*>(vcache) + kv_head_base(D, layer_off, b, kh) * ES;
     auto issue = [&](int j) {  // one thread: tile j's rows into stage j % kVStages
         const int st = j % kVStages, t0 = j * kVTile, nt = min(kVTile, np - t0);
         mbar_arrive_expect_tx(&bars[st], (uint32_t)(nt * row_bytes));
-        for (int r = 0; r < nt; ++r)
-            bulk_g2s(vring + st * stage_bytes + r * row_bytes, vrow0 + (long long)(t0 + r) * vstride,
-                     (uint32_t)row_bytes, &bars[st]);
+        bulk_g2s(vring + st * stage_bytes, vrow0 + (long long)t0 * row_bytes, (uint32_t)(nt * row_bytes), &bars[st]);
     };
     if (tid == 0)
         for (int j = 0; j < min(kVStages, ntiles); ++j) issue(j);
 
+#pragma unroll 4
     for (int e = tid; e < D.kv_mul * np; e += blockDim.x) {
         const int m = e / np, t = e % np;
         S[m * D.seq_len + t] = att[((long long)b * D.n_heads + kh * D.kv_mul + m) * D.seq_len + t];
@@ -295,11 +411,7 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
         for (int t = lane; t < np; t += 32) s[t] = libm::expf_ref(__fsub_rn(s[t], mx));
         __syncwarp();
         float inv = 0.0f;
-        if (lane == 0) {
-            float sum = 0.0f;
-            for (int t = 0; t < np; ++t) sum = __fadd_rn(sum, s[t]);
-            inv = __fdiv_rn(1.0f, sum);
-        }
+        if (lane == 0) inv = __fdiv_rn(1.0f, chain_sum(s, np));
         inv = __shfl_sync(0xffffffffu, inv, 0);
         for (int t = lane; t < np; t += 32) s[t] = __fmul_rn(s[t], inv);
     }
@@ -321,21 +433,32 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
         if (s_abort) break;
         const int t0 = j * kVTile, nt = min(kVTile, np - t0);
         const unsigned char* vt = vring + st * stage_bytes;
-        if (e0 < nout) {
-            const float* sp = S + m0 * D.seq_len + t0;
-            for (int r = 0; r < nt; ++r) {
-                const float v = KVT ? h2f_ref(reinterpret_cast<const uint16_t*>(vt + r * row_bytes)[i0])
-                                    : reinterpret_cast<const float*>(vt + r * row_bytes)[i0];
-                acc0 = __fadd_rn(acc0, __fmul_rn(sp[r], v));
+        // Both running sums advance position by position; their products are
+        // formed eight positions ahead of the dependent adds.
+        const bool h0 = e0 < nout, h1 = e1 < nout;
+        const float* sp0 = S + (h0 ? m0 : 0) * D.seq_len + t0;
+        const float* sp1 = S + (h1 ? m1 : 0) * D.seq_len + t0;
+        auto vat = [&](int r, int i) {
+            return KVT ? h2f_ref(reinterpret_cast<const uint16_t*>(vt + r * row_bytes)[i])
+                       : reinterpret_cast<const float*>(vt + r * row_bytes)[i];
+        };
+        int r = 0;
+        for (; r + 8 <= nt; r += 8) {
+            float p0[8], p1[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                p0[k] = h0 ? __fmul_rn(sp0[r + k], vat(r + k, i0)) : 0.0f;
+                p1[k] = h1 ? __fmul_rn(sp1[r + k], vat(r + k, i1)) : 0.0f;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                acc0 = __fadd_rn(acc0, p0[k]);
+                acc1 = __fadd_rn(acc1, p1[k]);
             }
         }
-        if (e1 < nout) {
-            const float* sp = S + m1 * D.seq_len + t0;
-            for (int r = 0; r < nt; ++r) {
-                const float v = KVT ? h2f_ref(reinterpret_cast<const uint16_t*>(vt + r * row_bytes)[i1])
-                                    : reinterpret_cast<const float*>(vt + r * row_bytes)[i1];
-                acc1 = __fadd_rn(acc1, __fmul_rn(sp[r], v));
-            }
+        for (; r < nt; ++r) {
+            if (h0) acc0 = __fadd_rn(acc0, __fmul_rn(sp0[r], vat(r, i0)));
+            if (h1) acc1 = __fadd_rn(acc1, __fmul_rn(sp1[r], vat(r, i1)));
         }
         __syncthreads();  // stage st is free again
         if (tid == 0 && j + kVStages < ntiles) {
@@ -353,16 +476,12 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
     }
     if (e0 < nout) xa[(long long)b * D.q_dim + (long long)(kh * D.kv_mul + m0) * hd + i0] = acc0;
     if (e1 < nout) xa[(long long)b * D.q_dim + (long long)(kh * D.kv_mul + m1) * hd + i1] = acc1;
-}
-
-// h1 = silu(h1) * h3 (src/runtime.c:15-17, 277-279).
-__global__ void k_silu_mul(float* __restrict__ h1, const float* __restrict__ h3, long long n)
-{
-    pdl_wait();
-    pdl_trigger();
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-        const float v = h1[i];
-        h1[i] = __fmul_rn(__fdiv_rn(v, __fadd_rn(1.0f, libm::expf_ref(-v))), h3[i]);
+    // With head_dim a multiple of 32 a warp holds one whole 32-element block
+    // of the attention output: quantize it for the O projection here.
+    if (tg.n) {
+        const int g0 = kh * D.kv_mul * hd;  // first output element of this KV head
+        if (e0 - lane + 31 < nout) tgts_write(tg, b, (g0 + e0) >> 5, lane, acc0);
+        if (e1 - lane + 31 < nout) tgts_write(tg, b, (g0 + e1) >> 5, lane, acc1);
     }
 }
 
@@ -495,6 +614,10 @@ struct quantr_decoder {
     // plans
     std::vector<quantr_program*> p_qkv, p_o, p_ffn13, p_w2, p_sh13, p_sh2;
     quantr_program* p_head = nullptr;
+    // Activation layouts the norm / attention kernels quantize into directly
+    // (one-token decoders; n = 0 where the program quantizes its own input).
+    std::vector<Tgts> t_qkv, t_o, t_ffn;
+    Tgts t_head{};
     cudaStream_t stream = nullptr;
     cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
     int nodes_decode = 0, nodes_prefill = 0;
@@ -569,6 +692,7 @@ struct ProgJob {
     long long ldx;
     float* out;
     long long ldo;
+    const float* xmul = nullptr;  // input silu(x) * xmul (the down projection's SwiGLU)
 };
 
 // Threads of the softmax/value kernel: each owns one or two running sums.
@@ -585,9 +709,12 @@ size_t att_v_smem(const Dims& D)
 int make_program(quantr_decoder* d, const std::vector<ProgJob>& js, quantr_program** out)
 {
     std::vector<quantr_gemv_job> jobs;
-    for (const ProgJob& j : js)
+    std::vector<const float*> xm;
+    for (const ProgJob& j : js) {
         jobs.push_back(quantr_gemv_job{j.w, j.type, j.n, j.d, d->D.B, j.x, j.ldx, j.out, j.ldo});
-    return quantr_program_create(out, jobs.data(), (int)jobs.size());
+        xm.push_back(j.xmul);
+    }
+    return program_create_ex(out, jobs.data(), xm.data(), (int)jobs.size());
 }
 
 // Enqueues one step on `s`.  with_head: final norm, head GEMV and greedy pick.
@@ -601,37 +728,32 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
     if (e == cudaSuccess)
         e = launch_ex(&k_embed, dim3((D.dim + 255) / 256, D.B), dim3(256), 0, c, d->x, (const int*)d->tok, d->embd,
                       d->embd_type, d->embd_rb, D.dim, D.vocab);
-    const size_t norm_smem = (size_t)(D.dim + 4) * sizeof(float);
+    const size_t norm_smem = (size_t)2 * D.dim * sizeof(float);
     const long long layer_kv = (long long)D.B * D.seq_len * D.kv_dim;
     for (int l = 0; l < d->n_layers && e == cudaSuccess; ++l) {
         const long long loff = (long long)l * layer_kv;
         e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)(l ? d->delta : nullptr),
-                      d->rms_att[l], d->xb, D.dim);
+                      d->rms_att[l], d->xb, D.dim, d->t_qkv[l]);
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_qkv[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
-        e = launch_ex(&k_rope_store, dim3((D.q_dim / 2 + 127) / 128, D.B), dim3(128), 0, c, d->q,
-                      (const float*)d->kc, (const float*)d->vc, (const int*)d->pos, (const float2*)d->rope,
-                      d->kcache, d->vcache, loff, D);
-        if (e != cudaSuccess) break;
         const size_t ssm = (size_t)(kScoreTile * (D.hd + 1) + D.kv_mul * D.hd) * sizeof(float);
-        e = launch_ex(&k_att_scores, dim3(D.B * D.n_kv, (D.seq_len + kScoreTile - 1) / kScoreTile),
-                      dim3(kScoreTile, D.kv_mul), ssm, c, (const float*)d->q, (const void*)d->kcache, loff,
-                      (const int*)d->pos, d->att, D);
+        e = launch_ex(D.kv_type ? &k_att_scores<1> : &k_att_scores<0>,
+                      dim3(D.B * D.n_kv, (D.seq_len + kScoreTile - 1) / kScoreTile),
+                      dim3(kScoreTile, D.kv_mul), ssm, c, (const float*)d->q, (const float*)d->kc,
+                      (const float*)d->vc, (const float2*)d->rope, d->kcache, d->vcache, loff, (const int*)d->pos,
+                      d->att, D);
         if (e != cudaSuccess) break;
         e = launch_ex(D.kv_type ? &k_att_softmax_v<1> : &k_att_softmax_v<0>, dim3(D.B * D.n_kv),
                       dim3(att_v_threads(D)), att_v_smem(D), c, (const float*)d->att, (const void*)d->vcache, loff,
-                      (const int*)d->pos, d->xa, device_error_word(), D);
+                      (const int*)d->pos, d->xa, device_error_word(), D, d->t_o[l]);
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_o[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
         e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)d->delta, d->rms_ffn[l],
-                      d->xb, D.dim);
+                      d->xb, D.dim, d->t_ffn[l]);
         if (e != cudaSuccess) break;
         if (d->E == 0) {
             if (quantr_program_run(d->p_ffn13[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
-            const long long n = (long long)D.B * D.hidden;
-            e = launch_ex(&k_silu_mul, dim3((unsigned)std::min<long long>((n + 255) / 256, 4096)), dim3(256), 0, c,
-                          d->hb, (const float*)d->hb2, n);
-            if (e != cudaSuccess) break;
+            // W2's activation quantizer forms silu(h1) * h3 itself.
             if (quantr_program_run(d->p_w2[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
         } else {
             int* err = device_error_word();
@@ -673,10 +795,6 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
             if (e != cudaSuccess) break;
             if (d->shexp) {
                 if (quantr_program_run(d->p_sh13[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
-                const long long n = (long long)D.B * d->shexp;
-                e = launch_ex(&k_silu_mul, dim3((unsigned)std::min<long long>((n + 255) / 256, 4096)), dim3(256), 0,
-                              c, d->hb, (const float*)d->hb2, n);
-                if (e != cudaSuccess) break;
                 if (quantr_program_run(d->p_sh2[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
                 e = launch_gemv_f32(d->sh_gate[l], d->xb, D.dim, d->gdot, 1, 1, D.dim, D.B, c);
                 if (e != cudaSuccess) break;
@@ -688,7 +806,7 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
     }
     if (e == cudaSuccess && with_head) {
         e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)d->delta, d->rms_final,
-                      d->xb, D.dim);
+                      d->xb, D.dim, d->t_head);
         if (e == cudaSuccess && quantr_program_run(d->p_head, s) != QUANTR_OK) return QUANTR_ERR_CUDA;
         if (e == cudaSuccess)
             e = launch_ex(&k_argmax, dim3(D.B), dim3(1024), 0, c, (const float*)d->logits, (long long)D.vocab,
@@ -794,8 +912,8 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
     d->E = m->expert_count;
     d->K = m->expert_used_count;
     d->shexp = m->expert_count > 0 && m->shexp_w1 ? m->shexp_hidden_dim : 0;
-    if (D.kv_mul > 32 || att_v_smem(D) > kSmemMax || D.kv_mul * hd > 2048 || (hd * (D.kv_type ? 2 : 4)) % 16 ||
-        (size_t)(kScoreTile * (hd + 1) + D.kv_mul * hd) * 4 > kSmemMax || (size_t)(D.dim + 4) * 4 > 48 * 1024) {
+    if (D.kv_mul > 32 || att_v_smem(D) > kSmemMax || D.kv_mul * hd > 2048 || (hd * (D.kv_type ? 2 : 4)) % 16 || hd % 8 ||
+        (size_t)(kScoreTile * (hd + 1) + D.kv_mul * hd) * 4 > kSmemMax || (size_t)2 * D.dim * 4 > 48 * 1024 || D.dim % 4) {
         delete d;
         return QUANTR_ERR_TOO_LARGE;
     }
@@ -881,6 +999,10 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
             if (d->shexp) ok = ok && s1[l] && s2[l] && s3[l] && d->sh_gate[l];
         }
     }
+    // The norm kernels read the norm weights as 16-byte words.
+    for (int l = 0; l < L && ok; ++l)
+        ok = !((uintptr_t)d->rms_att[l] & 15) && !((uintptr_t)d->rms_ffn[l] & 15);
+    ok = ok && !((uintptr_t)d->rms_final & 15);
     if (!ok) return fail(QUANTR_ERR_BAD_ARG);
 
     // ---- activations, caches, tables ----
@@ -976,7 +1098,7 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
                               &p);
             if (rc) return fail(rc);
             d->p_ffn13.push_back(p);
-            rc = make_program(d, {{w2[l], m->w2_type[l], m->dim, hid, d->hb, hid, d->delta, m->dim}}, &p);
+            rc = make_program(d, {{w2[l], m->w2_type[l], m->dim, hid, d->hb, hid, d->delta, m->dim, d->hb2}}, &p);
             if (rc) return fail(rc);
             d->p_w2.push_back(p);
         } else if (d->shexp) {
@@ -986,7 +1108,7 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
                               &p);
             if (rc) return fail(rc);
             d->p_sh13.push_back(p);
-            rc = make_program(d, {{s2[l], m->shexp_w2_type[l], m->dim, sh, d->hb, sh, d->sh, m->dim}}, &p);
+            rc = make_program(d, {{s2[l], m->shexp_w2_type[l], m->dim, sh, d->hb, sh, d->sh, m->dim, d->hb2}}, &p);
             if (rc) return fail(rc);
             d->p_sh2.push_back(p);
         }
@@ -996,6 +1118,26 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
                               &d->p_head);
         if (rc) return fail(rc);
     }
+    // One-token decoders: the kernels producing the inputs of the Q/K/V, O,
+    // W1/W3 and head programs quantize them straight into the engine's
+    // layout, and those programs skip their own quantizer launch.
+    auto external = [&](quantr_program* p, const float* x) {
+        Tgts t{};
+        if (B != 1 || !p) return t;
+        const int n = program_act_targets(p, x, t.t, 3);
+        if (n > 0 && program_external_quant(p, true) == QUANTR_OK) t.n = n;
+        return t;
+    };
+    d->t_qkv.assign(L, Tgts{});
+    d->t_o.assign(L, Tgts{});
+    d->t_ffn.assign(L, Tgts{});
+    for (int l = 0; l < L; ++l) {
+        d->t_qkv[l] = external(d->p_qkv[l], d->xb);
+        if (hd % 32 == 0) d->t_o[l] = external(d->p_o[l], d->xa);
+        if (d->E == 0) d->t_ffn[l] = external(d->p_ffn13[l], d->xb);
+    }
+    d->t_head = external(d->p_head, d->xb);
+
     // Per-step bytes: every linear once, norms, one embedding row per sequence.
     size_t wb = 0;
     for (int l = 0; l < L; ++l) {
@@ -1015,7 +1157,8 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
     {
         const int ssm = (kScoreTile * (hd + 1) + D.kv_mul * hd) * 4;
         const int vsm = (int)att_v_smem(D);
-        if (cudaFuncSetAttribute(k_att_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) != cudaSuccess ||
+        if (cudaFuncSetAttribute(k_att_scores<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) != cudaSuccess ||
+            cudaFuncSetAttribute(k_att_scores<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) != cudaSuccess ||
             cudaFuncSetAttribute(k_att_softmax_v<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) !=
                 cudaSuccess ||
             cudaFuncSetAttribute(k_att_softmax_v<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) != cudaSuccess)

@@ -37,9 +37,11 @@
 #include "quantr_cuda.h"
 
 #include "device_common.cuh"
+#include "engine_act.cuh"
 #include "formats.cuh"
 #include "kernels.cuh"
 #include "launch_util.cuh"
+#include "libm_ref.cuh"
 #include "quant_decode.cuh"
 
 #include <algorithm>
@@ -134,6 +136,7 @@ static_assert(offsetof(ProgParams, inline_job) % 16 == 0, "inline job must be 16
 // One quantization task: B rows of fp32 x -> the compact act layout.
 struct QTask {
     const float* x;
+    const float* xmul;  // non-null: the input is silu(x) * xmul, elementwise
     uint8_t* act;
     long long ldx;
     long long blk0;  // first global block index of this task
@@ -148,13 +151,6 @@ struct QParams {
     QTask inline_task;
 };
 
-// Position of element e (0..31) of a unit in the permuted activation layout.
-__device__ __forceinline__ int perm_pos(uint32_t type, int e)
-{
-    if (type == T_Q4_K || type == T_Q5_K) return (e & ~7) + ((e & 1) << 2) + ((e & 7) >> 1);
-    if (type == T_Q6_K) return (e & ~15) + ((e & 3) << 2) + ((e & 15) >> 2);
-    return e;
-}
 
 // Integer -> float conversions of the consumers.  Every converted value is an
 // integer of magnitude below 2^22, so adding it to the bit pattern of
@@ -195,22 +191,9 @@ __global__ void __launch_bounds__(256) k_quant_tasks(const __grid_constant__ QPa
         const QTask& T = tasks[lo];
         const long long local = gb - T.blk0;
         const int t = (int)(local / T.U), b = (int)(local - (long long)t * T.U);
-        const float v = T.x[(long long)t * T.ldx + (long long)b * 32 + lane];
-        // Stored unit: K-quant activations go sub-block-major (block 8s+j of
-        // the row -> unit j*nsb + s) so consumer lanes on neighbouring
-        // super-blocks read neighbouring units; Q8_0 keeps block order.
-        const int u = T.type == T_Q8_0 ? b : (b & 7) * (T.U >> 3) + (b >> 3);
-        const float a = fabsf(v);
-        const uint32_t abits = (a == a) ? __float_as_uint(a) : 0u;  // the reference skips NaN
-        const float amax = __uint_as_float(__reduce_max_sync(0xffffffffu, abits));
-        const float dd = __fdiv_rn(amax, 127.0f);
-        const float id = (dd != 0.0f) ? __fdiv_rn(1.0f, dd) : 0.0f;
-        const int8_t qq = lrintf_to_i8(__fmul_rn(v, id));
-        const int sum = __reduce_add_sync(0xffffffffu, (int)qq);
-        T.act[((long long)t * T.U + u) * 32 + perm_pos(T.type, lane)] = (uint8_t)qq;
-        if (lane == 0)
-            reinterpret_cast<uint2*>(T.act + T.ds_off)[t * T.U + u] =
-                make_uint2(__float_as_uint(h2f_ref(f2h_ref(dd))), __float_as_uint((float)sum));
+        const long long xi = (long long)t * T.ldx + (long long)b * 32 + lane;
+        const float v = T.xmul ? libm::swiglu_ref(T.x[xi], T.xmul[xi]) : T.x[xi];
+        act_write_block(T.act, T.ds_off, T.U, T.type, t, b, lane, v);
     }
 }
 
@@ -599,6 +582,7 @@ struct JobIn {
     long long ldx;
     float* out;
     long long ldo;
+    const float* xmul = nullptr;  // input is silu(x) * xmul (same strides)
 };
 
 int units_of(uint32_t type, int d) { return (d / block_elems(type)) * block_units(type); }
@@ -684,7 +668,7 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
 {
     pl = Plan{};
     if (njobs <= 0) return QUANTR_ERR_BAD_ARG;
-    std::map<std::tuple<const float*, long long, int, int, int, int>, int> dedupe;  // x,ldx,d,B,U,perm -> task
+    std::map<std::tuple<const float*, const float*, long long, int, int, int, int>, int> dedupe;  // x,xmul,ldx,d,B,U,perm
     constexpr size_t kSlotW = QR_ENG_SLOT_KB * 1024, kTermMax = 16 * 1024;
     std::vector<JobDesc> all;
     for (int j = 0; j < njobs; ++j) {
@@ -720,12 +704,13 @@ int make_plan(const JobIn* in, int njobs, uint8_t* act_base, int sms, bool table
         R = std::min<long long>(R, ((a.n + gR - 1) / gR) * gR);
         J.R = (int)R;
         const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
-        auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, J.U, perm);
+        auto key = std::make_tuple(a.x, a.xmul, a.ldx, a.d, a.B, J.U, perm);
         auto it = dedupe.find(key);
         int ti;
         if (it == dedupe.end()) {
             QTask t{};
             t.x = a.x;
+            t.xmul = a.xmul;
             t.ldx = a.ldx;
             t.U = J.U;
             t.B = a.B;
@@ -797,7 +782,7 @@ cudaError_t launch_program(const SubPlan& sp, const ProgParams& pp, const Launch
 
 // Launches the quantizer over every task, then one engine launch per
 // sub-plan (a single job travels inline when the sub-plan has no table).
-cudaError_t launch_plan(Plan& pl, const QTask* d_tasks, int* err, cudaStream_t stream)
+cudaError_t launch_plan(Plan& pl, const QTask* d_tasks, int* err, cudaStream_t stream, bool skip_quant = false)
 {
     LaunchCfg c;
     c.stream = stream;
@@ -806,7 +791,7 @@ cudaError_t launch_plan(Plan& pl, const QTask* d_tasks, int* err, cudaStream_t s
     qp.tasks = d_tasks;
     if (!d_tasks) qp.inline_task = pl.tasks[0];
     const long long qgrid = std::max(1LL, std::min<long long>((qp.total_blocks + 7) / 8, 8LL * device_sm_count()));
-    e = launch_ex(&k_quant_tasks, dim3((unsigned)qgrid), dim3(256), 0, c, qp);
+    if (!skip_quant) e = launch_ex(&k_quant_tasks, dim3((unsigned)qgrid), dim3(256), 0, c, qp);
     for (auto& sp : pl.subs) {
         if (e != cudaSuccess) return e;
         ProgParams pp = sp.pp;
@@ -872,6 +857,7 @@ constexpr int kTcMinB = QR_TC_MIN_B;
 struct quantr_program {
     int device;
     bool has_engine = false;
+    bool external_quant = false;  // the engine's inputs are quantized by the caller
     qr::eng::Plan plan;  // sub-plans own their device job tables
     qr::eng::QTask* d_tasks = nullptr;
     uint8_t* d_act = nullptr;
@@ -882,6 +868,33 @@ extern "C" {
 
 int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int njobs)
 {
+    if (!out || !jobs || njobs <= 0) return QUANTR_ERR_BAD_ARG;
+    std::vector<const float*> none((size_t)njobs, nullptr);
+    return qr::program_create_ex(out, jobs, none.data(), njobs);
+}
+
+} // extern "C"
+
+int qr::program_act_targets(const quantr_program* p, const float* x, ActTarget* out, int max)
+{
+    if (!p || !p->has_engine) return 0;
+    int n = 0;
+    for (const eng::QTask& t : p->plan.tasks)
+        if (t.x == x && n < max) out[n++] = ActTarget{t.act, t.ds_off, t.U, t.B, t.type};
+    return n;
+}
+
+int qr::program_external_quant(quantr_program* p, bool on)
+{
+    if (!p || !p->has_engine || !p->tc.empty()) return QUANTR_ERR_BAD_ARG;
+    for (const eng::QTask& t : p->plan.tasks)
+        if (t.xmul || t.B != 1) return QUANTR_ERR_BAD_ARG;
+    p->external_quant = on;
+    return QUANTR_OK;
+}
+
+int qr::program_create_ex(quantr_program** out, const quantr_gemv_job* jobs, const float* const* xmul, int njobs)
+{
     using namespace qr;
     if (!out || !jobs || njobs <= 0) return QUANTR_ERR_BAD_ARG;
     *out = nullptr;
@@ -889,19 +902,25 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     std::vector<GemvJobIn> tcj;
     for (int j = 0; j < njobs; ++j) {
         const quantr_gemv_job& J = jobs[j];
+        const float* xm = xmul ? xmul[j] : nullptr;
         if (J.B > kTcMaxB && J.type != T_F32 && J.x && J.out && J.ldx >= J.d && J.ldo >= J.n) {
             // Wider jobs (a prefill chunk) run as kTcMaxB-token slices of the
             // same weights: tokens [b0, b0 + Bs) of x and out.
-            for (int b0 = 0; b0 < J.B; b0 += kTcMaxB)
-                tcj.push_back(GemvJobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d,
-                                        std::min(kTcMaxB, J.B - b0), J.x + (long long)b0 * J.ldx, J.ldx,
-                                        J.out + (long long)b0 * J.ldo, J.ldo});
-        } else if (J.B >= kTcMinB && J.B <= kTcMaxB && J.type != T_F32)
-            tcj.push_back(GemvJobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out,
-                                    J.ldo});
-        else
-            in.push_back(eng::JobIn{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out,
-                                    J.ldo});
+            for (int b0 = 0; b0 < J.B; b0 += kTcMaxB) {
+                GemvJobIn g{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, std::min(kTcMaxB, J.B - b0),
+                            J.x + (long long)b0 * J.ldx, J.ldx, J.out + (long long)b0 * J.ldo, J.ldo};
+                g.xmul = xm ? xm + (long long)b0 * J.ldx : nullptr;
+                tcj.push_back(g);
+            }
+        } else if (J.B >= kTcMinB && J.B <= kTcMaxB && J.type != T_F32) {
+            GemvJobIn g{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out, J.ldo};
+            g.xmul = xm;
+            tcj.push_back(g);
+        } else {
+            eng::JobIn e{static_cast<const uint8_t*>(J.w), J.type, J.n, J.d, J.B, J.x, J.ldx, J.out, J.ldo};
+            e.xmul = xm;
+            in.push_back(e);
+        }
     }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -962,6 +981,8 @@ int quantr_program_create(quantr_program** out, const quantr_gemv_job* jobs, int
     return QUANTR_OK;
 }
 
+extern "C" {
+
 int quantr_program_run(quantr_program* p, void* stream)
 {
     if (!p) return QUANTR_ERR_BAD_ARG;
@@ -970,7 +991,8 @@ int quantr_program_run(quantr_program* p, void* stream)
     if (dev != p->device) return QUANTR_ERR_BAD_ARG;
     int* err = qr::device_error_word();
     cudaError_t e = cudaSuccess;
-    if (p->has_engine) e = qr::eng::launch_plan(p->plan, p->d_tasks, err, static_cast<cudaStream_t>(stream));
+    if (p->has_engine)
+        e = qr::eng::launch_plan(p->plan, p->d_tasks, err, static_cast<cudaStream_t>(stream), p->external_quant);
     for (auto* tp : p->tc)
         if (e == cudaSuccess) e = qr::tc_plan_run(tp, err, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) {

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include "quantr_cuda.h"
+
 namespace qr {
 
 // Quantized activations in the layout the GEMV kernels read: for token t and
@@ -116,6 +118,9 @@ struct GemvJobIn {
     // and records ([U] x N x 16 bytes, tensor-core layout): x is unused.
     const uint8_t* act = nullptr;
     const uint8_t* ds = nullptr;
+    // Non-null: the GEMV input is silu(x) * xmul elementwise (the reference's
+    // SwiGLU product feeding the down projection), formed by the quantizer.
+    const float* xmul = nullptr;
 };
 
 // Plans a tensor-core program (B <= kTcMaxB per job, at most kTcMaxJobs
@@ -129,6 +134,28 @@ int tc_plan_create(const GemvJobIn* jobs, int njobs, TcPlan** out);
 cudaError_t tc_plan_run(TcPlan* plan, int* err, cudaStream_t stream);
 void tc_plan_destroy(TcPlan* plan);
 void tc_plan_info(const TcPlan* plan, int* items, int* grid, int* smem);
+
+// Where a program's persistent-engine jobs expect one input's quantized
+// activations: the engine layout of k_quant_tasks (int8 quants of unit u of
+// token t at act[(t*U + u)*32 + perm(type, e)], records (fp32 decoded scale,
+// fp32 quant sum) at act + ds_off, K-quant units stored sub-block-major).
+struct ActTarget {
+    uint8_t* act;
+    uint32_t ds_off;
+    int U, B, type;
+};
+// Targets of input x (one per element order the jobs reading x need); returns
+// how many (<= max).  0 when x is not an engine input of the program.
+int program_act_targets(const quantr_program* p, const float* x, ActTarget* out, int max);
+// When on, quantr_program_run skips the engine's activation quantizer: the
+// caller's kernel writes every target before the program runs.  Only for
+// programs whose every job runs on the engine (one token, no SwiGLU input).
+int program_external_quant(quantr_program* p, bool on);
+
+// quantr_program_create with, per job, an optional second input: a non-null
+// xmul[j] makes job j's input silu(x) * xmul (same shape and strides as x),
+// formed inside the activation quantizer.  xmul may be null (no job has one).
+int program_create_ex(quantr_program** out, const quantr_gemv_job* jobs, const float* const* xmul, int njobs);
 
 // ---- routed MoE block (moe.cu) ----
 

@@ -169,5 +169,13 @@ QR_HD float expf_ref(float x)
     return d2f(y);
 }
 
+#ifdef __CUDACC__
+// silu of the reference's runtime (src/runtime.c:15-17): x / (1 + expf(-x)).
+__device__ __forceinline__ float silu_ref(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, expf_ref(-x))); }
+// The reference's SwiGLU input to the down projection: silu(h1) * h3
+// (src/runtime.c:254-256, 277-279).
+__device__ __forceinline__ float swiglu_ref(float h1, float h3) { return __fmul_rn(silu_ref(h1), h3); }
+#endif
+
 } // namespace libm
 } // namespace qr

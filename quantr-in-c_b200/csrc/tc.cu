@@ -69,6 +69,7 @@
 #include "formats.cuh"
 #include "kernels.cuh"
 #include "launch_util.cuh"
+#include "libm_ref.cuh"
 #include "quant_decode.cuh"
 
 #include <algorithm>
@@ -283,6 +284,7 @@ __device__ __forceinline__ bool elect_one()
 
 struct TcQTask {
     const float* x;
+    const float* xmul;  // non-null: the input is silu(x) * xmul, elementwise
     uint8_t* act;
     uint8_t* ds;
     long long ldx;
@@ -358,6 +360,11 @@ __global__ void __launch_bounds__(256) k_tc_quant(const __grid_constant__ TcQPar
         } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = src[i];
+        }
+        if (T.xmul) {
+            const float* m3 = T.xmul + (long long)t * T.ldx + (long long)u * 32;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = libm::swiglu_ref(v[i], m3[i]);
         }
         // amax = max |x| over the block, NaN ignored (src/quant.c:149-152).
         uint32_t abits = 0;
@@ -1099,7 +1106,7 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
     cudaGetDevice(&P->device);
     // Activation tasks, one per distinct (x, ldx, d, B, element order); the
     // operand layout depends on the weight type only through that order.
-    std::map<std::tuple<const float*, long long, int, int, int>, int> dedupe;
+    std::map<std::tuple<const float*, const float*, long long, int, int, int>, int> dedupe;
     size_t act_total = 0;
     long long blocks = 0;
     int Nmax = 16, Bmax = 1, item = 0;
@@ -1163,12 +1170,13 @@ int tc_plan_create(const GemvJobIn* in, int njobs, TcPlan** out)
             continue;
         }
         const int perm = a.type == T_Q8_0 ? 0 : (a.type == T_Q6_K ? 2 : 1);
-        auto key = std::make_tuple(a.x, a.ldx, a.d, a.B, perm);
+        auto key = std::make_tuple(a.x, a.xmul, a.ldx, a.d, a.B, perm);
         auto it = dedupe.find(key);
         int ti;
         if (it == dedupe.end()) {
             TcQTask t{};
             t.x = a.x;
+            t.xmul = a.xmul;
             t.ldx = a.ldx;
             t.U = (int)J.U;
             t.B = a.B;
