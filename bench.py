@@ -54,7 +54,7 @@ import synth  # noqa: E402
 
 METRIC = "quantized GEMV HBM GB/s (% of 8 TB/s); decode tok/s at 1/2/4/8 B200 vs host CPU"
 HIDDEN, FFN, LAYERS = 896, 4864, 24
-Q8_0, Q4_K = 8, 12
+Q8_0, Q4_K, Q6_K = 8, 12, 14
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
 # DRAM bytes (read + write) of one k_program launch of the c2 step at batch 1
@@ -473,7 +473,20 @@ def ours_arm(args):
                "sample": (f"{done} full steps ({len(shapes)} GEMVs each, {el:.1f} s) of the same workload, "
                           f"reference src/quant.c {variant} build")}
 
-    sharded = None if args.no_sharded else sharded_forms(args, dev, world, rank)
+    sharded = None
+    if not args.no_sharded:
+        own_group = world == 1 and not dist.is_initialized()
+        if own_group:  # the forms run their collectives over a one-rank group
+            import datetime
+            import socket
+            with socket.socket() as so:
+                so.bind(("127.0.0.1", 0))
+                port = so.getsockname()[1]
+            dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                                    timeout=datetime.timedelta(seconds=120), device_id=dev)
+        sharded = sharded_forms(args, dev, world, rank)
+        if own_group:
+            dist.destroy_process_group()
     decode = None
     if rank == 0 and world == 1 and not args.no_decode:
         decode = decode_c3(args, dev, s)

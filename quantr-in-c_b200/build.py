@@ -17,9 +17,9 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "lib")
 LIB = os.path.join(LIBDIR, "libquantr_cuda.so")
-SOURCES = ["gemv.cu", "engine.cu", "tc.cu", "moe.cu", "api.cu", "noalloc.cu", "decode.cu"]
+SOURCES = ["gemv.cu", "engine.cu", "tc.cu", "moe.cu", "api.cu", "noalloc.cu", "decode.cu", "decode_persist.cu"]
 HEADERS = ["formats.cuh", "kernels.cuh", "device_common.cuh", "quant_decode.cuh", "launch_util.cuh",
-           "libm_ref.cuh"]
+           "libm_ref.cuh", "engine_act.cuh", "decode_persist.cuh"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -30,6 +30,7 @@
 // the functions the reference calls per token, and read from a table.
 #include "quantr_cuda.h"
 
+#include "decode_persist.cuh"
 #include "device_common.cuh"
 #include "engine_act.cuh"
 #include "formats.cuh"
@@ -40,6 +41,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -618,6 +620,13 @@ struct quantr_decoder {
     // (one-token decoders; n = 0 where the program quantizes its own input).
     std::vector<Tgts> t_qkv, t_o, t_ffn;
     Tgts t_head{};
+    // One-token dense models: every layer in one persistent kernel per step
+    // (decode_persist.cu); the head and the greedy pick follow as kernels.
+    bool persist = false;
+    uint32_t persist_type = 0;
+    int persist_grid = 0;
+    size_t persist_smem = 0;
+    dp::Params pp{};
     cudaStream_t stream = nullptr;
     cudaGraphExec_t g_decode = nullptr, g_prefill = nullptr;
     int nodes_decode = 0, nodes_prefill = 0;
@@ -725,12 +734,13 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
     c.stream = s;
     cudaError_t e = launch_ex(&k_feed, dim3(1), dim3(std::max(32, (D.B + 31) / 32 * 32)), 0, c, d->ctl, d->tok,
                               d->pos, (const int*)d->prompt, (const int*)d->next, D.B, D.seq_len);
-    if (e == cudaSuccess)
+    if (e == cudaSuccess && !d->persist)
         e = launch_ex(&k_embed, dim3((D.dim + 255) / 256, D.B), dim3(256), 0, c, d->x, (const int*)d->tok, d->embd,
                       d->embd_type, d->embd_rb, D.dim, D.vocab);
     const size_t norm_smem = (size_t)2 * D.dim * sizeof(float);
     const long long layer_kv = (long long)D.B * D.seq_len * D.kv_dim;
-    for (int l = 0; l < d->n_layers && e == cudaSuccess; ++l) {
+    if (e == cudaSuccess && d->persist) e = launch_persist(d->pp, d->persist_type, d->persist_grid, d->persist_smem, s);
+    for (int l = 0; l < d->n_layers && e == cudaSuccess && !d->persist; ++l) {
         const long long loff = (long long)l * layer_kv;
         e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)(l ? d->delta : nullptr),
                       d->rms_att[l], d->xb, D.dim, d->t_qkv[l]);
@@ -1137,6 +1147,98 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
         if (d->E == 0) d->t_ffn[l] = external(d->p_ffn13[l], d->xb);
     }
     d->t_head = external(d->p_head, d->xb);
+
+    // Persistent one-token path (decode_persist.cu): dense layers whose
+    // linears share one type with 16-byte multiple row sizes.  Bit-identical
+    // to the launch-per-stage step but measured slower on B200 (its per-CTA
+    // stages are latency-bound), so it runs only when QUANTR_DECODE_PERSIST=1
+    // is set when the decoder is created.
+    const char* pe = std::getenv("QUANTR_DECODE_PERSIST");
+    if (B == 1 && d->E == 0 && pe && pe[0] == '1') {
+        const uint32_t T = m->wq_type[0];
+        bool elig = type_supported(T) && m->dim % 256 == 0 && D.q_dim % 256 == 0 && hid % 256 == 0 &&
+                    D.kv_dim % 32 == 0 && hd <= dp::kPersistThreads && D.n_heads <= device_sm_count() &&
+                    std::max({m->dim, D.q_dim, hid}) <= dp::kPersistMaxVec;
+        for (int l = 0; l < L && elig; ++l)
+            elig = m->wq_type[l] == T && m->wk_type[l] == T && m->wv_type[l] == T && m->wo_type[l] == T &&
+                   m->w1_type[l] == T && m->w2_type[l] == T && m->w3_type[l] == T;
+        for (int dd : {m->dim, D.q_dim, hid})
+            if (elig) elig = row_bytes(T, dd) % 16 == 0;
+        if (elig) elig = d->embd_rb == 0 || dequant_extent_host(d->embd_type, m->dim) == m->dim;
+        int dev = 0, coop = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+        if (elig && coop) {
+            const int grid = device_sm_count();
+            std::vector<dp::Stage> st((size_t)L * 4);
+            std::vector<dp::LayerW> lw((size_t)L);
+            auto units = [&](int dd) { return (int)((dd / block_elems(T)) * block_units(T)); };
+            for (int l = 0; l < L; ++l) {
+                lw[l] = dp::LayerW{d->rms_att[l], d->rms_ffn[l]};
+                dp::Stage& a = st[(size_t)l * 4 + 0];
+                a.nmat = 3;
+                a.w[0] = wq[l]; a.w[1] = wk[l]; a.w[2] = wv[l];
+                a.rows[0] = D.q_dim; a.rows[1] = D.kv_dim; a.rows[2] = D.kv_dim;
+                a.out[0] = d->q; a.out[1] = d->kc; a.out[2] = d->vc;
+                a.rb = (int)row_bytes(T, m->dim); a.U = units(m->dim); a.total = D.q_dim + 2LL * D.kv_dim;
+                dp::Stage& o = st[(size_t)l * 4 + 1];
+                o.nmat = 1; o.w[0] = wo[l]; o.rows[0] = m->dim; o.out[0] = d->delta;
+                o.rb = (int)row_bytes(T, D.q_dim); o.U = units(D.q_dim); o.total = m->dim;
+                dp::Stage& f = st[(size_t)l * 4 + 2];
+                f.nmat = 2; f.w[0] = w1[l]; f.w[1] = w3[l]; f.rows[0] = hid; f.rows[1] = hid;
+                f.out[0] = d->hb; f.out[1] = d->hb2;
+                f.rb = (int)row_bytes(T, m->dim); f.U = units(m->dim); f.total = 2LL * hid;
+                dp::Stage& w = st[(size_t)l * 4 + 3];
+                w.nmat = 1; w.w[0] = w2[l]; w.rows[0] = m->dim; w.out[0] = d->delta;
+                w.rb = (int)row_bytes(T, hid); w.U = units(hid); w.total = m->dim;
+            }
+            dp::Params& P = d->pp;
+            P.L = L;
+            P.dim = m->dim; P.q_dim = D.q_dim; P.kv_dim = D.kv_dim; P.hd = hd; P.n_heads = D.n_heads;
+            P.n_kv = D.n_kv; P.kv_mul = D.kv_mul; P.hidden = hid; P.seq_len = D.seq_len; P.vocab = D.vocab;
+            P.kv_type = D.kv_type; P.inv_sqrt = D.inv_sqrt;
+            P.tok = d->tok; P.pos = d->pos;
+            P.embd = d->embd; P.embd_type = d->embd_type; P.embd_rb = d->embd_rb;
+            P.q = d->q; P.kc = d->kc; P.vc = d->vc; P.xa = d->xa; P.delta = d->delta; P.h1 = d->hb; P.h3 = d->hb2;
+            P.kcache = d->kcache; P.vcache = d->vcache; P.layer_kv = (long long)B * D.seq_len * D.kv_dim;
+            P.rope = d->rope; P.err = device_error_word();
+            P.stages = st.data();  // host copy while sizing
+            size_t smem = 0;
+            int rc2 = persist_layout(P, T, grid, &smem);
+            float* x1 = nullptr;
+            dp::Stage* dst = nullptr;
+            dp::LayerW* dlw = nullptr;
+            unsigned* bar = nullptr;
+            if (rc2 == QUANTR_OK) {
+                cudaError_t e2 = dev_alloc(d, &x1, (size_t)m->dim);
+                if (e2 == cudaSuccess) e2 = dev_alloc(d, &dst, st.size());
+                if (e2 == cudaSuccess) e2 = dev_alloc(d, &dlw, lw.size());
+                if (e2 == cudaSuccess) e2 = dev_alloc(d, &bar, 4);
+                if (e2 == cudaSuccess)
+                    e2 = cudaMemcpy(dst, st.data(), st.size() * sizeof(dp::Stage), cudaMemcpyHostToDevice);
+                if (e2 == cudaSuccess)
+                    e2 = cudaMemcpy(dlw, lw.data(), lw.size() * sizeof(dp::LayerW), cudaMemcpyHostToDevice);
+                if (e2 == cudaSuccess) e2 = persist_set_smem(T, D.kv_type, smem);
+                int per_sm = 0;
+                if (e2 == cudaSuccess)
+                    e2 = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                        &per_sm, (const void*)persist_kernel(T, D.kv_type), dp::kPersistThreads, smem);
+                if (e2 == cudaSuccess && per_sm >= 1) {
+                    P.stages = dst;
+                    P.layers = dlw;
+                    P.X[0] = d->x;
+                    P.X[1] = x1;
+                    P.bar = bar;
+                    d->persist = true;
+                    d->persist_type = T;
+                    d->persist_grid = grid;
+                    d->persist_smem = smem;
+                } else {
+                    cudaGetLastError();
+                }
+            }
+        }
+    }
 
     // Per-step bytes: every linear once, norms, one embedding row per sequence.
     size_t wb = 0;

@@ -73,6 +73,12 @@ __host__ __device__ __forceinline__ uint32_t f2h_ref(float f)
     return s | ((uint32_t)e << 10) | ((x >> 13) & 0x3FFu);
 }
 
+// Elements of an n-element row that dequantize_row defines (whole blocks).
+__host__ __device__ inline int dequant_extent_host(uint32_t type, int n)
+{
+    return type == T_Q8_0 ? (n / 32) * 32 : (type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) ? (n / 256) * 256 : 0;
+}
+
 #ifdef __CUDACC__
 // Element e of a packed row, decoded as the reference's dequantize_row does
 // (src/quant.c:160-240): Q8_0 q*d; K types q*sc - m (Q4_K/Q5_K) or

@@ -124,6 +124,23 @@ def test_generate_matches_oracle(qr_gpu, spec):
     assert len(set(toks[0].tolist())) > 3
 
 
+def test_persistent_one_token_kernel(qr_gpu, monkeypatch):
+    """The persistent single-launch step (csrc/decode_persist.cu, opt-in with
+    QUANTR_DECODE_PERSIST=1): identical tokens and bit-identical logits."""
+    monkeypatch.setenv("QUANTR_DECODE_PERSIST", "1")
+    spec = dense(layers=3)
+    run_generate(qr_gpu, spec)
+    model = ms.build(spec, seed=21)
+    dec = _decoder(qr_gpu, model)
+    try:
+        assert dec.info()["launches_per_decode_step"] <= 8  # feed, barrier reset, persistent kernel, head
+        orc = _oracle(model)
+        for pos, t in enumerate(ms.prompt(spec, 6, seed=5)[0]):
+            _same(dec.forward_runtime(int(t), pos), orc.forward(int(t), pos))
+    finally:
+        dec.close()
+
+
 def test_generate_batched_sequences(qr_gpu):
     """Three independent sequences with their own prompts and KV caches; the
     GEMVs run as 3-token tensor-core jobs."""
