@@ -51,7 +51,7 @@ namespace dec {
 constexpr int kMaxBatch = 1024;
 constexpr size_t kSmemMax = 227 * 1024;
 
-enum : int { MODE_EXPLICIT = 0, MODE_PREFILL = 1, MODE_DECODE = 2 };
+enum : int { MODE_EXPLICIT = 0, MODE_PREFILL = 1, MODE_DECODE = 2, MODE_PREFILL_CHUNK = 3 };
 
 // Device control block: what the feed kernel at the start of each step does.
 struct Ctl {
@@ -81,6 +81,8 @@ __device__ __forceinline__ void tgts_write(const Tgts& tg, int t, int b, int lan
 struct Dims {
     int B, dim, q_dim, kv_dim, hd, n_heads, n_kv, kv_mul, seq_len, hidden, vocab, kv_type;
     float inv_sqrt;
+    int kv_B;        // sequences the KV cache holds
+    int seq_stride;  // KV-cache sequence of step row b = b * seq_stride (0: every row is one sequence's position)
 };
 
 // ------------------------------------------------------------- kernels --
@@ -99,11 +101,17 @@ __global__ void k_feed(Ctl* ctl, int* tok, int* pos, const int* prompt, const in
         } else if (mode == MODE_DECODE) {
             tok[b] = i == 0 ? prompt[(long long)b * n + n - 1] : next[b];
             pos[b] = (n + i) % seq_len;
+        } else if (mode == MODE_PREFILL_CHUNK) {
+            // Rows are consecutive prompt positions of one sequence; rows
+            // past the prompt get position -1 and are skipped.
+            const int idx = s * B + b;
+            tok[b] = idx < n ? prompt[idx] : 0;
+            pos[b] = idx < n ? idx : -1;
         }
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (mode == MODE_PREFILL) ctl->step = s + 1;
+        if (mode == MODE_PREFILL || mode == MODE_PREFILL_CHUNK) ctl->step = s + 1;
         if (mode == MODE_DECODE) ctl->dstep = i + 1;
     }
     pdl_trigger();
@@ -252,7 +260,32 @@ __device__ __forceinline__ void rot(float a, float b, float2 cs, float& o0, floa
 // element (src/runtime.c:129-132, 143, 181), only the addresses differ.
 __device__ __forceinline__ long long kv_head_base(const Dims& D, long long layer_off, int b, int kh)
 {
-    return layer_off + ((long long)b * D.n_kv + kh) * D.seq_len * D.hd;
+    return layer_off + ((long long)b * D.seq_stride * D.n_kv + kh) * D.seq_len * D.hd;
+}
+
+// K (rotated) and V rows of every step row's position into the cache, for
+// steps whose rows are positions of one sequence (chunked prefill): all rows
+// are stored before any row's scores read them.  Rows with pos < 0 skip.
+template <int KVT>
+__global__ void k_rope_store_rows(const float* __restrict__ kc, const float* __restrict__ vc,
+                                  const float2* __restrict__ rope, void* kcache, void* vcache, long long layer_off,
+                                  const int* __restrict__ pos, Dims D)
+{
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;  // pair index within kv_dim
+    const int p = pos[b];
+    if (p < 0 || 2 * j >= D.kv_dim) return;
+    const int i = 2 * j, kh = i / D.hd, ii = i - kh * D.hd;
+    const float2 cs = rope[(long long)p * (D.q_dim / 2) + j];
+    const long long kb = (long long)b * D.kv_dim;
+    const long long row = kv_head_base(D, layer_off, b, kh) + (long long)p * D.hd + ii;
+    const float k0 = kc[kb + i], k1 = kc[kb + i + 1];
+    kv_put(kcache, KVT, row, __fsub_rn(__fmul_rn(k0, cs.x), __fmul_rn(k1, cs.y)));
+    kv_put(kcache, KVT, row + 1, __fadd_rn(__fmul_rn(k0, cs.y), __fmul_rn(k1, cs.x)));
+    kv_put(vcache, KVT, row, vc[kb + i]);
+    kv_put(vcache, KVT, row + 1, vc[kb + i + 1]);
 }
 
 // RoPE (src/runtime.c:19-41) fused with the scores (:139-157): each CTA
@@ -262,7 +295,7 @@ __device__ __forceinline__ long long kv_head_base(const Dims& D, long long layer
 // stores the key and value rows into the cache (:129-132).  Then
 // att[b][h][t] = dot_ref(q_h, k_t) * (1/sqrt(head_dim)).  Threads: x = position
 // in the tile, y = query head of the group.
-template <int KVT>
+template <int KVT, bool FUSED>
 __global__ void k_att_scores(const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
                              const float2* __restrict__ rope, void* kcache, void* vcache, long long layer_off,
                              const int* __restrict__ pos, float* __restrict__ att, Dims D)
@@ -273,7 +306,7 @@ __global__ void k_att_scores(const float* __restrict__ q, const float* __restric
     const int b = blockIdx.x / D.n_kv, kh = blockIdx.x % D.n_kv;
     const int t0 = blockIdx.y * kScoreTile;
     const int p = pos[b];
-    if (t0 > p) return;
+    if (p < 0 || t0 > p) return;
     const int hd = D.hd, ld = hd + 1;  // padded rows: lanes read one column of different rows
     float* Ks = sm;
     float* Qs = sm + kScoreTile * ld;
@@ -281,7 +314,7 @@ __global__ void k_att_scores(const float* __restrict__ q, const float* __restric
     const int nt = min(kScoreTile, p - t0 + 1);
     const float2* rp = rope + (long long)p * (D.q_dim / 2);
     const long long q0 = (long long)b * D.q_dim + (long long)kh * D.kv_mul * hd;
-    const bool here = p < t0 + kScoreTile;  // this tile holds the current position
+    const bool here = FUSED && p < t0 + kScoreTile;  // this tile holds the current position (stored here)
     const long long hb = kv_head_base(D, layer_off, b, kh);
     // Cached rows t0 .. (here ? p-1 : t0+nt-1): contiguous, 16-byte words.
     const int ncached = nt - (here ? 1 : 0);
@@ -384,6 +417,7 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
     pdl_wait();
     pdl_trigger();
     const int p = pos[b], np = p + 1;
+    if (p < 0) return;
     const int ntiles = (np + kVTile - 1) / kVTile;
     // The head's value rows are contiguous: one bulk copy per tile.
     const unsigned char* vrow0 =
@@ -622,6 +656,8 @@ struct quantr_decoder {
     Tgts t_head{};
     // One-token dense models: every layer in one persistent kernel per step
     // (decode_persist.cu); the head and the greedy pick follow as kernels.
+    bool child = false;          // a chunked-prefill decoder sharing its parent's KV cache
+    quantr_decoder* pf = nullptr;  // this decoder's chunked-prefill child (one-sequence decoders)
     bool persist = false;
     uint32_t persist_type = 0;
     int persist_grid = 0;
@@ -738,7 +774,8 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
         e = launch_ex(&k_embed, dim3((D.dim + 255) / 256, D.B), dim3(256), 0, c, d->x, (const int*)d->tok, d->embd,
                       d->embd_type, d->embd_rb, D.dim, D.vocab);
     const size_t norm_smem = (size_t)2 * D.dim * sizeof(float);
-    const long long layer_kv = (long long)D.B * D.seq_len * D.kv_dim;
+    const long long layer_kv = (long long)D.kv_B * D.seq_len * D.kv_dim;
+    const bool chunk = D.seq_stride == 0;  // rows are positions of one sequence (chunked prefill)
     if (e == cudaSuccess && d->persist) e = launch_persist(d->pp, d->persist_type, d->persist_grid, d->persist_smem, s);
     for (int l = 0; l < d->n_layers && e == cudaSuccess && !d->persist; ++l) {
         const long long loff = (long long)l * layer_kv;
@@ -747,7 +784,14 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_qkv[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
         const size_t ssm = (size_t)(kScoreTile * (D.hd + 1) + D.kv_mul * D.hd) * sizeof(float);
-        e = launch_ex(D.kv_type ? &k_att_scores<1> : &k_att_scores<0>,
+        if (chunk) {
+            e = launch_ex(D.kv_type ? &k_rope_store_rows<1> : &k_rope_store_rows<0>,
+                          dim3((D.kv_dim / 2 + 127) / 128, D.B), dim3(128), 0, c, (const float*)d->kc,
+                          (const float*)d->vc, (const float2*)d->rope, d->kcache, d->vcache, loff, (const int*)d->pos, D);
+            if (e != cudaSuccess) break;
+        }
+        e = launch_ex(D.kv_type ? (chunk ? &k_att_scores<1, false> : &k_att_scores<1, true>)
+                                : (chunk ? &k_att_scores<0, false> : &k_att_scores<0, true>),
                       dim3(D.B * D.n_kv, (D.seq_len + kScoreTile - 1) / kScoreTile),
                       dim3(kScoreTile, D.kv_mul), ssm, c, (const float*)d->q, (const float*)d->kc,
                       (const float*)d->vc, (const float2*)d->rope, d->kcache, d->vcache, loff, (const int*)d->pos,
@@ -850,6 +894,10 @@ int capture(quantr_decoder* d, bool with_head, cudaGraphExec_t* out, int* nodes)
 void destroy(quantr_decoder* d)
 {
     if (!d) return;
+    if (d->pf) {
+        destroy(d->pf);
+        d->pf = nullptr;
+    }
     int prev = -1;
     cudaGetDevice(&prev);
     cudaSetDevice(d->device);
@@ -888,7 +936,15 @@ void rope_table(std::vector<float2>& t, int seq_len, int q_dim, int head_dim, fl
 
 extern "C" {
 
-int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch)
+} // extern "C"
+
+namespace {
+constexpr int kPrefillChunk = 64;  // prompt positions per chunked-prefill step
+
+// parent != null: a chunked-prefill decoder for parent's single sequence: its
+// `batch` rows are consecutive prompt positions, it shares the parent's KV
+// cache, and it only has a prefill graph.
+int create_impl(quantr_decoder** out, const quantr_model* m, int batch, quantr_decoder* parent)
 {
     if (!out || !m) return QUANTR_ERR_BAD_ARG;
     *out = nullptr;
@@ -918,6 +974,9 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
     D.vocab = m->vocab_size;
     D.kv_type = m->kv_type == 1 ? 1 : 0;
     D.inv_sqrt = 1.0f / std::sqrt((float)hd);
+    D.kv_B = parent ? parent->D.kv_B : batch;
+    D.seq_stride = parent ? 0 : 1;
+    d->child = parent != nullptr;
     d->n_layers = m->n_layers;
     d->E = m->expert_count;
     d->K = m->expert_used_count;
@@ -1042,12 +1101,17 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
     d->ring_cap = std::max(D.seq_len, 4096);
     A(&d->ring, (size_t)B * d->ring_cap);
     A(&d->ctl, 1);
-    const size_t kv_elems = (size_t)L * B * D.seq_len * D.kv_dim;
-    uint8_t *kcb = nullptr, *vcb = nullptr;
-    A(&kcb, kv_elems * (D.kv_type ? 2 : 4));
-    A(&vcb, kv_elems * (D.kv_type ? 2 : 4));
-    d->kcache = kcb;
-    d->vcache = vcb;
+    const size_t kv_elems = (size_t)L * D.kv_B * D.seq_len * D.kv_dim;
+    if (parent) {
+        d->kcache = parent->kcache;
+        d->vcache = parent->vcache;
+    } else {
+        uint8_t *kcb = nullptr, *vcb = nullptr;
+        A(&kcb, kv_elems * (D.kv_type ? 2 : 4));
+        A(&vcb, kv_elems * (D.kv_type ? 2 : 4));
+        d->kcache = kcb;
+        d->vcache = vcb;
+    }
     if (d->E) {
         A(&d->moe_o, (size_t)B * d->K * m->dim);
         A(&d->sel, (size_t)B * d->K);
@@ -1123,7 +1187,7 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
             d->p_sh2.push_back(p);
         }
     }
-    {
+    if (!parent) {
         int rc = make_program(d, {{wcls, m->wcls_type, D.vocab, m->dim, d->xb, m->dim, d->logits, D.vocab}},
                               &d->p_head);
         if (rc) return fail(rc);
@@ -1146,7 +1210,7 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
         if (hd % 32 == 0) d->t_o[l] = external(d->p_o[l], d->xa);
         if (d->E == 0) d->t_ffn[l] = external(d->p_ffn13[l], d->xb);
     }
-    d->t_head = external(d->p_head, d->xb);
+    if (!parent) d->t_head = external(d->p_head, d->xb);
 
     // Persistent one-token path (decode_persist.cu): dense layers whose
     // linears share one type with 16-byte multiple row sizes.  Bit-identical
@@ -1259,8 +1323,14 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
     {
         const int ssm = (kScoreTile * (hd + 1) + D.kv_mul * hd) * 4;
         const int vsm = (int)att_v_smem(D);
-        if (cudaFuncSetAttribute(k_att_scores<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) != cudaSuccess ||
-            cudaFuncSetAttribute(k_att_scores<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) != cudaSuccess ||
+        if (cudaFuncSetAttribute(k_att_scores<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_att_scores<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_att_scores<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(k_att_scores<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
+                cudaSuccess ||
             cudaFuncSetAttribute(k_att_softmax_v<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) !=
                 cudaSuccess ||
             cudaFuncSetAttribute(k_att_softmax_v<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) != cudaSuccess)
@@ -1270,18 +1340,48 @@ int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch
     // ---- warm-up (MoE tensor-core plans are made on their first call), then
     // clean caches and the two graphs ----
     k_ctl_set<<<1, 1, 0, d->stream>>>(d->ctl, MODE_EXPLICIT, 0, d->ring_cap);
-    int rc = enqueue_step(d, d->stream, true);
+    int rc = enqueue_step(d, d->stream, !parent);
     if (rc) return fail(rc);
     if (cudaStreamSynchronize(d->stream) != cudaSuccess) return fail(QUANTR_ERR_CUDA);
+    // The warm-up wrote garbage rows; the cache starts zeroed like the
+    // reference's calloc'd one (src/model.c:128-137).
     if (cudaMemsetAsync(d->kcache, 0, kv_elems * (D.kv_type ? 2 : 4), d->stream) != cudaSuccess ||
         cudaMemsetAsync(d->vcache, 0, kv_elems * (D.kv_type ? 2 : 4), d->stream) != cudaSuccess)
         return fail(QUANTR_ERR_CUDA);
-    rc = capture(d, true, &d->g_decode, &d->nodes_decode);
+    if (!parent) rc = capture(d, true, &d->g_decode, &d->nodes_decode);
     if (!rc) rc = capture(d, false, &d->g_prefill, &d->nodes_prefill);
     if (rc) return fail(rc);
     if (cudaStreamSynchronize(d->stream) != cudaSuccess) return fail(QUANTR_ERR_CUDA);
     d->load_ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
     *out = d;
+    return QUANTR_OK;
+}
+
+} // namespace
+
+extern "C" {
+
+int quantr_decoder_create(quantr_decoder** out, const quantr_model* m, int batch)
+{
+    int rc = create_impl(out, m, batch, nullptr);
+    if (rc || batch != 1) return rc;
+    // One sequence: prompts are prefilled kPrefillChunk positions per step
+    // (the tokens' GEMVs as tensor-core jobs), which needs the whole prompt
+    // within seq_len.  Without the chunked decoder prefill is per position.
+    quantr_decoder* d = *out;
+    quantr_decoder* pf = nullptr;
+    if (m->seq_len >= 2 && create_impl(&pf, m, std::min(kPrefillChunk, m->seq_len), d) == QUANTR_OK) {
+        d->pf = pf;
+        d->device_bytes += pf->device_bytes;
+        const size_t kv = (size_t)m->n_layers * d->D.kv_B * d->D.seq_len * d->D.kv_dim * (d->D.kv_type ? 2 : 4);
+        if (cudaMemset(d->kcache, 0, kv) != cudaSuccess || cudaMemset(d->vcache, 0, kv) != cudaSuccess) {
+            cudaGetLastError();
+            destroy(d);
+            *out = nullptr;
+            return QUANTR_ERR_CUDA;
+        }
+    }
+    cudaGetLastError();
     return QUANTR_OK;
 }
 
@@ -1307,6 +1407,39 @@ int quantr_decoder_step_dev(quantr_decoder* d, const int* tokens, const int* pos
     return code_of(e);
 }
 
+} // extern "C"
+
+namespace {
+// Prefill of the n_prompt positions whose tokens are in d->prompt (and, for a
+// chunked prefill, in d->pf->prompt): chunked-prefill graph replays when the
+// decoder has one, else one prefill-graph replay per position.
+cudaError_t enqueue_prefill(quantr_decoder* d, int n_prompt, cudaStream_t s)
+{
+    cudaError_t e = cudaSuccess;
+    if (d->pf && n_prompt <= d->D.seq_len) {
+        quantr_decoder* c = d->pf;
+        k_ctl_set<<<1, 1, 0, s>>>(c->ctl, MODE_PREFILL_CHUNK, n_prompt, c->ring_cap);
+        e = cudaGetLastError();
+        for (int i = 0; i * c->D.B < n_prompt && e == cudaSuccess; ++i) e = cudaGraphLaunch(c->g_prefill, s);
+        return e;
+    }
+    k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n_prompt, d->ring_cap);
+    e = cudaGetLastError();
+    for (int i = 0; i < n_prompt && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    return e;
+}
+
+// Copies a prompt into the decoder's (and its chunked child's) prompt buffer.
+cudaError_t put_prompt(quantr_decoder* d, const int* prompt, size_t bytes, cudaMemcpyKind kind, cudaStream_t s)
+{
+    cudaError_t e = cudaMemcpyAsync(d->prompt, prompt, bytes, kind, s);
+    if (e == cudaSuccess && d->pf) e = cudaMemcpyAsync(d->pf->prompt, prompt, bytes, kind, s);
+    return e;
+}
+} // namespace
+
+extern "C" {
+
 int quantr_decoder_generate(quantr_decoder* d, const int* prompt, int n_prompt, int steps, int* out)
 {
     if (!d || !prompt || n_prompt < 1 || n_prompt > d->prompt_cap || steps < 0 || (steps && !out))
@@ -1315,12 +1448,8 @@ int quantr_decoder_generate(quantr_decoder* d, const int* prompt, int n_prompt, 
     for (long long i = 0; i < (long long)B * n_prompt; ++i)
         if (prompt[i] < 0 || prompt[i] >= d->D.vocab) return QUANTR_ERR_BAD_ARG;
     cudaStream_t s = d->stream;
-    cudaError_t e = cudaMemcpyAsync(d->prompt, prompt, (size_t)B * n_prompt * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) {
-        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n_prompt, d->ring_cap);
-        e = cudaGetLastError();
-    }
-    for (int i = 0; i < n_prompt && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    cudaError_t e = put_prompt(d, prompt, (size_t)B * n_prompt * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = enqueue_prefill(d, n_prompt, s);
     if (e == cudaSuccess) {
         k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_DECODE, n_prompt, d->ring_cap);
         e = cudaGetLastError();
@@ -1352,12 +1481,8 @@ int quantr_decoder_generate_dev(quantr_decoder* d, const int* prompt, int n_prom
         return QUANTR_ERR_BAD_ARG;
     const int B = d->D.B;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemcpyAsync(d->prompt, prompt, (size_t)B * n_prompt * 4, cudaMemcpyDeviceToDevice, s);
-    if (e == cudaSuccess) {
-        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n_prompt, d->ring_cap);
-        e = cudaGetLastError();
-    }
-    for (int i = 0; i < n_prompt && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    cudaError_t e = put_prompt(d, prompt, (size_t)B * n_prompt * 4, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = enqueue_prefill(d, n_prompt, s);
     if (e == cudaSuccess && steps) {
         k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_DECODE, n_prompt, d->ring_cap);
         e = cudaGetLastError();
@@ -1403,12 +1528,8 @@ void quantr_prefill_runtime(quantr_decoder* d, const int* tokens, int n)
     for (int i = 0; i < n; ++i)
         if (tokens[i] < 0 || tokens[i] >= d->D.vocab) return;
     cudaStream_t s = d->stream;
-    cudaError_t e = cudaMemcpyAsync(d->prompt, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s);
-    if (e == cudaSuccess) {
-        k_ctl_set<<<1, 1, 0, s>>>(d->ctl, MODE_PREFILL, n, d->ring_cap);
-        e = cudaGetLastError();
-    }
-    for (int i = 0; i < n && e == cudaSuccess; ++i) e = cudaGraphLaunch(d->g_prefill, s);
+    cudaError_t e = put_prompt(d, tokens, (size_t)n * 4, cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = enqueue_prefill(d, n, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) cudaGetLastError();
 }
