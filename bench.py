@@ -487,9 +487,13 @@ def ours_arm(args):
         sharded = sharded_forms(args, dev, world, rank)
         if own_group:
             dist.destroy_process_group()
-    decode = None
+    decode = c5 = c4 = None
     if rank == 0 and world == 1 and not args.no_decode:
         decode = decode_c3(args, dev, s)
+    if rank == 0 and world == 1 and not args.no_c4:
+        c4 = moe_c4(args, dev, s)
+    if rank == 0 and world == 1 and not args.no_c5:
+        c5 = decode_c5(args, dev, s)
 
     peak, peak_kind = load_peaks()
     if rank == 0:
@@ -522,6 +526,8 @@ def ours_arm(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,
             "decode_c3": decode,
+            "moe_c4": c4,
+            "decode_c5": c5,
             "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
@@ -753,6 +759,222 @@ def decode_c3(args, dev, s):
     return res
 
 
+def _cudart():
+    """The CUDA runtime torch loaded (for raw device-to-device copies)."""
+    import ctypes
+    import glob
+
+    import torch
+    libdir = os.path.join(os.path.dirname(torch.__file__), "lib")
+    for cand in sorted(glob.glob(os.path.join(libdir, "libcudart.so*"))) + \
+            sorted(glob.glob("/usr/local/cuda/lib64/libcudart.so*")):
+        try:
+            return ctypes.CDLL(cand)
+        except OSError:
+            pass
+    raise OSError("libcudart not found")
+
+
+def decode_c5(args, dev, s):
+    """BASELINE config c5 on the device decoder: Qwen3-30B-A3B shape (48
+    layers, hidden 2048, 32/4 heads of head_dim 128, 128 experts top-8 of
+    768, vocab 151936, all Q4_K), 64 sequences each with a seeded 1024-token
+    KV context (cache filled with N(0, 1) values; the decode step's cost does
+    not depend on them), then greedy decode steps at positions 1024, 1025, ...
+    Time per step = CUDA events over `steps` step calls after warm-up."""
+    import ctypes
+
+    import torch
+
+    import model_synth as ms
+    import quantr
+    spec = ms.qwen3_moe(seq_len=1024 + max(8, args.c5_steps + 8))
+    t0 = time.perf_counter()
+    model = ms.build(spec, seed=5)
+    t_build = time.perf_counter() - t0
+    B, ctx = 64, 1024
+    t0 = time.perf_counter()
+    dec = quantr.Decoder(model, batch=B)
+    torch.cuda.synchronize()
+    t_load = time.perf_counter() - t0
+    info = dec.info()
+    kptr, vptr, kv_bytes = dec.kv()
+    g = torch.Generator(device=dev)
+    g.manual_seed(55)
+    chunk = 1 << 28  # floats per fill
+    buf = torch.empty(chunk, dtype=torch.float32, device=dev)
+    rt = _cudart()
+    for base in (kptr, vptr):
+        off = 0
+        while off < kv_bytes:
+            n = min(chunk * 4, kv_bytes - off)
+            buf.normal_(generator=g)
+            assert rt.cudaMemcpy(ctypes.c_void_p(base + off), ctypes.c_void_p(buf.data_ptr()), ctypes.c_size_t(n),
+                                 3) == 0
+            off += n
+    del buf
+    torch.cuda.synchronize()
+    tok = torch.from_numpy(ms.prompt(spec, 1, seed=8, batch=B)[:, 0].copy()).to(dev)
+    pos = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+
+    def steps(n):
+        with torch.cuda.stream(s):
+            for _ in range(n):
+                dec.step_dev(tok.data_ptr(), pos.data_ptr(), None, 0, tok.data_ptr(), s.cuda_stream)
+                pos.add_(1)
+
+    steps(args.warmup)
+    torch.cuda.synchronize()
+    pos.fill_(ctx)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(s):
+        e0.record(s)
+    steps(args.c5_steps)
+    with torch.cuda.stream(s):
+        e1.record(s)
+    torch.cuda.synchronize()
+    st = quantr.device_status(0)
+    ms_step = e0.elapsed_time(e1) / args.c5_steps
+    # Bytes per step: dense weights + the head + every expert (each is chosen
+    # by at least one of the 64 tokens with probability 1 - (120/128)^64 =
+    # 0.984) + the KV rows read (64 sequences at context ctx + step).
+    ebytes = spec.n_layers * spec.expert_count * (
+        2 * spec.hidden_dim * ms.row_bytes(ms.Q4_K, spec.dim) + spec.dim * ms.row_bytes(ms.Q4_K, spec.hidden_dim))
+    kv_step = info["kv_bytes_per_position"] * B * (ctx + (args.c5_steps + 1) / 2.0)
+    bytes_step = info["weight_bytes_per_step"] + ebytes + kv_step
+    gbs = bytes_step / (ms_step / 1e3) / 1e9
+    peak, _ = load_peaks()
+    res = {
+        "workload": ("c5: Qwen3-30B-A3B shape (48 layers, hidden 2048, 32/4 heads, head_dim 128, 128 experts "
+                     "top-8 x 768, vocab 151936), all Q4_K, fp32 KV; 64 sequences, each at a seeded 1024-token "
+                     f"context, {args.c5_steps} greedy steps; seeded random weights"),
+        "tok_per_s": round(B / (ms_step / 1e3), 1), "ms_per_step": round(ms_step, 3),
+        "bytes_per_step": int(bytes_step), "achieved_GBs": round(gbs, 1), "hbm_frac": round(gbs / peak, 4),
+        "kv_bytes_per_step": int(kv_step), "launches_per_step": info["launches_per_decode_step"],
+        "device_status": st, "model_build_s": round(t_build, 1), "decoder_create_s": round(t_load, 1),
+        "device_bytes": info["device_bytes"] + 2 * kv_bytes,
+    }
+    dec.close()
+    if not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import forward  # test infrastructure: the CPU baseline leg only
+        threads = os.cpu_count() or 1
+        r = forward.Restated(model, threads=threads)
+        r.forward(5, 0)
+        t0 = time.perf_counter()
+        done = 0
+        while done < 2 or (time.perf_counter() - t0 < args.cpu_seconds and done < 64):
+            r.forward(5 + done, done + 1)
+            done += 1
+        sec = (time.perf_counter() - t0) / done
+        r.close()
+        res["cpu_baseline"] = {"value": round(1.0 / sec, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                               "sample": (f"{done} restated forward_runtime calls (head_dim 128 is not expressible "
+                                          f"in the reference; oracle/forward_oracle.c) at positions 1..{done} of one "
+                                          f"sequence, {sec:.2f} s each")}
+    del model
+    return res
+
+
+def moe_c4(args, dev, s):
+    """BASELINE config c4: one Qwen1.5-MoE-A2.7B-shape MoE layer for 64 tokens
+    - router logits N(0, 1), 60 experts top-4 (intermediate 1408, gate/up Q5_K,
+    down Q6_K) through quantr_moe_dev, then the shared expert (5632, same
+    types) with its sigmoid gate through quantr_moe_shared_dev - as one CUDA
+    graph, CUDA events over `steps` replays."""
+    import torch
+
+    import quantr
+    rng = synth.rng_for(44)
+    T, E, k, dim, hid, sh = 64, 60, 4, 2048, 1408, 5632
+    Q5_K = 13
+    w1 = torch.from_numpy(np.stack([synth.matrix(rng, Q5_K, hid, dim) for _ in range(E)])).to(dev)
+    w3 = torch.from_numpy(np.stack([synth.matrix(rng, Q5_K, hid, dim) for _ in range(E)])).to(dev)
+    w2 = torch.from_numpy(np.stack([synth.matrix(rng, Q6_K, dim, hid) for _ in range(E)])).to(dev)
+    s1 = torch.from_numpy(synth.matrix(rng, Q5_K, sh, dim)).to(dev)
+    s3 = torch.from_numpy(synth.matrix(rng, Q5_K, sh, dim)).to(dev)
+    s2 = torch.from_numpy(synth.matrix(rng, Q6_K, dim, sh)).to(dev)
+    gate = torch.from_numpy((rng.standard_normal(dim, dtype=np.float32) * np.float32(0.02)).astype(np.float32)).to(dev)
+    xb = torch.from_numpy(synth.activations(rng, T, dim)).to(dev)
+    lg = torch.from_numpy(rng.standard_normal((T, E), dtype=np.float32)).to(dev)
+    out = torch.empty(T, dim, device=dev)
+    wsb = quantr.moe_workspace_bytes(T, E, k, dim, hid)
+    ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
+    ew = [quantr.ExpertWeights(t.data_ptr(), t[0].numel(), None, ty) for t, ty in ((w1, Q5_K), (w3, Q5_K),
+                                                                                    (w2, Q6_K))]
+    sel = torch.empty(T, k, dtype=torch.int32, device=dev)
+
+    def layer(stream):
+        quantr.moe_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, E, k, *ew, dim, hid, ws.data_ptr(), wsb,
+                       logits=lg.data_ptr(), ldl=E, sel=sel.data_ptr(), stream=stream)
+        quantr.moe_shared_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, gate.data_ptr(), s1.data_ptr(), Q5_K,
+                              s3.data_ptr(), Q5_K, s2.data_ptr(), Q6_K, dim, sh, stream)
+
+    with torch.cuda.stream(s):
+        layer(s.cuda_stream)  # plans (allocating) before capture
+        s.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=s):
+            layer(s.cuda_stream)
+        for _ in range(args.warmup):
+            gr.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            gr.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    chosen = np.unique(sel.cpu().numpy())
+    rb1, rb2 = w1[0].numel(), w2[0].numel()
+    bytes_layer = len(chosen) * (2 * rb1 + rb2) + s1.numel() + s3.numel() + s2.numel() + 4 * dim
+    gbs = bytes_layer / (us / 1e6) / 1e9
+    peak, _ = load_peaks()
+    res = {"workload": ("c4: Qwen1.5-MoE-A2.7B-shape MoE layer, 64 tokens, router logits N(0,1), 60 experts "
+                        "top-4 x 1408 (gate/up Q5_K, down Q6_K) + shared expert 5632 with sigmoid gate"),
+           "us_per_layer": round(us, 2), "tokens_per_s": round(T / (us / 1e6), 1),
+           "experts_chosen": int(len(chosen)), "bytes_per_layer": int(bytes_layer), "achieved_GBs": round(gbs, 1),
+           "hbm_frac": round(gbs / peak, 4),
+           "device_status": quantr.device_status(0)}
+    if not args.no_cpu_baseline:
+        # The reference's matmul_q_fused for the layer's GEMVs (per token: 4
+        # experts x 3 plus the shared expert's 3; routing and softmax omitted).
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import ctypes
+
+        import oracle
+        variant = oracle.best_cpu_variant()
+        lib = oracle.RefLib(variant) if oracle.ref_available(variant) else oracle.Oracle()
+        f = lib.fn["matmul_q_fused"]
+        threads = os.cpu_count() or 1
+        hw = [t.cpu().numpy() for t in (w1, w3, w2)]
+        hs = [t.cpu().numpy() for t in (s1, s3, s2)]
+        xh = xb.cpu().numpy()
+        selh = sel.cpu().numpy()
+        o1 = np.empty(max(hid, sh), np.float32)
+        o2 = np.empty(dim, np.float32)
+        P = ctypes.c_void_p
+        t0 = time.perf_counter()
+        done = 0
+        while done < T and (done < 2 or time.perf_counter() - t0 < args.cpu_seconds):
+            x = xh[done]
+            for e in selh[done]:
+                f(o1.ctypes.data_as(P), x.ctypes.data_as(P), hw[0][e].ctypes.data_as(P), Q5_K, hid, dim, threads)
+                f(o1.ctypes.data_as(P), x.ctypes.data_as(P), hw[1][e].ctypes.data_as(P), Q5_K, hid, dim, threads)
+                f(o2.ctypes.data_as(P), o1.ctypes.data_as(P), hw[2][e].ctypes.data_as(P), Q6_K, dim, hid, threads)
+            f(o1.ctypes.data_as(P), x.ctypes.data_as(P), hs[0].ctypes.data_as(P), Q5_K, sh, dim, threads)
+            f(o1.ctypes.data_as(P), x.ctypes.data_as(P), hs[1].ctypes.data_as(P), Q5_K, sh, dim, threads)
+            f(o2.ctypes.data_as(P), o1.ctypes.data_as(P), hs[2].ctypes.data_as(P), Q6_K, dim, sh, threads)
+            done += 1
+        sec = (time.perf_counter() - t0) / done
+        res["cpu_baseline"] = {"value": round(1.0 / sec, 2), "unit": "tokens/s", "cores": threads,
+                               "kind": "reference" if oracle.ref_available(variant) else "port",
+                               "sample": (f"{done} tokens of the layer's 15 matmul_q_fused calls each "
+                                          f"({variant} build; routing omitted), {sec * 1e3:.1f} ms per token")}
+    del gr
+    return res
+
+
 def int8_peak(device=0):
     """Dense int8 tensor throughput of this GPU (TOP/s): torch._int_mm (a cuBLASLt
     int8 x int8 -> int32 GEMM) of 8192^3, best of 20 after warm-up, CUDA events.
@@ -790,6 +1012,9 @@ def main():
     ap.add_argument("--no-c1", action="store_true", help="skip the c1 Q8_0 GEMV line")
     ap.add_argument("--no-decode", action="store_true", help="skip the c3 decode line")
     ap.add_argument("--no-sharded", action="store_true", help="skip the tensor/expert-parallel forms")
+    ap.add_argument("--no-c4", action="store_true", help="skip the c4 MoE layer line")
+    ap.add_argument("--no-c5", action="store_true", help="skip the c5 decode line (48 layers, 17 GB of weights)")
+    ap.add_argument("--c5-steps", type=int, default=16)
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")

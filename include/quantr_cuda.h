@@ -279,6 +279,22 @@ int quantr_moe_experts_dev(float* o, const float* xb, long long ldx, int T, cons
 int quantr_moe_combine_dev(float* out, long long ldo, const float* o, const int* sel, const float* wts, int T, int k,
                            int dim, void* stream);
 
+/* The shared expert of a Qwen1.5-MoE-style block, added after the routed
+ * experts (no counterpart in the reference, which loads no shared expert,
+ * src/model.c:401-446; restated from its dense FFN, src/runtime.c:270-284):
+ * for every token t, out[t*ldo + i] += o_i * g with
+ * o = W2.(silu(W1.xb_t) * (W3.xb_t)) (W1 the gate projection, hidden x dim;
+ * W3 up, hidden x dim; W2 down, dim x hidden; the same GEMVs and SwiGLU as
+ * the dense FFN) and g = 1/(1 + expf(-(gate . xb_t))), gate . xb_t in
+ * matmul_ref order, the add a single fp32 add after the routed sum.  ldo must
+ * equal dim.  Device pointers, asynchronous on `stream`; the first call with
+ * a configuration (pointers, T, shapes) plans the GEMVs and allocates their
+ * buffers - make it before any stream capture - later calls allocate
+ * nothing. */
+int quantr_moe_shared_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* gate,
+                          const void* w1, uint32_t t1, const void* w3, uint32_t t3, const void* w2, uint32_t t2,
+                          int dim, int hidden, void* stream);
+
 /* Host-pointer, synchronous form for the reference's runtime: w1/w3/w2 are the
  * per-layer arrays of E expert pointers (w->expert_w1[l], ..., include/types.h:
  * 68-70), each inside a range registered with quantr_gpu_register_weights
@@ -396,6 +412,13 @@ int quantr_decoder_launches(const quantr_decoder* dec, int* decode_step, int* pr
  * the next call) and prefill_runtime. */
 const float* quantr_forward_runtime(quantr_decoder* dec, int token, int pos);
 void quantr_prefill_runtime(quantr_decoder* dec, const int* tokens, int n_tokens);
+
+/* The decoder's KV caches (device memory, `bytes` each): element i of head h
+ * at position t of sequence b in layer l is at
+ * (((l*batch + b)*n_kv_heads + h)*seq_len + t)*head_dim + i, fp32 or fp16
+ * per kv_type.  For restoring a saved context (the reference keeps its cache
+ * in RunState, src/model.c:128-137) or seeding one. */
+int quantr_decoder_kv(const quantr_decoder* dec, void** key_cache, void** value_cache, size_t* bytes);
 
 /* Bytes the decode step reads that do not depend on the position (weights of
  * one token: every linear, the head, the norms, one embedding row) and the

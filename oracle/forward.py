@@ -80,9 +80,9 @@ def describe(model):
     if s.expert_count:
         m.ffn_gate_inp = ptrs([f"router.{l}" for l in range(L)])
         for w in ("exp_w1", "exp_w2", "exp_w3"):
-            per_layer = [ptrs([f"{w}.{l}.{e}" for e in range(s.expert_count)]) for l in range(L)]
+            per_layer = [arr(_vp, [model.expert_ptr(w, l, e) for e in range(s.expert_count)]) for l in range(L)]
             setattr(m, "expert_" + w[4:], arr(_P(_vp), per_layer))
-            setattr(m, w + "_type", types([f"{w}.{l}.0" for l in range(L)]))
+            setattr(m, w + "_type", types([f"{w}.{l}" for l in range(L)]))
     m.head_dim = s.head_dim
     if s.shexp_hidden_dim:
         m.shexp_hidden_dim = s.shexp_hidden_dim

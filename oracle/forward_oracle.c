@@ -195,17 +195,34 @@ static void moe(qo_state* s, int l)
         matmul_q(s->q, s->hb, m->expert_w2[l][e], m->exp_w2_type[l], dim, hidden, s->threads);
         for (int i = 0; i < dim; i++) s->xb2[i] += s->q[i] * ew[ki];
     }
-    if (m->shexp_hidden_dim > 0 && m->shexp_w1) {
-        const int sh = m->shexp_hidden_dim;
-        matmul_q(s->hb, s->xb, m->shexp_w1[l], m->shexp_w1_type[l], sh, dim, s->threads);
-        matmul_q(s->hb2, s->xb, m->shexp_w3[l], m->shexp_w3_type[l], sh, dim, s->threads);
-        for (int i = 0; i < sh; i++) s->hb[i] = silu(s->hb[i]) * s->hb2[i];
-        matmul_q(s->sh, s->hb, m->shexp_w2[l], m->shexp_w2_type[l], dim, sh, s->threads);
-        float g = 0.0f;
-        qo_matmul_f32(&g, s->xb, m->shexp_gate[l], 1, dim);
-        g = 1.0f / (1.0f + expf(-g));
-        for (int i = 0; i < dim; i++) s->xb2[i] += s->sh[i] * g;
+    if (m->shexp_hidden_dim > 0 && m->shexp_w1)
+        qo_shared_expert(s->xb2, s->xb, m->shexp_gate[l], m->shexp_w1[l], m->shexp_w1_type[l], m->shexp_w3[l],
+                         m->shexp_w3_type[l], m->shexp_w2[l], m->shexp_w2_type[l], dim, m->shexp_hidden_dim,
+                         s->threads);
+}
+
+/* Shared expert (restated from the dense FFN, src/runtime.c:270-284, plus the
+ * sigmoid gate): out[i] += (W2.(silu(W1.xb) * W3.xb))[i] * g,
+ * g = 1/(1 + expf(-(gate . xb))) with gate . xb in matmul_ref order. */
+void qo_shared_expert(float* out, const float* xb, const float* gate, const void* w1, uint32_t t1, const void* w3,
+                      uint32_t t3, const void* w2, uint32_t t2, int dim, int hidden, int threads)
+{
+    float* h1 = (float*)malloc((size_t)hidden * sizeof(float));
+    float* h3 = (float*)malloc((size_t)hidden * sizeof(float));
+    float* o = (float*)malloc((size_t)dim * sizeof(float));
+    if (!h1 || !h3 || !o) {
+        free(h1); free(h3); free(o);
+        return;
     }
+    matmul_q(h1, xb, w1, t1, hidden, dim, threads);
+    matmul_q(h3, xb, w3, t3, hidden, dim, threads);
+    for (int i = 0; i < hidden; i++) h1[i] = silu(h1[i]) * h3[i];
+    matmul_q(o, h1, w2, t2, dim, hidden, threads);
+    float g = 0.0f;
+    qo_matmul_f32(&g, xb, gate, 1, dim);
+    g = 1.0f / (1.0f + expf(-g));
+    for (int i = 0; i < dim; i++) out[i] += o[i] * g;
+    free(h1); free(h3); free(o);
 }
 
 const float* qo_forward(qo_state* s, int token, int pos)

@@ -128,6 +128,8 @@ class Oracle(_QuantLib):
         L.qo_matmul_f32.argtypes = [_vp, _vp, _vp, _i, _i]
         L.qo_expf_mismatches.restype = _l
         L.qo_expf_mismatches.argtypes = [_vp, _u32, _l]
+        L.qo_shared_expert.restype = None
+        L.qo_shared_expert.argtypes = [_vp, _vp, _vp, _vp, _u32, _vp, _u32, _vp, _u32, _i, _i, _i]
         L.qo_moe_token.restype = _i
         L.qo_moe_token.argtypes = [_vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _vp, _u32, _l, _vp, _u32, _l,
                                    _vp, _u32, _l, _i, _i]
@@ -143,6 +145,13 @@ class Oracle(_QuantLib):
         of the floats with bit patterns first, first + 1, ..."""
         got = np.ascontiguousarray(got, np.float32)
         return int(self.L.qo_expf_mismatches(_p(got), first, got.size))
+
+    def shared_expert(self, out, xb, gate, w1, t1, w3, t3, w2, t2, dim, hidden):
+        """out (float32[dim], updated in place) += the gated shared expert of xb."""
+        self.L.qo_shared_expert(_p(out), _p(np.ascontiguousarray(xb, np.float32)),
+                                _p(np.ascontiguousarray(gate, np.float32)), _p(w1), t1, _p(w3), t3, _p(w2), t2, dim,
+                                hidden, os.cpu_count() or 1)
+        return out
 
     def unit_partials(self, w, type_, n, d, xq):
         units = (d // 32) if type_ == 8 else 8 * (d // 256)

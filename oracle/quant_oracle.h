@@ -140,6 +140,11 @@ typedef struct {
     const float* const* shexp_gate;    /* dim F32 per layer */
 } qo_model;
 
+/* Shared expert + sigmoid gate added to out (a Qwen1.5-MoE block's tail). */
+void qo_shared_expert(float* out, const float* xb, const float* gate, const void* w1, uint32_t t1,
+                      const void* w3, uint32_t t3, const void* w2, uint32_t t2, int dim, int hidden,
+                      int threads);
+
 typedef struct qo_state qo_state;
 qo_state*    qo_open(const qo_model* m, int threads);
 void         qo_close(qo_state* s);

@@ -43,6 +43,9 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <vector>
 
 namespace qr {
@@ -1541,6 +1544,97 @@ int quantr_debug_expf_dev(float* out, uint32_t first, long long n, void* stream)
     k_debug_expf<<<(unsigned)std::min<long long>((n + 255) / 256, 148 * 64), 256, 0,
                    static_cast<cudaStream_t>(stream)>>>(out, first, n);
     return code_of(cudaGetLastError());
+}
+
+} // extern "C"
+
+namespace {
+// Plans of quantr_moe_shared_dev, one per configuration (first call plans).
+struct SharedPlan {
+    quantr_program* p13 = nullptr;
+    quantr_program* p2 = nullptr;
+    float *h1 = nullptr, *h3 = nullptr, *o = nullptr, *g = nullptr;
+};
+std::mutex g_shared_mu;
+std::map<std::tuple<int, const void*, const void*, const void*, const float*, const float*, float*, int, int, int,
+                    long long, long long>,
+         SharedPlan>
+    g_shared;
+} // namespace
+
+extern "C" {
+
+int quantr_moe_shared_dev(float* out, long long ldo, const float* xb, long long ldx, int T, const float* gate,
+                          const void* w1, uint32_t t1, const void* w3, uint32_t t3, const void* w2, uint32_t t2,
+                          int dim, int hidden, void* stream)
+{
+    if (T <= 0) return QUANTR_OK;
+    if (!out || !xb || !gate || !w1 || !w2 || !w3 || dim <= 0 || hidden <= 0 || ldo < dim || ldx < dim ||
+        T > kMaxBatch)
+        return QUANTR_ERR_BAD_ARG;
+    if (!type_supported(t1) || !type_supported(t2) || !type_supported(t3)) return QUANTR_ERR_UNSUPPORTED_TYPE;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    SharedPlan* P = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_shared_mu);
+        auto key = std::make_tuple(dev, w1, w3, w2, xb, gate, out, T, dim, hidden, ldo, ldx);
+        auto it = g_shared.find(key);
+        if (it == g_shared.end()) {
+            SharedPlan sp;
+            cudaError_t e = cudaMalloc(&sp.h1, (size_t)T * hidden * 4);
+            if (e == cudaSuccess) e = cudaMalloc(&sp.h3, (size_t)T * hidden * 4);
+            if (e == cudaSuccess) e = cudaMalloc(&sp.o, (size_t)T * dim * 4);
+            if (e == cudaSuccess) e = cudaMalloc(&sp.g, (size_t)T * 4);
+            int rc = e == cudaSuccess ? QUANTR_OK : QUANTR_ERR_OOM;
+            if (!rc) {
+                quantr_gemv_job j13[2] = {{w1, t1, hidden, dim, T, xb, ldx, sp.h1, hidden},
+                                          {w3, t3, hidden, dim, T, xb, ldx, sp.h3, hidden}};
+                rc = quantr_program_create(&sp.p13, j13, 2);
+            }
+            if (!rc) {
+                quantr_gemv_job j2 = {w2, t2, dim, hidden, T, sp.h1, hidden, sp.o, dim};
+                const float* xm = sp.h3;
+                rc = program_create_ex(&sp.p2, &j2, &xm, 1);
+            }
+            if (rc) {
+                cudaGetLastError();
+                quantr_program_destroy(sp.p13);
+                quantr_program_destroy(sp.p2);
+                cudaFree(sp.h1);
+                cudaFree(sp.h3);
+                cudaFree(sp.o);
+                cudaFree(sp.g);
+                return rc;
+            }
+            it = g_shared.emplace(key, sp).first;
+        }
+        P = &it->second;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    LaunchCfg c;
+    c.stream = s;
+    if (quantr_program_run(P->p13, s) != QUANTR_OK || quantr_program_run(P->p2, s) != QUANTR_OK)
+        return QUANTR_ERR_CUDA;
+    cudaError_t e = launch_gemv_f32(gate, xb, ldx, P->g, 1, 1, dim, T, c);
+    if (e == cudaSuccess) {
+        if (ldo == dim)
+            e = launch_ex(&k_shexp_add, dim3((dim + 255) / 256, T), dim3(256), 0, c, out, (const float*)P->o,
+                          (const float*)P->g, dim);
+        else
+            e = cudaErrorInvalidValue;
+    }
+    return code_of(e);
+}
+
+int quantr_decoder_kv(const quantr_decoder* d, void** key_cache, void** value_cache, size_t* bytes)
+{
+    if (!d) return QUANTR_ERR_BAD_ARG;
+    if (key_cache) *key_cache = d->kcache;
+    if (value_cache) *value_cache = d->vcache;
+    if (bytes)
+        *bytes = (size_t)d->n_layers * d->D.kv_B * d->D.seq_len * d->D.kv_dim * (d->D.kv_type ? 2 : 4);
+    return QUANTR_OK;
 }
 
 int quantr_decoder_info(const quantr_decoder* d, size_t* weight_bytes, size_t* kv_bytes_per_position,

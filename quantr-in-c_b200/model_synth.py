@@ -115,7 +115,8 @@ def pack(rng, t, n, d, sigma):
         return out.reshape(n, nb * 34)
     nsb = d // 256
     bb = synth.BLOCK_BYTES[t]
-    blk = rng.integers(0, 256, size=(n, nsb, bb), dtype=np.uint8)
+    nbytes = n * nsb * bb
+    blk = rng.bit_generator.random_raw((nbytes + 7) // 8).view(np.uint8)[:nbytes].reshape(n, nsb, bb)
     jit = (1.0 + 0.1 * rng.standard_normal((n, nsb), np.float32)).astype(np.float32)
     if t in (Q4_K, Q5_K):
         levels = 16 if t == Q4_K else 32
@@ -155,6 +156,11 @@ class Model:
     def type_of(self, name):
         return self.off[name][2]
 
+    def expert_ptr(self, proj, layer, e):
+        """Host address of expert e of merged projection proj ("exp_w1", ...)."""
+        o, nb, _ = self.off[f"{proj}.{layer}"]
+        return self.buf.ctypes.data + o + e * (nb // self.spec.expert_count)
+
 
 def tensor_list(s):
     """(name, type, rows, cols, sigma) in load order."""
@@ -166,12 +172,14 @@ def tensor_list(s):
                 (f"wq.{l}", s.wtype, s.q_dim, s.dim, sig(s.dim)), (f"wk.{l}", s.wtype, s.kv_dim, s.dim, sig(s.dim)),
                 (f"wv.{l}", s.wtype, s.kv_dim, s.dim, sig(s.dim)), (f"wo.{l}", s.wtype, s.dim, s.q_dim, sig(s.q_dim))]
         if s.expert_count:
+            # merged expert tensors (GGUF *_exps, src/model.c:409-419): expert e
+            # of a projection is rows [e*n, (e+1)*n)
             t1, t3, t2 = s.exp_types
-            out += [(f"router.{l}", F32, s.expert_count, s.dim, sig(s.dim))]
-            for e in range(s.expert_count):
-                out += [(f"exp_w1.{l}.{e}", t1, s.hidden_dim, s.dim, sig(s.dim)),
-                        (f"exp_w3.{l}.{e}", t3, s.hidden_dim, s.dim, sig(s.dim)),
-                        (f"exp_w2.{l}.{e}", t2, s.dim, s.hidden_dim, sig(s.hidden_dim))]
+            E = s.expert_count
+            out += [(f"router.{l}", F32, E, s.dim, sig(s.dim)),
+                    (f"exp_w1.{l}", t1, E * s.hidden_dim, s.dim, sig(s.dim)),
+                    (f"exp_w3.{l}", t3, E * s.hidden_dim, s.dim, sig(s.dim)),
+                    (f"exp_w2.{l}", t2, E * s.dim, s.hidden_dim, sig(s.hidden_dim))]
             if s.shexp_hidden_dim:
                 a, b, c = s.shexp_types
                 sh = s.shexp_hidden_dim
@@ -185,9 +193,14 @@ def tensor_list(s):
     return out
 
 
-def build(spec, seed=0):
-    """The model's tensors packed into one 32-byte aligned host buffer."""
-    rng = synth.rng_for(seed)
+def build(spec, seed=0, threads=None):
+    """The model's tensors packed into one 32-byte aligned host buffer.
+
+    Tensor i is drawn from its own PCG64 stream seeded by (seed, i), so the
+    tensors can be generated on all host cores and the bytes do not depend
+    on the thread count."""
+    import os
+    from concurrent.futures import ThreadPoolExecutor
     tl = tensor_list(spec)
     off, pos = {}, 0
     for name, t, n, d, _ in tl:
@@ -195,13 +208,19 @@ def build(spec, seed=0):
         off[name] = (pos, nb, t)
         pos = (pos + nb + ALIGN - 1) // ALIGN * ALIGN
     buf = np.zeros(pos + ALIGN, np.uint8)
-    for name, t, n, d, sigma in tl:
+
+    def one(i):
+        name, t, n, d, sigma = tl[i]
+        rng = np.random.Generator(np.random.PCG64(np.random.SeedSequence([seed, i])))
         o, nb, _ = off[name]
         if sigma is None:  # RMSNorm weight: 1 + N(0, 0.02)
             w = (1.0 + 0.02 * rng.standard_normal(d, dtype=np.float32)).astype(np.float32)
             buf[o:o + nb] = w.view(np.uint8)
         else:
             buf[o:o + nb] = pack(rng, t, n, d, sigma).reshape(-1)
+
+    with ThreadPoolExecutor(max_workers=threads or os.cpu_count() or 1) as ex:
+        list(ex.map(one, range(len(tl))))
     return Model(spec, buf, off)
 
 

@@ -75,6 +75,8 @@ SIGNATURES = {
     "quantr_dequantize_rows_dev": (_i, [_vp, _ll, _vp, _ll, _u32, _i, _i, _vp]),
     "quantr_decoder_generate_dev": (_i, [_vp, _vp, _i, _i, _vp, _vp]),
     "quantr_decoder_launches": (_i, [_vp, _c.POINTER(_i), _c.POINTER(_i)]),
+    "quantr_decoder_kv": (_i, [_vp, _c.POINTER(_vp), _c.POINTER(_vp), _c.POINTER(_sz)]),
+    "quantr_moe_shared_dev": (_i, [_vp, _ll, _vp, _ll, _i, _vp, _vp, _u32, _vp, _u32, _vp, _u32, _i, _i, _vp]),
 }
 
 
@@ -317,6 +319,14 @@ def moe_combine_dev(out, ldo, o, sel, wts, T, k, dim, stream=0):
         raise QuantrError(rc, "quantr_moe_combine_dev")
 
 
+def moe_shared_dev(out, ldo, xb, ldx, T, gate, w1, t1, w3, t3, w2, t2, dim, hidden, stream=0):
+    """quantr_moe_shared_dev: out += sigmoid(gate.xb) * shared-expert FFN(xb)."""
+    rc = lib().quantr_moe_shared_dev(out, ldo, xb, ldx, T, gate, w1, t1, w3, t3, w2, t2, dim, hidden,
+                                     stream or None)
+    if rc:
+        raise QuantrError(rc, "quantr_moe_shared_dev")
+
+
 def moe_layer(xb, E, k, w1, t1, w3, t3, w2, t2, dim, hidden, router=None, logits=None):
     """quantr_moe_layer with host arrays.  w1/w3/w2: lists of E host arrays
     (views into registered arrays); returns (out, sel, wts, rc)."""
@@ -397,9 +407,9 @@ def describe_model(model):
     if s.expert_count:
         m.ffn_gate_inp = ptrs([f"router.{l}" for l in range(L)])
         for w in ("exp_w1", "exp_w2", "exp_w3"):
-            per_layer = [ptrs([f"{w}.{l}.{e}" for e in range(s.expert_count)]) for l in range(L)]
+            per_layer = [arr(_vp, [model.expert_ptr(w, l, e) for e in range(s.expert_count)]) for l in range(L)]
             setattr(m, "expert_" + w[4:], arr(_P(_vp), per_layer))
-            setattr(m, w + "_type", types([f"{w}.{l}.0" for l in range(L)]))
+            setattr(m, w + "_type", types([f"{w}.{l}" for l in range(L)]))
     m.head_dim = s.head_dim
     if s.shexp_hidden_dim:
         m.shexp_hidden_dim = s.shexp_hidden_dim
@@ -462,6 +472,12 @@ class Decoder:
         rc = lib().quantr_decoder_generate_dev(self._h, prompt, n_prompt, steps, out, stream or None)
         if rc:
             raise QuantrError(rc, "quantr_decoder_generate_dev")
+
+    def kv(self):
+        """(key cache, value cache) device addresses and bytes of each."""
+        k, v, n = ctypes.c_void_p(), ctypes.c_void_p(), ctypes.c_size_t()
+        lib().quantr_decoder_kv(self._h, ctypes.byref(k), ctypes.byref(v), ctypes.byref(n))
+        return k.value, v.value, n.value
 
     def info(self):
         a, b, c = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()

@@ -168,6 +168,15 @@ def test_generate_moe_batched_tensor_cores(qr_gpu):
     run_generate(qr_gpu, spec, batch=20, n_prompt=5, steps=6)
 
 
+def test_c5_layer_shapes_batch64(qr_gpu):
+    """BASELINE config c5's layer at full width (hidden 2048, 32/4 heads of
+    head_dim 128, 128 experts top-8 of intermediate 768, all Q4_K), 2 layers,
+    64 sequences: every sequence's greedy tokens identical to the per-sequence
+    restated forward_runtime (the oracle c5 names)."""
+    spec = ms.qwen3_moe(layers=2, vocab=1024, seq_len=16)
+    run_generate(qr_gpu, spec, seed=12, n_prompt=4, steps=4, batch=64)
+
+
 def test_step_dev_matches_forward(qr_gpu):
     """quantr_decoder_step_dev with device tokens/positions, two sequences at
     different positions."""

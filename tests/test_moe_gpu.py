@@ -130,6 +130,42 @@ def test_moe_c4_layer(qr_gpu, orc):
     print(f"c4 bit-identical fraction {exact:.6f}")
 
 
+def test_moe_c4_layer_with_shared_expert(qr_gpu, orc):
+    """BASELINE config c4 complete: the routed experts (60 of 1408, top-4,
+    gate/up Q5_K, down Q6_K) plus the shared expert of 5632 with its sigmoid
+    gate (quantr_moe_shared_dev), 64 tokens; bit-identical to the oracle's
+    routed block followed by qo_shared_expert."""
+    c = make_case(13, T=64, E=60, k=4, dim=2048, hidden=1408, t1=Q5_K, t3=Q5_K, t2=Q6_K)
+    rng = synth.rng_for(14)
+    sh = 5632
+    w1s, w3s = synth.matrix(rng, Q5_K, sh, 2048), synth.matrix(rng, Q5_K, sh, 2048)
+    w2s = synth.matrix(rng, Q6_K, 2048, sh)
+    gate = (rng.standard_normal(2048, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    T, dim = c["T"], c["dim"]
+    xb = _dev(c["xb"])
+    out = torch.full((T, dim), float("nan"), device="cuda")
+    ws_bytes = qr_gpu.moe_workspace_bytes(T, c["E"], c["k"], dim, c["hidden"])
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device="cuda")
+    lg = _dev(c["logits"])
+    d1, d3, d2, dg = _dev(w1s), _dev(w3s), _dev(w2s), _dev(gate)
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):  # the second call reuses the plans of the first
+        qr_gpu.moe_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, c["E"], c["k"], c["w1"].weights(qr_gpu),
+                       c["w3"].weights(qr_gpu), c["w2"].weights(qr_gpu), dim, c["hidden"], ws.data_ptr(), ws_bytes,
+                       logits=lg.data_ptr(), ldl=c["E"], stream=stream)
+        qr_gpu.moe_shared_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, dg.data_ptr(), d1.data_ptr(), Q5_K,
+                              d3.data_ptr(), Q5_K, d2.data_ptr(), Q6_K, dim, sh, stream)
+        torch.cuda.synchronize()
+        got = out.cpu().numpy()
+        want, _, _ = oracle_case(orc, c)
+        want = np.array(want, np.float32)
+        for t in range(T):
+            orc.shared_expert(want[t], c["xb"][t], gate, w1s, Q5_K, w3s, Q5_K, w2s, Q6_K, dim, sh)
+        assert np.all(np.abs(got - want) <= ATOL + RTOL * np.abs(want))
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    assert qr_gpu.device_status() == 0
+
+
 def test_moe_c5_layer(qr_gpu, orc):
     """Qwen3-30B-A3B experts: E=128, top-8, I=768 (3 SB), all Q4_K."""
     c = make_case(4, T=16, E=128, k=8, dim=2048, hidden=768, t1=Q4_K, t3=Q4_K, t2=Q4_K)
