@@ -187,6 +187,21 @@ __device__ __forceinline__ int8_t lrintf_to_i8(float v)
     return fabsf(v) < 9.2233720368547758e18f ? (int8_t)__float2ll_rn(v) : (int8_t)0;
 }
 
+// 16-byte cp.async (global -> shared, bypassing L1) and its group fences.
+// The copies of a thread are complete and visible to it after cp_wait<N>()
+// leaves at most N of its newest groups pending; other threads see them after
+// a barrier.
+__device__ __forceinline__ void cp16(uint32_t dst, const void* src)
+{
+    asm volatile("cp.async.cg.shared.global.L2::128B [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait()
+{
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // dp4a with unsigned bytes in `a` and signed bytes in `b`.
 __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c)
 {

@@ -217,37 +217,83 @@ __global__ void __launch_bounds__(kThreads) k_gemv(KParams p)
 
 // F32 weights (reference src/quant.c:455-461, which is KernelOps matmul_ref,
 // src/kernels.c:18-28): one thread per (row, token) summing row[j]*x[j] left
-// to right.  A CTA covers RT rows x TT tokens; 32-column tiles of the weights
-// and of x pass through shared memory.
-template <int RT, int TT>
+// to right.  A CTA covers RT rows x TT tokens; KT-column tiles of the weights
+// and of x stream through a 3-stage shared-memory ring (16-byte cp.async when
+// rows are 16-byte aligned, plain loads otherwise), so two tiles are in
+// flight while one is summed.  Tile rows have a stride of KT + 4 floats, so
+// the 128-bit reads of 8 consecutive rows hit distinct banks.
+constexpr int kF32Stages = 3;
+
+template <int RT, int TT, int KT>
+constexpr size_t f32_smem() { return (size_t)kF32Stages * (RT + TT) * (KT + 4) * sizeof(float); }
+
+template <int RT, int TT, int KT>
 __global__ void __launch_bounds__(RT * TT)
     k_gemv_f32(const float* __restrict__ w, const float* __restrict__ x, long long ldx, float* __restrict__ out,
                long long ldo, int n, int d, int B)
 {
-    constexpr int kWarps = RT * TT / 32;
-    __shared__ float tile[RT][33];
-    __shared__ float xt[TT][33];
+    constexpr int NT = RT * TT, KS = KT + 4, S = kF32Stages, WS = RT * KS, XS = TT * KS;
+    extern __shared__ __align__(16) float fsm[];
     pdl_trigger();
-    pdl_wait();
-    const int r0 = blockIdx.x * RT, t0 = blockIdx.y * TT;
-    const int tid = threadIdx.x;
+    const int r0 = blockIdx.x * RT, t0 = blockIdx.y * TT, tid = threadIdx.x;
     const int rr = tid % RT, tt = tid / RT;
-    const int lane = tid & 31, warp = tid >> 5;
-    float acc = 0.0f;
-    for (int c0 = 0; c0 < d; c0 += 32) {
-        const int cw = min(32, d - c0);
-        __syncthreads();
-        for (int q = warp; q < RT; q += kWarps) {
-            const int r = r0 + q;
-            tile[q][lane] = (r < n && lane < cw) ? w[(long long)r * d + c0 + lane] : 0.0f;
+    const int ntile = (d + KT - 1) / KT;
+    const bool wal = ((uintptr_t)w & 15) == 0 && (d & 3) == 0;
+    const bool xal = ((uintptr_t)x & 15) == 0 && (ldx & 3) == 0;
+    // Tile c of `rows` rows starting at g0 of src (row stride ld) -> dst.
+    auto load = [&](float* dst, const float* src, long long ld, int g0, int rows, int lim, bool al, int c) {
+        const int c0 = c * KT;
+        for (int q = tid; q < rows * (KT / 4); q += NT) {
+            const int r = q / (KT / 4), k = 4 * (q - r * (KT / 4));
+            const int g = g0 + r, col = c0 + k;
+            if (g >= lim || col >= d) continue;
+            float* sd = dst + r * KS + k;
+            const float* gs = src + (long long)g * ld + col;
+            if (al) {
+                cp16(sptr(sd), gs);
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    if (col + e < d) sd[e] = gs[e];
+            }
         }
-        for (int q = warp; q < TT; q += kWarps) {
-            const int t = t0 + q;
-            xt[q][lane] = (t < B && lane < cw) ? x[(long long)t * ldx + c0 + lane] : 0.0f;
-        }
-        __syncthreads();
-        for (int c = 0; c < cw; ++c) acc = __fadd_rn(acc, __fmul_rn(tile[rr][c], xt[tt][c]));
+    };
+    auto stage = [&](int c) { return fsm + (c % S) * (WS + XS); };
+#pragma unroll
+    for (int c = 0; c < S - 1; ++c)
+        if (c < ntile) load(stage(c), w, d, r0, RT, n, wal, c);  // weights never depend on the previous kernel
+    pdl_wait();
+#pragma unroll
+    for (int c = 0; c < S - 1; ++c) {
+        if (c < ntile) load(stage(c) + WS, x, ldx, t0, TT, B, xal, c);
+        cp_commit();
     }
+    float acc = 0.0f;
+    for (int c = 0; c < ntile; ++c) {
+        __syncthreads();  // the stage refilled next was read in the previous iteration
+        const int cn = c + S - 1;
+        if (cn < ntile) {
+            load(stage(cn), w, d, r0, RT, n, wal, cn);
+            load(stage(cn) + WS, x, ldx, t0, TT, B, xal, cn);
+        }
+        cp_commit();
+        cp_wait<S - 1>();
+        __syncthreads();
+        const float* wt = stage(c) + rr * KS;
+        const float* xt = stage(c) + WS + tt * KS;
+        const int cw = min(KT, d - c * KT);
+        int j = 0;
+        for (; j + 4 <= cw; j += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(wt + j);
+            const float4 b = *reinterpret_cast<const float4*>(xt + j);
+            acc = __fadd_rn(acc, __fmul_rn(a.x, b.x));
+            acc = __fadd_rn(acc, __fmul_rn(a.y, b.y));
+            acc = __fadd_rn(acc, __fmul_rn(a.z, b.z));
+            acc = __fadd_rn(acc, __fmul_rn(a.w, b.w));
+        }
+        for (; j < cw; ++j) acc = __fadd_rn(acc, __fmul_rn(wt[j], xt[j]));
+    }
+    cp_wait<0>();
     if (r0 + rr < n && t0 + tt < B) out[(long long)(t0 + tt) * ldo + r0 + rr] = acc;
 }
 
@@ -436,10 +482,19 @@ cudaError_t launch_gemv_f32(const float* w, const float* x, long long ldx, float
                             int d, int B, const LaunchCfg& c)
 {
     if (n <= 0 || B <= 0) return cudaSuccess;
-    if (B == 1)
-        return launch_ex(&k_gemv_f32<128, 1>, dim3((n + 127) / 128), dim3(128), 0, c, w, x, ldx, out, ldo, n, d, B);
-    return launch_ex(&k_gemv_f32<32, 4>, dim3((n + 31) / 32, (B + 3) / 4), dim3(128), 0, c, w, x, ldx, out, ldo, n,
-                     d, B);
+    static int dev1 = -1, dev4 = -1;
+    if (B == 1) {
+        constexpr size_t sm = f32_smem<128, 1, 64>();
+        cudaError_t e = ensure_smem_attr(&k_gemv_f32<128, 1, 64>, (int)sm, dev1);
+        if (e != cudaSuccess) return e;
+        return launch_ex(&k_gemv_f32<128, 1, 64>, dim3((n + 127) / 128), dim3(128), sm, c, w, x, ldx, out, ldo, n, d,
+                         B);
+    }
+    constexpr size_t sm = f32_smem<32, 4, 128>();
+    cudaError_t e = ensure_smem_attr(&k_gemv_f32<32, 4, 128>, (int)sm, dev4);
+    if (e != cudaSuccess) return e;
+    return launch_ex(&k_gemv_f32<32, 4, 128>, dim3((n + 31) / 32, (B + 3) / 4), dim3(128), sm, c, w, x, ldx, out, ldo,
+                     n, d, B);
 }
 
 cudaError_t launch_dequantize_rows(float* out, long long ldo, const uint8_t* src, long long src_stride, uint32_t type,

@@ -289,3 +289,27 @@ def test_launch_counter_moves(qr_gpu):
     before = qr_gpu.launch_count()
     qr_gpu.matmul_q_fused(np.ones(256, np.float32), np.zeros((4, 144), np.uint8), 12, 4, 256)
     assert qr_gpu.launch_count() >= before + 2  # quantizer + GEMV
+
+
+@pytest.mark.parametrize("n,d,B,ldx_pad,xoff", [(128, 2048, 64, 0, 0), (1, 2048, 64, 0, 0), (60, 2048, 1, 0, 0),
+                                                (200, 2048, 1, 0, 0), (37, 1001, 5, 3, 1), (130, 333, 7, 0, 2),
+                                                (64, 64, 3, 4, 0)])
+def test_f32_gemv_shapes(qr_gpu, orc, n, d, B, ldx_pad, xoff):
+    """F32 weights (routers, the shared-expert gate): the reference's
+    matmul_ref order per (row, token), bit for bit, for aligned rows (16-byte
+    copies), odd widths and misaligned or padded activations (plain loads)."""
+    rng = synth.rng_for(n * 131 + d + B)
+    w = (rng.standard_normal((n, d), dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    x = synth.activations(rng, B, d)
+    ldx = d + ldx_pad
+    xbuf = np.zeros(xoff + B * ldx, np.float32)
+    for t in range(B):
+        xbuf[xoff + t * ldx:xoff + t * ldx + d] = x[t]
+    wd, xd = _dev(w), _dev(xbuf)
+    out = torch.full((B, n), float("nan"), device="cuda")
+    ws = torch.empty(max(256, qr_gpu.workspace_bytes(d, B)), dtype=torch.uint8, device="cuda")
+    qr_gpu.gemv_dev(out.data_ptr(), n, xd.data_ptr() + 4 * xoff, ldx, wd.data_ptr(), 0, n, d, B, ws.data_ptr(),
+                    ws.numel(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    want = np.stack([orc.matmul_f32(x[t], w, n, d) for t in range(B)])
+    assert_bit_exact(out.cpu().numpy(), want)
