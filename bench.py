@@ -28,7 +28,15 @@ batch_sweep : the rest of the c2 sweep (batch 4 and 16 by default, --sweep)
          on the same weights, timed like `value`; jobs of 2+ tokens run on
          the tensor-core kernel.
 c1_q8_0 : BASELINE config c1 (Q8_0 5632x2048 GEMV, batch 1), 16 distinct
-         copies per replay so every replay streams from HBM (--no-c1 skips).
+         copies per replay so every replay streams from HBM (--no-c1 skips),
+         with its own CPU baseline (the reference's matmul_q_fused).
+decode_c3, moe_c4, decode_c5 : BASELINE configs c3 (TinyLlama decode, batch
+         1), c4 (one Qwen1.5-MoE layer with shared expert, 64 tokens) and c5
+         (Qwen3-30B-A3B decode, 64 sequences), each with its CPU baseline.
+int8_compute : the compute-bound int8 case (one c5 expert, 1024 tokens per
+         GEMV) in TOP/s against the int8 tensor peak measured in-process.
+sharded : the two multi-GPU forms (row-sharded head GEMV with all-gather,
+         expert-parallel MoE with all-to-all dispatch) with parity flags.
 N > 1  : every rank runs its own replica of the step on its GPU (the GEMV
          metric shards by independent work; no collective on the data path),
          so scaling is weak.
@@ -179,6 +187,37 @@ def cpu_reference_run(layers, B, steps, warmup, budget_s=None):
     el = time.perf_counter() - t0
     nbytes = sum(gemv_bytes(t, n, d, B) for t, n, d, _ in shapes)
     return nbytes * done / el / 1e9, el, done, threads, variant, kind
+
+
+def cpu_c1_run(budget_s):
+    """The reference's matmul_q_fused on the c1 shape (Q8_0 5632x2048, batch
+    1) on this host, over 16 distinct weight copies like the GPU line.
+    Returns (GB/s, calls, threads, variant, kind)."""
+    import ctypes
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    threads = os.cpu_count() or 1
+    import oracle  # test infrastructure: the CPU baseline leg only
+    variant = oracle.best_cpu_variant()
+    if oracle.ref_available(variant):
+        lib, kind = oracle.RefLib(variant), "reference"
+    else:
+        lib, kind, variant = oracle.Oracle(), "port", "restatement"
+    rng = synth.rng_for(12)
+    n, d = 5632, 2048
+    w0 = synth.matrix(rng, Q8_0, n, d)
+    ws = [w0.copy() for _ in range(16)]
+    x = synth.activations(rng, 1, d)[0]
+    out = np.empty(n, np.float32)
+    f = lib.fn["matmul_q_fused"]
+    P = ctypes.c_void_p
+    f(out.ctypes.data_as(P), x.ctypes.data_as(P), ws[0].ctypes.data_as(P), Q8_0, n, d, threads)
+    done = 0
+    t0 = time.perf_counter()
+    while done < 3 or (time.perf_counter() - t0 < budget_s and done < 100000):
+        f(out.ctypes.data_as(P), x.ctypes.data_as(P), ws[done % 16].ctypes.data_as(P), Q8_0, n, d, threads)
+        done += 1
+    el = time.perf_counter() - t0
+    return gemv_bytes(Q8_0, n, d, 1) * done / el / 1e9, done, threads, variant, kind
 
 
 def reference_arm(args):
@@ -379,6 +418,11 @@ def ours_arm(args):
               "frac_of_peak": round(nb / (t_ms / 1e3) / 1e9 / load_peaks()[0], 4),
               "workload": "c1: 16 distinct Q8_0 5632x2048 GEMVs per replay (196 MB > L2), batch 1"}
         del c1_w
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            gbs_c, done, threads, variant, kind = cpu_c1_run(min(5.0, args.cpu_seconds))
+            c1["cpu_baseline"] = {"value": round(gbs_c, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+                                  "sample": (f"{done} matmul_q_fused calls on the c1 shape over 16 distinct weight "
+                                             f"copies, reference src/quant.c {variant} build")}
 
     # End to end with HOST buffers, (a) through the C-ABI program call: every
     # step copies all 72 inputs from pinned host memory to the device, runs
@@ -487,7 +531,9 @@ def ours_arm(args):
         sharded = sharded_forms(args, dev, world, rank)
         if own_group:
             dist.destroy_process_group()
-    decode = c5 = c4 = None
+    decode = c5 = c4 = i8 = None
+    if rank == 0 and world == 1 and not args.no_int8:
+        i8 = int8_compute(args, dev, s)
     if rank == 0 and world == 1 and not args.no_decode:
         decode = decode_c3(args, dev, s)
     if rank == 0 and world == 1 and not args.no_c4:
@@ -528,6 +574,7 @@ def ours_arm(args):
             "decode_c3": decode,
             "moe_c4": c4,
             "decode_c5": c5,
+            "int8_compute": i8,
             "sharded": sharded,
         }
         print(json.dumps(line), flush=True)
@@ -975,6 +1022,52 @@ def moe_c4(args, dev, s):
     return res
 
 
+def int8_compute(args, dev, s):
+    """The compute-bound int8 case: one c5 expert's three projections (W1, W3
+    768x2048 and W2 2048x768, Q4_K) with 1024 tokens each, one program (the
+    tensor-core kernel, 64-token slices re-reading the weights from L2).
+    Reports int8 TOP/s (2*n*d*tokens per GEMV) against this GPU's dense int8
+    peak measured in the same process (cuBLASLt through torch._int_mm)."""
+    import torch
+
+    import quantr
+    rng = synth.rng_for(88)
+    T, hid, dim = 1024, 768, 2048
+    shapes = [(Q4_K, hid, dim), (Q4_K, hid, dim), (Q4_K, dim, hid)]
+    ws = [torch.from_numpy(synth.matrix(rng, t, n, d)).to(dev) for t, n, d in shapes]
+    xs = [torch.from_numpy(synth.activations(rng, T, d)).to(dev) for _, _, d in shapes]
+    os_ = [torch.empty(T, n, device=dev) for _, n, _ in shapes]
+    pr = quantr.Program([(w.data_ptr(), t, n, d, T, x.data_ptr(), d, o.data_ptr(), n)
+                         for (t, n, d), w, x, o in zip(shapes, ws, xs, os_)])
+    with torch.cuda.stream(s):
+        pr.run(s.cuda_stream)
+        s.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            pr.run(s.cuda_stream)
+        for _ in range(args.warmup):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    st = quantr.device_status(0)
+    ms = e0.elapsed_time(e1) / args.steps
+    del g
+    info = pr.info()
+    pr.close()
+    ops = sum(2.0 * n * d * T for _, n, d in shapes)
+    tops = ops / (ms / 1e3) / 1e12
+    peak = int8_peak(dev.index if dev.index is not None else 0)
+    return {"workload": ("one c5 expert (W1, W3 768x2048, W2 2048x768, Q4_K) with 1024 tokens per GEMV, one "
+                         "program on the tensor cores (64-token slices)"),
+            "us_per_program": round(ms * 1e3, 2), "int8_tops": round(tops, 2), "int8_peak_tops": round(peak, 1),
+            "frac_of_int8_peak": round(tops / peak, 4), "items": info["items"], "device_status": st,
+            "peak_how": "torch._int_mm 8192^3 int8 GEMM (cuBLASLt), best of 20, same process"}
+
+
 def int8_peak(device=0):
     """Dense int8 tensor throughput of this GPU (TOP/s): torch._int_mm (a cuBLASLt
     int8 x int8 -> int32 GEMM) of 8192^3, best of 20 after warm-up, CUDA events.
@@ -1014,6 +1107,7 @@ def main():
     ap.add_argument("--no-sharded", action="store_true", help="skip the tensor/expert-parallel forms")
     ap.add_argument("--no-c4", action="store_true", help="skip the c4 MoE layer line")
     ap.add_argument("--no-c5", action="store_true", help="skip the c5 decode line (48 layers, 17 GB of weights)")
+    ap.add_argument("--no-int8", action="store_true", help="skip the compute-bound int8 line")
     ap.add_argument("--c5-steps", type=int, default=16)
     ap.add_argument("--decode-steps", type=int, default=128)
     ap.add_argument("--int8-peak", action="store_true",
