@@ -199,9 +199,11 @@ class ExpertShardedMoE:
         dest = self.owner[sel_h[pair]] if pair.numel() else torch.zeros(0, dtype=torch.int64)
         order = torch.argsort(dest * (T * k + 1) + pair)
         pair, dest = pair[order], dest[order]
-        send_counts = torch.bincount(dest, minlength=self.world).to(torch.int64)
+        # 1. counts, exchanged on the tokens' device (NCCL takes device
+        # tensors only; gloo host ones)
+        send_counts = torch.bincount(dest, minlength=self.world).to(torch.int64).to(xb.device)
         recv_counts = torch.empty_like(send_counts)
-        self._a2a(recv_counts, send_counts, None, None)  # 1. counts
+        self._a2a(recv_counts, send_counts, None, None)
         sc, rc = send_counts.tolist(), recv_counts.tolist()
         n_send, n_recv = sum(sc), sum(rc)
         # 2. dispatch: Q8_0 rows of the pairs' tokens, and their expert ids.
