@@ -83,6 +83,7 @@ __device__ __forceinline__ void tgts_write(const Tgts& tg, int t, int b, int lan
 
 struct Dims {
     int B, dim, q_dim, kv_dim, hd, n_heads, n_kv, kv_mul, seq_len, hidden, vocab, kv_type;
+    int vst;  // value-row stages of the attention kernel's ring (set with its shared-memory size)
     float inv_sqrt;
     int kv_B;        // sequences the KV cache holds
     int seq_stride;  // KV-cache sequence of step row b = b * seq_stride (0: every row is one sequence's position)
@@ -310,7 +311,9 @@ __global__ void k_att_scores(const float* __restrict__ q, const float* __restric
     const int t0 = blockIdx.y * kScoreTile;
     const int p = pos[b];
     if (p < 0 || t0 > p) return;
-    const int hd = D.hd, ld = hd + 1;  // padded rows: lanes read one column of different rows
+    // Rows padded to hd + 4 floats: 16-byte aligned, and the 128-bit reads of
+    // 8 consecutive rows (one per lane) hit distinct banks (hd % 32 == 0).
+    const int hd = D.hd, ld = hd + 4;
     float* Ks = sm;
     float* Qs = sm + kScoreTile * ld;
     const int nthr = blockDim.x * blockDim.y, tid = threadIdx.y * blockDim.x + threadIdx.x;
@@ -329,19 +332,12 @@ __global__ void k_att_scores(const float* __restrict__ q, const float* __restric
     for (int wd = tid; wd < words; wd += nthr) {
         const uint4 v = src[wd];
         const int e = wd * EPW, tt = e / hd, i = e % hd;
-        float* dst = Ks + tt * ld + i;
+        float4* dst = reinterpret_cast<float4*>(Ks + tt * ld + i);
         if (KVT) {
-            const uint32_t h[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                dst[2 * k] = h2f_ref(h[k] & 0xFFFFu);
-                dst[2 * k + 1] = h2f_ref(h[k] >> 16);
-            }
+            dst[0] = make_float4(h2f_ref(v.x & 0xFFFFu), h2f_ref(v.x >> 16), h2f_ref(v.y & 0xFFFFu), h2f_ref(v.y >> 16));
+            dst[1] = make_float4(h2f_ref(v.z & 0xFFFFu), h2f_ref(v.z >> 16), h2f_ref(v.w & 0xFFFFu), h2f_ref(v.w >> 16));
         } else {
-            dst[0] = __uint_as_float(v.x);
-            dst[1] = __uint_as_float(v.y);
-            dst[2] = __uint_as_float(v.z);
-            dst[3] = __uint_as_float(v.w);
+            dst[0] = make_float4(__uint_as_float(v.x), __uint_as_float(v.y), __uint_as_float(v.z), __uint_as_float(v.w));
         }
     }
     for (int e = 2 * tid; e < D.kv_mul * hd; e += 2 * nthr) {
@@ -367,52 +363,66 @@ __global__ void k_att_scores(const float* __restrict__ q, const float* __restric
     __syncthreads();
     const int tt = threadIdx.x, m = threadIdx.y;
     if (tt < nt && m < D.kv_mul) {
-        const float* kr = Ks + tt * ld;
-        const float* qh = Qs + m * hd;
+        // dot_ref order: element 0, 1, 2, ... (4 per 128-bit load; hd % 8 == 0)
+        const float4* kr = reinterpret_cast<const float4*>(Ks + tt * ld);
+        const float4* qh = reinterpret_cast<const float4*>(Qs + m * hd);
         float s = 0.0f;
-        int i = 0;
-        for (; i + 8 <= hd; i += 8) {
-            float pr[8];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) pr[k] = __fmul_rn(qh[i + k], kr[i + k]);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) s = __fadd_rn(s, pr[k]);
+#pragma unroll 4
+        for (int i4 = 0; i4 < hd / 4; ++i4) {
+            const float4 a = qh[i4], k = kr[i4];
+            const float p0 = __fmul_rn(a.x, k.x), p1 = __fmul_rn(a.y, k.y), p2 = __fmul_rn(a.z, k.z),
+                        p3 = __fmul_rn(a.w, k.w);
+            s = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(s, p0), p1), p2), p3);
         }
-        for (; i < hd; ++i) s = __fadd_rn(s, __fmul_rn(qh[i], kr[i]));
         const int h = kh * D.kv_mul + m;
         att[((long long)b * D.n_heads + h) * D.seq_len + t0 + tt] = __fmul_rn(s, D.inv_sqrt);
     }
 }
 
-constexpr int kVTile = 64;    // value rows per pipeline stage
-constexpr int kVStages = 3;   // stages in flight
+constexpr int kVTile = 32;       // value rows per pipeline stage
+constexpr int kVMaxStages = 64;  // most stages of the ring (Dims::vst)
+
+// Score rows in shared memory: seq_len rounded up to 32, plus 4 floats, so
+// rows are 16-byte aligned and two heads' rows start in different banks.
+__host__ __device__ inline int att_sstride(int seq_len) { return ((seq_len + 31) & ~31) + 4; }
+// Threads: one per 4 consecutive output elements of the kv_mul heads, and at
+// least one warp per head (the softmax runs a head per warp), in whole warps.
+__host__ __device__ inline int att_v_threads_of(int kv_mul, int hd)
+{
+    const int t = (kv_mul * hd / 4 + 31) / 32 * 32;
+    return t > 32 * kv_mul ? t : 32 * kv_mul;
+}
 
 // Per (sequence, KV head): softmax_ref of each query head's scores
 // (src/kernels.c:191-207) and out_h[i] = sum over positions, in order, of
 // att_h[t] * v_t[i] from 0 (src/runtime.c:171-194).  The kv_mul heads share
-// the value rows, which stream through a ring of shared-memory stages by
-// bulk copies (one per row, mbarrier completion; the first stages are in
-// flight while the softmax runs), so each running sum reads shared memory
-// and the rows are read from memory once per KV head.
+// the value rows, which stream through a ring of shared-memory stages (one
+// bulk copy per tile of rows, mbarrier completion; the first stages are in
+// flight while the softmax runs), so the rows are read from memory once per
+// KV head.  Each thread owns 4 consecutive elements of one head's output:
+// four independent running sums that advance position by position, fed by
+// 128-bit reads of 4 scores and of each row's 4 elements.
 template <int KVT>
 __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __restrict__ vcache, long long layer_off,
                                 const int* __restrict__ pos, float* __restrict__ xa, int* err, Dims D,
                                 const __grid_constant__ Tgts tg)
 {
     extern __shared__ __align__(16) unsigned char smraw[];
-    __shared__ __align__(8) uint64_t bars[kVStages];
+    __shared__ __align__(8) uint64_t bars[kVMaxStages];
     __shared__ int s_abort;
     constexpr int ES = KVT ? 2 : 4;
     const int hd = D.hd;
     const int row_bytes = hd * ES;
     const int stage_bytes = kVTile * row_bytes;
-    unsigned char* vring = smraw;                                        // [kVStages][kVTile][hd]
-    float* S = reinterpret_cast<float*>(smraw + kVStages * stage_bytes);  // [kv_mul][seq_len]
+    const int ss = att_sstride(D.seq_len);
+    const int NS = D.vst;  // stages in flight
+    unsigned char* vring = smraw;                                  // [NS][kVTile][hd]
+    float* S = reinterpret_cast<float*>(smraw + NS * stage_bytes);  // [kv_mul][ss]
     const int b = blockIdx.x / D.n_kv, kh = blockIdx.x % D.n_kv;
     const int tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     if (tid == 0) {
-        for (int i = 0; i < kVStages; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
         s_abort = 0;
     }
@@ -425,28 +435,30 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
     // The head's value rows are contiguous: one bulk copy per tile.
     const unsigned char* vrow0 =
         static_cast<const unsigned char*>(vcache) + kv_head_base(D, layer_off, b, kh) * ES;
-    auto issue = [&](int j) {  // one thread: tile j's rows into stage j % kVStages
-        const int st = j % kVStages, t0 = j * kVTile, nt = min(kVTile, np - t0);
+    auto issue = [&](int j) {  // one thread: tile j's rows into stage j % NS
+        const int st = j % NS, t0 = j * kVTile, nt = min(kVTile, np - t0);
         mbar_arrive_expect_tx(&bars[st], (uint32_t)(nt * row_bytes));
         bulk_g2s(vring + st * stage_bytes, vrow0 + (long long)t0 * row_bytes, (uint32_t)(nt * row_bytes), &bars[st]);
     };
     if (tid == 0)
-        for (int j = 0; j < min(kVStages, ntiles); ++j) issue(j);
+        for (int j = 0; j < min(NS, ntiles); ++j) issue(j);
 
-#pragma unroll 4
-    for (int e = tid; e < D.kv_mul * np; e += blockDim.x) {
-        const int m = e / np, t = e % np;
-        S[m * D.seq_len + t] = att[((long long)b * D.n_heads + kh * D.kv_mul + m) * D.seq_len + t];
-    }
-    __syncthreads();
     for (int m = warp; m < D.kv_mul; m += nwarps) {
-        float* s = S + m * D.seq_len;
-        // max: x[0], then any strictly greater value (a NaN at 0 sticks).
-        float mx = s[0];
-        const bool nan0 = mx != mx;
-        for (int t = lane; t < np; t += 32) mx = fmaxf(mx, s[t]);
+        // Warp m copies head m's scores into shared memory and takes their
+        // maximum: x[0], then any strictly greater value (a NaN at 0 sticks).
+        float* s = S + m * ss;
+        const float* a = att + ((long long)b * D.n_heads + kh * D.kv_mul + m) * D.seq_len;
+        const float a0 = a[0];
+        float mx = a0;
+#pragma unroll 4
+        for (int t = lane; t < np; t += 32) {
+            const float v = a[t];
+            s[t] = v;
+            mx = fmaxf(mx, v);
+        }
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (nan0) mx = s[0];
+        if (a0 != a0) mx = a0;
+        __syncwarp();
         for (int t = lane; t < np; t += 32) s[t] = libm::expf_ref(__fsub_rn(s[t], mx));
         __syncwarp();
         float inv = 0.0f;
@@ -456,53 +468,58 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
     }
     __syncthreads();
 
-    // Running sums: thread (m, i) for e = tid; kv_mul * hd <= 2 * blockDim.
-    const int nout = D.kv_mul * hd;
-    const int e0 = tid, e1 = tid + blockDim.x;
-    const int m0 = e0 / hd, i0 = e0 % hd, m1 = e1 / hd, i1 = e1 % hd;
-    float acc0 = 0.0f, acc1 = 0.0f;
-    int issued = min(kVStages, ntiles);  // meaningful in thread 0
+    // Thread (m, q): outputs 4q .. 4q+3 of head m.
+    const int nq = hd / 4, nout = D.kv_mul * hd;
+    const bool live = tid < D.kv_mul * nq;
+    const int m = live ? tid / nq : 0, q = live ? tid % nq : 0;
+    float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+    int issued = min(NS, ntiles);  // meaningful in thread 0
     int j = 0;
     for (; j < ntiles; ++j) {
-        const int st = j % kVStages;
+        const int st = j % NS;
         // Every thread waits on the same stage; a wait that gives up (250 ms)
         // raises the CTA's abort flag, which the barrier makes uniform.
-        if (!mbar_wait_bounded(&bars[st], (uint32_t)((j / kVStages) & 1), err, &s_abort)) s_abort = 1;
+        if (!mbar_wait_bounded(&bars[st], (uint32_t)((j / NS) & 1), err, &s_abort)) s_abort = 1;
         __syncthreads();
         if (s_abort) break;
         const int t0 = j * kVTile, nt = min(kVTile, np - t0);
-        const unsigned char* vt = vring + st * stage_bytes;
-        // Both running sums advance position by position; their products are
-        // formed eight positions ahead of the dependent adds.
-        const bool h0 = e0 < nout, h1 = e1 < nout;
-        const float* sp0 = S + (h0 ? m0 : 0) * D.seq_len + t0;
-        const float* sp1 = S + (h1 ? m1 : 0) * D.seq_len + t0;
-        auto vat = [&](int r, int i) {
-            return KVT ? h2f_ref(reinterpret_cast<const uint16_t*>(vt + r * row_bytes)[i])
-                       : reinterpret_cast<const float*>(vt + r * row_bytes)[i];
+        const unsigned char* vt = vring + st * stage_bytes + (KVT ? 8 : 16) * q;
+        auto vrow = [&](int r) {
+            if (KVT) {
+                const uint2 h = *reinterpret_cast<const uint2*>(vt + r * row_bytes);
+                return make_float4(h2f_ref(h.x & 0xFFFFu), h2f_ref(h.x >> 16), h2f_ref(h.y & 0xFFFFu),
+                                   h2f_ref(h.y >> 16));
+            }
+            return *reinterpret_cast<const float4*>(vt + r * row_bytes);
         };
-        int r = 0;
-        for (; r + 8 <= nt; r += 8) {
-            float p0[8], p1[8];
+        const float* sp = S + m * ss + t0;
+        if (live) {
+            int r = 0;
+            for (; r + 4 <= nt; r += 4) {
+                const float4 s4 = *reinterpret_cast<const float4*>(sp + r);
+                const float sv[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                p0[k] = h0 ? __fmul_rn(sp0[r + k], vat(r + k, i0)) : 0.0f;
-                p1[k] = h1 ? __fmul_rn(sp1[r + k], vat(r + k, i1)) : 0.0f;
+                for (int k = 0; k < 4; ++k) {
+                    const float4 v = vrow(r + k);
+                    a0 = __fadd_rn(a0, __fmul_rn(sv[k], v.x));
+                    a1 = __fadd_rn(a1, __fmul_rn(sv[k], v.y));
+                    a2 = __fadd_rn(a2, __fmul_rn(sv[k], v.z));
+                    a3 = __fadd_rn(a3, __fmul_rn(sv[k], v.w));
+                }
             }
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                acc0 = __fadd_rn(acc0, p0[k]);
-                acc1 = __fadd_rn(acc1, p1[k]);
+            for (; r < nt; ++r) {
+                const float sc = sp[r];
+                const float4 v = vrow(r);
+                a0 = __fadd_rn(a0, __fmul_rn(sc, v.x));
+                a1 = __fadd_rn(a1, __fmul_rn(sc, v.y));
+                a2 = __fadd_rn(a2, __fmul_rn(sc, v.z));
+                a3 = __fadd_rn(a3, __fmul_rn(sc, v.w));
             }
-        }
-        for (; r < nt; ++r) {
-            if (h0) acc0 = __fadd_rn(acc0, __fmul_rn(sp0[r], vat(r, i0)));
-            if (h1) acc1 = __fadd_rn(acc1, __fmul_rn(sp1[r], vat(r, i1)));
         }
         __syncthreads();  // stage st is free again
-        if (tid == 0 && j + kVStages < ntiles) {
-            issue(j + kVStages);
-            issued = j + kVStages + 1;
+        if (tid == 0 && j + NS < ntiles) {
+            issue(j + NS);
+            issued = j + NS + 1;
         }
     }
     if (j < ntiles) {
@@ -510,17 +527,28 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
         // its shared memory is released; the output is not written.
         if (tid == 0)
             for (int jj = j; jj < issued; ++jj)
-                mbar_wait_bounded(&bars[jj % kVStages], (uint32_t)((jj / kVStages) & 1), err, nullptr);
+                mbar_wait_bounded(&bars[jj % NS], (uint32_t)((jj / NS) & 1), err, nullptr);
         return;
     }
-    if (e0 < nout) xa[(long long)b * D.q_dim + (long long)(kh * D.kv_mul + m0) * hd + i0] = acc0;
-    if (e1 < nout) xa[(long long)b * D.q_dim + (long long)(kh * D.kv_mul + m1) * hd + i1] = acc1;
-    // With head_dim a multiple of 32 a warp holds one whole 32-element block
-    // of the attention output: quantize it for the O projection here.
+    if (live)
+        *reinterpret_cast<float4*>(xa + (long long)b * D.q_dim + (long long)(kh * D.kv_mul + m) * hd + 4 * q) =
+            make_float4(a0, a1, a2, a3);
+    // With head_dim a multiple of 32, warp w holds output elements
+    // [128w, 128w + 128) of this KV head: four whole 32-element blocks of the
+    // attention output, quantized here for the O projection (element l of a
+    // block comes from lane 8*block + l/4, component l % 4).
     if (tg.n) {
         const int g0 = kh * D.kv_mul * hd;  // first output element of this KV head
-        if (e0 - lane + 31 < nout) tgts_write(tg, b, (g0 + e0) >> 5, lane, acc0);
-        if (e1 - lane + 31 < nout) tgts_write(tg, b, (g0 + e1) >> 5, lane, acc1);
+#pragma unroll
+        for (int bq = 0; bq < 4; ++bq) {
+            const int src = 8 * bq + (lane >> 2);
+            const float c0 = __shfl_sync(0xffffffffu, a0, src), c1 = __shfl_sync(0xffffffffu, a1, src);
+            const float c2 = __shfl_sync(0xffffffffu, a2, src), c3 = __shfl_sync(0xffffffffu, a3, src);
+            const int c = lane & 3;
+            const float v = c == 0 ? c0 : c == 1 ? c1 : c == 2 ? c2 : c3;
+            const int e = 128 * warp + 32 * bq;
+            if (e < nout) tgts_write(tg, b, (g0 + e) >> 5, lane, v);
+        }
     }
 }
 
@@ -744,14 +772,23 @@ struct ProgJob {
 };
 
 // Threads of the softmax/value kernel: each owns one or two running sums.
-int att_v_threads(const Dims& D)
-{
-    const int nout = D.kv_mul * D.hd;
-    return std::min(1024, std::max(128, ((nout + 1) / 2 + 31) / 32 * 32));
-}
+int att_v_threads(const Dims& D) { return att_v_threads_of(D.kv_mul, D.hd); }
 size_t att_v_smem(const Dims& D)
 {
-    return (size_t)kVStages * kVTile * D.hd * (D.kv_type ? 2 : 4) + (size_t)D.kv_mul * D.seq_len * 4;
+    return (size_t)D.vst * kVTile * D.hd * (D.kv_type ? 2 : 4) + (size_t)D.kv_mul * att_sstride(D.seq_len) * 4;
+}
+// Stages of the value ring: with at least one CTA per SM (batched steps) as
+// many as leave room for two CTAs per SM; with fewer CTAs (one sequence) as
+// many as fit, up to every tile of the context, so the copies of a whole head
+// are in flight at once.
+int att_v_stages(const Dims& D, int sms)
+{
+    const size_t stage = (size_t)kVTile * D.hd * (D.kv_type ? 2 : 4);
+    const size_t scores = (size_t)D.kv_mul * att_sstride(D.seq_len) * 4;
+    const size_t budget = (D.B * D.n_kv >= sms ? kSmemMax / 2 : kSmemMax) - 1024;
+    const long long fit = budget > scores ? (long long)((budget - scores) / stage) : 0;
+    const int tiles = (D.seq_len + kVTile - 1) / kVTile;
+    return (int)std::max<long long>(2, std::min<long long>({fit, (long long)tiles, (long long)kVMaxStages}));
 }
 
 int make_program(quantr_decoder* d, const std::vector<ProgJob>& js, quantr_program** out)
@@ -786,7 +823,7 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
                       d->rms_att[l], d->xb, D.dim, d->t_qkv[l]);
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_qkv[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
-        const size_t ssm = (size_t)(kScoreTile * (D.hd + 1) + D.kv_mul * D.hd) * sizeof(float);
+        const size_t ssm = (size_t)(kScoreTile * (D.hd + 4) + D.kv_mul * D.hd) * sizeof(float);
         if (chunk) {
             e = launch_ex(D.kv_type ? &k_rope_store_rows<1> : &k_rope_store_rows<0>,
                           dim3((D.kv_dim / 2 + 127) / 128, D.B), dim3(128), 0, c, (const float*)d->kc,
@@ -979,13 +1016,14 @@ int create_impl(quantr_decoder** out, const quantr_model* m, int batch, quantr_d
     D.inv_sqrt = 1.0f / std::sqrt((float)hd);
     D.kv_B = parent ? parent->D.kv_B : batch;
     D.seq_stride = parent ? 0 : 1;
+    D.vst = att_v_stages(D, device_sm_count());
     d->child = parent != nullptr;
     d->n_layers = m->n_layers;
     d->E = m->expert_count;
     d->K = m->expert_used_count;
     d->shexp = m->expert_count > 0 && m->shexp_w1 ? m->shexp_hidden_dim : 0;
     if (D.kv_mul > 32 || att_v_smem(D) > kSmemMax || D.kv_mul * hd > 2048 || (hd * (D.kv_type ? 2 : 4)) % 16 || hd % 8 ||
-        (size_t)(kScoreTile * (hd + 1) + D.kv_mul * hd) * 4 > kSmemMax || (size_t)2 * D.dim * 4 > 48 * 1024 || D.dim % 4) {
+        (size_t)(kScoreTile * (hd + 4) + D.kv_mul * hd) * 4 > kSmemMax || (size_t)2 * D.dim * 4 > 48 * 1024 || D.dim % 4) {
         delete d;
         return QUANTR_ERR_TOO_LARGE;
     }
@@ -1322,21 +1360,21 @@ int create_impl(quantr_decoder** out, const quantr_model* m, int batch, quantr_d
     d->weight_bytes = wb;
     d->kv_pos_bytes = (size_t)L * 2 * D.kv_dim * (D.kv_type ? 2 : 4);
 
-    // Dynamic shared memory of the attention kernels beyond the default 48 KB.
+    // Dynamic shared memory of the attention kernels beyond the default 48 KB:
+    // raised to what this decoder needs, never lowered (another decoder's
+    // captured steps may need more).
     {
-        const int ssm = (kScoreTile * (hd + 1) + D.kv_mul * hd) * 4;
+        const int ssm = (kScoreTile * (hd + 4) + D.kv_mul * hd) * 4;
         const int vsm = (int)att_v_smem(D);
-        if (cudaFuncSetAttribute(k_att_scores<0, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(k_att_scores<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(k_att_scores<0, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(k_att_scores<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ssm) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(k_att_softmax_v<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) !=
-                cudaSuccess ||
-            cudaFuncSetAttribute(k_att_softmax_v<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, vsm) != cudaSuccess)
+        auto raise = [](const void* f, int bytes) {
+            cudaFuncAttributes fa{};
+            if (cudaFuncGetAttributes(&fa, f) != cudaSuccess) return false;
+            if (fa.maxDynamicSharedSizeBytes >= bytes) return true;
+            return cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+        };
+        if (!raise((const void*)k_att_scores<0, true>, ssm) || !raise((const void*)k_att_scores<1, true>, ssm) ||
+            !raise((const void*)k_att_scores<0, false>, ssm) || !raise((const void*)k_att_scores<1, false>, ssm) ||
+            !raise((const void*)k_att_softmax_v<0>, vsm) || !raise((const void*)k_att_softmax_v<1>, vsm))
             return fail(QUANTR_ERR_CUDA);
     }
 

@@ -145,13 +145,22 @@ class RowShardedGemv:
         w_host = np.asarray(w_host, np.uint8).reshape(n, rb) if n * rb else np.zeros((n, 0), np.uint8)
         self.w = backend.upload(w_host[self.r0:self.r1])
 
+        self._bufs = {}
+
     def __call__(self, x):
+        # Buffers per batch size, allocated once (a call allocates nothing, so
+        # it can be captured in a CUDA graph with its all-gather).
         B = x.shape[0]
-        local = self.backend.zeros(B, self.npad)
+        if B not in self._bufs:
+            self._bufs[B] = (self.backend.zeros(B, self.npad), self.backend.zeros(self.world * B * self.npad))
+        local, gathered = self._bufs[B]
         if self.r1 > self.r0:
             self.backend.gemv(local, self.npad, x, self.w, self.type, self.r1 - self.r0, self.d)
-        gathered = self.backend.zeros(self.world * B * self.npad)
+        if self.world == 1:
+            return local[:, :self.n]
         dist.all_gather_into_tensor(gathered, local.reshape(-1), group=self.group)
+        if B == 1:
+            return gathered.view(1, self.world * self.npad)[:, :self.n]
         full = gathered.view(self.world, B, self.npad).permute(1, 0, 2).reshape(B, self.world * self.npad)
         return full[:, :self.n]
 
