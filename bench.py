@@ -1081,6 +1081,32 @@ def int8_compute(args, dev, s):
             "peak_how": "torch._int_mm 8192^3 int8 GEMM (cuBLASLt), best of 20, same process"}
 
 
+def profile_case(name, steps):
+    """A small case of one configuration for ncu captures (a few GB on the
+    device at most): `c5` runs `steps` decode steps of the c5 layer shape
+    (2 layers, vocab 1024, 64 sequences at position 1024, KV cache zeros).
+    Prints the device status only."""
+    import torch
+
+    import model_synth as ms
+    import quantr
+    assert quantr.lib().quantr_gpu_init(0) == 0
+    if name != "c5":
+        raise ValueError(name)
+    spec = ms.qwen3_moe(layers=2, vocab=1024, seq_len=1040)
+    model = ms.build(spec, seed=5)
+    B = 64
+    dec = quantr.Decoder(model, batch=B)
+    tok = torch.from_numpy(ms.prompt(spec, 1, seed=8, batch=B)[:, 0].copy()).cuda()
+    pos = torch.full((B,), 1024, dtype=torch.int32, device="cuda")
+    s = torch.cuda.current_stream().cuda_stream
+    for _ in range(steps):
+        dec.step_dev(tok.data_ptr(), pos.data_ptr(), None, 0, tok.data_ptr(), s)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
+    dec.close()
+
+
 def int8_peak(device=0):
     """Dense int8 tensor throughput of this GPU (TOP/s): torch._int_mm (a cuBLASLt
     int8 x int8 -> int32 GEMM) of 8192^3, best of 20 after warm-up, CUDA events.
@@ -1123,6 +1149,8 @@ def main():
     ap.add_argument("--no-int8", action="store_true", help="skip the compute-bound int8 line")
     ap.add_argument("--c5-steps", type=int, default=16)
     ap.add_argument("--decode-steps", type=int, default=128)
+    ap.add_argument("--profile-case", choices=["c5"], default=None,
+                    help="run a small case of a configuration for ncu captures and exit")
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")
     ap.add_argument("--sweep", type=lambda v: [int(b) for b in v.split(",") if b], default=[4, 16],
@@ -1130,6 +1158,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.profile_case:
+        profile_case(args.profile_case, args.steps)
+        return
     if args.int8_peak:
         print(json.dumps({"int8_dense_tops": round(int8_peak(), 1),
                           "how": "torch._int_mm 8192^3 int8 GEMM (cuBLASLt), best of 20, CUDA events"}))
