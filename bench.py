@@ -1083,14 +1083,53 @@ def int8_compute(args, dev, s):
 
 def profile_case(name, steps):
     """A small case of one configuration for ncu captures (a few GB on the
-    device at most): `c5` runs `steps` decode steps of the c5 layer shape
-    (2 layers, vocab 1024, 64 sequences at position 1024, KV cache zeros).
+    device at most), `steps` runs of it:
+      c1  one program of 16 Q8_0 5632x2048 GEMVs, batch 1 (196 MB);
+      c4  the c4 MoE layer (60 experts top-4, 64 tokens) through quantr_moe_dev;
+      c5  decode steps of the c5 layer shape (2 layers, vocab 1024, 64
+          sequences at position 1024, KV cache zeros).
     Prints the device status only."""
     import torch
 
     import model_synth as ms
     import quantr
     assert quantr.lib().quantr_gpu_init(0) == 0
+    dev = torch.device("cuda", 0)
+    s = torch.cuda.current_stream().cuda_stream
+    if name == "c1":
+        rng = synth.rng_for(7)
+        w = torch.from_numpy(synth.matrix(rng, Q8_0, 5632, 2048)).to(dev)
+        ws = [w.clone() for _ in range(16)]
+        xs = [torch.from_numpy(synth.activations(rng, 1, 2048)).to(dev) for _ in ws]
+        os_ = [torch.empty(1, 5632, device=dev) for _ in ws]
+        pr = quantr.Program([(wi.data_ptr(), Q8_0, 5632, 2048, 1, x.data_ptr(), 2048, o.data_ptr(), 5632)
+                             for wi, x, o in zip(ws, xs, os_)])
+        for _ in range(steps):
+            pr.run(s)
+        torch.cuda.synchronize()
+        pr.close()
+        print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
+        return
+    if name == "c4":
+        rng = synth.rng_for(44)
+        T, E, k, dim, hid = 64, 60, 4, 2048, 1408
+        Q5_K = 13
+        w1 = torch.from_numpy(np.stack([synth.matrix(rng, Q5_K, hid, dim) for _ in range(E)])).to(dev)
+        w3 = torch.from_numpy(np.stack([synth.matrix(rng, Q5_K, hid, dim) for _ in range(E)])).to(dev)
+        w2 = torch.from_numpy(np.stack([synth.matrix(rng, Q6_K, dim, hid) for _ in range(E)])).to(dev)
+        xb = torch.from_numpy(synth.activations(rng, T, dim)).to(dev)
+        lg = torch.from_numpy(rng.standard_normal((T, E), dtype=np.float32)).to(dev)
+        out = torch.empty(T, dim, device=dev)
+        wsb = quantr.moe_workspace_bytes(T, E, k, dim, hid)
+        wsp = torch.empty(wsb, dtype=torch.uint8, device=dev)
+        ew = [quantr.ExpertWeights(t.data_ptr(), t[0].numel(), None, ty) for t, ty in ((w1, Q5_K), (w3, Q5_K),
+                                                                                        (w2, Q6_K))]
+        for _ in range(steps):
+            quantr.moe_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, E, k, *ew, dim, hid, wsp.data_ptr(), wsb,
+                           logits=lg.data_ptr(), ldl=E, stream=s)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
+        return
     if name != "c5":
         raise ValueError(name)
     spec = ms.qwen3_moe(layers=2, vocab=1024, seq_len=1040)
@@ -1099,7 +1138,6 @@ def profile_case(name, steps):
     dec = quantr.Decoder(model, batch=B)
     tok = torch.from_numpy(ms.prompt(spec, 1, seed=8, batch=B)[:, 0].copy()).cuda()
     pos = torch.full((B,), 1024, dtype=torch.int32, device="cuda")
-    s = torch.cuda.current_stream().cuda_stream
     for _ in range(steps):
         dec.step_dev(tok.data_ptr(), pos.data_ptr(), None, 0, tok.data_ptr(), s)
     torch.cuda.synchronize()
@@ -1149,7 +1187,7 @@ def main():
     ap.add_argument("--no-int8", action="store_true", help="skip the compute-bound int8 line")
     ap.add_argument("--c5-steps", type=int, default=16)
     ap.add_argument("--decode-steps", type=int, default=128)
-    ap.add_argument("--profile-case", choices=["c5"], default=None,
+    ap.add_argument("--profile-case", choices=["c1", "c4", "c5"], default=None,
                     help="run a small case of a configuration for ncu captures and exit")
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")
