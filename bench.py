@@ -534,8 +534,19 @@ def ours_arm(args):
     decode = c5 = c4 = i8 = None
     if rank == 0 and world == 1 and not args.no_int8:
         i8 = int8_compute(args, dev, s)
-    if rank == 0 and world == 1 and not args.no_decode:
-        decode = decode_c3(args, dev, s)
+    if not args.no_decode:
+        # c3 decode on every GPU (N > 1: one replica per rank, no collective
+        # on the data path); rank 0 reports the aggregate from the slowest rank.
+        decode = decode_c3(args, dev, s, cpu=(rank == 0 and world == 1))
+        if world > 1:
+            ms_all = [None] * world
+            dist.all_gather_object(ms_all, decode["ms_per_token"])
+            decode["ranks"] = world
+            decode["per_rank_ms_per_token"] = ms_all
+            decode["tok_per_s_aggregate"] = round(world * 1e3 / max(ms_all), 1)
+            decode["aggregate_how"] = "N replicas (one sequence each), N x 1000 / max over ranks of ms per token"
+        if rank != 0:
+            decode = None
     if rank == 0 and world == 1 and not args.no_c4:
         c4 = moe_c4(args, dev, s)
     if rank == 0 and world == 1 and not args.no_c5:
@@ -744,7 +755,7 @@ def cpu_forward_run(spec, model_seed, prompt, positions, budget_s):
     return el / done, done, threads, kind
 
 
-def decode_c3(args, dev, s):
+def decode_c3(args, dev, s, cpu=True):
     """BASELINE config c3 on the device decoder: TinyLlama-1.1B shape, 512
     prompt tokens prefilled, then greedy decode.  Decode time per token is
     the difference of two CUDA-event-timed generate runs (512 + K and 512 + 0
@@ -811,7 +822,7 @@ def decode_c3(args, dev, s):
         "device_bytes": info["device_bytes"],
     }
     dec.close()
-    if not args.no_cpu_baseline:
+    if cpu and not args.no_cpu_baseline:
         sec, done, threads, kind = cpu_forward_run(spec, 1, prompt_h[0], 1000, args.cpu_seconds)
         res["cpu_baseline"] = {"value": round(1.0 / sec, 3), "unit": "tok/s", "cores": threads, "kind": kind,
                                "sample": (f"{done} forward_runtime calls at positions 0..{done - 1} on the same "

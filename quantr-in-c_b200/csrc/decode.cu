@@ -163,7 +163,8 @@ __device__ __forceinline__ float chain_sum(const float* __restrict__ p, int n, f
 // issued in one round (float4, all threads) and the rest runs out of shared
 // memory: the weight vector before the dependency wait, x (+ delta) after it;
 // one thread then walks the sum of squares while the others wait.
-__global__ void __launch_bounds__(256) k_rmsnorm(float* __restrict__ x, const float* __restrict__ delta,
+constexpr int kNormThreads = 1024;  // 32 warps: the quantization tail is 2 blocks per warp at dim 2048
+__global__ void __launch_bounds__(kNormThreads) k_rmsnorm(float* __restrict__ x, const float* __restrict__ delta,
                                                  const float* __restrict__ w, float* __restrict__ out, int dim,
                                                  const __grid_constant__ Tgts tg)
 {
@@ -819,7 +820,7 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
     if (e == cudaSuccess && d->persist) e = launch_persist(d->pp, d->persist_type, d->persist_grid, d->persist_smem, s);
     for (int l = 0; l < d->n_layers && e == cudaSuccess && !d->persist; ++l) {
         const long long loff = (long long)l * layer_kv;
-        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)(l ? d->delta : nullptr),
+        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(kNormThreads), norm_smem, c, d->x, (const float*)(l ? d->delta : nullptr),
                       d->rms_att[l], d->xb, D.dim, d->t_qkv[l]);
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_qkv[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
@@ -842,7 +843,7 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
                       (const int*)d->pos, d->xa, device_error_word(), D, d->t_o[l]);
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_o[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
-        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)d->delta, d->rms_ffn[l],
+        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(kNormThreads), norm_smem, c, d->x, (const float*)d->delta, d->rms_ffn[l],
                       d->xb, D.dim, d->t_ffn[l]);
         if (e != cudaSuccess) break;
         if (d->E == 0) {
@@ -899,7 +900,7 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
         }
     }
     if (e == cudaSuccess && with_head) {
-        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(256), norm_smem, c, d->x, (const float*)d->delta, d->rms_final,
+        e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(kNormThreads), norm_smem, c, d->x, (const float*)d->delta, d->rms_final,
                       d->xb, D.dim, d->t_head);
         if (e == cudaSuccess && quantr_program_run(d->p_head, s) != QUANTR_OK) return QUANTR_ERR_CUDA;
         if (e == cudaSuccess)
