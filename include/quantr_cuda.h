@@ -142,7 +142,11 @@ size_t quantr_gemv_workspace_bytes(int d, int B);
  * quantization of x into `workspace`.  Asynchronous on `stream`
  * (a cudaStream_t; NULL = legacy default stream).  Launches use programmatic
  * dependent launch, so the weight stream of this GEMV overlaps the kernel that
- * produced x.  Returns a QUANTR_* code. */
+ * produced x.  With B >= 2 (16-byte aligned quantized weights) the GEMV runs
+ * on the tensor cores: the first call for a given (w, type, n, d, B, x, ldx,
+ * out, ldo) plans it and allocates its activation tiles (up to 64 such plans
+ * are kept per process); later calls allocate nothing.  Returns a QUANTR_*
+ * code. */
 int quantr_gemv_dev(float* out, long long ldo, const float* x, long long ldx, const void* w, uint32_t type,
                     int n, int d, int B, void* workspace, size_t workspace_bytes, void* stream);
 

@@ -216,7 +216,9 @@ int fused_host(float* out, const float* x, const void* w, uint32_t type, int n, 
         if (type == T_F32) {
             e = launch_gemv_f32((const float*)wdev, dx, d, dout, n, n, d, B, c);
         } else {
-            e = launch_gemv_engine(wdev, type, n, d, B, dx, d, dout, n, g.ws, g.ws_bytes, derr, g.stream);
+            e = launch_gemv_tc(wdev, type, n, d, B, dx, d, dout, n, derr, g.stream);  // 2+ tokens
+            if (e == cudaErrorNotSupported)
+                e = launch_gemv_engine(wdev, type, n, d, B, dx, d, dout, n, g.ws, g.ws_bytes, derr, g.stream);
             if (e == cudaErrorNotSupported) {  // shapes the engine does not take
                 ActQ a = actq_carve(g.ws, d, B);
                 e = launch_quantize(dx, d, d, B, a, nullptr, derr, c);
@@ -578,6 +580,11 @@ static int gemv_dev_common(float* out, long long ldo, const float* x, long long 
     if (!type_supported(type)) return QUANTR_ERR_UNSUPPORTED_TYPE;
     if (!ws || ws_bytes < actq_bytes(d, B)) return QUANTR_ERR_WORKSPACE;
     int* err = device_error_word();
+    if (x && !isum && B >= 2) {
+        // 2+ tokens: the tensor-core kernel (16-byte aligned weights).
+        e = launch_gemv_tc((const uint8_t*)w, type, n, d, B, x, ldx, out, ldo, err, c.stream);
+        if (e != cudaErrorNotSupported) return code_of(e);
+    }
     if (x && !isum && ((uintptr_t)ws & 15) == 0) {
         // Fast path: the persistent engine (16-byte aligned weights, B <= 16).
         e = launch_gemv_engine((const uint8_t*)w, type, n, d, B, x, ldx, out, ldo, ws, ws_bytes, err, c.stream);

@@ -928,31 +928,7 @@ int qr::program_create_ex(quantr_program** out, const quantr_gemv_job* jobs, con
         return QUANTR_ERR_NO_DEVICE;
     }
     const int sms = device_sm_count();
-    // A tensor-core program with fewer 128-row tiles than SMs leaves most SMs
-    // idle while a few run long epilogues (one per token column): split the
-    // widest job's tokens in two (16-aligned) until every SM has a tile.
-    // Each token's outputs are independent, so results do not change.
-    {
-        auto tiles = [&]() {
-            long long t = 0;
-            for (const auto& g : tcj) t += (g.n + 127) / 128;
-            return t;
-        };
-        while (!tcj.empty() && tiles() < sms && tcj.size() < (size_t)kTcMaxJobs) {
-            size_t wi = 0;
-            for (size_t i = 1; i < tcj.size(); ++i)
-                if (tcj[i].B > tcj[wi].B) wi = i;
-            if (tcj[wi].B <= 16) break;
-            GemvJobIn hi = tcj[wi];
-            const int keep = ((tcj[wi].B / 2 + 15) / 16) * 16;
-            tcj[wi].B = keep;
-            hi.B -= keep;
-            hi.x += (long long)keep * hi.ldx;
-            hi.out += (long long)keep * hi.ldo;
-            if (hi.xmul) hi.xmul += (long long)keep * hi.ldx;
-            tcj.push_back(hi);
-        }
-    }
+    tc_split_narrow(tcj, sms);
     eng::Plan sizing;
     int rc = in.empty() ? QUANTR_OK : eng::make_plan(in.data(), (int)in.size(), nullptr, sms, true, sizing);
     if (rc) return rc;

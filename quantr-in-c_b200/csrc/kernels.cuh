@@ -3,6 +3,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
+#include <vector>
 
 #include "quantr_cuda.h"
 
@@ -131,6 +132,15 @@ struct TcPlan;
 constexpr int kTcMaxB = 64;
 constexpr int kTcMaxJobs = 128;
 int tc_plan_create(const GemvJobIn* jobs, int njobs, TcPlan** out);
+// A tensor-core job list with fewer 128-row tiles than SMs leaves most SMs
+// idle while a few run long epilogues: splits the widest job's tokens in two
+// (16-aligned) until every SM has a tile (results do not change).
+void tc_split_narrow(std::vector<GemvJobIn>& jobs, int sms);
+// One GEMV of 2+ tokens on the tensor cores, planned (and its activation
+// tiles allocated) on the first call for these arguments and cached;
+// cudaErrorNotSupported for shapes the tensor-core kernel does not take.
+cudaError_t launch_gemv_tc(const uint8_t* w, uint32_t type, int n, int d, int B, const float* x, long long ldx,
+                           float* out, long long ldo, int* err, cudaStream_t stream);
 cudaError_t tc_plan_run(TcPlan* plan, int* err, cudaStream_t stream);
 void tc_plan_destroy(TcPlan* plan);
 void tc_plan_info(const TcPlan* plan, int* items, int* grid, int* smem);

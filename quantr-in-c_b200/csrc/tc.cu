@@ -80,6 +80,7 @@
 #include <tuple>
 #include <utility>
 #include <vector>
+#include <mutex>
 
 namespace qr {
 namespace tc {
@@ -1427,6 +1428,75 @@ cudaError_t tc_plan_run(TcPlan* P, int* err, cudaStream_t stream)
     if (pp.ncol <= 16) return launch_tc<QR_TC_N16_DG, QR_TC_N16_EG, 16 / QR_TC_N16_EG>(P, pp, c);
     if (pp.ncol == 32) return launch_tc<1, 4, 8>(P, pp, c);
     return launch_tc<1, 4, 16>(P, pp, c);
+}
+
+void tc_split_narrow(std::vector<GemvJobIn>& tcj, int sms)
+{
+    auto tiles = [&]() {
+        long long t = 0;
+        for (const auto& g : tcj) t += (g.n + 127) / 128;
+        return t;
+    };
+    while (!tcj.empty() && tiles() < sms && tcj.size() < (size_t)kTcMaxJobs) {
+        size_t wi = 0;
+        for (size_t i = 1; i < tcj.size(); ++i)
+            if (tcj[i].B > tcj[wi].B) wi = i;
+        if (tcj[wi].B <= 16 || tcj[wi].g_counts) break;
+        GemvJobIn hi = tcj[wi];
+        const int keep = ((tcj[wi].B / 2 + 15) / 16) * 16;
+        tcj[wi].B = keep;
+        hi.B -= keep;
+        hi.x += (long long)keep * hi.ldx;
+        hi.out += (long long)keep * hi.ldo;
+        if (hi.xmul) hi.xmul += (long long)keep * hi.ldx;
+        tcj.push_back(hi);
+    }
+}
+
+cudaError_t launch_gemv_tc(const uint8_t* w, uint32_t type, int n, int d, int B, const float* x, long long ldx,
+                           float* out, long long ldo, int* err, cudaStream_t stream)
+{
+    if (B < 2 || n <= 0 || !x || !out || ldx < d || ldo < n || ((uintptr_t)w & 15) ||
+        !(type == T_Q8_0 || type == T_Q4_K || type == T_Q5_K || type == T_Q6_K) || row_bytes(type, d) <= 0)
+        return cudaErrorNotSupported;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    using Key = std::tuple<int, const uint8_t*, uint32_t, int, int, int, const float*, long long, float*, long long>;
+    static std::mutex mu;
+    static std::map<Key, std::vector<TcPlan*>> cache;
+    std::lock_guard<std::mutex> lk(mu);  // held while the plans are enqueued
+    const Key key{dev, w, type, n, d, B, x, ldx, out, ldo};
+    auto it = cache.find(key);
+    if (it == cache.end()) {
+        if (cache.size() >= 64) {  // bounded: drop every plan (tc_plan_destroy synchronises the device)
+            for (auto& kv : cache)
+                for (TcPlan* p : kv.second) tc_plan_destroy(p);
+            cache.clear();
+        }
+        std::vector<GemvJobIn> jobs;
+        for (int b0 = 0; b0 < B; b0 += kTcMaxB)
+            jobs.push_back(GemvJobIn{w, type, n, d, std::min(kTcMaxB, B - b0), x + (long long)b0 * ldx, ldx,
+                                     out + (long long)b0 * ldo, ldo});
+        tc_split_narrow(jobs, device_sm_count());
+        std::vector<TcPlan*> plans;
+        for (size_t j0 = 0; j0 < jobs.size(); j0 += kTcMaxJobs) {
+            TcPlan* p = nullptr;
+            if (tc_plan_create(jobs.data() + j0, (int)std::min<size_t>(kTcMaxJobs, jobs.size() - j0), &p) != 0) {
+                for (TcPlan* q : plans) tc_plan_destroy(q);
+                plans.clear();
+                cudaGetLastError();
+                break;
+            }
+            plans.push_back(p);
+        }
+        it = cache.emplace(key, std::move(plans)).first;
+    }
+    if (it->second.empty()) return cudaErrorNotSupported;
+    for (TcPlan* p : it->second) {
+        const cudaError_t e = tc_plan_run(p, err, stream);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 void tc_plan_destroy(TcPlan* P)
