@@ -1098,7 +1098,8 @@ def profile_case(name, steps):
       c1  one program of 16 Q8_0 5632x2048 GEMVs, batch 1 (196 MB);
       c4  the c4 MoE layer (60 experts top-4, 64 tokens) through quantr_moe_dev;
       c5  decode steps of the c5 layer shape (2 layers, vocab 1024, 64
-          sequences at position 1024, KV cache zeros).
+          sequences at position 1024, KV cache zeros);
+      int8  the int8_compute line's program (one c5 expert, 1024 tokens).
     Prints the device status only."""
     import torch
 
@@ -1139,6 +1140,21 @@ def profile_case(name, steps):
             quantr.moe_dev(out.data_ptr(), dim, xb.data_ptr(), dim, T, E, k, *ew, dim, hid, wsp.data_ptr(), wsb,
                            logits=lg.data_ptr(), ldl=E, stream=s)
         torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
+        return
+    if name == "int8":  # the int8_compute line's program: one c5 expert, 1024 tokens per GEMV
+        rng = synth.rng_for(88)
+        T, hid, dimx = 1024, 768, 2048
+        shapes = [(Q4_K, hid, dimx), (Q4_K, hid, dimx), (Q4_K, dimx, hid)]
+        ws = [torch.from_numpy(synth.matrix(rng, t, n, d)).to(dev) for t, n, d in shapes]
+        xs = [torch.from_numpy(synth.activations(rng, T, d)).to(dev) for _, _, d in shapes]
+        os_ = [torch.empty(T, n, device=dev) for _, n, _ in shapes]
+        pr = quantr.Program([(w.data_ptr(), t, n, d, T, x.data_ptr(), d, o.data_ptr(), n)
+                             for (t, n, d), w, x, o in zip(shapes, ws, xs, os_)])
+        for _ in range(steps):
+            pr.run(s)
+        torch.cuda.synchronize()
+        pr.close()
         print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
         return
     if name != "c5":
@@ -1198,7 +1214,7 @@ def main():
     ap.add_argument("--no-int8", action="store_true", help="skip the compute-bound int8 line")
     ap.add_argument("--c5-steps", type=int, default=16)
     ap.add_argument("--decode-steps", type=int, default=128)
-    ap.add_argument("--profile-case", choices=["c1", "c4", "c5"], default=None,
+    ap.add_argument("--profile-case", choices=["c1", "c4", "c5", "int8"], default=None,
                     help="run a small case of a configuration for ncu captures and exit")
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")
