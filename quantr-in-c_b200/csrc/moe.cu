@@ -472,7 +472,11 @@ struct MoeWs {
 };
 
 // Chunks of 16 pairs per local expert on the tensor-core path (an expert has
-// at most T pairs: a token picks an expert once; the path takes T <= kTcMaxB).
+// at most T pairs: a token picks an expert once).  The path takes T <=
+// kMoeTcMaxT: its operand tiles are laid out for that worst case per expert
+// (the workspace grows with T; about 0.5 GB at T = 512 with 128 experts of
+// the c5 shape).
+constexpr int kMoeTcMaxT = 1024;
 int moe_tc_chunks(int T) { return (T + 15) / 16; }
 
 size_t a256(size_t v) { return (v + 255) & ~size_t(255); }
@@ -499,7 +503,7 @@ MoeWs moe_layout(int T, int E, int k, int dim, int hidden)
     // Operand tiles per local expert for the tensor-core path (W1, W3 when its
     // element order differs, W2): up to d/32 units x 16 columns x (32 quant +
     // 16 record bytes) per chunk.
-    const size_t ch = T <= kTcMaxB ? (size_t)E * moe_tc_chunks(T) : 0;
+    const size_t ch = T <= kMoeTcMaxT ? (size_t)E * moe_tc_chunks(T) : 0;
     w.t1 = take(ch * (dim / 32) * 512);
     w.r1 = take(ch * (dim / 32) * 256);
     w.t3 = take(ch * (dim / 32) * 512);
@@ -676,7 +680,7 @@ bool w3_own_tiles(const MoeExperts& a)
 
 const MoeTcPlans* moe_tc_plans(const MoeExperts& a, const MoeWs& L)
 {
-    if (a.T < kMoeTcMinT || a.T > kTcMaxB || !tc_type(a.w1.type) || !tc_type(a.w3.type) || !tc_type(a.w2.type) ||
+    if (a.T < kMoeTcMinT || a.T > kMoeTcMaxT || !tc_type(a.w1.type) || !tc_type(a.w3.type) || !tc_type(a.w2.type) ||
         row_bytes(a.w1.type, a.dim) <= 0 || row_bytes(a.w3.type, a.dim) <= 0 || row_bytes(a.w2.type, a.hidden) <= 0 ||
         ((uintptr_t)a.xb & 3))
         return nullptr;

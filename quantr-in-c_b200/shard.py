@@ -11,7 +11,8 @@ np-row shards assembles out.
 
 Expert-parallel MoE (src/runtime.c:202-269), tokens and experts both split.
 Rank r holds its own tokens and owns experts [E*r/P, E*(r+1)/P).  Each rank
-routes its tokens (the router is per token), then:
+routes its tokens (the router is per token) and orders its (token, slot)
+pairs by destination on the device, then:
   1. counts: every rank tells every other how many (token, slot) pairs it
      will send it (all_to_all_single of P counts);
   2. dispatch: each pair's activation row goes to the owner of its expert as
@@ -190,6 +191,7 @@ class ExpertShardedMoE:
             stride = int(np.prod(w.shape[1:])) if w.ndim > 1 else 0
             self.mats.append((backend.upload(local), stride, t))
         self.stats = {}
+        self._owner_dev = None
 
     def _a2a(self, out, inp, out_splits, in_splits):
         if self.world == 1:
@@ -201,28 +203,33 @@ class ExpertShardedMoE:
         T, dim, k = xb.shape[0], self.dim, self.k
         be = self.backend
         sel, wts = be.route(xb, self.E, k, router=self.router, logits=logits)
-        # Dispatch plan: valid pairs ordered by destination rank, then pair
-        # index (plain integer bookkeeping on the host).
-        sel_h = sel.cpu().reshape(-1).to(torch.int64)
-        pair = torch.nonzero(sel_h >= 0).reshape(-1)
-        dest = self.owner[sel_h[pair]] if pair.numel() else torch.zeros(0, dtype=torch.int64)
-        order = torch.argsort(dest * (T * k + 1) + pair)
-        pair, dest = pair[order], dest[order]
-        # 1. counts, exchanged on the tokens' device (NCCL takes device
-        # tensors only; gloo host ones)
-        send_counts = torch.bincount(dest, minlength=self.world).to(torch.int64).to(xb.device)
+        # Dispatch plan on the tokens' device: valid pairs ordered by
+        # destination rank, then pair index (pairs without an expert go last).
+        dev = xb.device
+        if self._owner_dev is None or self._owner_dev.device != dev:
+            self._owner_dev = self.owner.to(dev)
+        selv = sel.reshape(-1).to(torch.int64)
+        valid = selv >= 0
+        dest = torch.where(valid, self._owner_dev[selv.clamp(min=0)], torch.full_like(selv, self.world))
+        order = torch.argsort(dest * (T * k + 1) + torch.arange(T * k, device=dev))
+        # 1. counts (NCCL takes device tensors only; gloo host ones); the one
+        # value that comes back to the host is the pair counts, which size
+        # the variable-length exchanges.
+        send_counts = torch.bincount(dest, minlength=self.world + 1)[:self.world].to(torch.int64)
         recv_counts = torch.empty_like(send_counts)
         self._a2a(recv_counts, send_counts, None, None)
-        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        counts = torch.cat([send_counts, recv_counts]).tolist()
+        sc, rc = counts[:self.world], counts[self.world:]
+        pair = order[:sum(sc)]
+        sel_h = selv
         n_send, n_recv = sum(sc), sum(rc)
         # 2. dispatch: Q8_0 rows of the pairs' tokens, and their expert ids.
         xq = be.quantize_q8_0(xb)
-        dev = xq.device
-        tok = (pair // k).to(dev)
+        tok = pair // k
         send_q = xq.index_select(0, tok) if n_send else xq[:0]
         recv_q = torch.empty(n_recv, xq.shape[1], dtype=torch.uint8, device=dev)
         self._a2a(recv_q, send_q, rc, sc)
-        send_e = sel_h[pair].to(torch.int32).to(dev)
+        send_e = sel_h[pair].to(torch.int32)
         recv_e = torch.empty(n_recv, dtype=torch.int32, device=dev)
         self._a2a(recv_e, send_e, rc, sc)
         # 3. local experts on the received pairs (one slot each).
@@ -235,7 +242,7 @@ class ExpertShardedMoE:
         self._a2a(o_back, o_recv, sc, rc)
         o = be.zeros(T * k, dim)
         if n_send:
-            o.index_copy_(0, pair.to(o.device), o_back)
+            o.index_copy_(0, pair, o_back)
         self.stats = {"pairs_sent": n_send, "pairs_received": n_recv,
                       "dispatch_bytes": n_send * (xq.shape[1] + 4), "return_bytes": n_send * dim * 4}
         return be.combine(o, sel, wts, dim), sel, wts

@@ -398,3 +398,13 @@ def test_moe_tc_repeat_call_new_tokens(qr_gpu, orc):
                        logits=lg.data_ptr(), ldl=E, sel=sel.data_ptr(), wts=wts.data_ptr(), stream=s)
         torch.cuda.synchronize()
         check((out.cpu().numpy(), sel.cpu().numpy(), wts.cpu().numpy()), oracle_case(orc, c))
+
+
+@pytest.mark.parametrize("T,k", [(200, 2), (512, 1)])
+def test_moe_tc_more_tokens_than_a_job(qr_gpu, orc, T, k):
+    """More tokens than one tensor-core job holds (64): the experts stage
+    still runs as gathered 16-pair passes per expert (the expert-parallel
+    owner's case: its received pairs are 512 one-slot tokens at the c5
+    shape)."""
+    c = make_case(31 + T, T=T, E=12, k=k, dim=512, hidden=256, t1=Q4_K, t3=Q4_K, t2=Q4_K)
+    check(run_dev(qr_gpu, c), oracle_case(orc, c))
