@@ -1096,6 +1096,7 @@ def profile_case(name, steps):
     """A small case of one configuration for ncu captures (a few GB on the
     device at most), `steps` runs of it:
       c1  one program of 16 Q8_0 5632x2048 GEMVs, batch 1 (196 MB);
+      c3  decode steps of the c3 shape (2 layers) at position 512, batch 1;
       c4  the c4 MoE layer (60 experts top-4, 64 tokens) through quantr_moe_dev;
       c5  decode steps of the c5 layer shape (2 layers, vocab 1024, 64
           sequences at position 1024, KV cache zeros);
@@ -1157,6 +1158,18 @@ def profile_case(name, steps):
         pr.close()
         print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
         return
+    if name == "c3":  # decode steps of the c3 shape (2 layers) at position 512, batch 1
+        spec = ms.tinyllama(layers=2)
+        model = ms.build(spec, seed=1)
+        dec = quantr.Decoder(model)
+        tok = torch.tensor([5], dtype=torch.int32, device="cuda")
+        pos = torch.full((1,), 512, dtype=torch.int32, device="cuda")
+        for _ in range(steps):
+            dec.step_dev(tok.data_ptr(), pos.data_ptr(), None, 0, tok.data_ptr(), s)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": name, "steps": steps, "device_status": quantr.device_status(0)}))
+        dec.close()
+        return
     if name != "c5":
         raise ValueError(name)
     spec = ms.qwen3_moe(layers=2, vocab=1024, seq_len=1040)
@@ -1214,7 +1227,7 @@ def main():
     ap.add_argument("--no-int8", action="store_true", help="skip the compute-bound int8 line")
     ap.add_argument("--c5-steps", type=int, default=16)
     ap.add_argument("--decode-steps", type=int, default=128)
-    ap.add_argument("--profile-case", choices=["c1", "c4", "c5", "int8"], default=None,
+    ap.add_argument("--profile-case", choices=["c1", "c3", "c4", "c5", "int8"], default=None,
                     help="run a small case of a configuration for ncu captures and exit")
     ap.add_argument("--int8-peak", action="store_true",
                     help="only measure the GPU's dense int8 tensor throughput (cuBLASLt GEMM) and print it")

@@ -83,7 +83,8 @@ __device__ __forceinline__ void tgts_write(const Tgts& tg, int t, int b, int lan
 
 struct Dims {
     int B, dim, q_dim, kv_dim, hd, n_heads, n_kv, kv_mul, seq_len, hidden, vocab, kv_type;
-    int vst;  // value-row stages of the attention kernel's ring (set with its shared-memory size)
+    int vst;   // value-row stages of the attention kernel's ring (set with its shared-memory size)
+    int vsth;  // the same for the one-head-per-CTA variant
     float inv_sqrt;
     int kv_B;        // sequences the KV cache holds
     int seq_stride;  // KV-cache sequence of step row b = b * seq_stride (0: every row is one sequence's position)
@@ -553,6 +554,117 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
     }
 }
 
+// The same for steps with few KV heads (one sequence): one CTA per
+// (sequence, query head), so 8x more SMs share the work.  Warp 0 forms the
+// head's softmax exactly as above; thread i owns output element i and its
+// running sum over the positions, in order; each CTA streams its KV head's
+// value rows through its own ring (the other query heads of the group read
+// the same rows from L2).  With head_dim a multiple of 32, warp w holds
+// elements [32w, 32w + 32) of the head: one block of the O projection's input.
+template <int KVT>
+__global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* __restrict__ vcache,
+                                     long long layer_off, const int* __restrict__ pos, float* __restrict__ xa,
+                                     int* err, Dims D, const __grid_constant__ Tgts tg)
+{
+    extern __shared__ __align__(16) unsigned char smraw[];
+    __shared__ __align__(8) uint64_t bars[kVMaxStages];
+    __shared__ int s_abort;
+    constexpr int ES = KVT ? 2 : 4;
+    const int hd = D.hd;
+    const int row_bytes = hd * ES;
+    const int stage_bytes = kVTile * row_bytes;
+    const int NS = D.vsth;
+    unsigned char* vring = smraw;                                   // [NS][kVTile][hd]
+    float* S = reinterpret_cast<float*>(smraw + NS * stage_bytes);  // this head's scores
+    const int b = blockIdx.x / D.n_heads, h = blockIdx.x % D.n_heads, kh = h / D.kv_mul;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
+        mbar_fence_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    pdl_wait();
+    pdl_trigger();
+    const int p = pos[b], np = p + 1;
+    if (p < 0) return;
+    const int ntiles = (np + kVTile - 1) / kVTile;
+    const unsigned char* vrow0 =
+        static_cast<const unsigned char*>(vcache) + kv_head_base(D, layer_off, b, kh) * ES;
+    auto issue = [&](int j) {  // one thread: tile j's rows into stage j % NS
+        const int st = j % NS, t0 = j * kVTile, nt = min(kVTile, np - t0);
+        mbar_arrive_expect_tx(&bars[st], (uint32_t)(nt * row_bytes));
+        bulk_g2s(vring + st * stage_bytes, vrow0 + (long long)t0 * row_bytes, (uint32_t)(nt * row_bytes), &bars[st]);
+    };
+    if (tid == 0)
+        for (int j = 0; j < min(NS, ntiles); ++j) issue(j);
+    if (warp == 0) {
+        // softmax_ref of this head's scores: max from x[0] (a NaN at 0
+        // sticks), expf, left-to-right sum, scale.
+        const float* a = att + ((long long)b * D.n_heads + h) * D.seq_len;
+        const float a0 = a[0];
+        float mx = a0;
+#pragma unroll 4
+        for (int t = lane; t < np; t += 32) {
+            const float v = a[t];
+            S[t] = v;
+            mx = fmaxf(mx, v);
+        }
+        for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (a0 != a0) mx = a0;
+        __syncwarp();
+        for (int t = lane; t < np; t += 32) S[t] = libm::expf_ref(__fsub_rn(S[t], mx));
+        __syncwarp();
+        float inv = 0.0f;
+        if (lane == 0) inv = __fdiv_rn(1.0f, chain_sum(S, np));
+        inv = __shfl_sync(0xffffffffu, inv, 0);
+        for (int t = lane; t < np; t += 32) S[t] = __fmul_rn(S[t], inv);
+    }
+    __syncthreads();
+    const bool live = tid < hd;
+    float acc = 0.0f;
+    int issued = min(NS, ntiles);  // meaningful in thread 0
+    int j = 0;
+    for (; j < ntiles; ++j) {
+        const int st = j % NS;
+        if (!mbar_wait_bounded(&bars[st], (uint32_t)((j / NS) & 1), err, &s_abort)) s_abort = 1;
+        __syncthreads();
+        if (s_abort) break;
+        const int t0 = j * kVTile, nt = min(kVTile, np - t0);
+        const unsigned char* vt = vring + st * stage_bytes + ES * (live ? tid : 0);
+        auto vat = [&](int r) {
+            return KVT ? h2f_ref(*reinterpret_cast<const uint16_t*>(vt + r * row_bytes))
+                       : *reinterpret_cast<const float*>(vt + r * row_bytes);
+        };
+        const float* sp = S + t0;
+        if (live) {
+            int r = 0;
+            for (; r + 4 <= nt; r += 4) {
+                const float4 s4 = *reinterpret_cast<const float4*>(sp + r);
+                const float v0 = vat(r), v1 = vat(r + 1), v2 = vat(r + 2), v3 = vat(r + 3);
+                acc = __fadd_rn(acc, __fmul_rn(s4.x, v0));
+                acc = __fadd_rn(acc, __fmul_rn(s4.y, v1));
+                acc = __fadd_rn(acc, __fmul_rn(s4.z, v2));
+                acc = __fadd_rn(acc, __fmul_rn(s4.w, v3));
+            }
+            for (; r < nt; ++r) acc = __fadd_rn(acc, __fmul_rn(sp[r], vat(r)));
+        }
+        __syncthreads();  // stage st is free again
+        if (tid == 0 && j + NS < ntiles) {
+            issue(j + NS);
+            issued = j + NS + 1;
+        }
+    }
+    if (j < ntiles) {
+        if (tid == 0)
+            for (int jj = j; jj < issued; ++jj)
+                mbar_wait_bounded(&bars[jj % NS], (uint32_t)((jj / NS) & 1), err, nullptr);
+        return;
+    }
+    if (live) xa[(long long)b * D.q_dim + (long long)h * hd + tid] = acc;
+    if (tg.n && 32 * warp < hd) tgts_write(tg, b, (h * hd + 32 * warp) >> 5, lane, acc);
+}
+
 // delta += sh * sigmoid(g) per sequence (the shared expert's gated add).
 __global__ void k_shexp_add(float* __restrict__ delta, const float* __restrict__ sh, const float* __restrict__ g,
                             int dim)
@@ -782,6 +894,23 @@ size_t att_v_smem(const Dims& D)
 // many as leave room for two CTAs per SM; with fewer CTAs (one sequence) as
 // many as fit, up to every tile of the context, so the copies of a whole head
 // are in flight at once.
+// The one-head-per-CTA variant: its own score row and as many stages as fit.
+size_t att_vh_smem(const Dims& D)
+{
+    return (size_t)D.vsth * kVTile * D.hd * (D.kv_type ? 2 : 4) + (size_t)att_sstride(D.seq_len) * 4;
+}
+int att_vh_stages(const Dims& D)
+{
+    const size_t stage = (size_t)kVTile * D.hd * (D.kv_type ? 2 : 4);
+    const size_t budget = kSmemMax - 1024 - (size_t)att_sstride(D.seq_len) * 4;
+    const int tiles = (D.seq_len + kVTile - 1) / kVTile;
+    return (int)std::max<long long>(2, std::min<long long>({(long long)(budget / stage), (long long)tiles,
+                                                            (long long)kVMaxStages}));
+}
+// Steps with few KV heads in flight (one sequence) take the one-head-per-CTA
+// variant.
+bool att_per_head(const Dims& D, int sms) { return D.B * D.n_kv * 4 <= sms; }
+
 int att_v_stages(const Dims& D, int sms)
 {
     const size_t stage = (size_t)kVTile * D.hd * (D.kv_type ? 2 : 4);
@@ -838,9 +967,14 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
                       (const float*)d->vc, (const float2*)d->rope, d->kcache, d->vcache, loff, (const int*)d->pos,
                       d->att, D);
         if (e != cudaSuccess) break;
-        e = launch_ex(D.kv_type ? &k_att_softmax_v<1> : &k_att_softmax_v<0>, dim3(D.B * D.n_kv),
-                      dim3(att_v_threads(D)), att_v_smem(D), c, (const float*)d->att, (const void*)d->vcache, loff,
-                      (const int*)d->pos, d->xa, device_error_word(), D, d->t_o[l]);
+        if (att_per_head(D, device_sm_count()))
+            e = launch_ex(D.kv_type ? &k_att_softmax_v_head<1> : &k_att_softmax_v_head<0>, dim3(D.B * D.n_heads),
+                          dim3(std::max(32, (D.hd + 31) / 32 * 32)), att_vh_smem(D), c, (const float*)d->att,
+                          (const void*)d->vcache, loff, (const int*)d->pos, d->xa, device_error_word(), D, d->t_o[l]);
+        else
+            e = launch_ex(D.kv_type ? &k_att_softmax_v<1> : &k_att_softmax_v<0>, dim3(D.B * D.n_kv),
+                          dim3(att_v_threads(D)), att_v_smem(D), c, (const float*)d->att, (const void*)d->vcache,
+                          loff, (const int*)d->pos, d->xa, device_error_word(), D, d->t_o[l]);
         if (e != cudaSuccess) break;
         if (quantr_program_run(d->p_o[l], s) != QUANTR_OK) return QUANTR_ERR_CUDA;
         e = launch_ex(&k_rmsnorm, dim3(D.B), dim3(kNormThreads), norm_smem, c, d->x, (const float*)d->delta, d->rms_ffn[l],
@@ -1018,6 +1152,7 @@ int create_impl(quantr_decoder** out, const quantr_model* m, int batch, quantr_d
     D.kv_B = parent ? parent->D.kv_B : batch;
     D.seq_stride = parent ? 0 : 1;
     D.vst = att_v_stages(D, device_sm_count());
+    D.vsth = att_vh_stages(D);
     d->child = parent != nullptr;
     d->n_layers = m->n_layers;
     d->E = m->expert_count;
@@ -1375,7 +1510,9 @@ int create_impl(quantr_decoder** out, const quantr_model* m, int batch, quantr_d
         };
         if (!raise((const void*)k_att_scores<0, true>, ssm) || !raise((const void*)k_att_scores<1, true>, ssm) ||
             !raise((const void*)k_att_scores<0, false>, ssm) || !raise((const void*)k_att_scores<1, false>, ssm) ||
-            !raise((const void*)k_att_softmax_v<0>, vsm) || !raise((const void*)k_att_softmax_v<1>, vsm))
+            !raise((const void*)k_att_softmax_v<0>, vsm) || !raise((const void*)k_att_softmax_v<1>, vsm) ||
+            !raise((const void*)k_att_softmax_v_head<0>, (int)att_vh_smem(D)) ||
+            !raise((const void*)k_att_softmax_v_head<1>, (int)att_vh_smem(D)))
             return fail(QUANTR_ERR_CUDA);
     }
 
