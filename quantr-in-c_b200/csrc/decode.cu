@@ -146,13 +146,14 @@ __global__ void k_embed(float* __restrict__ x, const int* __restrict__ tok, cons
 // issued eight at a time ahead of the adds that consume them.
 __device__ __forceinline__ float chain_sum(const float* __restrict__ p, int n, float s = 0.0f)
 {
+    // 32 loads in flight, then 32 dependent adds: one load latency per 32 terms.
     int i = 0;
-    for (; i + 8 <= n; i += 8) {
-        float v[8];
+    for (; i + 32 <= n; i += 32) {
+        float v[32];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = p[i + k];
+        for (int k = 0; k < 32; ++k) v[k] = p[i + k];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s = __fadd_rn(s, v[k]);
+        for (int k = 0; k < 32; ++k) s = __fadd_rn(s, v[k]);
     }
     for (; i < n; ++i) s = __fadd_rn(s, p[i]);
     return s;
@@ -598,27 +599,33 @@ __global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* 
     };
     if (tid == 0)
         for (int j = 0; j < min(NS, ntiles); ++j) issue(j);
-    if (warp == 0) {
+    {
         // softmax_ref of this head's scores: max from x[0] (a NaN at 0
-        // sticks), expf, left-to-right sum, scale.
+        // sticks), expf, left-to-right sum (one thread), scale.  Every thread
+        // of the CTA copies and exponentiates its share.
+        __shared__ float s_red[32];
+        const int nthr = blockDim.x, nw = nthr >> 5;
         const float* a = att + ((long long)b * D.n_heads + h) * D.seq_len;
         const float a0 = a[0];
         float mx = a0;
-#pragma unroll 4
-        for (int t = lane; t < np; t += 32) {
+#pragma unroll 8
+        for (int t = tid; t < np; t += nthr) {
             const float v = a[t];
             S[t] = v;
             mx = fmaxf(mx, v);
         }
         for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) s_red[warp] = mx;
+        __syncthreads();
+        mx = s_red[0];
+        for (int w = 1; w < nw; ++w) mx = fmaxf(mx, s_red[w]);
         if (a0 != a0) mx = a0;
-        __syncwarp();
-        for (int t = lane; t < np; t += 32) S[t] = libm::expf_ref(__fsub_rn(S[t], mx));
-        __syncwarp();
-        float inv = 0.0f;
-        if (lane == 0) inv = __fdiv_rn(1.0f, chain_sum(S, np));
-        inv = __shfl_sync(0xffffffffu, inv, 0);
-        for (int t = lane; t < np; t += 32) S[t] = __fmul_rn(S[t], inv);
+        for (int t = tid; t < np; t += nthr) S[t] = libm::expf_ref(__fsub_rn(S[t], mx));
+        __syncthreads();
+        if (tid == 0) s_red[0] = __fdiv_rn(1.0f, chain_sum(S, np));
+        __syncthreads();
+        const float inv = s_red[0];
+        for (int t = tid; t < np; t += nthr) S[t] = __fmul_rn(S[t], inv);
     }
     __syncthreads();
     const bool live = tid < hd;
@@ -637,17 +644,24 @@ __global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* 
                        : *reinterpret_cast<const float*>(vt + r * row_bytes);
         };
         const float* sp = S + t0;
-        if (live) {
-            int r = 0;
-            for (; r + 4 <= nt; r += 4) {
-                const float4 s4 = *reinterpret_cast<const float4*>(sp + r);
-                const float v0 = vat(r), v1 = vat(r + 1), v2 = vat(r + 2), v3 = vat(r + 3);
-                acc = __fadd_rn(acc, __fmul_rn(s4.x, v0));
-                acc = __fadd_rn(acc, __fmul_rn(s4.y, v1));
-                acc = __fadd_rn(acc, __fmul_rn(s4.z, v2));
-                acc = __fadd_rn(acc, __fmul_rn(s4.w, v3));
+        if (live && nt == kVTile) {
+            // The tile's 32 scores and values into registers first, then the
+            // 32 dependent adds in position order.
+            float sv[kVTile], vv[kVTile];
+#pragma unroll
+            for (int q = 0; q < kVTile / 4; ++q) {
+                const float4 s4 = *reinterpret_cast<const float4*>(sp + 4 * q);
+                sv[4 * q] = s4.x;
+                sv[4 * q + 1] = s4.y;
+                sv[4 * q + 2] = s4.z;
+                sv[4 * q + 3] = s4.w;
             }
-            for (; r < nt; ++r) acc = __fadd_rn(acc, __fmul_rn(sp[r], vat(r)));
+#pragma unroll
+            for (int r = 0; r < kVTile; ++r) vv[r] = vat(r);
+#pragma unroll
+            for (int r = 0; r < kVTile; ++r) acc = __fadd_rn(acc, __fmul_rn(sv[r], vv[r]));
+        } else if (live) {
+            for (int r = 0; r < nt; ++r) acc = __fadd_rn(acc, __fmul_rn(sp[r], vat(r)));
         }
         __syncthreads();  // stage st is free again
         if (tid == 0 && j + NS < ntiles) {
