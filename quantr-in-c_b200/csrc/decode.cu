@@ -142,8 +142,7 @@ __global__ void k_embed(float* __restrict__ x, const int* __restrict__ tok, cons
 }
 
 // s = ((s + p[0]) + p[1]) + ... in fp32, left to right: the reference's
-// accumulation order.  The additions form one dependent chain; loads are
-// issued eight at a time ahead of the adds that consume them.
+// accumulation order.  The additions form one dependent chain.
 __device__ __forceinline__ float chain_sum(const float* __restrict__ p, int n, float s = 0.0f)
 {
     // 32 loads in flight, then 32 dependent adds: one load latency per 32 terms.
@@ -556,7 +555,7 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
 }
 
 // The same for steps with few KV heads (one sequence): one CTA per
-// (sequence, query head), so 8x more SMs share the work.  Warp 0 forms the
+// (sequence, query head), so 8x more SMs share the work.  The CTA forms the
 // head's softmax exactly as above; thread i owns output element i and its
 // running sum over the positions, in order; each CTA streams its KV head's
 // value rows through its own ring (the other query heads of the group read

@@ -86,6 +86,16 @@ constexpr unsigned kSuspendNs = QR_ENG_SUSPEND_NS;
 #ifndef QR_ENG_TERMS
 #define QR_ENG_TERMS 4
 #endif
+// Tile shrinking: a launch with fewer than QR_ENG_MIN_ITEMS_PCT / 100 items
+// per SM halves its tiles until it has that many.  Off by default: for the
+// small one-token programs of a decode step (2.4-13 MB of weights each) fewer,
+// larger items measured faster on B200 - the c3 step took 1.481 ms per token
+// at 2 items per SM, 1.331 at 1, 1.268 at 0.5 and 1.244 with no shrinking.
+// (A probable reason: a small launch then leaves SMs free, where the next
+// kernel of the step is resident before this one completes.)
+#ifndef QR_ENG_MIN_ITEMS_PCT
+#define QR_ENG_MIN_ITEMS_PCT 0
+#endif
 constexpr int kMaxS = QR_ENG_SLOTS, kMaxT = QR_ENG_TERMS;
 constexpr int kMaxB = 16;
 constexpr size_t kSmemMax = 227 * 1024;
@@ -598,14 +608,13 @@ size_t act_bytes_for(uint32_t type, int d, int B)
 // job table in shared memory (otherwise its single job travels inline).
 int layout_sub(SubPlan& sp, int sms, bool table)
 {
-    // Enough items to keep every SM busy: shrink tiles while there are fewer
-    // than two items per SM.
+    // Optional tile shrinking (QR_ENG_MIN_ITEMS_PCT, off by default).
     auto count_items = [&]() {
         long long t = 0;
         for (auto& J : sp.jobs) t += (J.n + J.R - 1) / J.R;
         return t;
     };
-    for (int iter = 0; iter < 16 && count_items() < 2LL * sms; ++iter) {
+    for (int iter = 0; iter < 16 && 100 * count_items() < (long long)QR_ENG_MIN_ITEMS_PCT * sms; ++iter) {
         bool changed = false;
         for (auto& J : sp.jobs) {
             const int gR = 16 / gcd_int(J.rb, 16);

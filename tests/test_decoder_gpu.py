@@ -124,6 +124,16 @@ def test_generate_matches_oracle(qr_gpu, spec):
     assert len(set(toks[0].tolist())) > 3
 
 
+@pytest.mark.parametrize("kv_type,seq_len,n_prompt", [(0, 640, 530), (1, 1024, 900)], ids=["fp32kv", "fp16kv"])
+def test_generate_long_context_value_ring(qr_gpu, kv_type, seq_len, n_prompt):
+    """One sequence at a context longer than the value ring of the
+    one-head-per-CTA softmax-V kernel holds (head_dim 128: 13 fp32 or 27 fp16
+    stages of 32 positions), so stages are refilled while the running sums
+    advance, over full tiles and a partial last tile: identical tokens."""
+    spec = dense(kv_type=kv_type, head_dim=128, n_heads=4, n_kv_heads=2, seq_len=seq_len)
+    run_generate(qr_gpu, spec, n_prompt=n_prompt, steps=6)
+
+
 def test_persistent_one_token_kernel(qr_gpu, monkeypatch):
     """The persistent single-launch step (csrc/decode_persist.cu, opt-in with
     QUANTR_DECODE_PERSIST=1): identical tokens and bit-identical logits."""
