@@ -383,6 +383,7 @@ __global__ void k_att_scores(const float* __restrict__ q, const float* __restric
 
 constexpr int kVTile = 32;       // value rows per pipeline stage
 constexpr int kVMaxStages = 64;  // most stages of the ring (Dims::vst)
+constexpr int kVHThreads = 256;  // threads of the one-head-per-CTA kernel's softmax
 
 // Score rows in shared memory: seq_len rounded up to 32, plus 4 floats, so
 // rows are 16-byte aligned and two heads' rows start in different banks.
@@ -555,8 +556,10 @@ __global__ void k_att_softmax_v(const float* __restrict__ att, const void* __res
 }
 
 // The same for steps with few KV heads (one sequence): one CTA per
-// (sequence, query head), so 8x more SMs share the work.  The CTA forms the
-// head's softmax exactly as above; thread i owns output element i and its
+// (sequence, query head), so 8x more SMs share the work.  All kVHThreads
+// threads form the head's softmax exactly as above (copies, maximum and
+// exponentials shared; one thread keeps the left-to-right sum); then only the
+// warps that own output elements stay: thread i owns output element i and its
 // running sum over the positions, in order; each CTA streams its KV head's
 // value rows through its own ring (the other query heads of the group read
 // the same rows from L2).  With head_dim a multiple of 32, warp w holds
@@ -578,6 +581,7 @@ __global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* 
     float* S = reinterpret_cast<float*>(smraw + NS * stage_bytes);  // this head's scores
     const int b = blockIdx.x / D.n_heads, h = blockIdx.x % D.n_heads, kh = h / D.kv_mul;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int vthreads = (hd + 31) / 32 * 32;  // the value loop's threads (whole warps)
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) mbar_init(&bars[i], 1);
         mbar_fence_init();
@@ -627,6 +631,7 @@ __global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* 
         for (int t = tid; t < np; t += nthr) S[t] = __fmul_rn(S[t], inv);
     }
     __syncthreads();
+    if (tid >= vthreads) return;  // the value loop synchronises its own warps only (barrier 1)
     const bool live = tid < hd;
     float acc = 0.0f;
     int issued = min(NS, ntiles);  // meaningful in thread 0
@@ -634,7 +639,7 @@ __global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* 
     for (; j < ntiles; ++j) {
         const int st = j % NS;
         if (!mbar_wait_bounded(&bars[st], (uint32_t)((j / NS) & 1), err, &s_abort)) s_abort = 1;
-        __syncthreads();
+        bar_sync_n(1, vthreads);
         if (s_abort) break;
         const int t0 = j * kVTile, nt = min(kVTile, np - t0);
         const unsigned char* vt = vring + st * stage_bytes + ES * (live ? tid : 0);
@@ -662,7 +667,7 @@ __global__ void k_att_softmax_v_head(const float* __restrict__ att, const void* 
         } else if (live) {
             for (int r = 0; r < nt; ++r) acc = __fadd_rn(acc, __fmul_rn(sp[r], vat(r)));
         }
-        __syncthreads();  // stage st is free again
+        bar_sync_n(1, vthreads);  // stage st is free again
         if (tid == 0 && j + NS < ntiles) {
             issue(j + NS);
             issued = j + NS + 1;
@@ -706,13 +711,39 @@ __global__ void __launch_bounds__(1024) k_argmax(const float* __restrict__ logit
     const float* l = logits + (long long)b * ldl;
     float bv = 0.0f;
     int bi = -1;
-    for (int i = threadIdx.x; i < vocab; i += blockDim.x) {
-        const float v = l[i];
+    // Each thread visits its logits in increasing index order (so among equal
+    // values it keeps the first); 16-byte loads, eight in flight per thread.
+    auto see = [&](float v, int i) {
         if (v == v && (bi < 0 || v > bv)) {
             bv = v;
             bi = i;
         }
+    };
+    int i0 = 0;
+    if ((reinterpret_cast<uintptr_t>(l) & 15) == 0) {
+        const int n4 = vocab >> 2;
+        const float4* l4 = reinterpret_cast<const float4*>(l);
+        for (int k0 = threadIdx.x; k0 < n4; k0 += 8 * blockDim.x) {
+            float4 v[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int k = k0 + u * blockDim.x;
+                v[u] = k < n4 ? l4[k] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int k = k0 + u * blockDim.x;
+                if (k < n4) {
+                    see(v[u].x, 4 * k);
+                    see(v[u].y, 4 * k + 1);
+                    see(v[u].z, 4 * k + 2);
+                    see(v[u].w, 4 * k + 3);
+                }
+            }
+        }
+        i0 = 4 * n4;
     }
+    for (int i = i0 + threadIdx.x; i < vocab; i += blockDim.x) see(l[i], i);
     auto better = [](float v2, int i2, float v1, int i1) {
         if (i2 < 0) return false;
         if (i1 < 0) return true;
@@ -982,7 +1013,7 @@ int enqueue_step(quantr_decoder* d, cudaStream_t s, bool with_head)
         if (e != cudaSuccess) break;
         if (att_per_head(D, device_sm_count()))
             e = launch_ex(D.kv_type ? &k_att_softmax_v_head<1> : &k_att_softmax_v_head<0>, dim3(D.B * D.n_heads),
-                          dim3(std::max(32, (D.hd + 31) / 32 * 32)), att_vh_smem(D), c, (const float*)d->att,
+                          dim3(std::max(kVHThreads, (D.hd + 31) / 32 * 32)), att_vh_smem(D), c, (const float*)d->att,
                           (const void*)d->vcache, loff, (const int*)d->pos, d->xa, device_error_word(), D, d->t_o[l]);
         else
             e = launch_ex(D.kv_type ? &k_att_softmax_v<1> : &k_att_softmax_v<0>, dim3(D.B * D.n_kv),

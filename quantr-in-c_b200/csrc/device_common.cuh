@@ -13,6 +13,12 @@ constexpr unsigned long long kWaitNs = 250000000ull;  // bounded waits: 250 ms
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+// Named barrier `id` (1..15) over `n` threads, a multiple of 32: only the
+// warps that reach it take part (barrier 0 is __syncthreads).
+__device__ __forceinline__ void bar_sync_n(int id, int n)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 
 __device__ __forceinline__ uint32_t sptr(const void* p)
 {
